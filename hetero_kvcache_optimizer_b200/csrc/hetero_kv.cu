@@ -1,0 +1,560 @@
+// libhetero_kv.so: the C ABI declared in include/hetero_kv.h.
+// Single translation unit (the device error word is shared by every kernel).
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <thread>
+
+#include "hkv_common.cuh"
+#include "hkv_decode.cuh"
+#include "hkv_quant.cuh"
+
+#define HKV_VERSION 100
+
+namespace {
+
+inline cudaStream_t S(hkv_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline hkv_status launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HKV_OK : HKV_ERR_CUDA;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+int device_sms() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> g(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+bool valid_group(int g) { return g == 32 || g == 64 || g == 128; }
+
+hkv_status check_store(const hkv_int4_store* s) {
+  if (!s) return HKV_ERR_ARG;
+  if (s->format != HKV_FMT_REF && s->format != HKV_FMT_FP16MIN) return HKV_ERR_ARG;
+  if (!valid_group(s->group)) return HKV_ERR_UNSUPPORTED;
+  if (s->page_tokens <= 0 || s->page_tokens % hkv::kTileI4) return HKV_ERR_ARG;
+  if (s->max_pages <= 0) return HKV_ERR_ARG;
+  if (!s->k.base || !s->v.base || !aligned16(s->k.base) || !aligned16(s->v.base)) return HKV_ERR_ARG;
+  const int64_t pb = hkv_side_page_bytes(s->format, s->group, s->page_tokens);
+  if (s->k.page_stride < pb || s->v.page_stride < pb) return HKV_ERR_ARG;
+  if (s->k.page_stride % 16 || s->v.page_stride % 16) return HKV_ERR_ARG;
+  if (s->len < 0) return HKV_ERR_ARG;
+  return HKV_OK;
+}
+
+hkv_status check_dense(const hkv_dense_kv* d) {
+  if (!d) return HKV_ERR_ARG;
+  if (d->dtype != HKV_DT_F16 && d->dtype != HKV_DT_BF16) return HKV_ERR_ARG;
+  if (!d->k || !d->v || !aligned16(d->k) || !aligned16(d->v)) return HKV_ERR_ARG;
+  if (d->stride_t % 8 || d->stride_h % 8 || d->stride_b % 8) return HKV_ERR_ARG;
+  if (d->capacity < 0 || d->len < 0 || d->len > d->capacity) return HKV_ERR_ARG;
+  return HKV_OK;
+}
+
+// --------------------------------------------------------------------------- decode plan
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  return std::atoi(v);
+}
+
+void plan_splits(int units, const hkv_int4_store* body, const hkv_dense_kv* dense, int* sb, int* sd) {
+  const int slots = device_sms() * 2;  // two 160-thread CTAs fit per SM (96 KB ring each)
+  const int waves = std::max(1, env_int("HKV_DECODE_WAVES", 2));
+  double bb = 0, bd = 0;
+  if (body && body->len > 0) {
+    const int ng = HKV_D / body->group;
+    const int meta = 4 * ng + (body->format == HKV_FMT_REF ? ng : 0);
+    bb = (double)body->len * 2 * (HKV_CODE_BYTES + meta);
+  }
+  if (dense && dense->len > 0) bd = (double)dense->len * 2 * HKV_D * 2;
+  const double per_cta = std::max(1.0, (double)units * (bb + bd) / ((double)slots * waves));
+  *sb = 0;
+  *sd = 0;
+  if (bb > 0) *sb = std::max(1, std::min(cdiv(body->len, hkv::kTileI4), (int)std::lround(bb / per_cta)));
+  if (bd > 0) *sd = std::max(1, std::min(cdiv(dense->len, hkv::kTileD), (int)std::lround(bd / per_cta)));
+}
+
+constexpr int kRingBytes = 96 * 1024;
+
+template <int FMT, int GROUP, typename DTy>
+hkv_status launch_decode_t(const hkv::DecodeParams& p, dim3 grid, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(hkv::decode_split_kernel<FMT, GROUP, DTy>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kRingBytes);
+  });
+  if (attr_err != cudaSuccess) return HKV_ERR_CUDA;
+  hkv::decode_split_kernel<FMT, GROUP, DTy><<<grid, hkv::kDecodeThreads, kRingBytes, st>>>(p);
+  return launch_status();
+}
+
+template <int FMT, int GROUP>
+hkv_status launch_decode_g(const hkv::DecodeParams& p, int ddt, dim3 grid, cudaStream_t st) {
+  if (ddt == HKV_DT_BF16) return launch_decode_t<FMT, GROUP, __nv_bfloat16>(p, grid, st);
+  return launch_decode_t<FMT, GROUP, __half>(p, grid, st);
+}
+
+template <int FMT>
+hkv_status launch_decode_f(const hkv::DecodeParams& p, int group, int ddt, dim3 grid, cudaStream_t st) {
+  switch (group) {
+    case 32: return launch_decode_g<FMT, 32>(p, ddt, grid, st);
+    case 64: return launch_decode_g<FMT, 64>(p, ddt, grid, st);
+    case 128: return launch_decode_g<FMT, 128>(p, ddt, grid, st);
+  }
+  return HKV_ERR_UNSUPPORTED;
+}
+
+// Runs the split kernel; leaves partials in the workspace. Returns the split count.
+hkv_status run_split(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, const hkv_int4_store* body,
+                     const hkv_dense_kv* dense, int B, int Hq, int Hkv, int D, float sm_scale, int splits_body,
+                     int splits_dense, void* workspace, size_t workspace_bytes, cudaStream_t st, int* S_out,
+                     float** po, float** pml) {
+  if (!q || (q_dtype != HKV_DT_F16 && q_dtype != HKV_DT_BF16)) return HKV_ERR_ARG;
+  if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv) return HKV_ERR_ARG;
+  const int G = Hq / Hkv;
+  if (G > 8) return HKV_ERR_UNSUPPORTED;
+  if (!body && !dense) return HKV_ERR_ARG;
+  hkv_status rc;
+  if (body && (rc = check_store(body)) != HKV_OK) return rc;
+  if (dense && (rc = check_dense(dense)) != HKV_OK) return rc;
+  if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
+  const int units = B * Hkv;
+  int sb = splits_body, sd = splits_dense;
+  if (sb <= 0 && sd <= 0) {
+    plan_splits(units, body, dense, &sb, &sd);
+  } else {
+    sb = std::max(sb, 0);
+    sd = std::max(sd, 0);
+  }
+  if (!body || body->len == 0) sb = 0;
+  if (!dense || dense->len == 0) sd = 0;
+  int chunk_b = 0, chunk_d = 0;
+  if (sb > 0) {
+    chunk_b = cdiv(cdiv(body->len, sb), hkv::kTileI4) * hkv::kTileI4;
+    sb = cdiv(body->len, chunk_b);
+  }
+  if (sd > 0) {
+    chunk_d = cdiv(cdiv(dense->len, sd), hkv::kTileD) * hkv::kTileD;
+    sd = cdiv(dense->len, chunk_d);
+  }
+  if (sb + sd == 0) {
+    // nothing to attend to: one empty split makes the kernel write a neutral
+    // partial (m = -inf, l = 0), so the merge emits zeros
+    sd = 1;
+    chunk_d = hkv::kTileD;
+  }
+  const int Stot = sb + sd;
+  const size_t need = hkv_decode_workspace_bytes(B, Hq, Hkv, D, Stot);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) return HKV_ERR_CAPACITY;
+  hkv::DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.q_dtype = q_dtype;
+  p.q_sb = q_sb;
+  p.q_sh = q_sh;
+  if (body) p.body = *body;
+  if (dense) p.dense = *dense;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = G;
+  p.qscale = static_cast<float>(static_cast<double>(sm_scale) * 1.4426950408889634);
+  p.splits_body = sb;
+  p.splits_dense = sd;
+  p.chunk_body = chunk_b;
+  p.chunk_dense = chunk_d;
+  p.ring_bytes = kRingBytes;
+  p.part_o = static_cast<float*>(workspace);
+  p.part_ml = p.part_o + (size_t)units * Stot * G * HKV_D;
+  *po = p.part_o;
+  *pml = p.part_ml;
+  *S_out = Stot;
+  const dim3 grid(Stot, units);
+  const int fmt = body ? body->format : HKV_FMT_REF;
+  const int group = body ? body->group : 32;
+  const int ddt = dense ? dense->dtype : HKV_DT_F16;
+  if (fmt == HKV_FMT_REF) return launch_decode_f<HKV_FMT_REF>(p, group, ddt, grid, st);
+  return launch_decode_f<HKV_FMT_FP16MIN>(p, group, ddt, grid, st);
+}
+
+hkv::MergeParams merge_internal(const float* po, const float* pml, int S, int Hq, int Hkv) {
+  hkv::MergeParams mp;
+  std::memset(&mp, 0, sizeof(mp));
+  const int G = Hq / Hkv;
+  mp.part_o = po;
+  mp.part_ml = pml;
+  mp.S = S;
+  mp.Hq = Hq;
+  mp.Hkv = Hkv;
+  mp.G = G;
+  mp.unit_o = (int64_t)S * G * HKV_D;
+  mp.split_o = (int64_t)G * HKV_D;
+  mp.unit_ml = (int64_t)S * G * 2;
+  mp.split_ml = (int64_t)G * 2;
+  return mp;
+}
+
+}  // namespace
+
+// =========================================================================== C ABI
+extern "C" {
+
+const char* hkv_status_str(hkv_status s) {
+  switch (s) {
+    case HKV_OK: return "HKV_OK";
+    case HKV_ERR_ARG: return "HKV_ERR_ARG: invalid argument";
+    case HKV_ERR_CUDA: return "HKV_ERR_CUDA: CUDA runtime error";
+    case HKV_ERR_TIMEOUT: return "HKV_ERR_TIMEOUT: bounded wait expired";
+    case HKV_ERR_UNSUPPORTED: return "HKV_ERR_UNSUPPORTED: unsupported configuration";
+    case HKV_ERR_CAPACITY: return "HKV_ERR_CAPACITY: destination or workspace too small";
+    case HKV_ERR_DEVICE: return "HKV_ERR_DEVICE: a kernel reported a device-side error";
+  }
+  return "HKV_ERR_UNKNOWN";
+}
+
+int hkv_version(void) { return HKV_VERSION; }
+
+hkv_status hkv_device_error(uint32_t* bits, int clear) {
+  if (!bits) return HKV_ERR_ARG;
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_hkv_dev_error, sizeof(v)) != cudaSuccess) return HKV_ERR_CUDA;
+  *bits = v;
+  if (clear) {
+    const unsigned int z = 0;
+    if (cudaMemcpyToSymbol(g_hkv_dev_error, &z, sizeof(z)) != cudaSuccess) return HKV_ERR_CUDA;
+  }
+  return HKV_OK;
+}
+
+int64_t hkv_side_page_bytes(int32_t format, int32_t group, int32_t page_tokens) {
+  if (!valid_group(group) || page_tokens <= 0) return -1;
+  const int ng = HKV_D / group;
+  const int per_tok = HKV_CODE_BYTES + 4 * ng + (format == HKV_FMT_REF ? ng : 0);
+  return (int64_t)page_tokens * per_tok;
+}
+
+// --------------------------------------------------------------------------- quantise
+hkv_status hkv_quantize_flat(const void* x, int32_t dtype, int64_t n, int32_t group, uint8_t* codes, float* scales,
+                             uint8_t* zps, hkv_stream_t stream) {
+  if (!x || !codes || !scales || !zps || n <= 0 || group <= 0) return HKV_ERR_ARG;
+  const int64_t ngroups = (n + group - 1) / group;
+  const int threads = 256;
+  const int64_t want = (ngroups + 7) / 8;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)device_sms() * 16));
+  switch (dtype) {
+    case HKV_DT_F16:
+      hkv::quantize_flat_kernel<__half><<<blocks, threads, 0, S(stream)>>>(static_cast<const __half*>(x), n, group,
+                                                                           ngroups, codes, scales, zps);
+      break;
+    case HKV_DT_BF16:
+      hkv::quantize_flat_kernel<__nv_bfloat16><<<blocks, threads, 0, S(stream)>>>(
+          static_cast<const __nv_bfloat16*>(x), n, group, ngroups, codes, scales, zps);
+      break;
+    case HKV_DT_F32:
+      hkv::quantize_flat_kernel<float><<<blocks, threads, 0, S(stream)>>>(static_cast<const float*>(x), n, group,
+                                                                          ngroups, codes, scales, zps);
+      break;
+    default: return HKV_ERR_ARG;
+  }
+  return launch_status();
+}
+
+hkv_status hkv_dequantize_flat(const uint8_t* codes, const float* scales, const uint8_t* zps, int64_t n,
+                               int32_t group, void* out, int32_t out_dtype, hkv_stream_t stream) {
+  if (!codes || !scales || !zps || !out || n <= 0 || group <= 0) return HKV_ERR_ARG;
+  const int threads = 256;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, (int64_t)device_sms() * 32));
+  switch (out_dtype) {
+    case HKV_DT_F16:
+      hkv::dequantize_flat_kernel<__half><<<blocks, threads, 0, S(stream)>>>(codes, scales, zps, n, group,
+                                                                             static_cast<__half*>(out));
+      break;
+    case HKV_DT_BF16:
+      hkv::dequantize_flat_kernel<__nv_bfloat16><<<blocks, threads, 0, S(stream)>>>(
+          codes, scales, zps, n, group, static_cast<__nv_bfloat16*>(out));
+      break;
+    case HKV_DT_F32:
+      hkv::dequantize_flat_kernel<float><<<blocks, threads, 0, S(stream)>>>(codes, scales, zps, n, group,
+                                                                            static_cast<float*>(out));
+      break;
+    default: return HKV_ERR_ARG;
+  }
+  return launch_status();
+}
+
+hkv_status hkv_quantize_pack(const void* x, int32_t dtype, int32_t B, int32_t H, int32_t T, int32_t D,
+                             int64_t stride_b, int64_t stride_h, int64_t stride_t, int32_t role,
+                             const hkv_int4_store* dst, const int32_t* dst_start, int32_t start,
+                             hkv_stream_t stream) {
+  if (!x || B <= 0 || H <= 0 || T < 0) return HKV_ERR_ARG;
+  if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
+  if (role != HKV_ROLE_K && role != HKV_ROLE_V) return HKV_ERR_ARG;
+  hkv_status rc = check_store(dst);
+  if (rc != HKV_OK) return rc;
+  if (!aligned16(x) || stride_b % 8 || stride_h % 8 || stride_t % 8) return HKV_ERR_ARG;
+  if (!dst_start && (start < 0 || (int64_t)start + T > (int64_t)dst->max_pages * dst->page_tokens))
+    return HKV_ERR_CAPACITY;
+  if (T == 0) return HKV_OK;
+  const int64_t ntok = (int64_t)B * H * T;
+  const int blocks = (int)((ntok + 15) / 16);
+  if (dtype == HKV_DT_F16) {
+    hkv::quantize_pack_kernel<__half><<<blocks, 256, 0, S(stream)>>>(static_cast<const __half*>(x), B, H, T, stride_b,
+                                                                     stride_h, stride_t, role, *dst, dst_start, start);
+  } else if (dtype == HKV_DT_BF16) {
+    hkv::quantize_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, S(stream)>>>(
+        static_cast<const __nv_bfloat16*>(x), B, H, T, stride_b, stride_h, stride_t, role, *dst, dst_start, start);
+  } else {
+    return HKV_ERR_ARG;
+  }
+  return launch_status();
+}
+
+hkv_status hkv_append_kv(const void* k_new, const void* v_new, int32_t dtype, int32_t B, int32_t H, int32_t D,
+                         int64_t stride_b, int64_t stride_h, const hkv_dense_kv* dense, int32_t sink,
+                         int32_t* dense_len, int32_t* ring_head, const hkv_int4_store* body, int32_t* body_len,
+                         hkv_stream_t stream) {
+  if (!k_new || !v_new || B <= 0 || H <= 0 || H > 32) return HKV_ERR_ARG;
+  if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
+  if (!dense_len || !ring_head || !body_len) return HKV_ERR_ARG;
+  hkv_status rc = check_dense(dense);
+  if (rc != HKV_OK) return rc;
+  if ((rc = check_store(body)) != HKV_OK) return rc;
+  if (dense->dtype != dtype) return HKV_ERR_ARG;
+  if (sink < 0 || sink > dense->capacity) return HKV_ERR_ARG;
+  if (!aligned16(k_new) || !aligned16(v_new) || stride_b % 8 || stride_h % 8) return HKV_ERR_ARG;
+  if (dtype == HKV_DT_F16) {
+    hkv::append_kv_kernel<__half><<<B, 32 * H, 0, S(stream)>>>(static_cast<const __half*>(k_new),
+                                                              static_cast<const __half*>(v_new), H, stride_b,
+                                                              stride_h, *dense, sink, dense_len, ring_head, *body,
+                                                              body_len);
+  } else if (dtype == HKV_DT_BF16) {
+    hkv::append_kv_kernel<__nv_bfloat16><<<B, 32 * H, 0, S(stream)>>>(
+        static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new), H, stride_b, stride_h,
+        *dense, sink, dense_len, ring_head, *body, body_len);
+  } else {
+    return HKV_ERR_ARG;
+  }
+  return launch_status();
+}
+
+hkv_status hkv_dequantize_pack(const hkv_int4_store* src, int32_t role, int32_t B, int32_t H, int32_t t0, int32_t T,
+                               void* out, int32_t out_dtype, hkv_stream_t stream) {
+  hkv_status rc = check_store(src);
+  if (rc != HKV_OK) return rc;
+  if (!out || B <= 0 || H <= 0 || t0 < 0 || T < 0) return HKV_ERR_ARG;
+  if ((int64_t)t0 + T > (int64_t)src->max_pages * src->page_tokens) return HKV_ERR_CAPACITY;
+  if (T == 0) return HKV_OK;
+  const int64_t ntok = (int64_t)B * H * T;
+  const int blocks = (int)((ntok + 1) / 2);
+  switch (out_dtype) {
+    case HKV_DT_F16:
+      hkv::dequantize_pack_kernel<__half><<<blocks, 256, 0, S(stream)>>>(*src, role, H, t0, T, ntok,
+                                                                        static_cast<__half*>(out));
+      break;
+    case HKV_DT_BF16:
+      hkv::dequantize_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, S(stream)>>>(*src, role, H, t0, T, ntok,
+                                                                               static_cast<__nv_bfloat16*>(out));
+      break;
+    case HKV_DT_F32:
+      hkv::dequantize_pack_kernel<float><<<blocks, 256, 0, S(stream)>>>(*src, role, H, t0, T, ntok,
+                                                                       static_cast<float*>(out));
+      break;
+    default: return HKV_ERR_ARG;
+  }
+  return launch_status();
+}
+
+hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8_t* zps, int32_t B, int32_t H,
+                          int32_t S_, int32_t group, int32_t role, const hkv_int4_store* dst, hkv_stream_t stream) {
+  hkv_status rc = check_store(dst);
+  if (rc != HKV_OK) return rc;
+  if (!codes || !scales || !zps || B <= 0 || H <= 0 || S_ < 0) return HKV_ERR_ARG;
+  if (dst->format != HKV_FMT_REF || dst->group != group) return HKV_ERR_ARG;
+  if (S_ > dst->max_pages * dst->page_tokens) return HKV_ERR_CAPACITY;
+  if (S_ == 0) return HKV_OK;
+  const int64_t ntok = (int64_t)B * H * S_;
+  hkv::repack_ref_kernel<<<(int)((ntok + 7) / 8), 256, 0, S(stream)>>>(codes, scales, zps, S_, group, role, *dst,
+                                                                       ntok);
+  return launch_status();
+}
+
+// --------------------------------------------------------------------------- decode
+size_t hkv_decode_workspace_bytes(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t splits) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || splits <= 0 || D != HKV_D) return 0;
+  return (size_t)B * Hkv * splits * (Hq / Hkv) * (HKV_D + 2) * sizeof(float);
+}
+
+hkv_status hkv_decode_plan(int32_t B, int32_t Hkv, const hkv_int4_store* body, const hkv_dense_kv* dense,
+                           int32_t* splits_body, int32_t* splits_dense) {
+  if (!splits_body || !splits_dense || B <= 0 || Hkv <= 0) return HKV_ERR_ARG;
+  int sb, sd;
+  plan_splits(B * Hkv, body, dense, &sb, &sd);
+  *splits_body = sb;
+  *splits_dense = sd;
+  return HKV_OK;
+}
+
+hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                           const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
+                           int32_t D, float sm_scale, int32_t splits_body, int32_t splits_dense, void* workspace,
+                           size_t workspace_bytes, void* out, int32_t out_dtype, int64_t out_stride_b,
+                           int64_t out_stride_h, hkv_stream_t stream) {
+  if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
+  int Stot = 0;
+  float *po = nullptr, *pml = nullptr;
+  hkv_status rc = run_split(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, splits_body,
+                            splits_dense, workspace, workspace_bytes, S(stream), &Stot, &po, &pml);
+  if (rc != HKV_OK) return rc;
+  hkv::MergeParams mp = merge_internal(po, pml, Stot, Hq, Hkv);
+  mp.out = out;
+  mp.out_dtype = out_dtype;
+  mp.out_sb = out_stride_b;
+  mp.out_sh = out_stride_h;
+  hkv::lse_merge_kernel<<<B * Hq, 128, 0, S(stream)>>>(mp);
+  return launch_status();
+}
+
+hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                   const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq,
+                                   int32_t Hkv, int32_t D, float sm_scale, int32_t splits_body, int32_t splits_dense,
+                                   void* workspace, size_t workspace_bytes, float* part_o, float* part_ml,
+                                   hkv_stream_t stream) {
+  if (!part_o || !part_ml) return HKV_ERR_ARG;
+  int Stot = 0;
+  float *po = nullptr, *pml = nullptr;
+  hkv_status rc = run_split(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, splits_body,
+                            splits_dense, workspace, workspace_bytes, S(stream), &Stot, &po, &pml);
+  if (rc != HKV_OK) return rc;
+  hkv::MergeParams mp = merge_internal(po, pml, Stot, Hq, Hkv);
+  mp.out_o = part_o;
+  mp.out_ml = part_ml;
+  hkv::lse_merge_kernel<<<B * Hq, 128, 0, S(stream)>>>(mp);
+  return launch_status();
+}
+
+hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B, int32_t Hq, int32_t D,
+                         void* out, int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                         hkv_stream_t stream) {
+  if (!part_o || !part_ml || !out || n <= 0 || B <= 0 || Hq <= 0) return HKV_ERR_ARG;
+  if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
+  if (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32) return HKV_ERR_ARG;
+  hkv::MergeParams mp;
+  std::memset(&mp, 0, sizeof(mp));
+  mp.part_o = part_o;
+  mp.part_ml = part_ml;
+  mp.S = n;
+  mp.Hq = Hq;
+  mp.Hkv = Hq;
+  mp.G = 1;
+  mp.unit_o = HKV_D;
+  mp.split_o = (int64_t)B * Hq * HKV_D;
+  mp.unit_ml = 2;
+  mp.split_ml = (int64_t)B * Hq * 2;
+  mp.out = out;
+  mp.out_dtype = out_dtype;
+  mp.out_sb = out_stride_b;
+  mp.out_sh = out_stride_h;
+  hkv::lse_merge_kernel<<<B * Hq, 128, 0, S(stream)>>>(mp);
+  return launch_status();
+}
+
+// --------------------------------------------------------------------------- prefetch
+struct hkv_prefetcher {
+  const uint8_t* host;
+  int64_t host_pages;
+  uint8_t* dev;
+  int64_t dev_pages;
+  int64_t page_bytes;
+  std::atomic<int64_t> bytes;
+};
+
+hkv_status hkv_prefetcher_create(const void* host_pool, int64_t host_pages, void* dev_pool, int64_t dev_pages,
+                                 int64_t page_bytes, hkv_prefetcher** out) {
+  if (!out || !host_pool || !dev_pool || host_pages <= 0 || dev_pages <= 0 || page_bytes <= 0) return HKV_ERR_ARG;
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, host_pool) != cudaSuccess) {
+    cudaGetLastError();
+    return HKV_ERR_ARG;
+  }
+  // the host pool must be page-locked, or every async copy silently serialises
+  if (attr.type != cudaMemoryTypeHost) return HKV_ERR_ARG;
+  hkv_prefetcher* pf = new (std::nothrow) hkv_prefetcher;
+  if (!pf) return HKV_ERR_CAPACITY;
+  pf->host = static_cast<const uint8_t*>(host_pool);
+  pf->host_pages = host_pages;
+  pf->dev = static_cast<uint8_t*>(dev_pool);
+  pf->dev_pages = dev_pages;
+  pf->page_bytes = page_bytes;
+  pf->bytes.store(0);
+  *out = pf;
+  return HKV_OK;
+}
+
+hkv_status hkv_prefetcher_destroy(hkv_prefetcher* pf) {
+  if (!pf) return HKV_ERR_ARG;
+  delete pf;
+  return HKV_OK;
+}
+
+hkv_status hkv_prefetch_submit(hkv_prefetcher* pf, const int32_t* src_pages, const int32_t* dst_slots, int32_t n,
+                               hkv_stream_t stream, hkv_event_t done) {
+  if (!pf || n < 0 || (n > 0 && (!src_pages || !dst_slots))) return HKV_ERR_ARG;
+  for (int i = 0; i < n; ++i) {
+    if (src_pages[i] < 0 || src_pages[i] >= pf->host_pages) return HKV_ERR_ARG;
+    if (dst_slots[i] < 0 || dst_slots[i] >= pf->dev_pages) return HKV_ERR_ARG;
+  }
+  int64_t total = 0;
+  int i = 0;
+  while (i < n) {
+    int run = 1;  // coalesce consecutive (src, dst) pairs into one copy
+    while (i + run < n && src_pages[i + run] == src_pages[i] + run && dst_slots[i + run] == dst_slots[i] + run) ++run;
+    const size_t bytes = (size_t)run * pf->page_bytes;
+    if (cudaMemcpyAsync(pf->dev + (int64_t)dst_slots[i] * pf->page_bytes,
+                        pf->host + (int64_t)src_pages[i] * pf->page_bytes, bytes, cudaMemcpyHostToDevice,
+                        S(stream)) != cudaSuccess)
+      return HKV_ERR_CUDA;
+    total += (int64_t)bytes;
+    i += run;
+  }
+  pf->bytes.fetch_add(total);
+  if (done && cudaEventRecord(reinterpret_cast<cudaEvent_t>(done), S(stream)) != cudaSuccess) return HKV_ERR_CUDA;
+  return HKV_OK;
+}
+
+int64_t hkv_prefetch_bytes(const hkv_prefetcher* pf) { return pf ? pf->bytes.load() : -1; }
+
+hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us) {
+  if (!ev) return HKV_ERR_ARG;
+  const auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    const cudaError_t q = cudaEventQuery(reinterpret_cast<cudaEvent_t>(ev));
+    if (q == cudaSuccess) return HKV_OK;
+    if (q != cudaErrorNotReady) {
+      cudaGetLastError();
+      return HKV_ERR_CUDA;
+    }
+    const auto el = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0);
+    if (el.count() >= timeout_us) return HKV_ERR_TIMEOUT;
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,187 @@
+"""Multi-layer tiered INT4 KV cache for decoding, built on libhetero_kv.
+
+Per layer it keeps the three zones of HeteroKVManager (src/memory/manager.py:
+sink + recent tail in fp16/bf16 HBM, the evicted body as packed INT4 pages)
+and runs one decode step as
+
+    append_kv  (new token -> recent ring; oldest ring row -> INT4 body)
+    decode     (split-KV GQA attention over body + sink/recent, LSE merge)
+
+All state (lengths, ring heads) lives on the device, so a whole multi-layer
+step can be captured once into a CUDA graph and replayed every token.
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+
+from . import _lib as L
+from . import kvstore as kv
+
+
+class TieredKVDecoder:
+    def __init__(self, num_layers: int, batch: int, q_heads: int, kv_heads: int, *,
+                 sink: int = 64, recent: int = 1024, body_capacity: int = 32768,
+                 fmt: str = "fp16min", group: int = 32, page_tokens: int = 256,
+                 kv_dtype: torch.dtype = torch.float16, out_dtype: torch.dtype = torch.float32,
+                 device="cuda", splits=(0, 0)):
+        self.num_layers, self.batch = num_layers, batch
+        self.q_heads, self.kv_heads = q_heads, kv_heads
+        self.sink, self.recent = sink, recent
+        self.fmt, self.group = fmt, group
+        self.kv_dtype, self.out_dtype = kv_dtype, out_dtype
+        self.device = torch.device(device)
+        self.splits = splits
+        self.stores: List[kv.Int4KVStore] = []
+        self.dense: List[kv.DenseKV] = []
+        for _ in range(num_layers):
+            self.stores.append(kv.Int4KVStore(batch, kv_heads, body_capacity, fmt=fmt, group=group,
+                                              page_tokens=page_tokens, device=self.device))
+            self.dense.append(kv.DenseKV(batch, kv_heads, sink + recent, dtype=kv_dtype,
+                                         device=self.device))
+        self.body_len = 0
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self._static = None
+
+    # ------------------------------------------------------------------ prefill
+    def prefill_layer(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """k, v [B, Hkv, S, 128]: the first ``sink`` tokens and the last
+        ``recent`` stay dense, the rest is quantised into the INT4 body."""
+        S = k.shape[2]
+        d, st = self.dense[layer], self.stores[layer]
+        ns = min(self.sink, S)
+        nr = min(self.recent, S - ns)
+        d.k[:, :, :ns] = k[:, :, :ns]
+        d.v[:, :, :ns] = v[:, :, :ns]
+        if nr:
+            d.k[:, :, self.sink:self.sink + nr] = k[:, :, S - nr:]
+            d.v[:, :, self.sink:self.sink + nr] = v[:, :, S - nr:]
+        nb = S - ns - nr
+        if nb:
+            kv.prefill(st, k[:, :, ns:ns + nb], v[:, :, ns:ns + nb])
+        else:
+            st.set_lengths(0)
+        d.set_lengths(ns + nr if ns == self.sink else ns)
+        d.ring_head.zero_()
+        self.body_len = nb
+
+    def set_state(self, body_len: int) -> None:
+        """Declare that every layer holds ``body_len`` INT4 tokens and a full sink + ring."""
+        for st, d in zip(self.stores, self.dense):
+            st.set_lengths(body_len)
+            d.set_lengths(self.sink + self.recent)
+            d.ring_head.zero_()
+        self.body_len = body_len
+
+    # ------------------------------------------------------------------ decode
+    def step_layer(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                   out: Optional[torch.Tensor] = None, len_hint: Optional[int] = None) -> torch.Tensor:
+        st, d = self.stores[layer], self.dense[layer]
+        kv.append_kv(k_new, v_new, d, self.sink, st)
+        hint = len_hint if len_hint is not None else self.body_len + 1
+        return kv.decode(q, st, d, out_dtype=self.out_dtype, out=out, splits=self.splits,
+                         body_len=hint, dense_len=self.sink + self.recent)
+
+    def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+             out: Optional[torch.Tensor] = None, len_hint: Optional[int] = None) -> torch.Tensor:
+        """q [L, B, Hq, 128], k_new/v_new [L, B, Hkv, 128] -> out [L, B, Hq, 128]."""
+        if out is None:
+            out = torch.empty(self.num_layers, self.batch, self.q_heads, 128, dtype=self.out_dtype,
+                              device=self.device)
+        for l in range(self.num_layers):
+            self.step_layer(l, q[l], k_new[l], v_new[l], out=out[l], len_hint=len_hint)
+        self.body_len += 1
+        return out
+
+    def decode_only(self, q: torch.Tensor, out: torch.Tensor, len_hint: Optional[int] = None) -> None:
+        """Attention of every layer without appending (cache unchanged)."""
+        hint = len_hint if len_hint is not None else self.body_len
+        for l in range(self.num_layers):
+            kv.decode(q[l], self.stores[l], self.dense[l], out_dtype=self.out_dtype, out=out[l],
+                      splits=self.splits, body_len=hint, dense_len=self.sink + self.recent)
+
+    # ------------------------------------------------------------------ CUDA graph
+    def capture(self, max_steps: int) -> None:
+        """Capture one decode step over static input/output buffers. The split
+        grid is sized for a body of ``body_len + max_steps`` tokens; device-side
+        lengths keep replays exact as the body grows."""
+        Lyr, B = self.num_layers, self.batch
+        q = torch.zeros(Lyr, B, self.q_heads, 128, dtype=torch.bfloat16, device=self.device)
+        kn = torch.zeros(Lyr, B, self.kv_heads, 128, dtype=self.kv_dtype, device=self.device)
+        vn = torch.zeros_like(kn)
+        out = torch.empty(Lyr, B, self.q_heads, 128, dtype=self.out_dtype, device=self.device)
+        hint = self.body_len + max_steps
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        g = torch.cuda.CUDAGraph()
+        # warm the library (function attributes, workspace) outside capture, on a
+        # throwaway copy of the state, then restore it
+        snap = self._snapshot()
+        with torch.cuda.stream(s):
+            for l in range(Lyr):
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+        s.synchronize()
+        self._restore(snap)
+        with torch.cuda.graph(g, stream=s):
+            for l in range(Lyr):
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.graph = g
+        self._static = (q, kn, vn, out)
+
+    def _snapshot(self):
+        return [(st.lengths.clone(), d.lengths.clone(), d.ring_head.clone(),
+                 d.k.clone(), d.v.clone()) for st, d in zip(self.stores, self.dense)]
+
+    def _restore(self, snap) -> None:
+        for (bl, dl, rh, k, v), st, d in zip(snap, self.stores, self.dense):
+            st.lengths.copy_(bl)
+            d.lengths.copy_(dl)
+            d.ring_head.copy_(rh)
+            d.k.copy_(k)
+            d.v.copy_(v)
+
+    @property
+    def static_buffers(self):
+        return self._static
+
+    def replay(self) -> None:
+        self.graph.replay()
+        self.body_len += 1
+
+    def step_host(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
+                  out_host: torch.Tensor) -> None:
+        """End-to-end step from (pinned) host buffers: H2D of the step's queries
+        and new K/V, the captured step, D2H of the attention outputs."""
+        q, kn, vn, out = self._static
+        q.copy_(q_host, non_blocking=True)
+        kn.copy_(k_host, non_blocking=True)
+        vn.copy_(v_host, non_blocking=True)
+        self.replay()
+        out_host.copy_(out, non_blocking=True)
+
+    # ------------------------------------------------------------------ accounting
+    def step_bytes(self, body_len: Optional[int] = None) -> int:
+        """Algorithmic HBM bytes of one decode step (all layers): each INT4 code,
+        meta, dense K/V byte, query and output read or written once, plus the
+        append (new token in, evicted row in, packed row out, ring row out)."""
+        nb = self.body_len if body_len is None else body_len
+        return self.num_layers * (self.layer_attn_bytes(nb + 1) + self.layer_append_bytes())
+
+    def layer_attn_bytes(self, body_tokens: int) -> int:
+        ng = 128 // self.group
+        meta = 4 * ng + (ng if self.fmt == "ref" else 0)
+        per_tok_body = 2 * (64 + meta)
+        esz = torch.tensor([], dtype=self.kv_dtype).element_size()
+        per_tok_dense = 2 * 128 * esz
+        units = self.batch * self.kv_heads
+        qo = self.batch * self.q_heads * 128 * (2 + torch.tensor([], dtype=self.out_dtype).element_size())
+        return units * (body_tokens * per_tok_body + (self.sink + self.recent) * per_tok_dense) + qo
+
+    def layer_append_bytes(self) -> int:
+        ng = 128 // self.group
+        meta = 4 * ng + (ng if self.fmt == "ref" else 0)
+        esz = torch.tensor([], dtype=self.kv_dtype).element_size()
+        units = self.batch * self.kv_heads
+        return units * 2 * (128 * esz * 3 + 64 + meta)

@@ -1,0 +1,343 @@
+"""PyTorch-facing wrappers over libhetero_kv: the packed INT4 page pool, the
+dense (sink + recent) segment, and the hot-path operations.
+
+Torch is plumbing here: it owns device memory and streams. Every computation
+runs in the CUDA kernels of libhetero_kv.so through its C ABI; tensors are
+passed as raw pointers plus sizes.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Tuple, Union
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float16: L.DT_F16, torch.bfloat16: L.DT_BF16, torch.float32: L.DT_F32}
+FORMATS = {"ref": L.FMT_REF, "fp16min": L.FMT_FP16MIN}
+HEAD_DIM = 128
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def _stream(stream: Optional[torch.cuda.Stream] = None) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError(
+                "hetero_kv kernels need CUDA tensors (HKV_ERR_UNSUPPORTED for CPU tensors: "
+                "there is no CPU fallback)")
+
+
+def side_page_bytes(fmt: str, group: int, page_tokens: int) -> int:
+    n = L.load().hkv_side_page_bytes(FORMATS[fmt], group, page_tokens)
+    if n <= 0:
+        raise ValueError(f"bad store geometry fmt={fmt} group={group} page_tokens={page_tokens}")
+    return int(n)
+
+
+class Int4KVStore:
+    """Packed INT4 body of a KV cache for B sequences x H KV heads.
+
+    Memory: one pool of pages, each page one contiguous blob [K side | V side]
+    (``2 * side_page_bytes`` bytes; 43,008 B for the reference format, group 32,
+    256-token pages), so that one host->device copy moves a whole page.
+
+    Dense mode (``num_pages=None``): unit u = b*H + h owns pages
+    [u*max_pages, (u+1)*max_pages) and no page table is used. Paged mode: the
+    caller provides ``num_pages`` and fills ``page_table`` [B*H, max_pages].
+    ``lengths`` [B] int32 on the device holds the tokens per sequence.
+    """
+
+    def __init__(self, batch: int, kv_heads: int, capacity: int, *, fmt: str = "ref",
+                 group: int = 32, page_tokens: int = 256, num_pages: Optional[int] = None,
+                 device: Union[str, torch.device] = "cuda"):
+        if fmt not in FORMATS:
+            raise ValueError(f"fmt must be one of {list(FORMATS)}")
+        if page_tokens % 128:
+            raise ValueError("page_tokens must be a multiple of 128")
+        self.batch, self.kv_heads, self.fmt, self.group = batch, kv_heads, fmt, group
+        self.page_tokens = page_tokens
+        self.max_pages = max(1, math.ceil(capacity / page_tokens))
+        self.capacity = self.max_pages * page_tokens
+        self.side_bytes = side_page_bytes(fmt, group, page_tokens)
+        self.page_bytes = 2 * self.side_bytes
+        units = batch * kv_heads
+        self.paged = num_pages is not None
+        self.num_pages = num_pages if self.paged else units * self.max_pages
+        self.device = torch.device(device)
+        self.pool = torch.empty(self.num_pages, self.page_bytes, dtype=torch.uint8, device=self.device)
+        self.page_table = (torch.full((units, self.max_pages), -1, dtype=torch.int32, device=self.device)
+                           if self.paged else None)
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=self.device)
+        self.len_hint = 0  # host-side upper bound of lengths (sizes the split-KV grid)
+
+    def struct(self, len_hint: Optional[int] = None) -> L.HkvInt4Store:
+        base = self.pool.data_ptr()
+        s = L.HkvInt4Store()
+        s.k = L.HkvInt4Side(base, self.page_bytes)
+        s.v = L.HkvInt4Side(base + self.side_bytes, self.page_bytes)
+        s.format = FORMATS[self.fmt]
+        s.group = self.group
+        s.page_tokens = self.page_tokens
+        s.max_pages = self.max_pages
+        s.page_table = self.page_table.data_ptr() if self.paged else None
+        s.lengths = self.lengths.data_ptr()
+        s.len = int(self.len_hint if len_hint is None else len_hint)
+        return s
+
+    def set_lengths(self, n: Union[int, torch.Tensor]) -> None:
+        if isinstance(n, int):
+            self.lengths.fill_(n)
+            self.len_hint = n
+        else:
+            self.lengths.copy_(n.to(torch.int32))
+            self.len_hint = int(n.max().item())
+
+    # raw views (tests / debugging)
+    def side_view(self, role: int) -> torch.Tensor:
+        off = 0 if role == L.ROLE_K else self.side_bytes
+        return self.pool[:, off:off + self.side_bytes]
+
+
+class DenseKV:
+    """Dense fp16/bf16 K/V segment [B, H, capacity, 128] (e.g. sink + recent ring)."""
+
+    def __init__(self, batch: int, kv_heads: int, capacity: int, dtype=torch.float16,
+                 device: Union[str, torch.device] = "cuda", k: Optional[torch.Tensor] = None,
+                 v: Optional[torch.Tensor] = None):
+        self.batch, self.kv_heads, self.capacity, self.dtype = batch, kv_heads, capacity, dtype
+        shape = (batch, kv_heads, capacity, HEAD_DIM)
+        self.k = k if k is not None else torch.zeros(shape, dtype=dtype, device=device)
+        self.v = v if v is not None else torch.zeros(shape, dtype=dtype, device=device)
+        assert self.k.shape == shape and self.v.shape == shape and self.k.stride() == self.v.stride()
+        assert self.k.stride(-1) == 1
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=self.k.device)
+        self.ring_head = torch.zeros(batch, dtype=torch.int32, device=self.k.device)
+        self.len_hint = 0
+
+    def struct(self, len_hint: Optional[int] = None) -> L.HkvDenseKV:
+        d = L.HkvDenseKV()
+        d.k = self.k.data_ptr()
+        d.v = self.v.data_ptr()
+        d.dtype = dtype_code(self.dtype)
+        d.capacity = self.capacity
+        d.stride_b, d.stride_h, d.stride_t = self.k.stride(0), self.k.stride(1), self.k.stride(2)
+        d.lengths = self.lengths.data_ptr()
+        d.len = int(self.len_hint if len_hint is None else len_hint)
+        return d
+
+    def set_lengths(self, n: int) -> None:
+        self.lengths.fill_(n)
+        self.len_hint = n
+
+
+# ----------------------------------------------------------------------------- workspace
+_ws_cache: dict = {}
+
+
+def workspace(nbytes: int, device: torch.device, stream=None) -> torch.Tensor:
+    """A per-(device, stream) scratch buffer for split-KV partials, grown on demand."""
+    key = (device.index, (stream or torch.cuda.current_stream(device)).cuda_stream)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
+# ----------------------------------------------------------------------------- operations
+def quantize_pack(x: torch.Tensor, store: Int4KVStore, role: int,
+                  start: Union[int, torch.Tensor] = 0, stream=None) -> None:
+    """Quantise x [B, H, T, 128] into side ``role`` of ``store`` at body slots
+    start + t (start: int, or [B] int32 device tensor). Does not touch lengths."""
+    _require_cuda(x)
+    B, H, T, D = x.shape
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    st = store.struct()
+    dst_start = start.data_ptr() if isinstance(start, torch.Tensor) else None
+    s0 = 0 if isinstance(start, torch.Tensor) else int(start)
+    L.check(L.load().hkv_quantize_pack(
+        x.data_ptr(), dtype_code(x.dtype), B, H, T, D, x.stride(0), x.stride(1), x.stride(2), role,
+        ctypes.byref(st), dst_start, s0, _stream(stream)), "hkv_quantize_pack")
+
+
+def prefill(store: Int4KVStore, k: torch.Tensor, v: torch.Tensor, start: int = 0, stream=None) -> None:
+    """Quantise a [B, H, T, 128] K/V chunk into body slots [start, start+T) and
+    set the (uniform) lengths to start + T."""
+    quantize_pack(k, store, L.ROLE_K, start, stream)
+    quantize_pack(v, store, L.ROLE_V, start, stream)
+    store.set_lengths(start + k.shape[2])
+
+
+def append_kv(k_new: torch.Tensor, v_new: torch.Tensor, dense: DenseKV, sink: int,
+              store: Int4KVStore, stream=None) -> None:
+    """One decode step of the cache: the new token enters the recent ring of
+    ``dense``; when the ring is full its oldest row is quantised into ``store``.
+    All state lives on the device (dense.lengths, dense.ring_head, store.lengths)."""
+    _require_cuda(k_new, v_new)
+    if k_new.dim() == 4:
+        k_new, v_new = k_new[:, :, 0], v_new[:, :, 0]
+    B, H, D = k_new.shape
+    ds, st = dense.struct(), store.struct()
+    L.check(L.load().hkv_append_kv(
+        k_new.data_ptr(), v_new.data_ptr(), dtype_code(k_new.dtype), B, H, D, k_new.stride(0),
+        k_new.stride(1), ctypes.byref(ds), sink, dense.lengths.data_ptr(),
+        dense.ring_head.data_ptr(), ctypes.byref(st), store.lengths.data_ptr(), _stream(stream)),
+        "hkv_append_kv")
+
+
+def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
+           sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
+           splits: Tuple[int, int] = (0, 0), out: Optional[torch.Tensor] = None,
+           body_len: Optional[int] = None, dense_len: Optional[int] = None,
+           stream=None) -> torch.Tensor:
+    """Decode attention of q [B, Hq, 128] (or [B, Hq, 1, 128]) over the INT4
+    body and/or the dense segment. Returns [B, Hq, 128] in ``out_dtype``."""
+    _require_cuda(q)
+    squeeze = q.dim() == 4
+    if squeeze:
+        q = q[:, :, 0]
+    B, Hq, D = q.shape
+    Hkv = (store or dense).kv_heads
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=out_dtype, device=q.device)
+    st = store.struct(body_len) if store is not None else None
+    ds = dense.struct(dense_len) if dense is not None else None
+    sb, sd = _plan(B, Hkv, st, ds, splits)
+    nbytes = L.load().hkv_decode_workspace_bytes(B, Hq, Hkv, D, max(1, sb + sd))
+    ws = workspace(nbytes, q.device, stream)
+    L.check(L.load().hkv_decode_attn(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1),
+        ctypes.byref(st) if st is not None else None, ctypes.byref(ds) if ds is not None else None,
+        B, Hq, Hkv, D, float(sm_scale), sb, sd, ws.data_ptr(), ws.numel(), out.data_ptr(),
+        dtype_code(out.dtype), out.stride(0), out.stride(1), _stream(stream)), "hkv_decode_attn")
+    return out[:, :, None, :] if squeeze else out
+
+
+def _plan(B, Hkv, st, ds, splits):
+    sb, sd = splits
+    if sb <= 0 and sd <= 0:
+        a, b = ctypes.c_int32(0), ctypes.c_int32(0)
+        L.check(L.load().hkv_decode_plan(B, Hkv, ctypes.byref(st) if st is not None else None,
+                                         ctypes.byref(ds) if ds is not None else None,
+                                         ctypes.byref(a), ctypes.byref(b)), "hkv_decode_plan")
+        sb, sd = a.value, b.value
+    return sb, sd
+
+
+def decode_partial(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
+                   sm_scale: Optional[float] = None, splits: Tuple[int, int] = (0, 0),
+                   out_o: Optional[torch.Tensor] = None, out_ml: Optional[torch.Tensor] = None,
+                   stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Un-normalised partial (o [B,Hq,128], (m, l) [B,Hq,2], base-2 logits) of the
+    attention over this GPU's share of the context; merge with ``lse_merge``."""
+    _require_cuda(q)
+    if q.dim() == 4:
+        q = q[:, :, 0]
+    B, Hq, D = q.shape
+    Hkv = (store or dense).kv_heads
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    out_o = out_o if out_o is not None else torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
+    out_ml = out_ml if out_ml is not None else torch.empty(B, Hq, 2, dtype=torch.float32, device=q.device)
+    st = store.struct() if store is not None else None
+    ds = dense.struct() if dense is not None else None
+    sb, sd = _plan(B, Hkv, st, ds, splits)
+    nbytes = L.load().hkv_decode_workspace_bytes(B, Hq, Hkv, D, max(1, sb + sd))
+    ws = workspace(nbytes, q.device, stream)
+    L.check(L.load().hkv_decode_attn_partial(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1),
+        ctypes.byref(st) if st is not None else None, ctypes.byref(ds) if ds is not None else None,
+        B, Hq, Hkv, D, float(sm_scale), sb, sd, ws.data_ptr(), ws.numel(), out_o.data_ptr(),
+        out_ml.data_ptr(), _stream(stream)), "hkv_decode_attn_partial")
+    return out_o, out_ml
+
+
+def lse_merge(parts_o: torch.Tensor, parts_ml: torch.Tensor, out_dtype=torch.float32,
+              out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Merge [n, B, Hq, 128] / [n, B, Hq, 2] partials into [B, Hq, 128]."""
+    _require_cuda(parts_o, parts_ml)
+    n, B, Hq, D = parts_o.shape
+    parts_o, parts_ml = parts_o.contiguous(), parts_ml.contiguous()
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=out_dtype, device=parts_o.device)
+    L.check(L.load().hkv_lse_merge(parts_o.data_ptr(), parts_ml.data_ptr(), n, B, Hq, D,
+                                   out.data_ptr(), dtype_code(out.dtype), out.stride(0),
+                                   out.stride(1), _stream(stream)), "hkv_lse_merge")
+    return out
+
+
+def dequantize_pack(store: Int4KVStore, role: int, t0: int, T: int,
+                    dtype=torch.bfloat16, stream=None) -> torch.Tensor:
+    """Dense [B, H, T, 128] copy of body tokens [t0, t0+T) of one side."""
+    out = torch.empty(store.batch, store.kv_heads, T, HEAD_DIM, dtype=dtype, device=store.device)
+    st = store.struct()
+    L.check(L.load().hkv_dequantize_pack(ctypes.byref(st), role, store.batch, store.kv_heads, t0, T,
+                                         out.data_ptr(), dtype_code(dtype), _stream(stream)),
+            "hkv_dequantize_pack")
+    return out
+
+
+def quantize_flat(x: torch.Tensor, group: int, stream=None):
+    """KVCompressor.compress contract: (codes u8 like x, scales f32 [ngroups], zps u8 [ngroups])."""
+    _require_cuda(x)
+    xc = x.contiguous()
+    n = xc.numel()
+    ng = (n + group - 1) // group
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(ng, dtype=torch.float32, device=x.device)
+    zps = torch.empty(ng, dtype=torch.uint8, device=x.device)
+    if n == 0:
+        return codes, scales, zps
+    L.check(L.load().hkv_quantize_flat(xc.data_ptr(), dtype_code(xc.dtype), n, group,
+                                       codes.data_ptr(), scales.data_ptr(), zps.data_ptr(),
+                                       _stream(stream)), "hkv_quantize_flat")
+    return codes, scales, zps
+
+
+def dequantize_flat(codes: torch.Tensor, scales: torch.Tensor, zps: torch.Tensor, group: int,
+                    dtype=torch.float16, stream=None) -> torch.Tensor:
+    _require_cuda(codes, scales, zps)
+    c = codes.contiguous()
+    s = scales.contiguous().to(torch.float32)
+    z = zps.contiguous()
+    if z.dtype != torch.uint8:
+        z = z.round().clamp(0, 255).to(torch.uint8)
+    out = torch.empty(codes.shape, dtype=dtype, device=codes.device)
+    if c.numel() == 0:
+        return out
+    L.check(L.load().hkv_dequantize_flat(c.data_ptr(), s.data_ptr(), z.data_ptr(), c.numel(), group,
+                                         out.data_ptr(), dtype_code(dtype), _stream(stream)),
+            "hkv_dequantize_flat")
+    return out
+
+
+def repack_ref(codes: torch.Tensor, scales: torch.Tensor, zps: torch.Tensor, group: int,
+               store: Int4KVStore, role: int, stream=None) -> None:
+    """Load the reference's unpacked representation (codes [B,H,S,128] u8,
+    flat f32 scales / u8 zps over groups) into body slots [0, S) of ``store``."""
+    _require_cuda(codes, scales, zps)
+    B, H, S_, D = codes.shape
+    c = codes.contiguous()
+    s = scales.contiguous().to(torch.float32)
+    z = zps.contiguous()
+    if z.dtype != torch.uint8:
+        z = z.round().clamp(0, 15).to(torch.uint8)
+    st = store.struct()
+    L.check(L.load().hkv_repack_ref(c.data_ptr(), s.data_ptr(), z.data_ptr(), B, H, S_, group, role,
+                                    ctypes.byref(st), _stream(stream)), "hkv_repack_ref")

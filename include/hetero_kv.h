@@ -1,0 +1,246 @@
+/*
+ * hetero_kv.h — C ABI of libhetero_kv.so, the B200 (sm_100a) INT4 KV-cache hot path.
+ *
+ * Three parts, each replacing a reference (kldxg123/Hetero-KVCache-Optimizer)
+ * interface on the same path:
+ *   1. quantise + nibble-pack K/V into an INT4 page pool   (replaces KVCompressor.compress,
+ *      src/quantization/kv_compressor.py:50-98, and the tail eviction in
+ *      HeteroKVManager._decode_update, src/memory/manager.py:640-664)
+ *   2. split-KV GQA decode attention straight from packed INT4 + an fp16/bf16
+ *      sink/recent segment, with a log-sum-exp merge     (replaces fused_dequant_attn_decode,
+ *      src/quantization/fused_dequant_attn.py:254-331 and its twin
+ *      src/quantization/kernels/fused_dequant_attn.py:301-368)
+ *   3. DRAM->HBM page prefetch on a side stream with per-page events
+ *                                                          (replaces AsyncPrefetcher,
+ *      src/policy/prefetcher.py:47-111, and the per-chunk .to(device) swap-in of
+ *      HeteroKVManager.swap_in_quantized, src/memory/manager.py:233-263)
+ *
+ * Conventions
+ *  - Every device pointer is caller-owned; nothing on these paths allocates.
+ *  - Every launch is stream-ordered on the cudaStream_t passed as `stream`
+ *    (NULL = legacy default stream). No call synchronises the device, except the
+ *    diagnostic hkv_device_error() and the bounded hkv_event_wait().
+ *  - Strides are in ELEMENTS; the last (head-dim) axis must be contiguous.
+ *  - Errors are integer statuses; no exception crosses the ABI.
+ *  - Kernels never trap: a bounded wait that expires, or a page id outside the
+ *    pool, sets a sticky device error word read back by hkv_device_error().
+ *
+ * Packed INT4 page layout (head_dim D = 128, G = D/group groups per token):
+ *   one page of one side (K or V) holds P tokens:
+ *     codes  [P][64]  u8   two 4-bit codes per byte, in the mma-fragment nibble
+ *                          order documented in oracle/kv_oracle.py (K per token,
+ *                          V per token pair)
+ *     scales [P][G]   f32  (HKV_FMT_REF)  or  [P][G] {f16 scale, f16 min} (HKV_FMT_FP16MIN)
+ *     zps    [P][G]   u8   (HKV_FMT_REF only)
+ *   => 84*P bytes (ref, group 32) or 80*P bytes (fp16min, group 32) per side.
+ */
+#ifndef HETERO_KV_H_
+#define HETERO_KV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default) /* the library is built with -fvisibility=hidden */
+#endif
+
+typedef int hkv_status;
+#define HKV_OK 0
+#define HKV_ERR_ARG 1          /* bad argument (shape, alignment, null pointer) */
+#define HKV_ERR_CUDA 2         /* a CUDA runtime call failed */
+#define HKV_ERR_TIMEOUT 3      /* a bounded wait expired */
+#define HKV_ERR_UNSUPPORTED 4  /* valid request this build does not implement */
+#define HKV_ERR_CAPACITY 5     /* destination too small */
+#define HKV_ERR_DEVICE 6       /* a kernel reported an error through the device error word */
+
+#define HKV_DT_F16 0
+#define HKV_DT_BF16 1
+#define HKV_DT_F32 2
+
+#define HKV_FMT_REF 0      /* fp32 scale, u8 zero-point: bit-exact with KVCompressor */
+#define HKV_FMT_FP16MIN 1  /* fp16 scale = (max-min)/15, fp16 zero = min */
+
+#define HKV_ROLE_K 0
+#define HKV_ROLE_V 1
+
+/* device error word bits (hkv_device_error) */
+#define HKV_DEVERR_TIMEOUT 1u
+#define HKV_DEVERR_BAD_PAGE 2u
+#define HKV_DEVERR_CAPACITY 4u
+
+typedef void* hkv_stream_t; /* cudaStream_t */
+typedef void* hkv_event_t;  /* cudaEvent_t */
+
+/* One side (K or V) of an INT4 page pool: page p starts at base + p*page_stride. */
+typedef struct hkv_int4_side {
+  void* base;
+  int64_t page_stride; /* bytes; multiple of 16 */
+} hkv_int4_side;
+
+/* Packed INT4 body of a KV cache. Token t of unit u = b*Hkv + h lives in page
+ *   page_table ? page_table[u*max_pages + t/P] : u*max_pages + t/P
+ * at slot t % P. A dense per-unit buffer is the special case page_table == NULL. */
+typedef struct hkv_int4_store {
+  hkv_int4_side k;
+  hkv_int4_side v;
+  int32_t format;            /* HKV_FMT_* */
+  int32_t group;             /* 32, 64 or 128 */
+  int32_t page_tokens;       /* P: multiple of 128 */
+  int32_t max_pages;         /* pages per unit (row length of page_table) */
+  const int32_t* page_table; /* [units][max_pages] int32 on device, or NULL */
+  const int32_t* lengths;    /* [B] int32 on device (tokens per sequence), or NULL */
+  int32_t len;               /* tokens when lengths == NULL; else an upper bound */
+  int32_t reserved;
+} hkv_int4_store;
+
+/* Dense fp16/bf16 K/V segment [B][Hkv][capacity][D] (e.g. sink + recent ring). */
+typedef struct hkv_dense_kv {
+  void* k;
+  void* v;
+  int32_t dtype;          /* HKV_DT_F16 or HKV_DT_BF16 */
+  int32_t capacity;       /* rows allocated per unit */
+  int64_t stride_b;       /* elements */
+  int64_t stride_h;
+  int64_t stride_t;
+  const int32_t* lengths; /* [B] int32 on device, or NULL */
+  int32_t len;            /* rows when lengths == NULL; else an upper bound */
+  int32_t reserved;
+} hkv_dense_kv;
+
+/* ---------------------------------------------------------------- misc */
+const char* hkv_status_str(hkv_status s);
+int hkv_version(void);
+/* Reads and optionally clears the sticky device error word (synchronises the device). */
+hkv_status hkv_device_error(uint32_t* bits, int clear);
+/* Bytes of one page of one side for a format/group/page size. */
+int64_t hkv_side_page_bytes(int32_t format, int32_t group, int32_t page_tokens);
+
+/* ---------------------------------------------------------------- 1. quantise
+ * Legacy flat quantiser, bit-exact with KVCompressor.compress
+ * (src/quantization/kv_compressor.py:66-98): x is a contiguous tensor of n
+ * elements (fp16/bf16/fp32), groups of `group` run over the flattened order,
+ * the last group is zero-padded. codes: n bytes (one code per byte),
+ * scales: ceil(n/group) f32, zps: ceil(n/group) u8. */
+hkv_status hkv_quantize_flat(const void* x, int32_t dtype, int64_t n, int32_t group,
+                             uint8_t* codes, float* scales, uint8_t* zps, hkv_stream_t stream);
+
+/* Legacy flat dequantiser, KVCompressor.decompress (kv_compressor.py:119-132):
+ * out[i] = (codes[i] - zps[i/group]) * scales[i/group], written as out_dtype. */
+hkv_status hkv_dequantize_flat(const uint8_t* codes, const float* scales, const uint8_t* zps,
+                               int64_t n, int32_t group, void* out, int32_t out_dtype,
+                               hkv_stream_t stream);
+
+/* Quantise x[B][H][T][128] (fp16/bf16, strides in elements) into one side of
+ * `dst` (role K or V): token t of unit (b,h) is written at body slot
+ * (dst_start ? dst_start[b] : start) + t. Per-group min/max, scale and
+ * zero-point are computed exactly as KVCompressor.compress does for a
+ * [.., 128] tensor (HKV_FMT_REF, bit-exact) or as the fp16min spec says.
+ * Replaces the compress() calls in HeteroKVManager._evict_to_dram
+ * (src/memory/manager.py:1231-1257). */
+hkv_status hkv_quantize_pack(const void* x, int32_t dtype, int32_t B, int32_t H, int32_t T,
+                             int32_t D, int64_t stride_b, int64_t stride_h, int64_t stride_t,
+                             int32_t role, const hkv_int4_store* dst, const int32_t* dst_start,
+                             int32_t start, hkv_stream_t stream);
+
+/* One decode step of the KV cache state machine of HeteroKVManager._decode_update
+ * (src/memory/manager.py:621-664), for K and V in one launch: per sequence b,
+ * if the recent ring (rows [sink, capacity) of `dense`) is full, its oldest row
+ * is quantised into the INT4 body at body_len[b] (which then advances); the
+ * new token is written into the ring. State arrays are [B] int32 on device and
+ * are updated in place: dense_len = sink + filled ring rows, ring_head = next
+ * ring slot. k_new/v_new: [B][H][128] with strides (elements). */
+hkv_status hkv_append_kv(const void* k_new, const void* v_new, int32_t dtype, int32_t B,
+                         int32_t H, int32_t D, int64_t stride_b, int64_t stride_h,
+                         const hkv_dense_kv* dense, int32_t sink, int32_t* dense_len,
+                         int32_t* ring_head, const hkv_int4_store* body, int32_t* body_len,
+                         hkv_stream_t stream);
+
+/* Dequantise tokens [t0, t0+T) of every unit of a store side to a dense
+ * [B][H][T][128] tensor (out_dtype, contiguous). Serves the BF16-returning
+ * AsyncPrefetcher.fetch_if_ready contract (src/policy/prefetcher.py:81-84). */
+hkv_status hkv_dequantize_pack(const hkv_int4_store* src, int32_t role, int32_t B, int32_t H,
+                               int32_t t0, int32_t T, void* out, int32_t out_dtype,
+                               hkv_stream_t stream);
+
+/* Convert the reference's unpacked representation (codes [B][H][S][128] u8
+ * one code per byte, scales f32 and zps u8 flat over groups of `group`) into
+ * tokens [0, S) of one side of an HKV_FMT_REF store. Used when the legacy
+ * fused_dequant_attn_decode signature is called with KVCompressor outputs. */
+hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8_t* zps,
+                          int32_t B, int32_t H, int32_t S, int32_t group, int32_t role,
+                          const hkv_int4_store* dst, hkv_stream_t stream);
+
+/* ---------------------------------------------------------------- 2. decode attention
+ * Workspace for `splits` partials per (b, kv head): units*splits*G*(D+2)*4 bytes. */
+size_t hkv_decode_workspace_bytes(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t splits);
+
+/* Split counts that fill the GPU for this shape (body, dense). */
+hkv_status hkv_decode_plan(int32_t B, int32_t Hkv, const hkv_int4_store* body,
+                           const hkv_dense_kv* dense, int32_t* splits_body,
+                           int32_t* splits_dense);
+
+/* out[b][hq][:] = softmax(q[b][hq] . K^T * sm_scale) V over the union of the
+ * INT4 body and the dense segment of KV head hq / (Hq/Hkv). q: [B][Hq][128]
+ * fp16/bf16; out: [B][Hq][128] in out_dtype (f32/f16/bf16). Either body or
+ * dense may be NULL. splits_* <= 0 picks hkv_decode_plan's values. Two
+ * launches: the split-KV kernel and the log-sum-exp merge. */
+hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b,
+                           int64_t q_stride_h, const hkv_int4_store* body,
+                           const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
+                           int32_t D, float sm_scale, int32_t splits_body,
+                           int32_t splits_dense, void* workspace, size_t workspace_bytes,
+                           void* out, int32_t out_dtype, int64_t out_stride_b,
+                           int64_t out_stride_h, hkv_stream_t stream);
+
+/* Same attention, but stops at one un-normalised partial per (b, hq):
+ * part_o [B][Hq][128] f32 = sum_t 2^(x_t - m) v_t, part_ml [B][Hq][2] f32 =
+ * (m, l) with x = score * sm_scale * log2(e) and l = sum_t 2^(x_t - m).
+ * For sequence-split attention across GPUs (partials all-gathered, then merged
+ * with hkv_lse_merge). */
+hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_stride_b,
+                                   int64_t q_stride_h, const hkv_int4_store* body,
+                                   const hkv_dense_kv* dense, int32_t B, int32_t Hq,
+                                   int32_t Hkv, int32_t D, float sm_scale,
+                                   int32_t splits_body, int32_t splits_dense, void* workspace,
+                                   size_t workspace_bytes, float* part_o, float* part_ml,
+                                   hkv_stream_t stream);
+
+/* Merge n partial sets laid out [n][B][Hq][128] / [n][B][Hq][2] (as produced by
+ * hkv_decode_attn_partial) into out [B][Hq][128] (out_dtype, strides in elements). */
+hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B,
+                         int32_t Hq, int32_t D, void* out, int32_t out_dtype,
+                         int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream);
+
+/* ---------------------------------------------------------------- 3. prefetch
+ * A prefetcher moves whole pages from a caller-owned pinned host pool to a
+ * caller-owned device pool, one cudaMemcpyAsync per run of consecutive page
+ * ids, on a caller-given side stream, and records an event when the batch has
+ * landed. Replaces AsyncPrefetcher (src/policy/prefetcher.py:21-122). */
+typedef struct hkv_prefetcher hkv_prefetcher;
+
+hkv_status hkv_prefetcher_create(const void* host_pool, int64_t host_pages, void* dev_pool,
+                                 int64_t dev_pages, int64_t page_bytes, hkv_prefetcher** out);
+hkv_status hkv_prefetcher_destroy(hkv_prefetcher* pf);
+/* Copy host pages src_pages[i] -> device slots dst_slots[i] (host int32 arrays)
+ * on `stream`, then record `done` (may be NULL) on it. */
+hkv_status hkv_prefetch_submit(hkv_prefetcher* pf, const int32_t* src_pages,
+                               const int32_t* dst_slots, int32_t n, hkv_stream_t stream,
+                               hkv_event_t done);
+/* Bytes submitted so far (for H2D GB/s accounting). */
+int64_t hkv_prefetch_bytes(const hkv_prefetcher* pf);
+/* Host-side bounded wait: polls the event until it completes or timeout_us
+ * elapses (HKV_ERR_TIMEOUT). Never blocks forever. */
+hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HETERO_KV_H_ */

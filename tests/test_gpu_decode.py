@@ -1,0 +1,238 @@
+"""GPU parity of the split-KV INT4 decode attention against the reference's
+dequant-then-SDPA (golden outputs) and the CPU oracle.
+
+Tolerance (benchmark spec): max |out - ref| <= 2e-3 * ||ref||_2 per (b, head).
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import kv_oracle as ko
+from tests.hkv_testutil import dequant_side, t16
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+K, V = 0, 1
+
+
+@pytest.fixture(scope="module")
+def hkv():
+    from hetero_kvcache_optimizer_b200 import kvstore
+    return kvstore
+
+
+def _body_store(hkv, k, v, fmt="ref", group=32, page_tokens=256, capacity=None):
+    B, H, S, _ = k.shape
+    store = hkv.Int4KVStore(B, H, capacity or max(S, 1), fmt=fmt, group=group, page_tokens=page_tokens)
+    if S:
+        hkv.prefill(store, t16(k), t16(v))
+    return store
+
+
+@pytest.mark.parametrize("splits", [(0, 0), (1, 0), (3, 0), (32, 0)])
+def test_cfg0_matches_reference(hkv, golden, splits):
+    digests, arrays = golden
+    d = digests["cfg0"]
+    k, v = ko.make_kv(d["seed"], d["B"], d["Hkv"], d["S"])
+    store = _body_store(hkv, k, v)
+    q = t16(arrays["cfg0_q"])
+    out = hkv.decode(q, store, None, splits=splits).cpu().numpy()
+    assert ko.rel_err(out, arrays["cfg0_out"]) < TOL
+
+
+def test_segmented_matches_reference(hkv, golden):
+    """sink fp16 | INT4 body | recent fp16, GQA 4 (reference golden)."""
+    digests, arrays = golden
+    d = digests["seg"]
+    B, Hkv, sink, body, recent = d["B"], d["Hkv"], d["sink"], d["body"], d["recent"]
+    k, v = ko.make_kv(d["seed"], B, Hkv, sink + body + recent)
+    store = _body_store(hkv, k[:, :, sink:sink + body], v[:, :, sink:sink + body])
+    dk = np.concatenate([k[:, :, :sink], k[:, :, sink + body:]], axis=2)
+    dv = np.concatenate([v[:, :, :sink], v[:, :, sink + body:]], axis=2)
+    dense = hkv.DenseKV(B, Hkv, sink + recent, k=t16(dk), v=t16(dv))
+    dense.set_lengths(sink + recent)
+    q = t16(arrays["seg_q"])
+    for splits in ((0, 0), (1, 1), (4, 3)):
+        out = hkv.decode(q, store, dense, splits=splits).cpu().numpy()
+        assert ko.rel_err(out, arrays["seg_out"]) < TOL, splits
+
+
+def test_legacy_per_token_matches_reference(hkv, golden):
+    """group 128 == head_dim, MHA, unpacked KVCompressor triple repacked."""
+    digests, arrays = golden
+    d = digests["legacy"]
+    B, H, S = d["B"], d["H"], d["S"]
+    k, v = ko.make_kv(d["seed"], B, H, S, outlier_channels=0)
+    store = hkv.Int4KVStore(B, H, S, fmt="ref", group=128)
+    for role, x in ((K, k), (V, v)):
+        q_, s_, z_ = hkv.quantize_flat(t16(x), 128)
+        hkv.repack_ref(q_, s_, z_, 128, store, role)
+    store.set_lengths(S)
+    q = t16(arrays["legacy_q"].astype(np.float32))
+    out = hkv.decode(q, store, None).cpu().numpy()
+    assert ko.rel_err(out, arrays["legacy_out"]) < TOL
+
+
+@pytest.mark.parametrize("fmt,group", [("ref", 32), ("ref", 64), ("ref", 128), ("fp16min", 32),
+                                       ("fp16min", 128)])
+@pytest.mark.parametrize("G", [1, 4, 7, 8])
+def test_formats_gqa_vs_oracle(hkv, fmt, group, G):
+    B, Hkv, S = 2, 2, 517
+    k, v = ko.make_kv(100 + G, B, Hkv, S)
+    store = _body_store(hkv, k, v, fmt=fmt, group=group)
+    q = ko.make_q(100 + G, B, Hkv * G).astype(np.float16).astype(np.float32)
+    ref = ko.decode_attention(q, dequant_side(store, K, S), dequant_side(store, V, S))
+    for qdt in (torch.float16, torch.bfloat16):
+        qq = t16(q, dtype=qdt)
+        qref = ref if qdt == torch.float16 else ko.decode_attention(
+            qq.float().cpu().numpy(), dequant_side(store, K, S), dequant_side(store, V, S))
+        out = hkv.decode(qq, store, None, splits=(3, 0)).cpu().numpy()
+        assert ko.rel_err(out, qref) < TOL, (qdt, fmt, group, G)
+
+
+@pytest.mark.parametrize("S", [1, 2, 15, 16, 17, 127, 128, 129, 255, 1000])
+def test_ragged_lengths_and_odd_sizes(hkv, S):
+    """Per-sequence device lengths; tails of every residue mod the tile size."""
+    B, Hkv, G = 3, 2, 4
+    k, v = ko.make_kv(S, B, Hkv, S)
+    store = _body_store(hkv, k, v)
+    lens = [S, max(1, S // 2), max(1, S - 1)]
+    store.set_lengths(torch.tensor(lens, dtype=torch.int32, device="cuda"))
+    q = ko.make_q(S, B, Hkv * G).astype(np.float16).astype(np.float32)
+    kd, vd = dequant_side(store, K, S), dequant_side(store, V, S)
+    out = hkv.decode(t16(q), store, None, splits=(2, 0)).cpu().numpy()
+    for b, L_ in enumerate(lens):
+        ref = ko.decode_attention(q[b:b + 1], kd[b:b + 1, :, :L_], vd[b:b + 1, :, :L_])
+        assert ko.rel_err(out[b:b + 1], ref) < TOL, (b, L_)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_dense_only_and_mixed_dtypes(hkv, dtype):
+    B, Hkv, G, Sd = 2, 4, 7, 200
+    k, v = ko.make_kv(3, B, Hkv, Sd)
+    dense = hkv.DenseKV(B, Hkv, 256, dtype=dtype)
+    dense.k[:, :, :Sd] = t16(k, dtype=dtype)
+    dense.v[:, :, :Sd] = t16(v, dtype=dtype)
+    dense.set_lengths(Sd)
+    q = ko.make_q(3, B, Hkv * G)
+    qt = t16(q, dtype=torch.bfloat16)
+    kd = dense.k[:, :, :Sd].float().cpu().numpy()
+    vd = dense.v[:, :, :Sd].float().cpu().numpy()
+    ref = ko.decode_attention(qt.float().cpu().numpy(), kd, vd)
+    for splits in ((0, 1), (0, 3), (0, 0)):
+        out = hkv.decode(qt, None, dense, splits=splits, out_dtype=torch.float32).cpu().numpy()
+        assert ko.rel_err(out, ref) < TOL, splits
+
+
+def test_empty_segments(hkv):
+    B, Hkv, G = 1, 2, 4
+    store = hkv.Int4KVStore(B, Hkv, 256)
+    dense = hkv.DenseKV(B, Hkv, 64)
+    q = torch.randn(B, Hkv * G, 128, device="cuda", dtype=torch.float16)
+    out = hkv.decode(q, store, dense)
+    assert torch.count_nonzero(out) == 0
+    # empty body, non-empty dense
+    dense.k[:, :, :5] = torch.randn(B, Hkv, 5, 128, device="cuda").half()
+    dense.v[:, :, :5] = torch.randn(B, Hkv, 5, 128, device="cuda").half()
+    dense.set_lengths(5)
+    out = hkv.decode(q, store, dense).cpu().numpy()
+    ref = ko.decode_attention(q.float().cpu().numpy(), dense.k[:, :, :5].float().cpu().numpy(),
+                              dense.v[:, :, :5].float().cpu().numpy())
+    assert ko.rel_err(out, ref) < TOL
+
+
+def test_deterministic(hkv):
+    k, v = ko.make_kv(8, 2, 8, 3000)
+    store = _body_store(hkv, k, v)
+    q = t16(ko.make_q(8, 2, 32))
+    a = hkv.decode(q, store, None).clone()
+    b = hkv.decode(q, store, None)
+    assert torch.equal(a, b)
+
+
+def test_paged_store_shuffled_pages(hkv):
+    B, Hkv, G, S = 2, 2, 4, 900
+    k, v = ko.make_kv(12, B, Hkv, S)
+    mp = 4
+    npages = 3 * B * Hkv * mp
+    store = hkv.Int4KVStore(B, Hkv, S, fmt="ref", group=32, page_tokens=256, num_pages=npages)
+    perm = np.random.default_rng(1).permutation(npages)[: B * Hkv * mp].reshape(B * Hkv, mp)
+    store.page_table.copy_(torch.from_numpy(perm.astype(np.int32)))
+    hkv.prefill(store, t16(k), t16(v))
+    q = ko.make_q(12, B, Hkv * G).astype(np.float16).astype(np.float32)
+    ref = ko.decode_attention(q, dequant_side(store, K, S), dequant_side(store, V, S))
+    out = hkv.decode(t16(q), store, None, splits=(3, 0)).cpu().numpy()
+    assert ko.rel_err(out, ref) < TOL
+
+
+def test_partial_and_lse_merge_equal_full(hkv):
+    """Sequence split across two 'ranks' + merge == attention over the whole context."""
+    B, Hkv, G, S = 2, 4, 4, 2000
+    k, v = ko.make_kv(13, B, Hkv, S)
+    full = _body_store(hkv, k, v)
+    a = _body_store(hkv, k[:, :, :1100], v[:, :, :1100])
+    b = _body_store(hkv, k[:, :, 1100:], v[:, :, 1100:])
+    q = t16(ko.make_q(13, B, Hkv * G))
+    ref = hkv.decode(q, full, None).cpu().numpy()
+    oa, ma = hkv.decode_partial(q, a, None)
+    ob, mb = hkv.decode_partial(q, b, None)
+    out = hkv.lse_merge(torch.stack([oa, ob]), torch.stack([ma, mb])).cpu().numpy()
+    assert ko.rel_err(out, ref) < 1e-4
+
+
+def test_append_then_decode_equals_oracle(hkv):
+    """The decode-step state machine (ring eviction -> INT4) followed by attention."""
+    B, Hkv, G, sink, ring = 2, 2, 4, 4, 60
+    S0 = 300
+    k, v = ko.make_kv(14, B, Hkv, S0 + 40)
+    store = hkv.Int4KVStore(B, Hkv, 1024)
+    dense = hkv.DenseKV(B, Hkv, sink + ring)
+    # prefill: sink | body | ring full
+    dense.k[:, :, :sink] = t16(k[:, :, :sink])
+    dense.v[:, :, :sink] = t16(v[:, :, :sink])
+    body_end = S0 - ring
+    hkv.quantize_pack(t16(k[:, :, sink:body_end]), store, K, 0)
+    hkv.quantize_pack(t16(v[:, :, sink:body_end]), store, V, 0)
+    store.set_lengths(body_end - sink)
+    dense.k[:, :, sink:] = t16(k[:, :, body_end:S0])
+    dense.v[:, :, sink:] = t16(v[:, :, body_end:S0])
+    dense.set_lengths(sink + ring)
+    for t in range(S0, S0 + 40):
+        hkv.append_kv(t16(k[:, :, t]), t16(v[:, :, t]), dense, sink, store)
+    store.len_hint = body_end - sink + 40
+    nb = body_end - sink + 40
+    q = ko.make_q(14, B, Hkv * G).astype(np.float16).astype(np.float32)
+    kd = np.concatenate([dequant_side(store, K, nb), dense.k.float().cpu().numpy()], axis=2)
+    vd = np.concatenate([dequant_side(store, V, nb), dense.v.float().cpu().numpy()], axis=2)
+    ref = ko.decode_attention(q, kd, vd)
+    out = hkv.decode(t16(q), store, dense).cpu().numpy()
+    assert ko.rel_err(out, ref) < TOL
+
+
+def test_full_size_cfg1_layer_vs_torch_fp32(hkv):
+    """Configuration-1 layer at full size (B8, Hq32/Hkv8, 31,680 INT4 + 1,088
+    fp16 tokens, fp16min), against an fp32 torch SDPA over the dequantised
+    cache (dequantize_pack is pinned bit-exact to the oracle above)."""
+    B, Hkv, G, nb, sink, recent = 8, 8, 4, 31680, 64, 1024
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    k = torch.randn(B, Hkv, nb, 128, device="cuda", generator=gen).half()
+    v = torch.randn(B, Hkv, nb, 128, device="cuda", generator=gen).half()
+    store = hkv.Int4KVStore(B, Hkv, nb, fmt="fp16min", group=32)
+    hkv.prefill(store, k, v)
+    del k, v
+    dense = hkv.DenseKV(B, Hkv, sink + recent)
+    dense.k.normal_(generator=gen)
+    dense.v.normal_(generator=gen)
+    dense.set_lengths(sink + recent)
+    q = torch.randn(B, Hkv * G, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    out = hkv.decode(q, store, dense)
+    kd = torch.cat([hkv.dequantize_pack(store, K, 0, nb, torch.float32), dense.k.float()], dim=2)
+    vd = torch.cat([hkv.dequantize_pack(store, V, 0, nb, torch.float32), dense.v.float()], dim=2)
+    kd = kd.repeat_interleave(G, dim=1)
+    vd = vd.repeat_interleave(G, dim=1)
+    s = torch.einsum("bhd,bhsd->bhs", q.float(), kd) / math.sqrt(128)
+    ref = torch.einsum("bhs,bhsd->bhd", torch.softmax(s, dim=-1), vd)
+    err = ((out - ref).abs().amax(-1) / ref.norm(dim=-1)).max().item()
+    assert err < TOL
