@@ -45,7 +45,7 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--fmt", default="fp16min", choices=["fp16min", "ref"])
     ap.add_argument("--layers", type=int, default=CFG1["layers"])
-    ap.add_argument("--splits", default="0,0", help="body,dense splits per unit (0,0 = auto)")
+    ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = two CTAs per SM)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
@@ -188,12 +188,11 @@ def main():
 
     c = CFG1
     body = c["ctx"] - c["sink"] - c["recent"]
-    sb, sd = (int(x) for x in args.splits.split(","))
     total_steps = args.warmup + args.steps + args.e2e_steps + 4
     eng = TieredKVDecoder(args.layers, c["batch"], c["q_heads"], c["kv_heads"], sink=c["sink"],
                           recent=c["recent"], body_capacity=body + total_steps + 8, fmt=args.fmt,
                           group=c["group"], kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
-                          splits=(sb, sd))
+                          ctas=args.ctas)
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     B, Hkv = c["batch"], c["kv_heads"]
     for l in range(args.layers):
@@ -311,7 +310,7 @@ def main():
                        "kv_format": args.fmt, "group": c["group"], "layers": args.layers,
                        "global_batch": c["batch"] * world, "seq_len": c["ctx"], "parallelism": f"shard{world}",
                        "l2": "no flush: per-step working set ~12 GB >> 126 MB L2",
-                       "splits": list(eng.splits)},
+                       "decode_grid": eng.ctas or "2 per SM"},
             "tokens_per_s": round(tok_s, 1),
             "pct_of_8TBs": round(100 * gbs / (NOMINAL_HBM_GBS * world), 2),
             "pct_of_measured_peak": round(100 * gbs / (peak * world), 2),

@@ -65,14 +65,12 @@ SIGNATURES = {
                               c_vp, c_vp, P_store, c_vp, c_vp]),
     "hkv_dequantize_pack": (c_i32, [P_store, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i32, c_vp]),
     "hkv_repack_ref": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, P_store, c_vp]),
-    "hkv_decode_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
-    "hkv_decode_plan": (c_i32, [c_i32, c_i32, P_store, P_dense, P_i32, P_i32]),
+    "hkv_decode_workspace_bytes": (c_sz, [P_store, P_dense, c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "hkv_decode_plan": (c_i32, [P_store, P_dense, c_i32, c_i32, c_i32, c_i32, P_i32, P_i32]),
     "hkv_decode_attn": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32, c_i32,
-                                c_i32, c_f32, c_i32, c_i32, c_vp, c_sz, c_vp, c_i32, c_i64, c_i64,
-                                c_vp]),
+                                c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_i32, c_i64, c_i64, c_vp]),
     "hkv_decode_attn_partial": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32,
-                                        c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_sz, c_vp, c_vp,
-                                        c_vp]),
+                                        c_i32, c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_vp, c_vp]),
     "hkv_lse_merge": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i32, c_i64, c_i64,
                               c_vp]),
     "hkv_prefetcher_create": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_i64, ctypes.POINTER(c_vp)]),

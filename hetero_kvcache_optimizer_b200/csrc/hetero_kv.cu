@@ -27,6 +27,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
+// The workspace starts with a region reserved for the per-unit merge counters
+// (one int32 per (sequence, KV head), at most kMaxUnits), so that calls of
+// different shapes sharing one workspace never see partials where counters live.
+constexpr int kMaxUnits = 65536;
+constexpr size_t kCounterBytes = (size_t)kMaxUnits * sizeof(int);
+
 int device_sms() {
   static std::mutex mu;
   static int cache[64] = {0};
@@ -73,97 +79,111 @@ int env_int(const char* name, int dflt) {
   return std::atoi(v);
 }
 
-void plan_splits(int units, const hkv_int4_store* body, const hkv_dense_kv* dense, int* sb, int* sd) {
-  const int slots = device_sms() * 2;  // two 160-thread CTAs fit per SM (96 KB ring each)
-  const int waves = std::max(1, env_int("HKV_DECODE_WAVES", 2));
-  double bb = 0, bd = 0;
-  if (body && body->len > 0) {
-    const int ng = HKV_D / body->group;
-    const int meta = 4 * ng + (body->format == HKV_FMT_REF ? ng : 0);
-    bb = (double)body->len * 2 * (HKV_CODE_BYTES + meta);
-  }
-  if (dense && dense->len > 0) bd = (double)dense->len * 2 * HKV_D * 2;
-  const double per_cta = std::max(1.0, (double)units * (bb + bd) / ((double)slots * waves));
-  *sb = 0;
-  *sd = 0;
-  if (bb > 0) *sb = std::max(1, std::min(cdiv(body->len, hkv::kTileI4), (int)std::lround(bb / per_cta)));
-  if (bd > 0) *sd = std::max(1, std::min(cdiv(dense->len, hkv::kTileD), (int)std::lround(bd / per_cta)));
-}
-
-constexpr int kRingBytes = 96 * 1024;
+constexpr int kDynSmemBudget = 110 * 1024;  // per CTA, two CTAs per SM
 
 template <int FMT, int GROUP, typename DTy>
-hkv_status launch_decode_t(const hkv::DecodeParams& p, dim3 grid, cudaStream_t st) {
+hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(hkv::decode_split_kernel<FMT, GROUP, DTy>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kRingBytes);
+    attr_err = cudaFuncSetAttribute(hkv::decode_kernel<FMT, GROUP, DTy>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemBudget);
   });
   if (attr_err != cudaSuccess) return HKV_ERR_CUDA;
-  hkv::decode_split_kernel<FMT, GROUP, DTy><<<grid, hkv::kDecodeThreads, kRingBytes, st>>>(p);
+  hkv::decode_kernel<FMT, GROUP, DTy><<<p.sc.C, hkv::kDecodeThreads, smem, st>>>(p);
   return launch_status();
 }
 
 template <int FMT, int GROUP>
-hkv_status launch_decode_g(const hkv::DecodeParams& p, int ddt, dim3 grid, cudaStream_t st) {
-  if (ddt == HKV_DT_BF16) return launch_decode_t<FMT, GROUP, __nv_bfloat16>(p, grid, st);
-  return launch_decode_t<FMT, GROUP, __half>(p, grid, st);
+hkv_status launch_decode_g(const hkv::DecodeParams& p, int ddt, int smem, cudaStream_t st) {
+  if (ddt == HKV_DT_BF16) return launch_decode_t<FMT, GROUP, __nv_bfloat16>(p, smem, st);
+  return launch_decode_t<FMT, GROUP, __half>(p, smem, st);
 }
 
 template <int FMT>
-hkv_status launch_decode_f(const hkv::DecodeParams& p, int group, int ddt, dim3 grid, cudaStream_t st) {
+hkv_status launch_decode_f(const hkv::DecodeParams& p, int group, int ddt, int smem, cudaStream_t st) {
   switch (group) {
-    case 32: return launch_decode_g<FMT, 32>(p, ddt, grid, st);
-    case 64: return launch_decode_g<FMT, 64>(p, ddt, grid, st);
-    case 128: return launch_decode_g<FMT, 128>(p, ddt, grid, st);
+    case 32: return launch_decode_g<FMT, 32>(p, ddt, smem, st);
+    case 64: return launch_decode_g<FMT, 64>(p, ddt, smem, st);
+    case 128: return launch_decode_g<FMT, 128>(p, ddt, smem, st);
   }
   return HKV_ERR_UNSUPPORTED;
 }
 
-// Runs the split kernel; leaves partials in the workspace. Returns the split count.
-hkv_status run_split(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, const hkv_int4_store* body,
-                     const hkv_dense_kv* dense, int B, int Hq, int Hkv, int D, float sm_scale, int splits_body,
-                     int splits_dense, void* workspace, size_t workspace_bytes, cudaStream_t st, int* S_out,
-                     float** po, float** pml) {
+// The persistent schedule: tiles per unit from the host length hints, bytes per
+// tile, grid size, and an upper bound of the partial slots per unit.
+struct Plan {
+  hkv::Sched sc;
+  int slot_bytes, nslots, meta_bytes, comb_bytes, smem;
+  size_t ws_bytes;
+};
+
+hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const hkv_dense_kv* dense, int ctas,
+                     Plan* out) {
+  const int G = Hq / Hkv;
+  hkv::Sched sc;
+  std::memset(&sc, 0, sizeof(sc));
+  sc.U = B * Hkv;
+  int group = 32, fmt = HKV_FMT_REF;
+  if (body) {
+    group = body->group;
+    fmt = body->format;
+    // with per-sequence device lengths a zero hint still gets one tile, so extra
+    // tiles can follow it when the true length is longer
+    sc.Tb = body->len > 0 ? cdiv(body->len, hkv::kTileI4) : (body->lengths ? 1 : 0);
+  }
+  if (dense) sc.Td = dense->len > 0 ? cdiv(dense->len, hkv::kTileD) : (dense->lengths ? 1 : 0);
+  if (sc.Tb + sc.Td == 0) sc.Td = 1;  // nothing to attend to: one empty tile yields zeros
+  const int ng = HKV_D / group;
+  sc.tb = (int64_t)hkv::kTileI4 * 2 * (HKV_CODE_BYTES + 4 * ng + (fmt == HKV_FMT_REF ? ng : 0));
+  sc.td = (int64_t)hkv::kTileD * 2 * HKV_D * 2;
+  sc.Ub = sc.Tb * sc.tb + sc.Td * sc.td;
+  sc.Btot = sc.Ub * sc.U;
+  const int64_t maxtile = std::max(sc.Tb ? sc.tb : 0, sc.Td ? sc.td : 0);
+  int C = ctas > 0 ? ctas : device_sms() * 2;
+  C = (int)std::max<int64_t>(1, std::min<int64_t>(C, sc.Btot / maxtile));  // every CTA owns >= 1 tile
+  sc.C = C;
+  const int64_t m = sc.Btot / C;
+  sc.S = (int)(sc.Ub / m) + 4;
+  Plan pl;
+  pl.sc = sc;
+  pl.meta_bytes = body ? hkv::meta_slot_bytes(group) : 0;
+  pl.slot_bytes = std::max(body ? hkv::i4_raw_bytes(fmt, group) : 0, dense ? hkv::dense_slot_bytes() : 0);
+  pl.slot_bytes = std::max(pl.slot_bytes, 128);
+  pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4;
+  const int avail = kDynSmemBudget - hkv::kMetaSlots * pl.meta_bytes - pl.comb_bytes;
+  pl.nslots = std::min(hkv::kMaxSlots, avail / pl.slot_bytes);
+  if (pl.nslots < 2) return HKV_ERR_UNSUPPORTED;
+  pl.smem = pl.nslots * pl.slot_bytes + hkv::kMetaSlots * pl.meta_bytes + pl.comb_bytes;
+  pl.ws_bytes = kCounterBytes + (size_t)sc.U * sc.S * G * (HKV_D + 2) * sizeof(float);
+  *out = pl;
+  return HKV_OK;
+}
+
+hkv_status check_decode_args(const void* q, int q_dtype, const hkv_int4_store* body, const hkv_dense_kv* dense,
+                             int B, int Hq, int Hkv, int D) {
   if (!q || (q_dtype != HKV_DT_F16 && q_dtype != HKV_DT_BF16)) return HKV_ERR_ARG;
   if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
   if (B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv) return HKV_ERR_ARG;
-  const int G = Hq / Hkv;
-  if (G > 8) return HKV_ERR_UNSUPPORTED;
+  if (Hq / Hkv > 8) return HKV_ERR_UNSUPPORTED;
+  if ((int64_t)B * Hkv > kMaxUnits) return HKV_ERR_UNSUPPORTED;
   if (!body && !dense) return HKV_ERR_ARG;
   hkv_status rc;
   if (body && (rc = check_store(body)) != HKV_OK) return rc;
   if (dense && (rc = check_dense(dense)) != HKV_OK) return rc;
+  return HKV_OK;
+}
+
+hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, const hkv_int4_store* body,
+                      const hkv_dense_kv* dense, int B, int Hq, int Hkv, int D, float sm_scale, int ctas,
+                      void* workspace, size_t workspace_bytes, void* out, int out_dtype, int64_t out_sb,
+                      int64_t out_sh, float* out_o, float* out_ml, cudaStream_t st) {
+  hkv_status rc = check_decode_args(q, q_dtype, body, dense, B, Hq, Hkv, D);
+  if (rc != HKV_OK) return rc;
   if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
-  const int units = B * Hkv;
-  int sb = splits_body, sd = splits_dense;
-  if (sb <= 0 && sd <= 0) {
-    plan_splits(units, body, dense, &sb, &sd);
-  } else {
-    sb = std::max(sb, 0);
-    sd = std::max(sd, 0);
-  }
-  if (!body || body->len == 0) sb = 0;
-  if (!dense || dense->len == 0) sd = 0;
-  int chunk_b = 0, chunk_d = 0;
-  if (sb > 0) {
-    chunk_b = cdiv(cdiv(body->len, sb), hkv::kTileI4) * hkv::kTileI4;
-    sb = cdiv(body->len, chunk_b);
-  }
-  if (sd > 0) {
-    chunk_d = cdiv(cdiv(dense->len, sd), hkv::kTileD) * hkv::kTileD;
-    sd = cdiv(dense->len, chunk_d);
-  }
-  if (sb + sd == 0) {
-    // nothing to attend to: one empty split makes the kernel write a neutral
-    // partial (m = -inf, l = 0), so the merge emits zeros
-    sd = 1;
-    chunk_d = hkv::kTileD;
-  }
-  const int Stot = sb + sd;
-  const size_t need = hkv_decode_workspace_bytes(B, Hq, Hkv, D, Stot);
-  if (!workspace || workspace_bytes < need || !aligned16(workspace)) return HKV_ERR_CAPACITY;
+  Plan pl;
+  if ((rc = make_plan(B, Hq, Hkv, body, dense, ctas, &pl)) != HKV_OK) return rc;
+  if (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)) return HKV_ERR_CAPACITY;
   hkv::DecodeParams p;
   std::memset(&p, 0, sizeof(p));
   p.q = q;
@@ -172,44 +192,31 @@ hkv_status run_split(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, con
   p.q_sh = q_sh;
   if (body) p.body = *body;
   if (dense) p.dense = *dense;
+  p.has_body = body != nullptr;
+  p.has_dense = dense != nullptr;
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
-  p.G = G;
+  p.G = Hq / Hkv;
   p.qscale = static_cast<float>(static_cast<double>(sm_scale) * 1.4426950408889634);
-  p.splits_body = sb;
-  p.splits_dense = sd;
-  p.chunk_body = chunk_b;
-  p.chunk_dense = chunk_d;
-  p.ring_bytes = kRingBytes;
-  p.part_o = static_cast<float*>(workspace);
-  p.part_ml = p.part_o + (size_t)units * Stot * G * HKV_D;
-  *po = p.part_o;
-  *pml = p.part_ml;
-  *S_out = Stot;
-  const dim3 grid(Stot, units);
+  p.sc = pl.sc;
+  p.slot_bytes = pl.slot_bytes;
+  p.nslots = pl.nslots;
+  p.meta_bytes = pl.meta_bytes;
+  p.counters = static_cast<int*>(workspace);
+  p.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
+  p.part_ml = p.part_o + (size_t)pl.sc.U * pl.sc.S * p.G * HKV_D;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.out_sb = out_sb;
+  p.out_sh = out_sh;
+  p.out_o = out_o;
+  p.out_ml = out_ml;
   const int fmt = body ? body->format : HKV_FMT_REF;
   const int group = body ? body->group : 32;
   const int ddt = dense ? dense->dtype : HKV_DT_F16;
-  if (fmt == HKV_FMT_REF) return launch_decode_f<HKV_FMT_REF>(p, group, ddt, grid, st);
-  return launch_decode_f<HKV_FMT_FP16MIN>(p, group, ddt, grid, st);
-}
-
-hkv::MergeParams merge_internal(const float* po, const float* pml, int S, int Hq, int Hkv) {
-  hkv::MergeParams mp;
-  std::memset(&mp, 0, sizeof(mp));
-  const int G = Hq / Hkv;
-  mp.part_o = po;
-  mp.part_ml = pml;
-  mp.S = S;
-  mp.Hq = Hq;
-  mp.Hkv = Hkv;
-  mp.G = G;
-  mp.unit_o = (int64_t)S * G * HKV_D;
-  mp.split_o = (int64_t)G * HKV_D;
-  mp.unit_ml = (int64_t)S * G * 2;
-  mp.split_ml = (int64_t)G * 2;
-  return mp;
+  if (fmt == HKV_FMT_REF) return launch_decode_f<HKV_FMT_REF>(p, group, ddt, pl.smem, st);
+  return launch_decode_f<HKV_FMT_FP16MIN>(p, group, ddt, pl.smem, st);
 }
 
 }  // namespace
@@ -397,57 +404,45 @@ hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8
 }
 
 // --------------------------------------------------------------------------- decode
-size_t hkv_decode_workspace_bytes(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t splits) {
-  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || splits <= 0 || D != HKV_D) return 0;
-  return (size_t)B * Hkv * splits * (Hq / Hkv) * (HKV_D + 2) * sizeof(float);
+size_t hkv_decode_workspace_bytes(const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq,
+                                  int32_t Hkv, int32_t D, int32_t ctas) {
+  static const uint16_t one = 0x3C00;
+  if (check_decode_args(&one, HKV_DT_F16, body, dense, B, Hq, Hkv, D) != HKV_OK) return 0;
+  Plan pl;
+  if (make_plan(B, Hq, Hkv, body, dense, ctas, &pl) != HKV_OK) return 0;
+  return pl.ws_bytes;
 }
 
-hkv_status hkv_decode_plan(int32_t B, int32_t Hkv, const hkv_int4_store* body, const hkv_dense_kv* dense,
-                           int32_t* splits_body, int32_t* splits_dense) {
-  if (!splits_body || !splits_dense || B <= 0 || Hkv <= 0) return HKV_ERR_ARG;
-  int sb, sd;
-  plan_splits(B * Hkv, body, dense, &sb, &sd);
-  *splits_body = sb;
-  *splits_dense = sd;
+hkv_status hkv_decode_plan(const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
+                           int32_t ctas, int32_t* grid, int32_t* slots_per_unit) {
+  if (!grid || !slots_per_unit) return HKV_ERR_ARG;
+  static const uint16_t one = 0x3C00;
+  hkv_status rc = check_decode_args(&one, HKV_DT_F16, body, dense, B, Hq, Hkv, HKV_D);
+  if (rc != HKV_OK) return rc;
+  Plan pl;
+  if ((rc = make_plan(B, Hq, Hkv, body, dense, ctas, &pl)) != HKV_OK) return rc;
+  *grid = pl.sc.C;
+  *slots_per_unit = pl.sc.S;
   return HKV_OK;
 }
 
 hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                            const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
-                           int32_t D, float sm_scale, int32_t splits_body, int32_t splits_dense, void* workspace,
-                           size_t workspace_bytes, void* out, int32_t out_dtype, int64_t out_stride_b,
-                           int64_t out_stride_h, hkv_stream_t stream) {
+                           int32_t D, float sm_scale, int32_t ctas, void* workspace, size_t workspace_bytes,
+                           void* out, int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                           hkv_stream_t stream) {
   if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
-  int Stot = 0;
-  float *po = nullptr, *pml = nullptr;
-  hkv_status rc = run_split(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, splits_body,
-                            splits_dense, workspace, workspace_bytes, S(stream), &Stot, &po, &pml);
-  if (rc != HKV_OK) return rc;
-  hkv::MergeParams mp = merge_internal(po, pml, Stot, Hq, Hkv);
-  mp.out = out;
-  mp.out_dtype = out_dtype;
-  mp.out_sb = out_stride_b;
-  mp.out_sh = out_stride_h;
-  hkv::lse_merge_kernel<<<B * Hq, 128, 0, S(stream)>>>(mp);
-  return launch_status();
+  return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
+                    workspace_bytes, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr, S(stream));
 }
 
 hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                                    const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq,
-                                   int32_t Hkv, int32_t D, float sm_scale, int32_t splits_body, int32_t splits_dense,
-                                   void* workspace, size_t workspace_bytes, float* part_o, float* part_ml,
-                                   hkv_stream_t stream) {
+                                   int32_t Hkv, int32_t D, float sm_scale, int32_t ctas, void* workspace,
+                                   size_t workspace_bytes, float* part_o, float* part_ml, hkv_stream_t stream) {
   if (!part_o || !part_ml) return HKV_ERR_ARG;
-  int Stot = 0;
-  float *po = nullptr, *pml = nullptr;
-  hkv_status rc = run_split(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, splits_body,
-                            splits_dense, workspace, workspace_bytes, S(stream), &Stot, &po, &pml);
-  if (rc != HKV_OK) return rc;
-  hkv::MergeParams mp = merge_internal(po, pml, Stot, Hq, Hkv);
-  mp.out_o = part_o;
-  mp.out_ml = part_ml;
-  hkv::lse_merge_kernel<<<B * Hq, 128, 0, S(stream)>>>(mp);
-  return launch_status();
+  return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
+                    workspace_bytes, nullptr, HKV_DT_F32, 0, 0, part_o, part_ml, S(stream));
 }
 
 hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B, int32_t Hq, int32_t D,
@@ -462,11 +457,7 @@ hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, i
   mp.part_ml = part_ml;
   mp.S = n;
   mp.Hq = Hq;
-  mp.Hkv = Hq;
-  mp.G = 1;
-  mp.unit_o = HKV_D;
   mp.split_o = (int64_t)B * Hq * HKV_D;
-  mp.unit_ml = 2;
   mp.split_ml = (int64_t)B * Hq * 2;
   mp.out = out;
   mp.out_dtype = out_dtype;

@@ -161,6 +161,24 @@ __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uin
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D = A * B + C with separate C (used to seed an accumulator with a bias).
+__device__ __forceinline__ void mma16816_c(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                           const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+        "f"(c[3]));
+}
+
+// Integer-only nibble -> f16 extraction (no f16 arithmetic):
+//   biased16(x)  : nibbles at bits 4..7 / 20..23 of x -> f16x2 (1024 + 16 n)
+//   biased1(x)   : nibbles at bits 0..3 / 16..19 of x -> f16x2 (1024 + n)
+// The bias is removed afterwards in fp32, folded into other terms.
+__device__ __forceinline__ uint32_t biased16(uint32_t x) { return lop3<0xEA>(x, 0x00F000F0u, 0x64006400u); }
+__device__ __forceinline__ uint32_t biased1(uint32_t x) { return lop3<0xEA>(x, 0x000F000Fu, 0x64006400u); }
+
 // 8x8 b16 matrix transpose across the warp (fragment layout in and out).
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;

@@ -25,14 +25,14 @@ class TieredKVDecoder:
                  sink: int = 64, recent: int = 1024, body_capacity: int = 32768,
                  fmt: str = "fp16min", group: int = 32, page_tokens: int = 256,
                  kv_dtype: torch.dtype = torch.float16, out_dtype: torch.dtype = torch.float32,
-                 device="cuda", splits=(0, 0)):
+                 device="cuda", ctas: int = 0):
         self.num_layers, self.batch = num_layers, batch
         self.q_heads, self.kv_heads = q_heads, kv_heads
         self.sink, self.recent = sink, recent
         self.fmt, self.group = fmt, group
         self.kv_dtype, self.out_dtype = kv_dtype, out_dtype
         self.device = torch.device(device)
-        self.splits = splits
+        self.ctas = ctas
         self.stores: List[kv.Int4KVStore] = []
         self.dense: List[kv.DenseKV] = []
         for _ in range(num_layers):
@@ -80,7 +80,7 @@ class TieredKVDecoder:
         st, d = self.stores[layer], self.dense[layer]
         kv.append_kv(k_new, v_new, d, self.sink, st)
         hint = len_hint if len_hint is not None else self.body_len + 1
-        return kv.decode(q, st, d, out_dtype=self.out_dtype, out=out, splits=self.splits,
+        return kv.decode(q, st, d, out_dtype=self.out_dtype, out=out, ctas=self.ctas,
                          body_len=hint, dense_len=self.sink + self.recent)
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
@@ -99,7 +99,7 @@ class TieredKVDecoder:
         hint = len_hint if len_hint is not None else self.body_len
         for l in range(self.num_layers):
             kv.decode(q[l], self.stores[l], self.dense[l], out_dtype=self.out_dtype, out=out[l],
-                      splits=self.splits, body_len=hint, dense_len=self.sink + self.recent)
+                      ctas=self.ctas, body_len=hint, dense_len=self.sink + self.recent)
 
     # ------------------------------------------------------------------ CUDA graph
     def capture(self, max_steps: int) -> None:

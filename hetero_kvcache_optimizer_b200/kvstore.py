@@ -148,11 +148,13 @@ _ws_cache: dict = {}
 
 
 def workspace(nbytes: int, device: torch.device, stream=None) -> torch.Tensor:
-    """A per-(device, stream) scratch buffer for split-KV partials, grown on demand."""
+    """A per-(device, stream) scratch buffer for split-KV partials, grown on
+    demand. Zeroed at allocation: its tail holds the per-unit merge counters,
+    which the decode kernel leaves at zero after every call."""
     key = (device.index, (stream or torch.cuda.current_stream(device)).cuda_stream)
     buf = _ws_cache.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _ws_cache[key] = buf
     return buf
 
@@ -201,11 +203,13 @@ def append_kv(k_new: torch.Tensor, v_new: torch.Tensor, dense: DenseKV, sink: in
 
 def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
            sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
-           splits: Tuple[int, int] = (0, 0), out: Optional[torch.Tensor] = None,
+           ctas: int = 0, out: Optional[torch.Tensor] = None,
            body_len: Optional[int] = None, dense_len: Optional[int] = None,
            stream=None) -> torch.Tensor:
     """Decode attention of q [B, Hq, 128] (or [B, Hq, 1, 128]) over the INT4
-    body and/or the dense segment. Returns [B, Hq, 128] in ``out_dtype``."""
+    body and/or the dense segment. Returns [B, Hq, 128] in ``out_dtype``.
+    ``ctas`` sets the persistent grid (0: two CTAs per SM); ``body_len`` /
+    ``dense_len`` override the host-side length hints that size the schedule."""
     _require_cuda(q)
     squeeze = q.dim() == 4
     if squeeze:
@@ -218,30 +222,35 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
         out = torch.empty(B, Hq, D, dtype=out_dtype, device=q.device)
     st = store.struct(body_len) if store is not None else None
     ds = dense.struct(dense_len) if dense is not None else None
-    sb, sd = _plan(B, Hkv, st, ds, splits)
-    nbytes = L.load().hkv_decode_workspace_bytes(B, Hq, Hkv, D, max(1, sb + sd))
+    pst = ctypes.byref(st) if st is not None else None
+    pds = ctypes.byref(ds) if ds is not None else None
+    lib = L.load()
+    nbytes = lib.hkv_decode_workspace_bytes(pst, pds, B, Hq, Hkv, D, ctas)
+    if nbytes == 0:
+        raise RuntimeError("hkv_decode_workspace_bytes: unsupported decode configuration")
     ws = workspace(nbytes, q.device, stream)
-    L.check(L.load().hkv_decode_attn(
-        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1),
-        ctypes.byref(st) if st is not None else None, ctypes.byref(ds) if ds is not None else None,
-        B, Hq, Hkv, D, float(sm_scale), sb, sd, ws.data_ptr(), ws.numel(), out.data_ptr(),
+    L.check(lib.hkv_decode_attn(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), pst, pds,
+        B, Hq, Hkv, D, float(sm_scale), ctas, ws.data_ptr(), ws.numel(), out.data_ptr(),
         dtype_code(out.dtype), out.stride(0), out.stride(1), _stream(stream)), "hkv_decode_attn")
     return out[:, :, None, :] if squeeze else out
 
 
-def _plan(B, Hkv, st, ds, splits):
-    sb, sd = splits
-    if sb <= 0 and sd <= 0:
-        a, b = ctypes.c_int32(0), ctypes.c_int32(0)
-        L.check(L.load().hkv_decode_plan(B, Hkv, ctypes.byref(st) if st is not None else None,
-                                         ctypes.byref(ds) if ds is not None else None,
-                                         ctypes.byref(a), ctypes.byref(b)), "hkv_decode_plan")
-        sb, sd = a.value, b.value
-    return sb, sd
+def decode_plan(store: Optional[Int4KVStore], dense: Optional[DenseKV], batch: int, q_heads: int,
+                ctas: int = 0) -> Tuple[int, int]:
+    """(grid, partial slots per unit) the decode kernel would use."""
+    st = store.struct() if store is not None else None
+    ds = dense.struct() if dense is not None else None
+    Hkv = (store or dense).kv_heads
+    g, s_ = ctypes.c_int32(0), ctypes.c_int32(0)
+    L.check(L.load().hkv_decode_plan(ctypes.byref(st) if st is not None else None,
+                                     ctypes.byref(ds) if ds is not None else None, batch, q_heads, Hkv,
+                                     ctas, ctypes.byref(g), ctypes.byref(s_)), "hkv_decode_plan")
+    return g.value, s_.value
 
 
 def decode_partial(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
-                   sm_scale: Optional[float] = None, splits: Tuple[int, int] = (0, 0),
+                   sm_scale: Optional[float] = None, ctas: int = 0,
                    out_o: Optional[torch.Tensor] = None, out_ml: Optional[torch.Tensor] = None,
                    stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Un-normalised partial (o [B,Hq,128], (m, l) [B,Hq,2], base-2 logits) of the
@@ -257,13 +266,16 @@ def decode_partial(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optiona
     out_ml = out_ml if out_ml is not None else torch.empty(B, Hq, 2, dtype=torch.float32, device=q.device)
     st = store.struct() if store is not None else None
     ds = dense.struct() if dense is not None else None
-    sb, sd = _plan(B, Hkv, st, ds, splits)
-    nbytes = L.load().hkv_decode_workspace_bytes(B, Hq, Hkv, D, max(1, sb + sd))
+    pst = ctypes.byref(st) if st is not None else None
+    pds = ctypes.byref(ds) if ds is not None else None
+    lib = L.load()
+    nbytes = lib.hkv_decode_workspace_bytes(pst, pds, B, Hq, Hkv, D, ctas)
+    if nbytes == 0:
+        raise RuntimeError("hkv_decode_workspace_bytes: unsupported decode configuration")
     ws = workspace(nbytes, q.device, stream)
-    L.check(L.load().hkv_decode_attn_partial(
-        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1),
-        ctypes.byref(st) if st is not None else None, ctypes.byref(ds) if ds is not None else None,
-        B, Hq, Hkv, D, float(sm_scale), sb, sd, ws.data_ptr(), ws.numel(), out_o.data_ptr(),
+    L.check(lib.hkv_decode_attn_partial(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), pst, pds,
+        B, Hq, Hkv, D, float(sm_scale), ctas, ws.data_ptr(), ws.numel(), out_o.data_ptr(),
         out_ml.data_ptr(), _stream(stream)), "hkv_decode_attn_partial")
     return out_o, out_ml
 

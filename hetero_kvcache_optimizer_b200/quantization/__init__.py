@@ -1,0 +1,6 @@
+from .kv_compressor import KVCompressor, PackedKV
+from .kernels.fused_dequant_attn import (
+    fused_dequant_attention,
+    fused_dequant_attn_decode,
+    fused_dequant_attn_forward,
+)

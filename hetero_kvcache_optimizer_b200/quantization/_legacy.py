@@ -1,0 +1,86 @@
+"""Shared adapter for the reference's fused_dequant_attn_* signatures.
+
+The reference's callers pass either per-token metadata ([B, H, S] scales and
+zero-points, group = head_dim; unified_benchmark.py:151-162) or the flat 1-D
+arrays KVCompressor.compress returns (group = any divisor of 128). Both are
+repacked on the GPU into the nibble-packed store (hkv_repack_ref), then the
+split-KV kernel runs. A packed ``Int4KVStore`` may be passed directly as
+``k_quant`` (then the other K/V arguments are ignored).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .. import _lib as L
+from .. import kvstore as kv
+
+
+def _as_4d(t: torch.Tensor, meta: bool = False) -> torch.Tensor:
+    # kernels/fused_dequant_attn.py:327-340 accepts 2-D [S, D] / 3-D [H, S, D] K/V
+    need = 3 if meta else 4
+    while t.dim() < need:
+        t = t.unsqueeze(0)
+    return t
+
+
+def build_store(k_quant, k_scales, k_zps, v_quant, v_scales, v_zps) -> kv.Int4KVStore:
+    if isinstance(k_quant, kv.Int4KVStore):
+        return k_quant
+    kq = _as_4d(k_quant)
+    vq = _as_4d(v_quant)
+    B, H, S, D = kq.shape
+    if D != 128:
+        raise ValueError("fused INT4 decode needs head_dim 128")
+    n = kq.numel()
+    ng = k_scales.numel()
+    if ng == 0 or n % ng:
+        raise ValueError("scales do not tile the K tensor into equal groups")
+    group = n // ng
+    if group not in (32, 64, 128):
+        raise ValueError(f"group size {group} unsupported (32, 64 or 128)")
+    store = kv.Int4KVStore(B, H, max(S, 1), fmt="ref", group=group, device=kq.device)
+    kv.repack_ref(kq, k_scales.reshape(-1), k_zps.reshape(-1), group, store, L.ROLE_K)
+    kv.repack_ref(vq, v_scales.reshape(-1), v_zps.reshape(-1), group, store, L.ROLE_V)
+    store.set_lengths(S)
+    return store
+
+
+def decode(q, store: kv.Int4KVStore, sm_scale: Optional[float], out_dtype) -> torch.Tensor:
+    """q [B, Hq, 1, D] -> [B, Hq, 1, D]."""
+    if q.dim() != 4 or q.shape[2] != 1:
+        raise ValueError(f"Decode expects [B,H,1,D], got {tuple(q.shape)}")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(q.shape[-1])
+    return kv.decode(q, store, None, sm_scale=sm_scale, out_dtype=out_dtype)
+
+
+def forward(q, store: kv.Int4KVStore, sm_scale: Optional[float], out_dtype) -> torch.Tensor:
+    """Multi-query (prefill-shaped) attention without a causal mask, as the
+    reference computes it (fused_dequant_attn.py:158-247). The Sq query rows of
+    each head are folded into GQA query heads (at most 8 per KV head per
+    launch), so the same split-KV kernel serves it."""
+    if q.dim() != 4:
+        raise ValueError(f"Forward expects [B,H,S,D], got {tuple(q.shape)}")
+    B, Hq, Sq, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    Hkv = store.kv_heads
+    G = Hq // Hkv
+    out = torch.empty(B, Hq, Sq, D, dtype=out_dtype, device=q.device)
+    step = max(1, 8 // G)
+    for s0 in range(0, Sq, step):
+        s1 = min(Sq, s0 + step)
+        n = s1 - s0
+        # [B, Hq, n, D] -> [B, Hkv, G, n, D] -> [B, Hkv*G*n, D]: KV head of row = row // (G*n)
+        qq = q[:, :, s0:s1].reshape(B, Hkv, G * n, D).reshape(B, Hkv * G * n, D).contiguous()
+        o = kv.decode(qq, _regroup(store, Hkv), None, sm_scale=sm_scale, out_dtype=out_dtype)
+        out[:, :, s0:s1] = o.reshape(B, Hkv, G, n, D).reshape(B, Hq, n, D)
+    return out
+
+
+def _regroup(store, Hkv):
+    assert store.kv_heads == Hkv
+    return store

@@ -175,26 +175,35 @@ hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8
                           const hkv_int4_store* dst, hkv_stream_t stream);
 
 /* ---------------------------------------------------------------- 2. decode attention
- * Workspace for `splits` partials per (b, kv head): units*splits*G*(D+2)*4 bytes. */
-size_t hkv_decode_workspace_bytes(int32_t B, int32_t Hq, int32_t Hkv, int32_t D, int32_t splits);
+ * One persistent launch: the (sequence, KV head) units' tile lists (128-token
+ * INT4 tiles, 32-token dense tiles) are cut into equal-byte ranges, one per CTA
+ * (`ctas` <= 0: two per SM); the last CTA to finish a unit merges its partials.
+ * The len fields of body/dense size the schedule; device lengths may exceed them
+ * (tokens are never dropped) at the cost of balance.
+ *
+ * Workspace: a 256 KiB region of per-unit int32 merge counters (B*Hkv <= 65536)
+ * followed by the split partials. The counter region must be zero-filled before
+ * the first call; every completed call leaves it at zero again, so one
+ * workspace serves calls of any shape. Calls that overlap on the GPU must use
+ * different workspaces. */
+size_t hkv_decode_workspace_bytes(const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B,
+                                  int32_t Hq, int32_t Hkv, int32_t D, int32_t ctas);
 
-/* Split counts that fill the GPU for this shape (body, dense). */
-hkv_status hkv_decode_plan(int32_t B, int32_t Hkv, const hkv_int4_store* body,
-                           const hkv_dense_kv* dense, int32_t* splits_body,
-                           int32_t* splits_dense);
+/* The grid and the partial slots per unit a call with these arguments uses. */
+hkv_status hkv_decode_plan(const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B,
+                           int32_t Hq, int32_t Hkv, int32_t ctas, int32_t* grid,
+                           int32_t* slots_per_unit);
 
 /* out[b][hq][:] = softmax(q[b][hq] . K^T * sm_scale) V over the union of the
- * INT4 body and the dense segment of KV head hq / (Hq/Hkv). q: [B][Hq][128]
- * fp16/bf16; out: [B][Hq][128] in out_dtype (f32/f16/bf16). Either body or
- * dense may be NULL. splits_* <= 0 picks hkv_decode_plan's values. Two
- * launches: the split-KV kernel and the log-sum-exp merge. */
+ * INT4 body and the dense segment of KV head hq / (Hq/Hkv) (G = Hq/Hkv <= 8).
+ * q: [B][Hq][128] fp16/bf16; out: [B][Hq][128] in out_dtype (f32/f16/bf16).
+ * Either body or dense may be NULL. */
 hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b,
                            int64_t q_stride_h, const hkv_int4_store* body,
                            const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
-                           int32_t D, float sm_scale, int32_t splits_body,
-                           int32_t splits_dense, void* workspace, size_t workspace_bytes,
-                           void* out, int32_t out_dtype, int64_t out_stride_b,
-                           int64_t out_stride_h, hkv_stream_t stream);
+                           int32_t D, float sm_scale, int32_t ctas, void* workspace,
+                           size_t workspace_bytes, void* out, int32_t out_dtype,
+                           int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream);
 
 /* Same attention, but stops at one un-normalised partial per (b, hq):
  * part_o [B][Hq][128] f32 = sum_t 2^(x_t - m) v_t, part_ml [B][Hq][2] f32 =
@@ -204,10 +213,9 @@ hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b,
 hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_stride_b,
                                    int64_t q_stride_h, const hkv_int4_store* body,
                                    const hkv_dense_kv* dense, int32_t B, int32_t Hq,
-                                   int32_t Hkv, int32_t D, float sm_scale,
-                                   int32_t splits_body, int32_t splits_dense, void* workspace,
-                                   size_t workspace_bytes, float* part_o, float* part_ml,
-                                   hkv_stream_t stream);
+                                   int32_t Hkv, int32_t D, float sm_scale, int32_t ctas,
+                                   void* workspace, size_t workspace_bytes, float* part_o,
+                                   float* part_ml, hkv_stream_t stream);
 
 /* Merge n partial sets laid out [n][B][Hq][128] / [n][B][Hq][2] (as produced by
  * hkv_decode_attn_partial) into out [B][Hq][128] (out_dtype, strides in elements). */

@@ -55,8 +55,8 @@ def test_host_only_entry_points(lib):
     assert so.hkv_side_page_bytes(1, 32, 256) == 256 * 80
     assert so.hkv_side_page_bytes(0, 128, 256) == 256 * 69
     assert so.hkv_side_page_bytes(0, 48, 256) == -1
-    assert so.hkv_decode_workspace_bytes(8, 32, 8, 128, 10) == 8 * 8 * 10 * 4 * 130 * 4
-    assert so.hkv_decode_workspace_bytes(8, 30, 8, 128, 10) == 0
+    # no body and no dense segment: nothing to plan
+    assert so.hkv_decode_workspace_bytes(None, None, 8, 32, 8, 128, 0) == 0
 
 
 def test_no_cpu_fallback(lib):

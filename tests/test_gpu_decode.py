@@ -31,14 +31,14 @@ def _body_store(hkv, k, v, fmt="ref", group=32, page_tokens=256, capacity=None):
     return store
 
 
-@pytest.mark.parametrize("splits", [(0, 0), (1, 0), (3, 0), (32, 0)])
-def test_cfg0_matches_reference(hkv, golden, splits):
+@pytest.mark.parametrize("ctas", [0, 1, 3, 7, 32, 500])
+def test_cfg0_matches_reference(hkv, golden, ctas):
     digests, arrays = golden
     d = digests["cfg0"]
     k, v = ko.make_kv(d["seed"], d["B"], d["Hkv"], d["S"])
     store = _body_store(hkv, k, v)
     q = t16(arrays["cfg0_q"])
-    out = hkv.decode(q, store, None, splits=splits).cpu().numpy()
+    out = hkv.decode(q, store, None, ctas=ctas).cpu().numpy()
     assert ko.rel_err(out, arrays["cfg0_out"]) < TOL
 
 
@@ -54,9 +54,9 @@ def test_segmented_matches_reference(hkv, golden):
     dense = hkv.DenseKV(B, Hkv, sink + recent, k=t16(dk), v=t16(dv))
     dense.set_lengths(sink + recent)
     q = t16(arrays["seg_q"])
-    for splits in ((0, 0), (1, 1), (4, 3)):
-        out = hkv.decode(q, store, dense, splits=splits).cpu().numpy()
-        assert ko.rel_err(out, arrays["seg_out"]) < TOL, splits
+    for ctas in (0, 1, 2, 5, 13, 64):
+        out = hkv.decode(q, store, dense, ctas=ctas).cpu().numpy()
+        assert ko.rel_err(out, arrays["seg_out"]) < TOL, ctas
 
 
 def test_legacy_per_token_matches_reference(hkv, golden):
@@ -88,7 +88,7 @@ def test_formats_gqa_vs_oracle(hkv, fmt, group, G):
         qq = t16(q, dtype=qdt)
         qref = ref if qdt == torch.float16 else ko.decode_attention(
             qq.float().cpu().numpy(), dequant_side(store, K, S), dequant_side(store, V, S))
-        out = hkv.decode(qq, store, None, splits=(3, 0)).cpu().numpy()
+        out = hkv.decode(qq, store, None, ctas=3).cpu().numpy()
         assert ko.rel_err(out, qref) < TOL, (qdt, fmt, group, G)
 
 
@@ -102,7 +102,7 @@ def test_ragged_lengths_and_odd_sizes(hkv, S):
     store.set_lengths(torch.tensor(lens, dtype=torch.int32, device="cuda"))
     q = ko.make_q(S, B, Hkv * G).astype(np.float16).astype(np.float32)
     kd, vd = dequant_side(store, K, S), dequant_side(store, V, S)
-    out = hkv.decode(t16(q), store, None, splits=(2, 0)).cpu().numpy()
+    out = hkv.decode(t16(q), store, None, ctas=5).cpu().numpy()
     for b, L_ in enumerate(lens):
         ref = ko.decode_attention(q[b:b + 1], kd[b:b + 1, :, :L_], vd[b:b + 1, :, :L_])
         assert ko.rel_err(out[b:b + 1], ref) < TOL, (b, L_)
@@ -121,9 +121,9 @@ def test_dense_only_and_mixed_dtypes(hkv, dtype):
     kd = dense.k[:, :, :Sd].float().cpu().numpy()
     vd = dense.v[:, :, :Sd].float().cpu().numpy()
     ref = ko.decode_attention(qt.float().cpu().numpy(), kd, vd)
-    for splits in ((0, 1), (0, 3), (0, 0)):
-        out = hkv.decode(qt, None, dense, splits=splits, out_dtype=torch.float32).cpu().numpy()
-        assert ko.rel_err(out, ref) < TOL, splits
+    for ctas in (1, 3, 0):
+        out = hkv.decode(qt, None, dense, ctas=ctas, out_dtype=torch.float32).cpu().numpy()
+        assert ko.rel_err(out, ref) < TOL, ctas
 
 
 def test_empty_segments(hkv):
@@ -163,7 +163,7 @@ def test_paged_store_shuffled_pages(hkv):
     hkv.prefill(store, t16(k), t16(v))
     q = ko.make_q(12, B, Hkv * G).astype(np.float16).astype(np.float32)
     ref = ko.decode_attention(q, dequant_side(store, K, S), dequant_side(store, V, S))
-    out = hkv.decode(t16(q), store, None, splits=(3, 0)).cpu().numpy()
+    out = hkv.decode(t16(q), store, None, ctas=3).cpu().numpy()
     assert ko.rel_err(out, ref) < TOL
 
 
@@ -179,7 +179,7 @@ def test_partial_and_lse_merge_equal_full(hkv):
     oa, ma = hkv.decode_partial(q, a, None)
     ob, mb = hkv.decode_partial(q, b, None)
     out = hkv.lse_merge(torch.stack([oa, ob]), torch.stack([ma, mb])).cpu().numpy()
-    assert ko.rel_err(out, ref) < 1e-4
+    assert ko.rel_err(out, ref) < 5e-4  # fp16 P rounding differs between split layouts
 
 
 def test_append_then_decode_equals_oracle(hkv):
@@ -236,3 +236,20 @@ def test_full_size_cfg1_layer_vs_torch_fp32(hkv):
     ref = torch.einsum("bhs,bhsd->bhd", torch.softmax(s, dim=-1), vd)
     err = ((out - ref).abs().amax(-1) / ref.norm(dim=-1)).max().item()
     assert err < TOL
+
+
+def test_workspace_reuse_across_shapes(hkv):
+    """One cached workspace serves calls whose split layouts differ (the merge
+    counters live in their own region and are left at zero by every call)."""
+    cases = []
+    for seed, (B, Hkv, G, S, splits) in enumerate([(1, 2, 4, 3000, 24), (4, 8, 4, 700, 2),
+                                                   (1, 2, 4, 3000, 24), (2, 4, 7, 1500, 0)]):
+        k, v = ko.make_kv(50 + seed, B, Hkv, S)
+        store = _body_store(hkv, k, v)
+        q = ko.make_q(50 + seed, B, Hkv * G).astype(np.float16).astype(np.float32)
+        ref = ko.decode_attention(q, dequant_side(store, K, S), dequant_side(store, V, S))
+        cases.append((store, q, ref, splits))
+    for _ in range(2):
+        for store, q, ref, splits in cases:
+            out = hkv.decode(t16(q), store, None, ctas=splits).cpu().numpy()
+            assert ko.rel_err(out, ref) < TOL
