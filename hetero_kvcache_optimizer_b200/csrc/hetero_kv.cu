@@ -81,6 +81,42 @@ int env_int(const char* name, int dflt) {
 
 constexpr int kDynSmemBudget = 110 * 1024;  // per CTA, two CTAs per SM
 
+// cuTensorMapEncodeTiled, fetched from the driver through the runtime (no link
+// dependency on libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// Dense K or V [B][Hkv][capacity][128] as a 4-D tensor (dim, token, head, batch);
+// boxes of 64 dims x 32 tokens land in shared memory with the 128-byte swizzle.
+hkv_status dense_map(CUtensorMap* m, const void* base, const hkv_dense_kv* d, int B, int Hkv) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return HKV_ERR_CUDA;
+  const cuuint64_t es = 2;
+  const cuuint64_t dims[4] = {HKV_D, (cuuint64_t)std::max(1, d->capacity), (cuuint64_t)Hkv, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)d->stride_t * es, (cuuint64_t)d->stride_h * es,
+                                 (cuuint64_t)d->stride_b * es};
+  const cuuint32_t box[4] = {64, (cuuint32_t)hkv::kTileD, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, d->dtype == HKV_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HKV_OK : HKV_ERR_ARG;
+}
+
 template <int FMT, int GROUP, typename DTy>
 hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st) {
   static std::once_flag once;
@@ -149,12 +185,13 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   pl.sc = sc;
   pl.meta_bytes = body ? hkv::meta_slot_bytes(group) : 0;
   pl.slot_bytes = std::max(body ? hkv::i4_raw_bytes(fmt, group) : 0, dense ? hkv::dense_slot_bytes() : 0);
-  pl.slot_bytes = std::max(pl.slot_bytes, 128);
+  pl.slot_bytes = (std::max(pl.slot_bytes, 1024) + 1023) / 1024 * 1024;  // swizzled dense halves need 1 KiB
   pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4;
-  const int avail = kDynSmemBudget - hkv::kMetaSlots * pl.meta_bytes - pl.comb_bytes;
+  const int avail = kDynSmemBudget - 1024 - hkv::kMetaSlots * pl.meta_bytes - pl.comb_bytes;
   pl.nslots = std::min(hkv::kMaxSlots, avail / pl.slot_bytes);
   if (pl.nslots < 2) return HKV_ERR_UNSUPPORTED;
-  pl.smem = pl.nslots * pl.slot_bytes + hkv::kMetaSlots * pl.meta_bytes + pl.comb_bytes;
+  // + 1 KiB so the kernel can align the ring to 1024 bytes
+  pl.smem = 1024 + pl.nslots * pl.slot_bytes + hkv::kMetaSlots * pl.meta_bytes + pl.comb_bytes;
   pl.ws_bytes = kCounterBytes + (size_t)sc.U * sc.S * G * (HKV_D + 2) * sizeof(float);
   *out = pl;
   return HKV_OK;
@@ -192,14 +229,22 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
   p.q_sh = q_sh;
   if (body) p.body = *body;
   if (dense) p.dense = *dense;
-  p.has_body = body != nullptr;
-  p.has_dense = dense != nullptr;
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
   p.G = Hq / Hkv;
   p.qscale = static_cast<float>(static_cast<double>(sm_scale) * 1.4426950408889634);
   p.sc = pl.sc;
+  if (dense) {
+    if ((rc = dense_map(&p.tmk, dense->k, dense, B, Hkv)) != HKV_OK) return rc;
+    if ((rc = dense_map(&p.tmv, dense->v, dense, B, Hkv)) != HKV_OK) return rc;
+  }
+  p.page_shift = -1;
+  if (body && (body->page_tokens & (body->page_tokens - 1)) == 0) {
+    int sh = 0;
+    while ((1 << sh) < body->page_tokens) ++sh;
+    p.page_shift = sh;
+  }
   p.slot_bytes = pl.slot_bytes;
   p.nslots = pl.nslots;
   p.meta_bytes = pl.meta_bytes;

@@ -5,21 +5,23 @@
 // 128-token INT4 body tiles, then 32-token dense tiles. Tiles are weighted by
 // their HBM bytes and the whole list (all units) is cut into one contiguous,
 // equal-byte range per CTA of a persistent grid (2 CTAs per SM). A CTA's range
-// covers pieces: runs of tiles of one (unit, segment). Each piece ends in an
-// un-normalised partial (m, l, O) for the unit's G query heads; the CTA that
-// delivers a unit's last partial merges them (log-sum-exp) into the output.
+// is a short sequence of pieces: runs of tiles of one (unit, segment). Each
+// piece ends in an un-normalised partial (m, l, O) for the unit's G query
+// heads; the CTA that delivers a unit's last partial merges them.
 //
 // Pipeline. Warp 4 is the producer. It streams tiles into a shared-memory ring
-// with 1-D bulk async copies (TMA engine, no multicast) that complete on
-// mbarriers, and expands each INT4 tile's group metadata (f16 or u8) into an
-// fp32 / f16x2 form the consumers use directly. Warps 0-3 consume with
-// m16n8k16 tensor-core MMAs (N = 8 query heads, G <= 8 used):
+// with the TMA engine (no multicast): INT4 tiles as 1-D bulk copies of their
+// code and metadata blocks, dense tiles as 2-D tensor copies with 128-byte
+// swizzle. It then expands each INT4 tile's group metadata (f16 or u8) into an
+// fp32 / f16x2 form, and zeroes what lies past the sequence length, before
+// releasing the tile to warps 0-3. Those compute with m16n8k16 tensor-core MMAs
+// (N = 8 query heads, G <= 8 used):
 //   S^T[tok][head] = K[tok][:] . Q^T      (M = 16 tokens, K = dims)
 //   O^T[dim][head] += V^T[dim][tok] . P^T (M = 16 dims,   K = tokens)
-// K and V fragments come straight from the packed nibbles (the page format's
-// nibble order is the fragment order) with integer-only ops: a nibble OR-ed
-// into the mantissa of 1024.0h is the exact f16 value 1024 + n (or 1024 + 16 n
-// for a high nibble). The biases are folded away in fp32:
+// INT4 K and V fragments come straight from the packed nibbles (the page
+// format's nibble order is the fragment order): a nibble OR-ed into the
+// mantissa of 1024.0h is the exact f16 value 1024 + n (or 1024 + 16 n for a
+// high nibble).
 //   K: half of each k-tile is (1024 + n), half (1024 + 16 n) against Q/16, and
 //      the accumulator starts at -1024 * sum(Q), so it ends at sum(n Q):
 //      score = sum_g s_g * acc_g + b_g * sum(Q_g)        (b = -z*s or min)
@@ -36,35 +38,37 @@ namespace hkv {
 constexpr int kConsumerWarps = 4;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kDecodeThreads = kConsumerThreads + 32;
-constexpr int kTileI4 = 128;    // tokens per INT4 tile (32 per consumer warp)
-constexpr int kTileD = 32;      // tokens per dense tile (8 per consumer warp)
-constexpr int kRowPitch = 272;  // bytes per dense row in shared memory (256 + 16: conflict-free ldmatrix)
+constexpr int kTileI4 = 128;  // tokens per INT4 tile (32 per consumer warp)
+constexpr int kTileD = 32;    // tokens per dense tile (8 per consumer warp)
 constexpr int kMaxSlots = 6;
 constexpr int kMetaSlots = 2;
 constexpr float kLazyRescale = 8.0f;
+constexpr int kDenseHalf = kTileD * 128;  // bytes of one 64-dim half of 32 dense rows (swizzled)
 
 // Equal-byte partition of the tile list over the persistent grid.
 struct Sched {
-  int U;          // units (B * Hkv)
-  int Tb, Td;     // body / dense tiles per unit (from the host-side length hints)
-  int C;          // CTAs
-  int S;          // partial slots per unit in the workspace
-  int64_t tb, td; // bytes per body / dense tile
-  int64_t Ub;     // bytes per unit
-  int64_t Btot;   // bytes in total
+  int U;           // units (B * Hkv)
+  int Tb, Td;      // body / dense tiles per unit (from the host-side length hints)
+  int C;           // CTAs
+  int S;           // partial slots per unit in the workspace
+  int64_t tb, td;  // bytes per body / dense tile
+  int64_t Ub;      // bytes per unit
+  int64_t Btot;    // bytes in total
 };
 
 struct DecodeParams {
+  CUtensorMap tmk;  // dense K [B][Hkv][cap][128] as 4-D (dim, token, head, batch), box 64 x 32
+  CUtensorMap tmv;
   const void* q;
   int q_dtype;
   int64_t q_sb, q_sh;
   hkv_int4_store body;
   hkv_dense_kv dense;
-  int has_body, has_dense;
   int B, Hq, Hkv, G;
   float qscale;  // sm_scale * log2(e)
   Sched sc;
   int slot_bytes, nslots, meta_bytes;
+  int page_shift;  // log2(page_tokens) when a power of two, else -1
   float* part_o;   // [U][S][G][128]  un-normalised partial outputs
   float* part_ml;  // [U][S][G][2]    (m, l), base-2 logits
   int* counters;   // [U]             zero before first use, self-resetting
@@ -79,11 +83,11 @@ __host__ __device__ constexpr int i4_raw_bytes(int fmt, int group) {
   return 2 * kTileI4 * HKV_CODE_BYTES + 2 * kTileI4 * 4 * (HKV_D / group) +
          (fmt == HKV_FMT_REF ? 2 * kTileI4 * (HKV_D / group) : 0);
 }
-__host__ __device__ constexpr int dense_slot_bytes() { return 2 * kTileD * kRowPitch; }
+__host__ __device__ constexpr int dense_slot_bytes() { return 4 * kDenseHalf; }
 // expanded metadata of one INT4 tile: K scale f32, K bias f32, V scale f16x2 (s,s), V bias f32
 __host__ __device__ constexpr int meta_slot_bytes(int group) { return kTileI4 * (HKV_D / group) * 16; }
 
-// ---------------------------------------------------------------- schedule arithmetic
+// ---------------------------------------------------------------- schedule arithmetic (per piece, not per tile)
 __device__ __forceinline__ int64_t cta_begin(const Sched& s, int c) { return (int64_t)c * s.Btot / s.C; }
 __device__ __forceinline__ int64_t tile_byte(const Sched& s, int u, int seg, int k) {
   return (int64_t)u * s.Ub + (seg == 0 ? (int64_t)k * s.tb : (int64_t)s.Tb * s.tb + (int64_t)k * s.td);
@@ -94,83 +98,78 @@ __device__ __forceinline__ int owner_of(const Sched& s, int64_t x) {
   return c;
 }
 
-struct TileRef {
-  int u, seg, k;
+// A piece: tiles [k0, k1) of segment seg of unit u (k1 includes tiles past the
+// hint when the true length needs them); tiles at or past kd hold no tokens.
+struct Piece {
+  int u, seg, k0, k1, kd, len;
   bool valid;
 };
 
-// First tile whose byte start lies in [cta_begin(c), cta_begin(c+1)).
-__device__ __forceinline__ TileRef first_tile(const Sched& s, int c) {
-  const int64_t x = cta_begin(s, c), end = cta_begin(s, c + 1);
-  TileRef t;
-  t.u = (int)(x / s.Ub);
-  const int64_t r = x - (int64_t)t.u * s.Ub;
-  if (s.Tb > 0 && r <= (int64_t)(s.Tb - 1) * s.tb) {
-    t.seg = 0;
-    t.k = (int)((r + s.tb - 1) / s.tb);
-  } else if (s.Td > 0 && r <= (int64_t)s.Tb * s.tb + (int64_t)(s.Td - 1) * s.td) {
-    t.seg = 1;
-    const int64_t rd = r - (int64_t)s.Tb * s.tb;
-    t.k = rd > 0 ? (int)((rd + s.td - 1) / s.td) : 0;
-  } else {
-    t.u += 1;
-    t.seg = s.Tb > 0 ? 0 : 1;
-    t.k = 0;
-  }
-  t.valid = t.u < s.U && tile_byte(s, t.u, t.seg, t.k) < end;
-  return t;
+__device__ __forceinline__ int seg_len(const DecodeParams& p, int u, int seg) {
+  const int b = u / p.Hkv;
+  if (seg == 0) return p.body.lengths ? p.body.lengths[b] : p.body.len;
+  return p.dense.lengths ? p.dense.lengths[b] : p.dense.len;
 }
 
-__device__ __forceinline__ int body_len(const DecodeParams& p, int u) {
-  return p.body.lengths ? p.body.lengths[u / p.Hkv] : p.body.len;
-}
-__device__ __forceinline__ int dense_len(const DecodeParams& p, int u) {
-  return p.dense.lengths ? p.dense.lengths[u / p.Hkv] : p.dense.len;
-}
-
-// Next tile of the CTA's range. Past its last hinted tile, a segment continues
-// with extra tiles while the unit's true length needs them (a stale hint can
-// unbalance the grid, never drop tokens); those belong to the same CTA.
-__device__ __forceinline__ void next_tile(const DecodeParams& p, int64_t end, TileRef& t) {
+__device__ __forceinline__ void piece_fill(const DecodeParams& p, int64_t end, Piece& pc) {
   const Sched& s = p.sc;
-  if (t.seg == 0) {
-    if (t.k + 1 < s.Tb) {
-      t.k++;
-      t.valid = tile_byte(s, t.u, 0, t.k) < end;
-      return;
-    }
-    if ((int64_t)kTileI4 * (t.k + 1) < body_len(p, t.u)) {
-      t.k++;
-      return;
-    }
-    if (s.Td > 0) {
-      t.seg = 1;
-      t.k = 0;
-      t.valid = tile_byte(s, t.u, 1, 0) < end;
-      return;
-    }
+  const int T = pc.seg == 0 ? s.Tb : s.Td;
+  const int64_t ts = pc.seg == 0 ? s.tb : s.td;
+  const int tile = pc.seg == 0 ? kTileI4 : kTileD;
+  const int64_t seg0 = tile_byte(s, pc.u, pc.seg, 0);
+  const int64_t kq = (end - 1 - seg0) / ts;
+  const int kl = kq < (int64_t)(T - 1) ? (int)kq : T - 1;  // last hinted tile starting in range
+  pc.len = seg_len(p, pc.u, pc.seg);
+  const int kneed = (pc.len + tile - 1) / tile;
+  pc.k1 = kl + 1;
+  // past its last hinted tile a segment continues while the true length needs it
+  // (a stale hint can unbalance the grid, never drop tokens)
+  if (kl == T - 1 && kneed > pc.k1) pc.k1 = kneed;
+  pc.kd = min(pc.k1, kneed);
+}
+
+__device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, int64_t end) {
+  const Sched& s = p.sc;
+  const int64_t x = cta_begin(s, c);
+  Piece pc;
+  pc.u = (int)(x / s.Ub);
+  const int64_t r = x - (int64_t)pc.u * s.Ub;
+  if (s.Tb > 0 && r <= (int64_t)(s.Tb - 1) * s.tb) {
+    pc.seg = 0;
+    pc.k0 = (int)((r + s.tb - 1) / s.tb);
+  } else if (s.Td > 0 && r <= (int64_t)s.Tb * s.tb + (int64_t)(s.Td - 1) * s.td) {
+    pc.seg = 1;
+    const int64_t rd = r - (int64_t)s.Tb * s.tb;
+    pc.k0 = rd > 0 ? (int)((rd + s.td - 1) / s.td) : 0;
   } else {
-    if (t.k + 1 < s.Td) {
-      t.k++;
-      t.valid = tile_byte(s, t.u, 1, t.k) < end;
-      return;
-    }
-    if ((int64_t)kTileD * (t.k + 1) < dense_len(p, t.u)) {
-      t.k++;
-      return;
-    }
+    pc.u += 1;
+    pc.seg = s.Tb > 0 ? 0 : 1;
+    pc.k0 = 0;
   }
-  t.u++;
-  t.seg = s.Tb > 0 ? 0 : 1;
-  t.k = 0;
-  t.valid = t.u < s.U && tile_byte(s, t.u, t.seg, 0) < end;
+  pc.valid = pc.u < s.U && tile_byte(s, pc.u, pc.seg, pc.k0) < end;
+  if (pc.valid) piece_fill(p, end, pc);
+  return pc;
 }
 
-__device__ __forceinline__ bool tile_has_data(const DecodeParams& p, const TileRef& t) {
-  return t.seg == 0 ? kTileI4 * t.k < body_len(p, t.u) : kTileD * t.k < dense_len(p, t.u);
+__device__ __forceinline__ void next_piece(const DecodeParams& p, int64_t end, Piece& pc) {
+  const Sched& s = p.sc;
+  const int T = pc.seg == 0 ? s.Tb : s.Td;
+  if (pc.k1 < T) {  // the range ended inside this segment
+    pc.valid = false;
+    return;
+  }
+  if (pc.seg == 0 && s.Td > 0) {
+    pc.seg = 1;
+  } else {
+    pc.u++;
+    pc.seg = s.Tb > 0 ? 0 : 1;
+  }
+  pc.k0 = 0;
+  pc.valid = pc.u < s.U && tile_byte(s, pc.u, pc.seg, 0) < end;
+  if (pc.valid) piece_fill(p, end, pc);
 }
 
-// Pieces (partials) of unit u: CTAs owning its body tiles, then its dense tiles.
+// Partials of unit u: one per CTA owning its body tiles, then per CTA owning its dense tiles.
 __device__ __forceinline__ void unit_pieces(const Sched& s, int u, int& b0, int& nb, int& d0, int& nd) {
   nb = nd = 0;
   b0 = d0 = 0;
@@ -183,6 +182,18 @@ __device__ __forceinline__ void unit_pieces(const Sched& s, int u, int& b0, int&
     nd = owner_of(s, tile_byte(s, u, 1, s.Td - 1)) - d0 + 1;
   }
 }
+
+// Ring position: slot index and the parity of its current use.
+struct Ring {
+  int slot;
+  uint32_t phase;
+  __device__ __forceinline__ void advance(int n) {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
 
 // ---------------------------------------------------------------- warp state / softmax
 // Thread (r = lane/4, j = lane%4) owns heads 2j and 2j+1 in every accumulator.
@@ -285,30 +296,22 @@ __device__ __forceinline__ void ld_row_u(const uint32_t* base, int row, uint32_t
   }
 }
 
-struct MetaPtrs {
-  const float* ks;
-  const float* kb;
-  const uint32_t* vs2;
-  const float* vb;
-};
-
 // Scores of 16 tokens x 8 heads: x = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)} (unscaled).
+// kc / ks / kb point at this thread's row r of the tile's K codes / K scale / K bias.
 template <int NG>
-__device__ __forceinline__ void k_scores(const uint8_t* codes, const MetaPtrs& mp, int t0,
+__device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, const float* kb,
                                          const uint32_t (&qf)[8][2], const float (&nbias)[NG][2],
                                          const float (&qsum)[NG][2], float (&x)[4]) {
   constexpr int WPG = 4 / NG;  // packed words per group
-  const int lane = threadIdx.x & 31;
-  const int r = lane >> 2, j = lane & 3;
-  const uint4 kA = *reinterpret_cast<const uint4*>(codes + (t0 + r) * HKV_CODE_BYTES + 16 * j);
-  const uint4 kB = *reinterpret_cast<const uint4*>(codes + (t0 + r + 8) * HKV_CODE_BYTES + 16 * j);
+  const uint4 kA = *reinterpret_cast<const uint4*>(kc);
+  const uint4 kB = *reinterpret_cast<const uint4*>(kc + 8 * HKV_CODE_BYTES);
   const uint32_t kwa[4] = {kA.x, kA.y, kA.z, kA.w};
   const uint32_t kwb[4] = {kB.x, kB.y, kB.z, kB.w};
   float sA[NG], sB[NG], bA[NG], bB[NG];
-  ld_row<NG>(mp.ks, t0 + r, sA);
-  ld_row<NG>(mp.ks, t0 + r + 8, sB);
-  ld_row<NG>(mp.kb, t0 + r, bA);
-  ld_row<NG>(mp.kb, t0 + r + 8, bB);
+  ld_row<NG>(ks, 0, sA);
+  ld_row<NG>(ks, 8, sB);
+  ld_row<NG>(kb, 0, bA);
+  ld_row<NG>(kb, 8, bB);
   x[0] = x[1] = x[2] = x[3] = 0.f;
   float c[4];
 #pragma unroll
@@ -339,20 +342,19 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   return d;
 }
 
-// O^T += V^T . (s P/16)^T for 16 tokens; P = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)} pre-scaled by 1/16.
-// Masked rows must come with P == 0.
+// O^T += V^T . (s P/16)^T for 16 tokens; P = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)}
+// pre-scaled by 1/16. vc points at this thread's V chunk (pair j, chunk r);
+// vs2 / vb at row r of the V scale (f16x2) / bias.
 template <int NG>
-__device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* codes, const MetaPtrs& mp, int t0,
-                                             const float (&P)[4]) {
+__device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* vc, const uint32_t* vs2,
+                                             const float* vb, const float (&P)[4]) {
   constexpr int WPG = 4 / NG;
-  const int lane = threadIdx.x & 31;
-  const int r = lane >> 2, j = lane & 3;
   uint32_t sA[NG], sB[NG];
   float bA[NG], bB[NG];
-  ld_row_u<NG>(mp.vs2, t0 + r, sA);
-  ld_row_u<NG>(mp.vs2, t0 + r + 8, sB);
-  ld_row<NG>(mp.vb, t0 + r, bA);
-  ld_row<NG>(mp.vb, t0 + r + 8, bB);
+  ld_row_u<NG>(vs2, 0, sA);
+  ld_row_u<NG>(vs2, 8, sB);
+  ld_row<NG>(vb, 0, bA);
+  ld_row<NG>(vb, 8, bB);
   const uint32_t pA = pack2<__half>(P[0], P[1]);
   const uint32_t pB = pack2<__half>(P[2], P[3]);
   uint32_t pb[NG][2];
@@ -363,9 +365,8 @@ __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* c
     ws.zacc[g][0] = fmaf(bA[g], P[0], fmaf(bB[g], P[2], ws.zacc[g][0]));
     ws.zacc[g][1] = fmaf(bA[g], P[1], fmaf(bB[g], P[3], ws.zacc[g][1]));
   }
-  const uint8_t* vc = codes + kTileI4 * HKV_CODE_BYTES;
-  const uint4 vA = *reinterpret_cast<const uint4*>(vc + (t0 + 2 * j) * HKV_CODE_BYTES + 16 * r);
-  const uint4 vB = *reinterpret_cast<const uint4*>(vc + (t0 + 8 + 2 * j) * HKV_CODE_BYTES + 16 * r);
+  const uint4 vA = *reinterpret_cast<const uint4*>(vc);
+  const uint4 vB = *reinterpret_cast<const uint4*>(vc + 8 * HKV_CODE_BYTES);
   const uint32_t vwa[4] = {vA.x, vA.y, vA.z, vA.w};
   const uint32_t vwb[4] = {vB.x, vB.y, vB.z, vB.w};
   // exact integer codes: the B operand carries s * P rounded to f16, so a bias
@@ -384,38 +385,39 @@ __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* c
 }
 
 // ---------------------------------------------------------------- dense consumer piece (8 tokens per warp)
+// A dense slot holds 32 rows of K then 32 rows of V, each split in two 64-dim
+// halves of [32 rows][128 B] written by TMA with the 128-byte swizzle: the
+// 16-byte chunk c of row i sits at i*128 + ((c ^ (i & 7)) << 4).
+__device__ __forceinline__ uint32_t swz(uint32_t half_base, int row, int chunk) {
+  return half_base + row * 128 + (((chunk ^ (row & 7)) & 7) << 4);
+}
+
 template <typename DTy, int NG>
-__device__ __forceinline__ void dense_subtile(WarpState<NG>& ws, const uint8_t* stg, int t0, int tok0, int hi,
-                                              const uint32_t (&qf)[8][2], int G, float qscale) {
+__device__ __forceinline__ void dense_subtile(WarpState<NG>& ws, uint32_t slot, int t0, bool ok,
+                                              const uint32_t (&qf)[8][2], bool h0, bool h1, float qscale) {
   const int lane = threadIdx.x & 31;
-  const int r = lane >> 2, j = lane & 3;
-  const uint32_t kb = smem_u32(stg);
-  const uint32_t vb = kb + kTileD * kRowPitch;
-  // rows r+8 of the 16-row fragments repeat rows r and are masked (P = 0)
-  const uint32_t krow = kb + (t0 + (lane & 7)) * kRowPitch + (lane >> 4) * 16;
+  const int row = t0 + (lane & 7);  // rows r+8 of the 16-row fragments repeat rows r and are masked
   float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int kt = 0; kt < 8; ++kt) {
     uint32_t a[4];
-    ldsm_x4(a, krow + kt * 32);
+    ldsm_x4(a, swz(slot + (kt >> 2) * kDenseHalf, row, 2 * (kt & 3) + (lane >> 4)));
     mma16816<DTy>(c, a, qf[kt][0], qf[kt][1]);
   }
-  const bool ok = tok0 + r < hi;
   float x[4];
-  x[0] = (ok && 2 * j < G) ? c[0] * qscale : -INFINITY;
-  x[1] = (ok && 2 * j + 1 < G) ? c[1] * qscale : -INFINITY;
+  x[0] = (ok && h0) ? c[0] * qscale : -INFINITY;
+  x[1] = (ok && h1) ? c[1] * qscale : -INFINITY;
   x[2] = -INFINITY;
   x[3] = -INFINITY;
   float P[4];
   softmax_step<NG, 4>(ws, x, P, 0.f);
   const uint32_t pb0 = movmatrix_t(pack2<DTy>(P[0], P[1]));
-  const uint32_t pb1 = 0u;  // tokens t0+8..15 are masked
-  const uint32_t vrow = vb + (t0 + (lane & 7)) * kRowPitch + ((lane >> 3) & 1) * 16;
+  const uint32_t vb = slot + 2 * kDenseHalf;
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
     uint32_t a[4];
-    ldsm_x4_t(a, vrow + mt * 32);
-    mma16816<DTy>(ws.o[mt], a, pb0, pb1);
+    ldsm_x4_t(a, swz(vb + (mt >> 2) * kDenseHalf, row, 2 * (mt & 3) + ((lane >> 3) & 1)));
+    mma16816<DTy>(ws.o[mt], a, pb0, 0u);
   }
 }
 
@@ -454,6 +456,15 @@ __device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int h
 }
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
+
+__device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // ---------------------------------------------------------------- producer helpers
 // Slots at or past `valid` (beyond the sequence length) may hold uninitialised
@@ -494,17 +505,51 @@ __device__ __forceinline__ void expand_meta(const uint8_t* raw, uint8_t* meta, i
   }
 }
 
+// Zero dense V rows [valid, 32) of a swizzled slot (whole 128-byte rows, so the
+// swizzle does not matter); rows past the sequence length may hold any bits.
+__device__ __forceinline__ void zero_dense_v_tail(uint8_t* slot, int valid, int lane) {
+  if (valid >= kTileD) return;
+  uint8_t* v = slot + 2 * kDenseHalf;
+  const int rows = kTileD - valid;
+  for (int i = lane; i < rows * 16; i += 32) {  // 2 halves x 8 chunks of 16 B per row
+    const int rr = valid + i / 16, h = (i >> 3) & 1, ch = i & 7;
+    *reinterpret_cast<uint4*>(v + h * kDenseHalf + rr * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  // order these generic-proxy writes before later TMA (async-proxy) writes to the slot
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Producer cursor over the CTA's tiles that hold tokens.
+struct Cursor {
+  Piece pc;
+  int k;
+  bool valid;
+};
+__device__ __forceinline__ void cursor_settle(const DecodeParams& p, int64_t end, Cursor& cu) {
+  while (cu.pc.valid && cu.k >= cu.pc.kd) {
+    next_piece(p, end, cu.pc);
+    cu.k = cu.pc.k0;
+  }
+  cu.valid = cu.pc.valid;
+}
+__device__ __forceinline__ void cursor_next(const DecodeParams& p, int64_t end, Cursor& cu) {
+  cu.k++;
+  cursor_settle(p, end, cu);
+}
+
 // ---------------------------------------------------------------- the persistent kernel
 template <int FMT, int GROUP, typename DTy>
-__global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_constant__ DecodeParams p) {
   constexpr int NG = HKV_D / GROUP;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t ready_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t empty_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t mempty_bar[kMetaSlots];
   __shared__ int s_last;
 
+  // the 128-byte swizzle of the dense tiles repeats every 1024 bytes: align the ring
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const Sched& sc = p.sc;
   const int c = blockIdx.x;
   const int64_t end = cta_begin(sc, c + 1);
@@ -527,81 +572,77 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const DecodeP
 
   if (warp == kConsumerWarps) {
     // ================================================================ producer warp
-    // Issue walks the tile list ahead of expansion by up to nsl loads.
-    TileRef it_issue = first_tile(sc, c), it_exp = it_issue;
-    int n_issue = 0, n_exp = 0, nb_exp = 0;
+    Cursor ci, ce;  // issue runs ahead of expansion by up to nsl tiles
+    ci.pc = first_piece(p, c, end);
+    ci.k = ci.pc.k0;
+    cursor_settle(p, end, ci);
+    ce = ci;
+    Ring ri{0, 0u}, re{0, 0u};
+    int n_issue = 0, nb_exp = 0;
     bool ok = true;
-    auto issue_one = [&](void) -> bool {
-      // advance to the next tile with data; returns false when the range is exhausted
-      while (it_issue.valid && !tile_has_data(p, it_issue)) next_tile(p, end, it_issue);
-      if (!it_issue.valid) return false;
-      const int slot = n_issue % nsl;
-      if (n_issue >= nsl && !mbar_wait(&empty_bar[slot], ((n_issue / nsl) & 1) ^ 1)) {
+    const uint32_t codes_b = kTileI4 * HKV_CODE_BYTES;
+    const uint32_t sc_b = kTileI4 * 4 * NG;
+    const uint32_t zp_b = FMT == HKV_FMT_REF ? kTileI4 * NG : 0;
+    auto issue_one = [&]() {
+      if (!ci.valid || !ok) return;
+      if (n_issue >= nsl && !mbar_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) {
         ok = false;
-        return false;
+        return;
       }
-      uint8_t* sb = ring + slot * p.slot_bytes;
-      const int u = it_issue.u;
-      if (it_issue.seg == 0) {
-        if (lane == 0) {
-          const int t = it_issue.k * kTileI4;
+      uint8_t* sb = ring + ri.slot * p.slot_bytes;
+      uint64_t* fb = &full_bar[ri.slot];
+      const int u = ci.pc.u;
+      if (lane == 0) {
+        if (ci.pc.seg == 0) {
+          const int t = ci.k * kTileI4;
           const int64_t page = store_page(p.body, u, t);
           if (page < 0) {
             hkv_flag_error(HKV_DEVERR_BAD_PAGE);
-            mbar_arrive(&full_bar[slot]);
+            mbar_arrive(fb);
           } else {
-            const uint32_t codes_b = kTileI4 * HKV_CODE_BYTES;
-            const uint32_t sc_b = kTileI4 * 4 * NG;
-            const uint32_t zp_b = FMT == HKV_FMT_REF ? kTileI4 * NG : 0;
-            const int off = t % p.body.page_tokens;
+            const int off = p.page_shift >= 0 ? t & ((1 << p.page_shift) - 1) : t % p.body.page_tokens;
             const SideAddr ka = side_addr(p.body.k, p.body, page, off);
             const SideAddr va = side_addr(p.body.v, p.body, page, off);
-            mbar_arrive_expect_tx(&full_bar[slot], 2 * (codes_b + sc_b + zp_b));
-            bulk_g2s(sb, ka.codes, codes_b, &full_bar[slot]);
-            bulk_g2s(sb + codes_b, va.codes, codes_b, &full_bar[slot]);
-            bulk_g2s(sb + 2 * codes_b, ka.scales, sc_b, &full_bar[slot]);
-            bulk_g2s(sb + 2 * codes_b + sc_b, va.scales, sc_b, &full_bar[slot]);
+            mbar_arrive_expect_tx(fb, 2 * (codes_b + sc_b + zp_b));
+            bulk_g2s(sb, ka.codes, codes_b, fb);
+            bulk_g2s(sb + codes_b, va.codes, codes_b, fb);
+            bulk_g2s(sb + 2 * codes_b, ka.scales, sc_b, fb);
+            bulk_g2s(sb + 2 * codes_b + sc_b, va.scales, sc_b, fb);
             if (FMT == HKV_FMT_REF) {
-              bulk_g2s(sb + 2 * codes_b + 2 * sc_b, ka.zps, zp_b, &full_bar[slot]);
-              bulk_g2s(sb + 2 * codes_b + 2 * sc_b + zp_b, va.zps, zp_b, &full_bar[slot]);
+              bulk_g2s(sb + 2 * codes_b + 2 * sc_b, ka.zps, zp_b, fb);
+              bulk_g2s(sb + 2 * codes_b + 2 * sc_b + zp_b, va.zps, zp_b, fb);
             }
           }
+        } else {
+          const int b = u / p.Hkv, hk = u % p.Hkv, t = ci.k * kTileD;
+          const uint32_t d = smem_u32(sb);
+          mbar_arrive_expect_tx(fb, dense_slot_bytes());
+          tma_tile_4d(d, &p.tmk, 0, t, hk, b, fb);
+          tma_tile_4d(d + kDenseHalf, &p.tmk, 64, t, hk, b, fb);
+          tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
+          tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
         }
-      } else {
-        const int b = u / p.Hkv, hk = u % p.Hkv;
-        const int hi = dense_len(p, u);
-        const DTy* kbase = static_cast<const DTy*>(p.dense.k) + b * p.dense.stride_b + hk * p.dense.stride_h;
-        const DTy* vbase = static_cast<const DTy*>(p.dense.v) + b * p.dense.stride_b + hk * p.dense.stride_h;
-        if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], 2 * kTileD * HKV_D * 2);
-        __syncwarp();
-        // rows past the length repeat the last valid row (finite data; masked by P = 0)
-        const int64_t src = min(it_issue.k * kTileD + lane, hi - 1);
-        bulk_g2s(sb + lane * kRowPitch, kbase + src * p.dense.stride_t, HKV_D * 2, &full_bar[slot]);
-        bulk_g2s(sb + kTileD * kRowPitch + lane * kRowPitch, vbase + src * p.dense.stride_t, HKV_D * 2,
-                 &full_bar[slot]);
       }
       n_issue++;
-      next_tile(p, end, it_issue);
-      return true;
+      ri.advance(nsl);
+      cursor_next(p, end, ci);
     };
-    for (int i = 0; i < nsl - 1 && issue_one(); ++i) {
-    }
-    while (ok) {
-      while (it_exp.valid && !tile_has_data(p, it_exp)) next_tile(p, end, it_exp);
-      if (!it_exp.valid) break;
-      const int slot = n_exp % nsl;
-      if (!mbar_wait(&full_bar[slot], (n_exp / nsl) & 1)) break;
-      if (it_exp.seg == 0) {
-        const int ms = nb_exp % kMetaSlots;
+    for (int i = 0; i < nsl - 1; ++i) issue_one();
+    while (ok && ce.valid) {
+      if (!mbar_wait(&full_bar[re.slot], re.phase)) break;
+      uint8_t* sb = ring + re.slot * p.slot_bytes;
+      if (ce.pc.seg == 0) {
+        const int ms = nb_exp & (kMetaSlots - 1);
         if (nb_exp >= kMetaSlots && !mbar_wait(&mempty_bar[ms], ((nb_exp / kMetaSlots) & 1) ^ 1)) break;
-        expand_meta<FMT, NG>(ring + slot * p.slot_bytes + 2 * kTileI4 * HKV_CODE_BYTES,
-                             meta_ring + ms * p.meta_bytes, lane, body_len(p, it_exp.u) - it_exp.k * kTileI4);
+        expand_meta<FMT, NG>(sb + 2 * codes_b, meta_ring + ms * p.meta_bytes, lane, ce.pc.len - ce.k * kTileI4);
         nb_exp++;
+      } else {
+        zero_dense_v_tail(sb, ce.pc.len - ce.k * kTileD, lane);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ready_bar[slot]);
-      n_exp++;
-      next_tile(p, end, it_exp);
+      if (lane == 0) mbar_arrive(&ready_bar[re.slot]);
+      re.advance(nsl);
+      cursor_next(p, end, ce);
       issue_one();
     }
     // drain: every issued copy must have landed before the CTA exits
@@ -613,210 +654,72 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const DecodeP
 
   // ================================================================== consumer warps
   WarpState<NG> ws;
-  ws_reset<NG>(ws);
   uint32_t qf[8][2];
   float qsum[NG][2], nbias[NG][2];
   const int r = lane >> 2, j = lane & 3;
   const bool h0 = 2 * j < p.G, h1 = 2 * j + 1 < p.G;
-  int n_load = 0, nb_load = 0;
-  TileRef it = first_tile(sc, c);
-  int cur_u = -1, cur_seg = -1;
-  bool alive = true;
+  const float qs = p.qscale;
+  Ring rc{0, 0u};
+  int nb_load = 0;
+  // per-thread offsets inside an INT4 slot / its expanded metadata
+  const int t0 = warp * 32;
+  const int kc_off = (t0 + r) * HKV_CODE_BYTES + 16 * j;
+  const int vc_off = kTileI4 * HKV_CODE_BYTES + (t0 + 2 * j) * HKV_CODE_BYTES + 16 * r;
+  const int mrow = (t0 + r) * NG;
 
-  auto begin_piece = [&](int u, int seg) {
-    const int b = u / p.Hkv, hk = u % p.Hkv;
-    float qa[8][2], qb[8][2];
-    if (seg == 0) {
-      load_q_frags<__half>(p, b, hk, true, qf, qa, qb);
-      float ps[NG], pbias[NG];
+  for (Piece pc = first_piece(p, c, end); pc.valid; next_piece(p, end, pc)) {
+    const int u = pc.u, b = u / p.Hkv, hk = u % p.Hkv;
+    // ---- begin piece: query fragments for this unit
+    {
+      float qa[8][2], qb[8][2];
+      if (pc.seg == 0) {
+        load_q_frags<__half>(p, b, hk, true, qf, qa, qb);
+        float ps[NG], pbias[NG];
 #pragma unroll
-      for (int g = 0; g < NG; ++g) ps[g] = pbias[g] = 0.f;
+        for (int g = 0; g < NG; ++g) ps[g] = pbias[g] = 0.f;
 #pragma unroll
-      for (int kt = 0; kt < 8; ++kt) {
-        const int g = (kt * 16) / GROUP;
-        ps[g] += qa[kt][0] + qa[kt][1] + 16.f * (qb[kt][0] + qb[kt][1]);
-        pbias[g] += qa[kt][0] + qa[kt][1] + qb[kt][0] + qb[kt][1];
+        for (int kt = 0; kt < 8; ++kt) {
+          const int g = (kt * 16) / GROUP;
+          ps[g] += qa[kt][0] + qa[kt][1] + 16.f * (qb[kt][0] + qb[kt][1]);
+          pbias[g] += qa[kt][0] + qa[kt][1] + qb[kt][0] + qb[kt][1];
+        }
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          ps[g] += __shfl_xor_sync(0xffffffffu, ps[g], 1);
+          ps[g] += __shfl_xor_sync(0xffffffffu, ps[g], 2);
+          pbias[g] += __shfl_xor_sync(0xffffffffu, pbias[g], 1);
+          pbias[g] += __shfl_xor_sync(0xffffffffu, pbias[g], 2);
+          qsum[g][0] = __shfl_sync(0xffffffffu, ps[g], (2 * j) * 4);
+          qsum[g][1] = __shfl_sync(0xffffffffu, ps[g], (2 * j + 1) * 4);
+          nbias[g][0] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j) * 4);
+          nbias[g][1] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j + 1) * 4);
+        }
+      } else {
+        load_q_frags<DTy>(p, b, hk, false, qf, qa, qb);
       }
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        ps[g] += __shfl_xor_sync(0xffffffffu, ps[g], 1);
-        ps[g] += __shfl_xor_sync(0xffffffffu, ps[g], 2);
-        pbias[g] += __shfl_xor_sync(0xffffffffu, pbias[g], 1);
-        pbias[g] += __shfl_xor_sync(0xffffffffu, pbias[g], 2);
-        qsum[g][0] = __shfl_sync(0xffffffffu, ps[g], (2 * j) * 4);
-        qsum[g][1] = __shfl_sync(0xffffffffu, ps[g], (2 * j + 1) * 4);
-        nbias[g][0] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j) * 4);
-        nbias[g][1] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j + 1) * 4);
-      }
-    } else {
-      load_q_frags<DTy>(p, b, hk, false, qf, qa, qb);
     }
     ws_reset<NG>(ws);
-    cur_u = u;
-    cur_seg = seg;
-  };
 
-  auto end_piece = [&]() {
-    // 1. per-warp partials to shared memory
-    const bool body = cur_seg == 0;
-    float l0 = ws.l[0], l1 = ws.l[1];
-#pragma unroll
-    for (int sft = 4; sft < 32; sft <<= 1) {
-      l0 += __shfl_xor_sync(0xffffffffu, l0, sft);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, sft);
-    }
-    float z[NG][2];
-#pragma unroll
-    for (int g = 0; g < NG; ++g) {
-      z[g][0] = body ? ws.zacc[g][0] : 0.f;
-      z[g][1] = body ? ws.zacc[g][1] : 0.f;
-#pragma unroll
-      for (int sft = 4; sft < 32; sft <<= 1) {
-        z[g][0] += __shfl_xor_sync(0xffffffffu, z[g][0], sft);
-        z[g][1] += __shfl_xor_sync(0xffffffffu, z[g][1], sft);
-      }
-    }
-    float* wo = comb + warp * p.G * HKV_D;
-    float* cml = comb + kConsumerWarps * p.G * HKV_D;  // [4][8][2]
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      const int d0 = 16 * mt + r, d1 = d0 + 8;
-      const int g = (16 * mt) / GROUP;
-      const float osc = body ? 16.f : 1.f;  // INT4 tiles accumulate with P/16
-      if (h0) {
-        wo[(2 * j) * HKV_D + d0] = osc * (ws.o[mt][0] + z[g][0]);
-        wo[(2 * j) * HKV_D + d1] = osc * (ws.o[mt][2] + z[g][0]);
-      }
-      if (h1) {
-        wo[(2 * j + 1) * HKV_D + d0] = osc * (ws.o[mt][1] + z[g][1]);
-        wo[(2 * j + 1) * HKV_D + d1] = osc * (ws.o[mt][3] + z[g][1]);
-      }
-    }
-    const float lsc = body ? 16.f : 1.f;  // INT4 tiles accumulate P/16
-    if (r == 0) {
-      cml[(warp * 8 + 2 * j) * 2] = ws.m[0];
-      cml[(warp * 8 + 2 * j) * 2 + 1] = l0 * lsc;
-      cml[(warp * 8 + 2 * j + 1) * 2] = ws.m[1];
-      cml[(warp * 8 + 2 * j + 1) * 2 + 1] = l1 * lsc;
-    }
-    consumer_sync();
-    // 2. combine the four warps into this piece's partial slot
-    const int u = cur_u;
-    int b0, nb, d0, nd;
-    unit_pieces(sc, u, b0, nb, d0, nd);
-    const int slot = cur_seg == 0 ? c - b0 : nb + c - d0;
-    float* po = p.part_o + ((int64_t)u * sc.S + slot) * p.G * HKV_D;
-    float* pml = p.part_ml + ((int64_t)u * sc.S + slot) * p.G * 2;
-    for (int idx = threadIdx.x; idx < p.G * HKV_D; idx += kConsumerThreads) {
-      const int h = idx / HKV_D, d = idx % HKV_D;
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cml[(w * 8 + h) * 2]);
-      float acc = 0.f, L = 0.f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          const float mw = cml[(w * 8 + h) * 2];
-          if (mw == -INFINITY) continue;
-          const float e = fast_exp2(mw - M);
-          acc = fmaf(e, comb[(w * p.G + h) * HKV_D + d], acc);
-          L = fmaf(e, cml[(w * 8 + h) * 2 + 1], L);
+    // ---- the piece's tiles that hold tokens
+    bool alive = true;
+    if (pc.seg == 0) {
+      for (int k = pc.k0; k < pc.kd; ++k) {
+        if (!mbar_wait(&ready_bar[rc.slot], rc.phase)) {
+          alive = false;
+          break;
         }
-      }
-      po[idx] = acc;
-      if (d == 0) {
-        pml[2 * h] = M;
-        pml[2 * h + 1] = L;
-      }
-    }
-    __threadfence();
-    consumer_sync();
-    if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[u], 1) == nb + nd - 1;
-    consumer_sync();
-    if (s_last) {
-      // 3. last piece of the unit: merge all its partials (warp w: heads w, w+4)
-      __threadfence();
-      const int n = nb + nd;
-      const int b = u / p.Hkv, hk = u % p.Hkv;
-      const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
-      const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
-      for (int h = warp; h < p.G; h += kConsumerWarps) {
-        float M = -INFINITY;
-        for (int k = lane; k < n; k += 32) M = fmaxf(M, __ldcg(ml_u + (k * p.G + h) * 2));
-#pragma unroll
-        for (int sft = 16; sft > 0; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
-        float L = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k0 = 0; k0 < n; k0 += 32) {
-          float wk = 0.f;
-          if (k0 + lane < n) {
-            const float mk = __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2);
-            wk = (mk == -INFINITY || M == -INFINITY) ? 0.f : fast_exp2(mk - M);
-            L = fmaf(wk, __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2 + 1), L);
-          }
-          const int kn = min(32, n - k0);
-          for (int kk = 0; kk < kn; ++kk) {
-            const float w = __shfl_sync(0xffffffffu, wk, kk);
-            if (w == 0.f) continue;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(o_u + ((k0 + kk) * p.G + h) * HKV_D) + lane);
-            acc.x = fmaf(w, v.x, acc.x);
-            acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z);
-            acc.w = fmaf(w, v.w, acc.w);
-          }
-        }
-#pragma unroll
-        for (int sft = 16; sft > 0; sft >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sft);
-        const int hq = hk * p.G + h;
-        if (p.out_o) {
-          reinterpret_cast<float4*>(p.out_o + ((int64_t)b * p.Hq + hq) * HKV_D)[lane] = acc;
-          if (lane == 0) {
-            p.out_ml[((int64_t)b * p.Hq + hq) * 2] = M;
-            p.out_ml[((int64_t)b * p.Hq + hq) * 2 + 1] = L;
-          }
-        } else {
-          const float inv = L > 0.f ? 1.f / L : 0.f;
-          const int64_t o = (int64_t)b * p.out_sb + (int64_t)hq * p.out_sh + 4 * lane;
-          store_any(p.out, p.out_dtype, o + 0, acc.x * inv);
-          store_any(p.out, p.out_dtype, o + 1, acc.y * inv);
-          store_any(p.out, p.out_dtype, o + 2, acc.z * inv);
-          store_any(p.out, p.out_dtype, o + 3, acc.w * inv);
-        }
-      }
-      consumer_sync();
-      if (threadIdx.x == 0) p.counters[u] = 0;
-    }
-    consumer_sync();  // the combine area is free again
-  };
-
-  const float qs = p.qscale;
-  while (it.valid && alive) {
-    if (it.u != cur_u || it.seg != cur_seg) {
-      if (cur_u >= 0) end_piece();
-      begin_piece(it.u, it.seg);
-    }
-    if (tile_has_data(p, it)) {
-      const int slot = n_load % nsl;
-      if (!mbar_wait(&ready_bar[slot], (n_load / nsl) & 1)) {
-        alive = false;
-        break;
-      }
-      const uint8_t* stg = ring + slot * p.slot_bytes;
-      if (it.seg == 0) {
-        const int ms = nb_load % kMetaSlots;
-        const uint8_t* mbase = meta_ring + ms * p.meta_bytes;
-        MetaPtrs mp;
-        mp.ks = reinterpret_cast<const float*>(mbase);
-        mp.kb = mp.ks + kTileI4 * NG;
-        mp.vs2 = reinterpret_cast<const uint32_t*>(mp.kb + kTileI4 * NG);
-        mp.vb = reinterpret_cast<const float*>(mp.vs2 + kTileI4 * NG);
-        const int hi = body_len(p, it.u);
-        const int t0 = warp * 32;
-        const int tok = it.k * kTileI4 + t0;
+        const uint8_t* stg = ring + rc.slot * p.slot_bytes;
+        const int ms = nb_load & (kMetaSlots - 1);
+        const float* mk = reinterpret_cast<const float*>(meta_ring + ms * p.meta_bytes);
+        const float* ks = mk + mrow;
+        const float* kb = mk + kTileI4 * NG + mrow;
+        const uint32_t* vs2 = reinterpret_cast<const uint32_t*>(mk + 2 * kTileI4 * NG) + mrow;
+        const float* vb = mk + 3 * kTileI4 * NG + mrow;
         float xa[4], xb[4], x[8], P[8];
-        k_scores<NG>(stg, mp, t0, qf, nbias, qsum, xa);
-        k_scores<NG>(stg, mp, t0 + 16, qf, nbias, qsum, xb);
-        if (tok + 32 <= hi) {
+        k_scores<NG>(stg + kc_off, ks, kb, qf, nbias, qsum, xa);
+        k_scores<NG>(stg + kc_off + 16 * HKV_CODE_BYTES, ks + 16 * NG, kb + 16 * NG, qf, nbias, qsum, xb);
+        const int tok = k * kTileI4 + t0;
+        if (tok + 32 <= pc.len) {
           x[0] = h0 ? xa[0] * qs : -INFINITY;
           x[1] = h1 ? xa[1] * qs : -INFINITY;
           x[2] = h0 ? xa[2] * qs : -INFINITY;
@@ -826,8 +729,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const DecodeP
           x[6] = h0 ? xb[2] * qs : -INFINITY;
           x[7] = h1 ? xb[3] * qs : -INFINITY;
         } else {
-          const bool ok0 = tok + r < hi, ok1 = tok + r + 8 < hi;
-          const bool ok2 = tok + 16 + r < hi, ok3 = tok + 24 + r < hi;
+          const bool ok0 = tok + r < pc.len, ok1 = tok + r + 8 < pc.len;
+          const bool ok2 = tok + 16 + r < pc.len, ok3 = tok + 24 + r < pc.len;
           x[0] = (ok0 && h0) ? xa[0] * qs : -INFINITY;
           x[1] = (ok0 && h1) ? xa[1] * qs : -INFINITY;
           x[2] = (ok1 && h0) ? xa[2] * qs : -INFINITY;
@@ -839,27 +742,165 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const DecodeP
         }
         softmax_step<NG, 8>(ws, x, P, 4.f);
         const float pa[4] = {P[0], P[1], P[2], P[3]};
-        const float pc[4] = {P[4], P[5], P[6], P[7]};
-        v_accumulate<NG>(ws, stg, mp, t0, pa);
-        v_accumulate<NG>(ws, stg, mp, t0 + 16, pc);
+        const float pc4[4] = {P[4], P[5], P[6], P[7]};
+        v_accumulate<NG>(ws, stg + vc_off, vs2, vb, pa);
+        v_accumulate<NG>(ws, stg + vc_off + 16 * HKV_CODE_BYTES, vs2 + 16 * NG, vb + 16 * NG, pc4);
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&empty_bar[slot]);
+          mbar_arrive(&empty_bar[rc.slot]);
           mbar_arrive(&mempty_bar[ms]);
         }
         nb_load++;
-      } else {
-        const int hi = dense_len(p, it.u);
-        const int t0 = warp * 8;
-        dense_subtile<DTy, NG>(ws, stg, t0, it.k * kTileD + t0, hi, qf, p.G, qs);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[slot]);
+        rc.advance(nsl);
       }
-      n_load++;
+    } else {
+      const int dt0 = warp * 8;
+      for (int k = pc.k0; k < pc.kd; ++k) {
+        if (!mbar_wait(&ready_bar[rc.slot], rc.phase)) {
+          alive = false;
+          break;
+        }
+        const uint32_t slot = smem_u32(ring + rc.slot * p.slot_bytes);
+        dense_subtile<DTy, NG>(ws, slot, dt0, k * kTileD + dt0 + r < pc.len, qf, h0, h1, qs);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);
+        rc.advance(nsl);
+      }
     }
-    next_tile(p, end, it);
+    if (!alive) {
+      ws_reset<NG>(ws);  // a timed-out wait leaves a neutral partial (the error word is set)
+    }
+
+    // ---- end piece: per-warp partials -> shared memory -> one partial for the piece
+    {
+      const bool body = pc.seg == 0;
+      float l0 = ws.l[0], l1 = ws.l[1];
+#pragma unroll
+      for (int sft = 4; sft < 32; sft <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, sft);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, sft);
+      }
+      float z[NG][2];
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        z[g][0] = body ? ws.zacc[g][0] : 0.f;
+        z[g][1] = body ? ws.zacc[g][1] : 0.f;
+#pragma unroll
+        for (int sft = 4; sft < 32; sft <<= 1) {
+          z[g][0] += __shfl_xor_sync(0xffffffffu, z[g][0], sft);
+          z[g][1] += __shfl_xor_sync(0xffffffffu, z[g][1], sft);
+        }
+      }
+      float* wo = comb + warp * p.G * HKV_D;
+      float* cml = comb + kConsumerWarps * p.G * HKV_D;  // [4][8][2]
+      const float osc = body ? 16.f : 1.f;                 // INT4 tiles accumulate with P/16
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int d0 = 16 * mt + r, d1 = d0 + 8;
+        const int g = (16 * mt) / GROUP;
+        if (h0) {
+          wo[(2 * j) * HKV_D + d0] = osc * (ws.o[mt][0] + z[g][0]);
+          wo[(2 * j) * HKV_D + d1] = osc * (ws.o[mt][2] + z[g][0]);
+        }
+        if (h1) {
+          wo[(2 * j + 1) * HKV_D + d0] = osc * (ws.o[mt][1] + z[g][1]);
+          wo[(2 * j + 1) * HKV_D + d1] = osc * (ws.o[mt][3] + z[g][1]);
+        }
+      }
+      if (r == 0) {
+        cml[(warp * 8 + 2 * j) * 2] = ws.m[0];
+        cml[(warp * 8 + 2 * j) * 2 + 1] = l0 * osc;
+        cml[(warp * 8 + 2 * j + 1) * 2] = ws.m[1];
+        cml[(warp * 8 + 2 * j + 1) * 2 + 1] = l1 * osc;
+      }
+      consumer_sync();
+      int b0, nb, d0, nd;
+      unit_pieces(sc, u, b0, nb, d0, nd);
+      const int slot = pc.seg == 0 ? c - b0 : nb + c - d0;
+      float* po = p.part_o + ((int64_t)u * sc.S + slot) * p.G * HKV_D;
+      float* pml = p.part_ml + ((int64_t)u * sc.S + slot) * p.G * 2;
+      for (int idx = threadIdx.x; idx < p.G * HKV_D; idx += kConsumerThreads) {
+        const int h = idx / HKV_D, d = idx % HKV_D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cml[(w * 8 + h) * 2]);
+        float acc = 0.f, L = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) {
+            const float mw = cml[(w * 8 + h) * 2];
+            if (mw == -INFINITY) continue;
+            const float e = fast_exp2(mw - M);
+            acc = fmaf(e, comb[(w * p.G + h) * HKV_D + d], acc);
+            L = fmaf(e, cml[(w * 8 + h) * 2 + 1], L);
+          }
+        }
+        po[idx] = acc;
+        if (d == 0) {
+          pml[2 * h] = M;
+          pml[2 * h + 1] = L;
+        }
+      }
+      __threadfence();
+      consumer_sync();
+      if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[u], 1) == nb + nd - 1;
+      consumer_sync();
+      if (s_last) {
+        // last piece of the unit: merge all its partials (warp w: heads w, w+4)
+        __threadfence();
+        const int n = nb + nd;
+        const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
+        const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
+        for (int h = warp; h < p.G; h += kConsumerWarps) {
+          float M = -INFINITY;
+          for (int k = lane; k < n; k += 32) M = fmaxf(M, __ldcg(ml_u + (k * p.G + h) * 2));
+#pragma unroll
+          for (int sft = 16; sft > 0; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
+          float L = 0.f;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int k0 = 0; k0 < n; k0 += 32) {
+            float wk = 0.f;
+            if (k0 + lane < n) {
+              const float mk = __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2);
+              wk = (mk == -INFINITY || M == -INFINITY) ? 0.f : fast_exp2(mk - M);
+              L = fmaf(wk, __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2 + 1), L);
+            }
+            const int kn = min(32, n - k0);
+            for (int kk = 0; kk < kn; ++kk) {
+              const float w = __shfl_sync(0xffffffffu, wk, kk);
+              if (w == 0.f) continue;
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(o_u + ((k0 + kk) * p.G + h) * HKV_D) + lane);
+              acc.x = fmaf(w, v.x, acc.x);
+              acc.y = fmaf(w, v.y, acc.y);
+              acc.z = fmaf(w, v.z, acc.z);
+              acc.w = fmaf(w, v.w, acc.w);
+            }
+          }
+#pragma unroll
+          for (int sft = 16; sft > 0; sft >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sft);
+          const int hq = hk * p.G + h;
+          if (p.out_o) {
+            reinterpret_cast<float4*>(p.out_o + ((int64_t)b * p.Hq + hq) * HKV_D)[lane] = acc;
+            if (lane == 0) {
+              p.out_ml[((int64_t)b * p.Hq + hq) * 2] = M;
+              p.out_ml[((int64_t)b * p.Hq + hq) * 2 + 1] = L;
+            }
+          } else {
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            const int64_t o = (int64_t)b * p.out_sb + (int64_t)hq * p.out_sh + 4 * lane;
+            store_any(p.out, p.out_dtype, o + 0, acc.x * inv);
+            store_any(p.out, p.out_dtype, o + 1, acc.y * inv);
+            store_any(p.out, p.out_dtype, o + 2, acc.z * inv);
+            store_any(p.out, p.out_dtype, o + 3, acc.w * inv);
+          }
+        }
+        consumer_sync();
+        if (threadIdx.x == 0) p.counters[u] = 0;
+      }
+      consumer_sync();  // the combine area is free again
+    }
+    if (!alive) break;
   }
-  if (cur_u >= 0) end_piece();
 }
 
 // ---------------------------------------------------------------- log-sum-exp merge (cross-GPU partials)
