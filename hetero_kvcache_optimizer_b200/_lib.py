@@ -56,6 +56,7 @@ SIGNATURES = {
     "hkv_status_str": (ctypes.c_char_p, [c_i32]),
     "hkv_version": (c_i32, []),
     "hkv_device_error": (c_i32, [ctypes.POINTER(c_u32), c_i32]),
+    "hkv_last_cuda_error": (c_i32, []),
     "hkv_side_page_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "hkv_quantize_flat": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "hkv_dequantize_flat": (c_i32, [c_vp, c_vp, c_vp, c_i64, c_i32, c_vp, c_i32, c_vp]),
@@ -88,6 +89,8 @@ class HkvError(RuntimeError):
     def __init__(self, status: int, what: str = ""):
         self.status = status
         msg = status_str(status) if _lib is not None else f"status {status}"
+        if status == HKV_ERR_CUDA and _lib is not None:
+            msg += f" (cudaError {_lib.hkv_last_cuda_error()})"
         super().__init__(f"{what}: {msg}" if what else msg)
 
 

@@ -18,9 +18,17 @@ namespace {
 
 inline cudaStream_t S(hkv_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Last CUDA runtime error seen by a library call on this host thread (hkv_last_cuda_error).
+thread_local int t_last_cuda_error = 0;
+
+inline hkv_status cuda_fail(cudaError_t e) {
+  t_last_cuda_error = static_cast<int>(e);
+  return HKV_ERR_CUDA;
+}
+
 inline hkv_status launch_status() {
   const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HKV_OK : HKV_ERR_CUDA;
+  return e == cudaSuccess ? HKV_OK : cuda_fail(e);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -73,13 +81,7 @@ hkv_status check_dense(const hkv_dense_kv* d) {
 }
 
 // --------------------------------------------------------------------------- decode plan
-int env_int(const char* name, int dflt) {
-  const char* v = std::getenv(name);
-  if (!v || !*v) return dflt;
-  return std::atoi(v);
-}
-
-constexpr int kDynSmemBudget = 110 * 1024;  // per CTA, two CTAs per SM
+constexpr int kDynSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in, static barriers aside)
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime (no link
 // dependency on libcuda).
@@ -125,7 +127,7 @@ hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st
     attr_err = cudaFuncSetAttribute(hkv::decode_kernel<FMT, GROUP, DTy>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemBudget);
   });
-  if (attr_err != cudaSuccess) return HKV_ERR_CUDA;
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err);
   hkv::decode_kernel<FMT, GROUP, DTy><<<p.sc.C, hkv::kDecodeThreads, smem, st>>>(p);
   return launch_status();
 }
@@ -150,7 +152,7 @@ hkv_status launch_decode_f(const hkv::DecodeParams& p, int group, int ddt, int s
 // tile, grid size, and an upper bound of the partial slots per unit.
 struct Plan {
   hkv::Sched sc;
-  int slot_bytes, nslots, meta_bytes, comb_bytes, smem;
+  int nslots, comb_bytes, smem;
   size_t ws_bytes;
 };
 
@@ -176,22 +178,19 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   sc.Ub = sc.Tb * sc.tb + sc.Td * sc.td;
   sc.Btot = sc.Ub * sc.U;
   const int64_t maxtile = std::max(sc.Tb ? sc.tb : 0, sc.Td ? sc.td : 0);
-  int C = ctas > 0 ? ctas : device_sms() * 2;
+  int C = ctas > 0 ? ctas : device_sms();
   C = (int)std::max<int64_t>(1, std::min<int64_t>(C, sc.Btot / maxtile));  // every CTA owns >= 1 tile
   sc.C = C;
   const int64_t m = sc.Btot / C;
   sc.S = (int)(sc.Ub / m) + 4;
   Plan pl;
   pl.sc = sc;
-  pl.meta_bytes = body ? hkv::meta_slot_bytes(group) : 0;
-  pl.slot_bytes = std::max(body ? hkv::i4_raw_bytes(fmt, group) : 0, dense ? hkv::dense_slot_bytes() : 0);
-  pl.slot_bytes = (std::max(pl.slot_bytes, 1024) + 1023) / 1024 * 1024;  // swizzled dense halves need 1 KiB
   pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4;
-  const int avail = kDynSmemBudget - 1024 - hkv::kMetaSlots * pl.meta_bytes - pl.comb_bytes;
-  pl.nslots = std::min(hkv::kMaxSlots, avail / pl.slot_bytes);
+  const int avail = kDynSmemBudget - 1024 - pl.comb_bytes;
+  pl.nslots = std::min(hkv::kMaxSlots, avail / hkv::kSlotBytes);
   if (pl.nslots < 2) return HKV_ERR_UNSUPPORTED;
   // + 1 KiB so the kernel can align the ring to 1024 bytes
-  pl.smem = 1024 + pl.nslots * pl.slot_bytes + hkv::kMetaSlots * pl.meta_bytes + pl.comb_bytes;
+  pl.smem = 1024 + pl.nslots * hkv::kSlotBytes + pl.comb_bytes;
   pl.ws_bytes = kCounterBytes + (size_t)sc.U * sc.S * G * (HKV_D + 2) * sizeof(float);
   *out = pl;
   return HKV_OK;
@@ -245,9 +244,7 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
     while ((1 << sh) < body->page_tokens) ++sh;
     p.page_shift = sh;
   }
-  p.slot_bytes = pl.slot_bytes;
   p.nslots = pl.nslots;
-  p.meta_bytes = pl.meta_bytes;
   p.counters = static_cast<int*>(workspace);
   p.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
   p.part_ml = p.part_o + (size_t)pl.sc.U * pl.sc.S * p.G * HKV_D;
@@ -287,14 +284,17 @@ int hkv_version(void) { return HKV_VERSION; }
 hkv_status hkv_device_error(uint32_t* bits, int clear) {
   if (!bits) return HKV_ERR_ARG;
   unsigned int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_hkv_dev_error, sizeof(v)) != cudaSuccess) return HKV_ERR_CUDA;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_hkv_dev_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e);
   *bits = v;
   if (clear) {
     const unsigned int z = 0;
-    if (cudaMemcpyToSymbol(g_hkv_dev_error, &z, sizeof(z)) != cudaSuccess) return HKV_ERR_CUDA;
+    if ((e = cudaMemcpyToSymbol(g_hkv_dev_error, &z, sizeof(z))) != cudaSuccess) return cuda_fail(e);
   }
   return HKV_OK;
 }
+
+int32_t hkv_last_cuda_error(void) { return t_last_cuda_error; }
 
 int64_t hkv_side_page_bytes(int32_t format, int32_t group, int32_t page_tokens) {
   if (!valid_group(group) || page_tokens <= 0) return -1;
@@ -563,15 +563,18 @@ hkv_status hkv_prefetch_submit(hkv_prefetcher* pf, const int32_t* src_pages, con
     int run = 1;  // coalesce consecutive (src, dst) pairs into one copy
     while (i + run < n && src_pages[i + run] == src_pages[i] + run && dst_slots[i + run] == dst_slots[i] + run) ++run;
     const size_t bytes = (size_t)run * pf->page_bytes;
-    if (cudaMemcpyAsync(pf->dev + (int64_t)dst_slots[i] * pf->page_bytes,
-                        pf->host + (int64_t)src_pages[i] * pf->page_bytes, bytes, cudaMemcpyHostToDevice,
-                        S(stream)) != cudaSuccess)
-      return HKV_ERR_CUDA;
+    const cudaError_t e = cudaMemcpyAsync(pf->dev + (int64_t)dst_slots[i] * pf->page_bytes,
+                                          pf->host + (int64_t)src_pages[i] * pf->page_bytes, bytes,
+                                          cudaMemcpyHostToDevice, S(stream));
+    if (e != cudaSuccess) return cuda_fail(e);
     total += (int64_t)bytes;
     i += run;
   }
   pf->bytes.fetch_add(total);
-  if (done && cudaEventRecord(reinterpret_cast<cudaEvent_t>(done), S(stream)) != cudaSuccess) return HKV_ERR_CUDA;
+  if (done) {
+    const cudaError_t e = cudaEventRecord(reinterpret_cast<cudaEvent_t>(done), S(stream));
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
   return HKV_OK;
 }
 
@@ -585,7 +588,7 @@ hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us) {
     if (q == cudaSuccess) return HKV_OK;
     if (q != cudaErrorNotReady) {
       cudaGetLastError();
-      return HKV_ERR_CUDA;
+      return cuda_fail(q);
     }
     const auto el = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0);
     if (el.count() >= timeout_us) return HKV_ERR_TIMEOUT;

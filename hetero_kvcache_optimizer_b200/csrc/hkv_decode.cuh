@@ -4,18 +4,20 @@
 // Schedule. The work of every (sequence, KV head) unit is a list of tiles:
 // 128-token INT4 body tiles, then 32-token dense tiles. Tiles are weighted by
 // their HBM bytes and the whole list (all units) is cut into one contiguous,
-// equal-byte range per CTA of a persistent grid (2 CTAs per SM). A CTA's range
-// is a short sequence of pieces: runs of tiles of one (unit, segment). Each
-// piece ends in an un-normalised partial (m, l, O) for the unit's G query
+// equal-byte range per CTA of a persistent grid (one CTA per SM). A CTA's
+// range is a short sequence of pieces: runs of tiles of one (unit, segment).
+// Each piece ends in an un-normalised partial (m, l, O) for the unit's G query
 // heads; the CTA that delivers a unit's last partial merges them.
 //
-// Pipeline. Warp 4 is the producer. It streams tiles into a shared-memory ring
-// with the TMA engine (no multicast): INT4 tiles as 1-D bulk copies of their
-// code and metadata blocks, dense tiles as 2-D tensor copies with 128-byte
-// swizzle. It then expands each INT4 tile's group metadata (f16 or u8) into an
-// fp32 / f16x2 form, and zeroes what lies past the sequence length, before
-// releasing the tile to warps 0-3. Those compute with m16n8k16 tensor-core MMAs
-// (N = 8 query heads, G <= 8 used):
+// Pipeline (320 threads). The loaded HBM latency on B200 is ~2.6 us, so an SM
+// needs ~128 KB of reads in flight to stream at full bandwidth: the ring has
+// eight 24 KB slots. Warp 8 issues the TMA copies (no multicast): INT4 tiles as
+// 1-D bulk copies of their code and metadata blocks, dense tiles as 2-D tensor
+// copies with 128-byte swizzle. Warp 9 expands each INT4 tile's group metadata
+// (f16 or u8) in place into fp32 / f16x2 and zeroes what lies past the sequence
+// length. Warps 0-7 are two consumer groups that take alternate tiles; each
+// warp computes 32 tokens of a tile with m16n8k16 tensor-core MMAs (N = 8
+// query heads, G <= 8 used):
 //   S^T[tok][head] = K[tok][:] . Q^T      (M = 16 tokens, K = dims)
 //   O^T[dim][head] += V^T[dim][tok] . P^T (M = 16 dims,   K = tokens)
 // INT4 K and V fragments come straight from the packed nibbles (the page
@@ -27,21 +29,25 @@
 //      score = sum_g s_g * acc_g + b_g * sum(Q_g)        (b = -z*s or min)
 //   V: codes are exact integers n (bias removed in f16), the B operand is
 //      s * P / 16, so O = 16 * (acc + sum_t b_t P_t / 16).
-// The online softmax is fp32 in the base-2 domain, one max-reduction per 32
-// tokens and warp, with a lazy rescale (the running max only moves when a tile
-// beats it by more than 2^8).
+// The online softmax is fp32 in the base-2 domain with a lazy rescale: the
+// running max only moves (one warp-wide max reduction) when a score beats it by
+// more than 2^8.
 #pragma once
 #include "hkv_common.cuh"
 
 namespace hkv {
 
-constexpr int kConsumerWarps = 4;
+constexpr int kGroupWarps = 4;                      // warps per consumer group
+constexpr int kConsumerWarps = 2 * kGroupWarps;     // two groups take alternate tiles
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kDecodeThreads = kConsumerThreads + 32;
+constexpr int kIssueWarp = kConsumerWarps;          // TMA issue
+constexpr int kExpandWarp = kConsumerWarps + 1;     // metadata expansion
+constexpr int kDecodeThreads = (kConsumerWarps + 2) * 32;
 constexpr int kTileI4 = 128;  // tokens per INT4 tile (32 per consumer warp)
 constexpr int kTileD = 32;    // tokens per dense tile (8 per consumer warp)
-constexpr int kMaxSlots = 6;
-constexpr int kMetaSlots = 2;
+constexpr int kMaxSlots = 8;
+constexpr int kSlotBytes = 24 * 1024;   // INT4: K codes 8 KB | V codes 8 KB | metadata 8 KB
+constexpr int kMetaOff = 16 * 1024;
 constexpr float kLazyRescale = 8.0f;
 constexpr int kDenseHalf = kTileD * 128;  // bytes of one 64-dim half of 32 dense rows (swizzled)
 
@@ -67,7 +73,7 @@ struct DecodeParams {
   int B, Hq, Hkv, G;
   float qscale;  // sm_scale * log2(e)
   Sched sc;
-  int slot_bytes, nslots, meta_bytes;
+  int nslots;
   int page_shift;  // log2(page_tokens) when a power of two, else -1
   float* part_o;   // [U][S][G][128]  un-normalised partial outputs
   float* part_ml;  // [U][S][G][2]    (m, l), base-2 logits
@@ -79,13 +85,16 @@ struct DecodeParams {
   float* out_ml;   // [B][Hq][2]
 };
 
-__host__ __device__ constexpr int i4_raw_bytes(int fmt, int group) {
-  return 2 * kTileI4 * HKV_CODE_BYTES + 2 * kTileI4 * 4 * (HKV_D / group) +
-         (fmt == HKV_FMT_REF ? 2 * kTileI4 * (HKV_D / group) : 0);
+// Raw metadata of one INT4 tile as copied: fp16min: K (s,min) f16x2 [128][NG] | V ...;
+// ref: K scales f32 [128][NG] | V scales | K zps u8 [128][NG] | V zps. Expanded in
+// place (floats): K scale [128][NG] | K bias [128][NG] | V scale pairs f16x2 [64][NG]
+// (tokens 2p, 2p+1) | V bias [128][NG].
+__host__ __device__ constexpr int meta_raw_bytes(int fmt, int group) {
+  return 2 * kTileI4 * 4 * (HKV_D / group) + (fmt == HKV_FMT_REF ? 2 * kTileI4 * (HKV_D / group) : 0);
 }
 __host__ __device__ constexpr int dense_slot_bytes() { return 4 * kDenseHalf; }
-// expanded metadata of one INT4 tile: K scale f32, K bias f32, V scale f16x2 (s,s), V bias f32
-__host__ __device__ constexpr int meta_slot_bytes(int group) { return kTileI4 * (HKV_D / group) * 16; }
+static_assert(kMetaOff + 14 * kTileI4 * 4 <= kSlotBytes, "expanded metadata (g32) must fit its slot");
+static_assert(2 * kTileI4 * HKV_CODE_BYTES == kMetaOff && dense_slot_bytes() <= kSlotBytes, "slot layout");
 
 // ---------------------------------------------------------------- schedule arithmetic (per piece, not per tile)
 __device__ __forceinline__ int64_t cta_begin(const Sched& s, int c) { return (int64_t)c * s.Btot / s.C; }
@@ -197,6 +206,10 @@ struct Ring {
 
 // ---------------------------------------------------------------- warp state / softmax
 // Thread (r = lane/4, j = lane%4) owns heads 2j and 2j+1 in every accumulator.
+// The running max starts at a finite "no score yet" value, so that 2^(x - m)
+// is 0 for a masked score (x = -inf) and never NaN, without a test per score.
+constexpr float kNoMax = -1.0e30f;
+
 template <int NG>
 struct WarpState {
   float o[8][4];      // O^T, m-tile mt: (dim 16mt+r | 16mt+r+8) x (head 2j | 2j+1)
@@ -212,28 +225,34 @@ __device__ __forceinline__ void ws_reset(WarpState<NG>& ws) {
   for (int mt = 0; mt < 8; ++mt) ws.o[mt][0] = ws.o[mt][1] = ws.o[mt][2] = ws.o[mt][3] = 0.f;
 #pragma unroll
   for (int g = 0; g < NG; ++g) ws.zacc[g][0] = ws.zacc[g][1] = 0.f;
-  ws.m[0] = ws.m[1] = ws.mo[0] = ws.mo[1] = -INFINITY;
+  ws.m[0] = ws.m[1] = ws.mo[0] = ws.mo[1] = kNoMax;
   ws.l[0] = ws.l[1] = 0.f;
 }
 
+// One online-softmax step over this thread's scores x (x[i] belongs to head
+// 2j + (i & 1); -inf = masked). The max moves only when some score beats it by
+// more than kLazyRescale, so the common step needs one vote and no cross-lane
+// max reduction. P = 2^(x - m - off) stays below 2^(8 - off).
 template <int NG, int N>
 __device__ __forceinline__ void softmax_step(WarpState<NG>& ws, const float (&x)[N], float (&P)[N], float off) {
-  float t0 = x[0], t1 = x[1];  // x[i] belongs to head 2j + (i & 1)
+  const float th0 = ws.m[0] + kLazyRescale, th1 = ws.m[1] + kLazyRescale;
+  bool need = false;
 #pragma unroll
-  for (int i = 2; i < N; i += 2) {
-    t0 = fmaxf(t0, x[i]);
-    t1 = fmaxf(t1, x[i + 1]);
-  }
-#pragma unroll
-  for (int s = 4; s < 32; s <<= 1) {
-    t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, s));
-    t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, s));
-  }
-  const bool need = (t0 > ws.m[0] + kLazyRescale) || (t1 > ws.m[1] + kLazyRescale);
+  for (int i = 0; i < N; i += 2) need |= (x[i] > th0) | (x[i + 1] > th1);
   if (__any_sync(0xffffffffu, need)) {
+    float t0 = x[0], t1 = x[1];
+#pragma unroll
+    for (int i = 2; i < N; i += 2) {
+      t0 = fmaxf(t0, x[i]);
+      t1 = fmaxf(t1, x[i + 1]);
+    }
+#pragma unroll
+    for (int s = 4; s < 32; s <<= 1) {
+      t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, s));
+      t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, s));
+    }
     const float n0 = fmaxf(ws.m[0], t0), n1 = fmaxf(ws.m[1], t1);
-    const float a0 = ws.m[0] == -INFINITY ? 0.f : fast_exp2(ws.m[0] - n0);
-    const float a1 = ws.m[1] == -INFINITY ? 0.f : fast_exp2(ws.m[1] - n1);
+    const float a0 = fast_exp2(ws.m[0] - n0), a1 = fast_exp2(ws.m[1] - n1);
     ws.m[0] = n0;
     ws.m[1] = n1;
     ws.mo[0] = n0 + off;
@@ -254,7 +273,7 @@ __device__ __forceinline__ void softmax_step(WarpState<NG>& ws, const float (&x)
     ws.l[1] *= a1;
   }
 #pragma unroll
-  for (int i = 0; i < N; ++i) P[i] = x[i] == -INFINITY ? 0.f : fast_exp2(x[i] - ws.mo[i & 1]);
+  for (int i = 0; i < N; ++i) P[i] = fast_exp2(x[i] - ws.mo[i & 1]);
 #pragma unroll
   for (int i = 0; i < N; i += 2) {
     ws.l[0] += P[i];
@@ -296,7 +315,8 @@ __device__ __forceinline__ void ld_row_u(const uint32_t* base, int row, uint32_t
   }
 }
 
-// Scores of 16 tokens x 8 heads: x = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)} (unscaled).
+// Scores of 16 tokens x 8 heads: x = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)},
+// already in base-2 logits (the expanded K scale and qsum carry sm_scale*log2 e).
 // kc / ks / kb point at this thread's row r of the tile's K codes / K scale / K bias.
 template <int NG>
 __device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, const float* kb,
@@ -343,25 +363,28 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
 }
 
 // O^T += V^T . (s P/16)^T for 16 tokens; P = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)}
-// pre-scaled by 1/16. vc points at this thread's V chunk (pair j, chunk r);
-// vs2 / vb at row r of the V scale (f16x2) / bias.
+// pre-scaled by 1/16. vc points at this thread's V chunk (pair j, chunk r), vsp
+// at the subtile's V scale pairs (pair 0 = its tokens 0, 1), vb at row r of the
+// V bias. P is transposed once into the B layout (token pair 2j, 2j+1 of head
+// r) and multiplied by the pair's per-group scales there.
 template <int NG>
-__device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* vc, const uint32_t* vs2,
+__device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* vc, const uint32_t* vsp,
                                              const float* vb, const float (&P)[4]) {
   constexpr int WPG = 4 / NG;
+  const int j = threadIdx.x & 3;
   uint32_t sA[NG], sB[NG];
   float bA[NG], bB[NG];
-  ld_row_u<NG>(vs2, 0, sA);
-  ld_row_u<NG>(vs2, 8, sB);
+  ld_row_u<NG>(vsp, j, sA);
+  ld_row_u<NG>(vsp, 4 + j, sB);
   ld_row<NG>(vb, 0, bA);
   ld_row<NG>(vb, 8, bB);
-  const uint32_t pA = pack2<__half>(P[0], P[1]);
-  const uint32_t pB = pack2<__half>(P[2], P[3]);
+  const uint32_t tA = movmatrix_t(pack2<__half>(P[0], P[1]));
+  const uint32_t tB = movmatrix_t(pack2<__half>(P[2], P[3]));
   uint32_t pb[NG][2];
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
-    pb[g][0] = movmatrix_t(hmul2(pA, sA[g]));
-    pb[g][1] = movmatrix_t(hmul2(pB, sB[g]));
+    pb[g][0] = hmul2(tA, sA[g]);
+    pb[g][1] = hmul2(tB, sB[g]);
     ws.zacc[g][0] = fmaf(bA[g], P[0], fmaf(bB[g], P[2], ws.zacc[g][0]));
     ws.zacc[g][1] = fmaf(bA[g], P[1], fmaf(bB[g], P[3], ws.zacc[g][1]));
   }
@@ -394,7 +417,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t half_base, int row, int chunk) 
 
 template <typename DTy, int NG>
 __device__ __forceinline__ void dense_subtile(WarpState<NG>& ws, uint32_t slot, int t0, bool ok,
-                                              const uint32_t (&qf)[8][2], bool h0, bool h1, float qscale) {
+                                              const uint32_t (&qf)[8][2], float qscale) {
   const int lane = threadIdx.x & 31;
   const int row = t0 + (lane & 7);  // rows r+8 of the 16-row fragments repeat rows r and are masked
   float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -405,8 +428,8 @@ __device__ __forceinline__ void dense_subtile(WarpState<NG>& ws, uint32_t slot, 
     mma16816<DTy>(c, a, qf[kt][0], qf[kt][1]);
   }
   float x[4];
-  x[0] = (ok && h0) ? c[0] * qscale : -INFINITY;
-  x[1] = (ok && h1) ? c[1] * qscale : -INFINITY;
+  x[0] = ok ? c[0] * qscale : -INFINITY;
+  x[1] = ok ? c[1] * qscale : -INFINITY;
   x[2] = -INFINITY;
   x[3] = -INFINITY;
   float P[4];
@@ -423,7 +446,8 @@ __device__ __forceinline__ void dense_subtile(WarpState<NG>& ws, uint32_t slot, 
 
 // Q^T B fragments for this lane: head r (= lane/4), dims 16kt + 2j + {0,1} in
 // qf[kt][0] and 16kt + 2j + {8,9} in qf[kt][1] (divided by 16 when hi_div16).
-// qa/qb return the values exactly as the tensor core sees them.
+// qa/qb return the values exactly as the tensor core sees them. Heads r >= G
+// get Q = 0: their scores are finite and their results are never stored.
 template <typename T>
 __device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int hk, bool hi_div16,
                                              uint32_t (&qf)[8][2], float (&qa)[8][2], float (&qb)[8][2]) {
@@ -455,7 +479,28 @@ __device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int h
   }
 }
 
+// Named barrier 1 over the consumer warps only (the TMA and expansion warps never join it).
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
+// Same barrier, returning whether v held on every consumer thread.
+__device__ __forceinline__ bool consumer_sync_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kConsumerThreads)
+      : "memory");
+  return r != 0;
+}
+
+// Bounded mbarrier wait with a warp-uniform outcome: lanes that reach the
+// timeout at different moments must not split the warp before the next
+// warp-synchronous instruction (mma.sync, shuffles, movmatrix).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
 
 __device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
                                             uint64_t* bar) {
@@ -466,43 +511,86 @@ __device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// ---------------------------------------------------------------- producer helpers
-// Slots at or past `valid` (beyond the sequence length) may hold uninitialised
-// pool bytes: their expanded scale and bias are written as zeros, so a masked
-// token (P = 0) contributes exactly 0 and never NaN.
+// ---------------------------------------------------------------- metadata expansion (warp kExpandWarp)
+// Expands one INT4 tile's metadata in place (all raw values are read into
+// registers before the first write). Entries are [token][group]; lane L holds
+// entries 128 it + 4 L + {0..3}. Tokens at or past `valid` (beyond the sequence
+// length) may hold uninitialised pool bytes: their scale and bias become 0, so
+// a masked token (P = 0) contributes exactly 0 and never NaN. The K scale is
+// multiplied by qs (sm_scale * log2 e) so scores come out as base-2 logits.
 template <int FMT, int NG>
-__device__ __forceinline__ void expand_meta(const uint8_t* raw, uint8_t* meta, int lane, int valid) {
-  // raw: K scales | V scales | K zps | V zps (ref) ; K (s,min) | V (s,min) (fp16min), each [128][NG]
-  float* ks = reinterpret_cast<float*>(meta);
-  float* kb = ks + kTileI4 * NG;
-  uint32_t* vs2 = reinterpret_cast<uint32_t*>(kb + kTileI4 * NG);
-  float* vb = reinterpret_cast<float*>(vs2 + kTileI4 * NG);
+__device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, float qs) {
   constexpr int N = kTileI4 * NG;
-#pragma unroll 4
-  for (int i = lane; i < N; i += 32) {
-    float sk, bk, sv, bv;
+  constexpr int IT = N / 128;
+  float sk[IT][4], bk[IT][4], sv[IT][4], bv[IT][4];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int e = 128 * it + 4 * lane;
     if (FMT == HKV_FMT_REF) {
-      const float* sc = reinterpret_cast<const float*>(raw);
-      const uint8_t* zp = raw + 2 * N * 4;
-      sk = sc[i];
-      sv = sc[N + i];
-      bk = -static_cast<float>(zp[i]) * sk;
-      bv = -static_cast<float>(zp[N + i]) * sv;
+      const float4 a = *reinterpret_cast<const float4*>(meta + 4 * e);
+      const float4 c = *reinterpret_cast<const float4*>(meta + 4 * N + 4 * e);
+      const uint32_t zk = *reinterpret_cast<const uint32_t*>(meta + 8 * N + e);
+      const uint32_t zv = *reinterpret_cast<const uint32_t*>(meta + 9 * N + e);
+      const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sk[it][i] = av[i];
+        sv[it][i] = cv[i];
+        bk[it][i] = -static_cast<float>((zk >> (8 * i)) & 0xffu) * av[i];
+        bv[it][i] = -static_cast<float>((zv >> (8 * i)) & 0xffu) * cv[i];
+      }
     } else {
-      const __half2* sm = reinterpret_cast<const __half2*>(raw);
-      const float2 fk = __half22float2(sm[i]);
-      const float2 fv = __half22float2(sm[N + i]);
-      sk = fk.x;
-      bk = fk.y;
-      sv = fv.x;
-      bv = fv.y;
+      const uint4 a = *reinterpret_cast<const uint4*>(meta + 4 * e);
+      const uint4 c = *reinterpret_cast<const uint4*>(meta + 4 * N + 4 * e);
+      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 fk = __half22float2(*reinterpret_cast<const __half2*>(&av[i]));
+        const float2 fv = __half22float2(*reinterpret_cast<const __half2*>(&cv[i]));
+        sk[it][i] = fk.x;
+        bk[it][i] = fk.y;
+        sv[it][i] = fv.x;
+        bv[it][i] = fv.y;
+      }
     }
-    if (i / NG >= valid) sk = bk = sv = bv = 0.f;
-    ks[i] = sk;
-    kb[i] = bk;
-    vs2[i] = pack2<__half>(sv, sv);
-    vb[i] = bv;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if ((e + i) / NG >= valid) sk[it][i] = bk[it][i] = sv[it][i] = bv[it][i] = 0.f;
+    }
   }
+  __syncwarp();
+  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + 8 * N);  // [N/NG/2 pairs][NG] f16x2
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int e = 128 * it + 4 * lane;
+    *reinterpret_cast<float4*>(meta + 4 * e) =
+        make_float4(sk[it][0] * qs, sk[it][1] * qs, sk[it][2] * qs, sk[it][3] * qs);
+    *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[it][0], bk[it][1], bk[it][2], bk[it][3]);
+    *reinterpret_cast<float4*>(meta + 10 * N + 4 * e) = make_float4(bv[it][0], bv[it][1], bv[it][2], bv[it][3]);
+    if constexpr (NG == 4) {
+      // lane holds token 32 it + lane; its pair partner is lane ^ 1
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, sv[it][i], 1);
+      if ((lane & 1) == 0) {
+        const int pair = 16 * it + (lane >> 1);
+        *reinterpret_cast<uint4*>(vsp + pair * 4) =
+            make_uint4(pack2<__half>(sv[it][0], o[0]), pack2<__half>(sv[it][1], o[1]),
+                       pack2<__half>(sv[it][2], o[2]), pack2<__half>(sv[it][3], o[3]));
+      }
+    } else if constexpr (NG == 2) {
+      // entries: (t, g0), (t, g1), (t+1, g0), (t+1, g1) with t = 64 it + 2 lane
+      const int pair = 32 * it + lane;
+      *reinterpret_cast<uint2*>(vsp + pair * 2) =
+          make_uint2(pack2<__half>(sv[it][0], sv[it][2]), pack2<__half>(sv[it][1], sv[it][3]));
+    } else {
+      // tokens 4 lane .. 4 lane + 3: pairs 2 lane, 2 lane + 1
+      *reinterpret_cast<uint2*>(vsp + 2 * lane) =
+          make_uint2(pack2<__half>(sv[it][0], sv[it][1]), pack2<__half>(sv[it][2], sv[it][3]));
+    }
+  }
+  // order these generic-proxy writes before later TMA (async-proxy) writes to the slot
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Zero dense V rows [valid, 32) of a swizzled slot (whole 128-byte rows, so the
@@ -515,11 +603,10 @@ __device__ __forceinline__ void zero_dense_v_tail(uint8_t* slot, int valid, int 
     const int rr = valid + i / 16, h = (i >> 3) & 1, ch = i & 7;
     *reinterpret_cast<uint4*>(v + h * kDenseHalf + rr * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
   }
-  // order these generic-proxy writes before later TMA (async-proxy) writes to the slot
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Producer cursor over the CTA's tiles that hold tokens.
+// Cursor over the CTA's tiles that hold tokens (the loads, in ring order).
 struct Cursor {
   Piece pc;
   int k;
@@ -532,6 +619,11 @@ __device__ __forceinline__ void cursor_settle(const DecodeParams& p, int64_t end
   }
   cu.valid = cu.pc.valid;
 }
+__device__ __forceinline__ void cursor_start(const DecodeParams& p, int c, int64_t end, Cursor& cu) {
+  cu.pc = first_piece(p, c, end);
+  cu.k = cu.pc.k0;
+  cursor_settle(p, end, cu);
+}
 __device__ __forceinline__ void cursor_next(const DecodeParams& p, int64_t end, Cursor& cu) {
   cu.k++;
   cursor_settle(p, end, cu);
@@ -539,13 +631,13 @@ __device__ __forceinline__ void cursor_next(const DecodeParams& p, int64_t end, 
 
 // ---------------------------------------------------------------- the persistent kernel
 template <int FMT, int GROUP, typename DTy>
-__global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
   constexpr int NG = HKV_D / GROUP;
+  constexpr int NM = kTileI4 * NG;  // metadata entries per array of a tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t ready_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t empty_bar[kMaxSlots];
-  __shared__ __align__(8) uint64_t mempty_bar[kMetaSlots];
   __shared__ int s_last;
 
   // the 128-byte swizzle of the dense tiles repeats every 1024 bytes: align the ring
@@ -555,47 +647,49 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
   const int64_t end = cta_begin(sc, c + 1);
   const int nsl = p.nslots;
   uint8_t* ring = smem;
-  uint8_t* meta_ring = smem + nsl * p.slot_bytes;
-  float* comb = reinterpret_cast<float*>(meta_ring + kMetaSlots * p.meta_bytes);  // [4][G][128] + [4][8][2]
+  float* comb = reinterpret_cast<float*>(ring + nsl * kSlotBytes);  // [8][G][128] + [8][8][2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < nsl; ++i) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&ready_bar[i], 1);
-      mbar_init(&empty_bar[i], kConsumerWarps);
+      mbar_init(&empty_bar[i], kGroupWarps);
     }
-    for (int i = 0; i < kMetaSlots; ++i) mbar_init(&mempty_bar[i], kConsumerWarps);
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
-    // ================================================================ producer warp
-    Cursor ci, ce;  // issue runs ahead of expansion by up to nsl tiles
-    ci.pc = first_piece(p, c, end);
-    ci.k = ci.pc.k0;
-    cursor_settle(p, end, ci);
-    ce = ci;
-    Ring ri{0, 0u}, re{0, 0u};
-    int n_issue = 0, nb_exp = 0;
-    bool ok = true;
+  if (warp == kIssueWarp) {
+    // ================================================================ TMA issue warp
+    Cursor cu;
+    cursor_start(p, c, end, cu);
+    Ring ri{0, 0u};
+    int n = 0;
+    // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
+    int pg_u = -1, pg0 = 0, pg_lane = -1;
     const uint32_t codes_b = kTileI4 * HKV_CODE_BYTES;
     const uint32_t sc_b = kTileI4 * 4 * NG;
     const uint32_t zp_b = FMT == HKV_FMT_REF ? kTileI4 * NG : 0;
-    auto issue_one = [&]() {
-      if (!ci.valid || !ok) return;
-      if (n_issue >= nsl && !mbar_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) {
-        ok = false;
-        return;
-      }
-      uint8_t* sb = ring + ri.slot * p.slot_bytes;
+    while (cu.valid) {
+      if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
+      uint8_t* sb = ring + ri.slot * kSlotBytes;
       uint64_t* fb = &full_bar[ri.slot];
-      const int u = ci.pc.u;
-      if (lane == 0) {
-        if (ci.pc.seg == 0) {
-          const int t = ci.k * kTileI4;
-          const int64_t page = store_page(p.body, u, t);
+      const int u = cu.pc.u;
+      if (cu.pc.seg == 0) {
+        const int t = cu.k * kTileI4;
+        const int pi = p.page_shift >= 0 ? t >> p.page_shift : t / p.body.page_tokens;
+        if (u != pg_u || pi < pg0 || pi >= pg0 + 32) {
+          pg_u = u;
+          pg0 = pi;
+          const int pl = pi + lane;
+          pg_lane = -1;
+          if (pl < p.body.max_pages)
+            pg_lane = p.body.page_table ? p.body.page_table[(int64_t)u * p.body.max_pages + pl]
+                                        : (int)((int64_t)u * p.body.max_pages + pl);
+        }
+        const int page = __shfl_sync(0xffffffffu, pg_lane, pi - pg0);
+        if (lane == 0) {
           if (page < 0) {
             hkv_flag_error(HKV_DEVERR_BAD_PAGE);
             mbar_arrive(fb);
@@ -606,69 +700,77 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
             mbar_arrive_expect_tx(fb, 2 * (codes_b + sc_b + zp_b));
             bulk_g2s(sb, ka.codes, codes_b, fb);
             bulk_g2s(sb + codes_b, va.codes, codes_b, fb);
-            bulk_g2s(sb + 2 * codes_b, ka.scales, sc_b, fb);
-            bulk_g2s(sb + 2 * codes_b + sc_b, va.scales, sc_b, fb);
+            bulk_g2s(sb + kMetaOff, ka.scales, sc_b, fb);
+            bulk_g2s(sb + kMetaOff + sc_b, va.scales, sc_b, fb);
             if (FMT == HKV_FMT_REF) {
-              bulk_g2s(sb + 2 * codes_b + 2 * sc_b, ka.zps, zp_b, fb);
-              bulk_g2s(sb + 2 * codes_b + 2 * sc_b + zp_b, va.zps, zp_b, fb);
+              bulk_g2s(sb + kMetaOff + 2 * sc_b, ka.zps, zp_b, fb);
+              bulk_g2s(sb + kMetaOff + 2 * sc_b + zp_b, va.zps, zp_b, fb);
             }
           }
-        } else {
-          const int b = u / p.Hkv, hk = u % p.Hkv, t = ci.k * kTileD;
-          const uint32_t d = smem_u32(sb);
-          mbar_arrive_expect_tx(fb, dense_slot_bytes());
-          tma_tile_4d(d, &p.tmk, 0, t, hk, b, fb);
-          tma_tile_4d(d + kDenseHalf, &p.tmk, 64, t, hk, b, fb);
-          tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
-          tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
         }
+      } else if (lane == 0) {
+        const int b = u / p.Hkv, hk = u - b * p.Hkv, t = cu.k * kTileD;
+        const uint32_t d = smem_u32(sb);
+        mbar_arrive_expect_tx(fb, dense_slot_bytes());
+        tma_tile_4d(d, &p.tmk, 0, t, hk, b, fb);
+        tma_tile_4d(d + kDenseHalf, &p.tmk, 64, t, hk, b, fb);
+        tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
+        tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
       }
-      n_issue++;
+      n++;
       ri.advance(nsl);
-      cursor_next(p, end, ci);
-    };
-    for (int i = 0; i < nsl - 1; ++i) issue_one();
-    while (ok && ce.valid) {
-      if (!mbar_wait(&full_bar[re.slot], re.phase)) break;
-      uint8_t* sb = ring + re.slot * p.slot_bytes;
-      if (ce.pc.seg == 0) {
-        const int ms = nb_exp & (kMetaSlots - 1);
-        if (nb_exp >= kMetaSlots && !mbar_wait(&mempty_bar[ms], ((nb_exp / kMetaSlots) & 1) ^ 1)) break;
-        expand_meta<FMT, NG>(sb + 2 * codes_b, meta_ring + ms * p.meta_bytes, lane, ce.pc.len - ce.k * kTileI4);
-        nb_exp++;
+      cursor_next(p, end, cu);
+    }
+    // every issued copy must have landed before the CTA exits
+    if (lane == 0) {
+      for (int i = max(0, n - nsl); i < n; ++i) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
+    }
+    return;
+  }
+
+  if (warp == kExpandWarp) {
+    // ================================================================ metadata expansion warp
+    Cursor cu;
+    cursor_start(p, c, end, cu);
+    Ring re{0, 0u};
+    while (cu.valid) {
+      if (!warp_wait(&full_bar[re.slot], re.phase)) break;
+      uint8_t* sb = ring + re.slot * kSlotBytes;
+      if (cu.pc.seg == 0) {
+        expand_meta<FMT, NG>(sb + kMetaOff, lane, cu.pc.len - cu.k * kTileI4, p.qscale);
       } else {
-        zero_dense_v_tail(sb, ce.pc.len - ce.k * kTileD, lane);
+        zero_dense_v_tail(sb, cu.pc.len - cu.k * kTileD, lane);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&ready_bar[re.slot]);
       re.advance(nsl);
-      cursor_next(p, end, ce);
-      issue_one();
-    }
-    // drain: every issued copy must have landed before the CTA exits
-    if (lane == 0) {
-      for (int i = max(0, n_issue - nsl); i < n_issue; ++i) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
+      cursor_next(p, end, cu);
     }
     return;
   }
 
   // ================================================================== consumer warps
+  // Group grp (warps 4 grp .. 4 grp + 3) takes the loads n with n % 2 == grp;
+  // warp wg of the group computes tokens [32 wg, 32 wg + 32) of an INT4 tile and
+  // [8 wg, 8 wg + 8) of a dense tile.
   WarpState<NG> ws;
   uint32_t qf[8][2];
   float qsum[NG][2], nbias[NG][2];
   const int r = lane >> 2, j = lane & 3;
+  const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
   const bool h0 = 2 * j < p.G, h1 = 2 * j + 1 < p.G;
   const float qs = p.qscale;
-  Ring rc{0, 0u};
-  int nb_load = 0;
-  // per-thread offsets inside an INT4 slot / its expanded metadata
-  const int t0 = warp * 32;
+  Ring rc{grp, 0u};  // ring position of this group's next load
+  int n_next = grp;  // index of this group's next load
+  int n_base = 0;    // index of the current piece's first load
+  const int t0 = wg * 32;
   const int kc_off = (t0 + r) * HKV_CODE_BYTES + 16 * j;
   const int vc_off = kTileI4 * HKV_CODE_BYTES + (t0 + 2 * j) * HKV_CODE_BYTES + 16 * r;
-  const int mrow = (t0 + r) * NG;
+  const int ks_off = (t0 + r) * NG;  // floats
+  const int vs_off = (t0 / 2) * NG;  // f16x2 words
 
   for (Piece pc = first_piece(p, c, end); pc.valid; next_piece(p, end, pc)) {
-    const int u = pc.u, b = u / p.Hkv, hk = u % p.Hkv;
+    const int u = pc.u, b = u / p.Hkv, hk = u - b * p.Hkv;
     // ---- begin piece: query fragments for this unit
     {
       float qa[8][2], qb[8][2];
@@ -689,8 +791,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
           ps[g] += __shfl_xor_sync(0xffffffffu, ps[g], 2);
           pbias[g] += __shfl_xor_sync(0xffffffffu, pbias[g], 1);
           pbias[g] += __shfl_xor_sync(0xffffffffu, pbias[g], 2);
-          qsum[g][0] = __shfl_sync(0xffffffffu, ps[g], (2 * j) * 4);
-          qsum[g][1] = __shfl_sync(0xffffffffu, ps[g], (2 * j + 1) * 4);
+          qsum[g][0] = qs * __shfl_sync(0xffffffffu, ps[g], (2 * j) * 4);
+          qsum[g][1] = qs * __shfl_sync(0xffffffffu, ps[g], (2 * j + 1) * 4);
           nbias[g][0] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j) * 4);
           nbias[g][1] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j + 1) * 4);
         }
@@ -700,76 +802,67 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
     }
     ws_reset<NG>(ws);
 
-    // ---- the piece's tiles that hold tokens
+    // ---- this group's share of the piece's tiles that hold tokens
     bool alive = true;
+    const int n_end = n_base + max(0, pc.kd - pc.k0);
     if (pc.seg == 0) {
-      for (int k = pc.k0; k < pc.kd; ++k) {
-        if (!mbar_wait(&ready_bar[rc.slot], rc.phase)) {
+      for (; n_next < n_end; n_next += 2) {
+        const int k = pc.k0 + (n_next - n_base);
+        if (!warp_wait(&ready_bar[rc.slot], rc.phase)) {
           alive = false;
           break;
         }
-        const uint8_t* stg = ring + rc.slot * p.slot_bytes;
-        const int ms = nb_load & (kMetaSlots - 1);
-        const float* mk = reinterpret_cast<const float*>(meta_ring + ms * p.meta_bytes);
-        const float* ks = mk + mrow;
-        const float* kb = mk + kTileI4 * NG + mrow;
-        const uint32_t* vs2 = reinterpret_cast<const uint32_t*>(mk + 2 * kTileI4 * NG) + mrow;
-        const float* vb = mk + 3 * kTileI4 * NG + mrow;
+        const uint8_t* stg = ring + rc.slot * kSlotBytes;
+        const float* mk = reinterpret_cast<const float*>(stg + kMetaOff);
+        const float* ks = mk + ks_off;
+        const float* kb = mk + NM + ks_off;
+        const uint32_t* vsp = reinterpret_cast<const uint32_t*>(mk + 2 * NM) + vs_off;
+        const float* vb = mk + 2 * NM + NM / 2 + ks_off;
         float xa[4], xb[4], x[8], P[8];
         k_scores<NG>(stg + kc_off, ks, kb, qf, nbias, qsum, xa);
         k_scores<NG>(stg + kc_off + 16 * HKV_CODE_BYTES, ks + 16 * NG, kb + 16 * NG, qf, nbias, qsum, xb);
         const int tok = k * kTileI4 + t0;
-        if (tok + 32 <= pc.len) {
-          x[0] = h0 ? xa[0] * qs : -INFINITY;
-          x[1] = h1 ? xa[1] * qs : -INFINITY;
-          x[2] = h0 ? xa[2] * qs : -INFINITY;
-          x[3] = h1 ? xa[3] * qs : -INFINITY;
-          x[4] = h0 ? xb[0] * qs : -INFINITY;
-          x[5] = h1 ? xb[1] * qs : -INFINITY;
-          x[6] = h0 ? xb[2] * qs : -INFINITY;
-          x[7] = h1 ? xb[3] * qs : -INFINITY;
-        } else {
-          const bool ok0 = tok + r < pc.len, ok1 = tok + r + 8 < pc.len;
-          const bool ok2 = tok + 16 + r < pc.len, ok3 = tok + 24 + r < pc.len;
-          x[0] = (ok0 && h0) ? xa[0] * qs : -INFINITY;
-          x[1] = (ok0 && h1) ? xa[1] * qs : -INFINITY;
-          x[2] = (ok1 && h0) ? xa[2] * qs : -INFINITY;
-          x[3] = (ok1 && h1) ? xa[3] * qs : -INFINITY;
-          x[4] = (ok2 && h0) ? xb[0] * qs : -INFINITY;
-          x[5] = (ok2 && h1) ? xb[1] * qs : -INFINITY;
-          x[6] = (ok3 && h0) ? xb[2] * qs : -INFINITY;
-          x[7] = (ok3 && h1) ? xb[3] * qs : -INFINITY;
+        x[0] = xa[0];
+        x[1] = xa[1];
+        x[2] = xa[2];
+        x[3] = xa[3];
+        x[4] = xb[0];
+        x[5] = xb[1];
+        x[6] = xb[2];
+        x[7] = xb[3];
+        if (tok + 32 > pc.len) {
+          if (tok + r >= pc.len) x[0] = x[1] = -INFINITY;
+          if (tok + r + 8 >= pc.len) x[2] = x[3] = -INFINITY;
+          if (tok + r + 16 >= pc.len) x[4] = x[5] = -INFINITY;
+          if (tok + r + 24 >= pc.len) x[6] = x[7] = -INFINITY;
         }
         softmax_step<NG, 8>(ws, x, P, 4.f);
         const float pa[4] = {P[0], P[1], P[2], P[3]};
         const float pc4[4] = {P[4], P[5], P[6], P[7]};
-        v_accumulate<NG>(ws, stg + vc_off, vs2, vb, pa);
-        v_accumulate<NG>(ws, stg + vc_off + 16 * HKV_CODE_BYTES, vs2 + 16 * NG, vb + 16 * NG, pc4);
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&empty_bar[rc.slot]);
-          mbar_arrive(&mempty_bar[ms]);
-        }
-        nb_load++;
-        rc.advance(nsl);
-      }
-    } else {
-      const int dt0 = warp * 8;
-      for (int k = pc.k0; k < pc.kd; ++k) {
-        if (!mbar_wait(&ready_bar[rc.slot], rc.phase)) {
-          alive = false;
-          break;
-        }
-        const uint32_t slot = smem_u32(ring + rc.slot * p.slot_bytes);
-        dense_subtile<DTy, NG>(ws, slot, dt0, k * kTileD + dt0 + r < pc.len, qf, h0, h1, qs);
+        v_accumulate<NG>(ws, stg + vc_off, vsp, vb, pa);
+        v_accumulate<NG>(ws, stg + vc_off + 16 * HKV_CODE_BYTES, vsp + 8 * NG, vb + 16 * NG, pc4);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);
         rc.advance(nsl);
+        rc.advance(nsl);
+      }
+    } else {
+      const int dt0 = wg * 8;
+      for (; n_next < n_end; n_next += 2) {
+        const int k = pc.k0 + (n_next - n_base);
+        if (!warp_wait(&ready_bar[rc.slot], rc.phase)) {
+          alive = false;
+          break;
+        }
+        const uint32_t slot = smem_u32(ring + rc.slot * kSlotBytes);
+        dense_subtile<DTy, NG>(ws, slot, dt0, k * kTileD + dt0 + r < pc.len, qf, qs);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);
+        rc.advance(nsl);
+        rc.advance(nsl);
       }
     }
-    if (!alive) {
-      ws_reset<NG>(ws);  // a timed-out wait leaves a neutral partial (the error word is set)
-    }
+    n_base = n_end;
 
     // ---- end piece: per-warp partials -> shared memory -> one partial for the piece
     {
@@ -792,7 +885,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
         }
       }
       float* wo = comb + warp * p.G * HKV_D;
-      float* cml = comb + kConsumerWarps * p.G * HKV_D;  // [4][8][2]
+      float* cml = comb + kConsumerWarps * p.G * HKV_D;  // [8 warps][8 heads][2]
       const float osc = body ? 16.f : 1.f;                 // INT4 tiles accumulate with P/16
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
@@ -813,7 +906,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
         cml[(warp * 8 + 2 * j + 1) * 2] = ws.m[1];
         cml[(warp * 8 + 2 * j + 1) * 2 + 1] = l1 * osc;
       }
-      consumer_sync();
+      // a timed-out wait anywhere ends every consumer warp after this piece
+      // (the error word is set; the partials written below are meaningless)
+      alive = consumer_sync_and(alive);
       int b0, nb, d0, nd;
       unit_pieces(sc, u, b0, nb, d0, nd);
       const int slot = pc.seg == 0 ? c - b0 : nb + c - d0;
@@ -821,19 +916,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
       float* pml = p.part_ml + ((int64_t)u * sc.S + slot) * p.G * 2;
       for (int idx = threadIdx.x; idx < p.G * HKV_D; idx += kConsumerThreads) {
         const int h = idx / HKV_D, d = idx % HKV_D;
-        float M = -INFINITY;
+        float M = kNoMax;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cml[(w * 8 + h) * 2]);
         float acc = 0.f, L = 0.f;
-        if (M != -INFINITY) {
 #pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) {
-            const float mw = cml[(w * 8 + h) * 2];
-            if (mw == -INFINITY) continue;
-            const float e = fast_exp2(mw - M);
-            acc = fmaf(e, comb[(w * p.G + h) * HKV_D + d], acc);
-            L = fmaf(e, cml[(w * 8 + h) * 2 + 1], L);
-          }
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float e = fast_exp2(cml[(w * 8 + h) * 2] - M);
+          acc = fmaf(e, comb[(w * p.G + h) * HKV_D + d], acc);
+          L = fmaf(e, cml[(w * 8 + h) * 2 + 1], L);
         }
         po[idx] = acc;
         if (d == 0) {
@@ -846,13 +937,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
       if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[u], 1) == nb + nd - 1;
       consumer_sync();
       if (s_last) {
-        // last piece of the unit: merge all its partials (warp w: heads w, w+4)
+        // last piece of the unit: merge all its partials (warp h: head h)
         __threadfence();
         const int n = nb + nd;
         const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
         const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
         for (int h = warp; h < p.G; h += kConsumerWarps) {
-          float M = -INFINITY;
+          float M = kNoMax;
           for (int k = lane; k < n; k += 32) M = fmaxf(M, __ldcg(ml_u + (k * p.G + h) * 2));
 #pragma unroll
           for (int sft = 16; sft > 0; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
@@ -861,8 +952,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
           for (int k0 = 0; k0 < n; k0 += 32) {
             float wk = 0.f;
             if (k0 + lane < n) {
-              const float mk = __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2);
-              wk = (mk == -INFINITY || M == -INFINITY) ? 0.f : fast_exp2(mk - M);
+              wk = fast_exp2(__ldcg(ml_u + ((k0 + lane) * p.G + h) * 2) - M);
               L = fmaf(wk, __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2 + 1), L);
             }
             const int kn = min(32, n - k0);
@@ -882,7 +972,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2) decode_kernel(const __grid_
           if (p.out_o) {
             reinterpret_cast<float4*>(p.out_o + ((int64_t)b * p.Hq + hq) * HKV_D)[lane] = acc;
             if (lane == 0) {
-              p.out_ml[((int64_t)b * p.Hq + hq) * 2] = M;
+              // a row that attended to no token reports m = -inf
+              p.out_ml[((int64_t)b * p.Hq + hq) * 2] = L > 0.f ? M : -INFINITY;
               p.out_ml[((int64_t)b * p.Hq + hq) * 2 + 1] = L;
             }
           } else {

@@ -116,6 +116,9 @@ const char* hkv_status_str(hkv_status s);
 int hkv_version(void);
 /* Reads and optionally clears the sticky device error word (synchronises the device). */
 hkv_status hkv_device_error(uint32_t* bits, int clear);
+/* cudaError_t value behind the last HKV_ERR_CUDA returned to this host thread
+ * (0 if none). No counterpart in the reference (it raises Python exceptions). */
+int32_t hkv_last_cuda_error(void);
 /* Bytes of one page of one side for a format/group/page size. */
 int64_t hkv_side_page_bytes(int32_t format, int32_t group, int32_t page_tokens);
 
