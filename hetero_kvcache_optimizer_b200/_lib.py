@@ -21,6 +21,8 @@ HKV_ERR_UNSUPPORTED = 4
 HKV_ERR_CAPACITY = 5
 HKV_ERR_DEVICE = 6
 
+STATIC_SCRATCH_BYTES = 8 << 20  # HKV_STATIC_SCRATCH_BYTES
+
 DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 FMT_REF, FMT_FP16MIN = 0, 1
 ROLE_K, ROLE_V = 0, 1
@@ -72,6 +74,8 @@ SIGNATURES = {
                                 c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_i32, c_i64, c_i64, c_vp]),
     "hkv_decode_attn_partial": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32,
                                         c_i32, c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_vp, c_vp]),
+    "hkv_decode_attn_static": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32, c_i32,
+                                       c_i32, c_f32, c_i32, c_vp, c_i32, c_i64, c_i64, c_vp]),
     "hkv_lse_merge": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i32, c_i64, c_i64,
                               c_vp]),
     "hkv_prefetcher_create": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_i64, ctypes.POINTER(c_vp)]),

@@ -14,6 +14,10 @@
 
 #define HKV_VERSION 100
 
+// Scratch of hkv_decode_attn_static (merge counters, then partials), for callers
+// that cannot allocate a workspace. Zero at module load; one per device.
+static __device__ __align__(256) unsigned char g_hkv_decode_scratch[HKV_STATIC_SCRATCH_BYTES];
+
 namespace {
 
 inline cudaStream_t S(hkv_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
@@ -77,6 +81,25 @@ hkv_status check_dense(const hkv_dense_kv* d) {
   if (!d->k || !d->v || !aligned16(d->k) || !aligned16(d->v)) return HKV_ERR_ARG;
   if (d->stride_t % 8 || d->stride_h % 8 || d->stride_b % 8) return HKV_ERR_ARG;
   if (d->capacity < 0 || d->len < 0 || d->len > d->capacity) return HKV_ERR_ARG;
+  return HKV_OK;
+}
+
+// Address of g_hkv_decode_scratch on the current device, looked up once per device.
+hkv_status static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= 64) return HKV_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> g(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_hkv_decode_scratch);
+    if (e != cudaSuccess) return cuda_fail(e);
+    addr[dev] = p;
+  }
+  *out = addr[dev];
   return HKV_OK;
 }
 
@@ -488,6 +511,27 @@ hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_str
   if (!part_o || !part_ml) return HKV_ERR_ARG;
   return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
                     workspace_bytes, nullptr, HKV_DT_F32, 0, 0, part_o, part_ml, S(stream));
+}
+
+hkv_status hkv_decode_attn_static(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                  const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq,
+                                  int32_t Hkv, int32_t D, float sm_scale, int32_t ctas, void* out, int32_t out_dtype,
+                                  int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream) {
+  if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
+  // size the request on the host first: an oversized one fails before any CUDA call
+  hkv_status rc = check_decode_args(q, q_dtype, body, dense, B, Hq, Hkv, D);
+  if (rc != HKV_OK) return rc;
+  Plan pl;
+  if ((rc = make_plan(B, Hq, Hkv, body, dense, ctas, &pl)) != HKV_OK) return rc;
+  if (pl.ws_bytes > HKV_STATIC_SCRATCH_BYTES) return HKV_ERR_CAPACITY;
+  void* scratch = nullptr;
+  if ((rc = static_scratch(&scratch)) != HKV_OK) return rc;
+  // the merge counters must start at zero; the partials are written before they are read
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)pl.sc.U * sizeof(int), S(stream));
+  if (e != cudaSuccess) return cuda_fail(e);
+  return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, scratch,
+                    HKV_STATIC_SCRATCH_BYTES, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr,
+                    S(stream));
 }
 
 hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B, int32_t Hq, int32_t D,

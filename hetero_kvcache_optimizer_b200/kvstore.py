@@ -236,6 +236,34 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
     return out[:, :, None, :] if squeeze else out
 
 
+def decode_static(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
+                  sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
+                  ctas: int = 0, out: Optional[torch.Tensor] = None,
+                  body_len: Optional[int] = None, dense_len: Optional[int] = None,
+                  stream=None) -> torch.Tensor:
+    """``decode`` through hkv_decode_attn_static: no workspace is allocated, the
+    library's per-device scratch array serves the merge (so calls on one device
+    must not overlap). Pass ``out`` to keep the call free of allocations."""
+    _require_cuda(q)
+    squeeze = q.dim() == 4
+    if squeeze:
+        q = q[:, :, 0]
+    B, Hq, D = q.shape
+    Hkv = (store or dense).kv_heads
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=out_dtype, device=q.device)
+    st = store.struct(body_len) if store is not None else None
+    ds = dense.struct(dense_len) if dense is not None else None
+    L.check(L.load().hkv_decode_attn_static(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1),
+        ctypes.byref(st) if st is not None else None, ctypes.byref(ds) if ds is not None else None,
+        B, Hq, Hkv, D, float(sm_scale), ctas, out.data_ptr(), dtype_code(out.dtype), out.stride(0),
+        out.stride(1), _stream(stream)), "hkv_decode_attn_static")
+    return out[:, :, None, :] if squeeze else out
+
+
 def decode_plan(store: Optional[Int4KVStore], dense: Optional[DenseKV], batch: int, q_heads: int,
                 ctas: int = 0) -> Tuple[int, int]:
     """(grid, partial slots per unit) the decode kernel would use."""

@@ -220,6 +220,30 @@ hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_str
                                    void* workspace, size_t workspace_bytes, float* part_o,
                                    float* part_ml, hkv_stream_t stream);
 
+/* Largest workspace hkv_decode_attn_static can serve from its built-in scratch. */
+#define HKV_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* hkv_decode_attn without a caller workspace: the merge counters and partials
+ * live in one library-owned device array of HKV_STATIC_SCRATCH_BYTES per GPU,
+ * so the call allocates nothing. For callers that have no device allocator to
+ * hand over a workspace (a plain C or FFI host without a tensor library), or
+ * that must not allocate inside a decode step. No counterpart in the reference
+ * (its Python path allocates freely).
+ * - The first call on a device looks up the array's address (and sets the
+ *   kernel's shared-memory attribute); make that first call before any stream
+ *   capture.
+ * - Every call on a device shares the one array: calls whose kernels may
+ *   overlap (different streams, or threads without ordering) race on it.
+ *   Each call clears the merge counters it uses on `stream` before its kernel.
+ * - Returns HKV_ERR_CAPACITY, without touching the device, when the request's
+ *   workspace (hkv_decode_workspace_bytes) exceeds HKV_STATIC_SCRATCH_BYTES. */
+hkv_status hkv_decode_attn_static(const void* q, int32_t q_dtype, int64_t q_stride_b,
+                                  int64_t q_stride_h, const hkv_int4_store* body,
+                                  const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
+                                  int32_t D, float sm_scale, int32_t ctas, void* out,
+                                  int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                                  hkv_stream_t stream);
+
 /* Merge n partial sets laid out [n][B][Hq][128] / [n][B][Hq][2] (as produced by
  * hkv_decode_attn_partial) into out [B][Hq][128] (out_dtype, strides in elements). */
 hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B,
