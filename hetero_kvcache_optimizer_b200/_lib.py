@@ -34,12 +34,8 @@ c_i32, c_i64, c_u32, c_f32, c_vp, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes
 P_i32 = ctypes.POINTER(ctypes.c_int32)
 
 
-class HkvInt4Side(ctypes.Structure):
-    _fields_ = [("base", c_vp), ("page_stride", c_i64)]
-
-
 class HkvInt4Store(ctypes.Structure):
-    _fields_ = [("k", HkvInt4Side), ("v", HkvInt4Side), ("format", c_i32), ("group", c_i32),
+    _fields_ = [("pages", c_vp), ("page_stride", c_i64), ("format", c_i32), ("group", c_i32),
                 ("page_tokens", c_i32), ("max_pages", c_i32), ("page_table", c_vp),
                 ("lengths", c_vp), ("len", c_i32), ("reserved", c_i32)]
 
@@ -59,7 +55,7 @@ SIGNATURES = {
     "hkv_version": (c_i32, []),
     "hkv_device_error": (c_i32, [ctypes.POINTER(c_u32), c_i32]),
     "hkv_last_cuda_error": (c_i32, []),
-    "hkv_side_page_bytes": (c_i64, [c_i32, c_i32, c_i32]),
+    "hkv_page_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "hkv_quantize_flat": (c_i32, [c_vp, c_i32, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "hkv_dequantize_flat": (c_i32, [c_vp, c_vp, c_vp, c_i64, c_i32, c_vp, c_i32, c_vp]),
     "hkv_quantize_pack": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64,

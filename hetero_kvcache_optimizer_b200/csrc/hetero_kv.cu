@@ -67,10 +67,9 @@ hkv_status check_store(const hkv_int4_store* s) {
   if (!valid_group(s->group)) return HKV_ERR_UNSUPPORTED;
   if (s->page_tokens <= 0 || s->page_tokens % hkv::kTileI4) return HKV_ERR_ARG;
   if (s->max_pages <= 0) return HKV_ERR_ARG;
-  if (!s->k.base || !s->v.base || !aligned16(s->k.base) || !aligned16(s->v.base)) return HKV_ERR_ARG;
-  const int64_t pb = hkv_side_page_bytes(s->format, s->group, s->page_tokens);
-  if (s->k.page_stride < pb || s->v.page_stride < pb) return HKV_ERR_ARG;
-  if (s->k.page_stride % 16 || s->v.page_stride % 16) return HKV_ERR_ARG;
+  if (!s->pages || !aligned16(s->pages)) return HKV_ERR_ARG;
+  const int64_t pb = hkv_page_bytes(s->format, s->group, s->page_tokens);
+  if (s->page_stride < pb || s->page_stride % 16) return HKV_ERR_ARG;
   if (s->len < 0) return HKV_ERR_ARG;
   return HKV_OK;
 }
@@ -319,11 +318,10 @@ hkv_status hkv_device_error(uint32_t* bits, int clear) {
 
 int32_t hkv_last_cuda_error(void) { return t_last_cuda_error; }
 
-int64_t hkv_side_page_bytes(int32_t format, int32_t group, int32_t page_tokens) {
-  if (!valid_group(group) || page_tokens <= 0) return -1;
-  const int ng = HKV_D / group;
-  const int per_tok = HKV_CODE_BYTES + 4 * ng + (format == HKV_FMT_REF ? ng : 0);
-  return (int64_t)page_tokens * per_tok;
+int64_t hkv_page_bytes(int32_t format, int32_t group, int32_t page_tokens) {
+  if (!valid_group(group) || page_tokens <= 0 || page_tokens % HKV_BLOCK_TOKENS) return -1;
+  if (format != HKV_FMT_REF && format != HKV_FMT_FP16MIN) return -1;
+  return (int64_t)(page_tokens / HKV_BLOCK_TOKENS) * block_bytes(format, group);
 }
 
 // --------------------------------------------------------------------------- quantise

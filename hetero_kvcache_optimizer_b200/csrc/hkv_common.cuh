@@ -204,11 +204,23 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 // ------------------------------------------------------------------ store addressing
-struct SideAddr {
-  const uint8_t* codes;
-  const uint8_t* scales;
-  const uint8_t* zps;
-};
+// A page is page_tokens/128 blocks of 128 tokens; a block holds, at these byte
+// offsets: K codes [128][64] | V codes [64 pairs][128] | K meta [128][ng] x 4 B |
+// V meta | K zps [128][ng] u8 | V zps (the zps only for HKV_FMT_REF).
+#define HKV_BLOCK_TOKENS 128
+#define HKV_V_CODES_OFF 8192
+#define HKV_META_OFF 16384
+
+__host__ __device__ constexpr int block_bytes(int fmt, int group) {
+  return HKV_BLOCK_TOKENS * (2 * HKV_CODE_BYTES + 8 * (HKV_D / group) + (fmt == HKV_FMT_REF ? 2 * (HKV_D / group) : 0));
+}
+// Byte offset of K (role 0) or V (role 1) meta / zps inside a block.
+__host__ __device__ constexpr int meta_off(int role, int ng) { return HKV_META_OFF + role * 512 * ng; }
+__host__ __device__ constexpr int zps_off(int role, int ng) { return HKV_META_OFF + 1024 * ng + role * 128 * ng; }
+// Byte offset, inside the V code area of a block, of the 16-byte chunk c of
+// token pair q. Rotating the chunks by 2q makes the decode kernel's fragment
+// loads (chunk r of pairs j = 0..3 in one quarter-warp) hit 8 distinct bank groups.
+__host__ __device__ constexpr int v_chunk_off(int q, int c) { return q * 128 + (((c + 2 * q) & 7) << 4); }
 
 // Page of token t of unit u, or -1 when the page id is out of the pool's table.
 __device__ __forceinline__ int64_t store_page(const hkv_int4_store& s, int u, int t) {
@@ -218,17 +230,15 @@ __device__ __forceinline__ int64_t store_page(const hkv_int4_store& s, int u, in
   return (int64_t)u * s.max_pages + pi;
 }
 
-__device__ __forceinline__ int meta_scale_bytes(int ng) { return 4 * ng; }
-
-// Byte addresses of token slot `off` of page `page` for one side.
-__device__ __forceinline__ SideAddr side_addr(const hkv_int4_side& sd, const hkv_int4_store& s,
-                                              int64_t page, int off) {
-  const int P = s.page_tokens;
-  const int ng = HKV_D / s.group;
-  const uint8_t* base = static_cast<const uint8_t*>(sd.base) + page * sd.page_stride;
-  SideAddr a;
-  a.codes = base + (int64_t)off * HKV_CODE_BYTES;
-  a.scales = base + (int64_t)P * HKV_CODE_BYTES + (int64_t)off * 4 * ng;
-  a.zps = base + (int64_t)P * (HKV_CODE_BYTES + 4 * ng) + (int64_t)off * ng;
-  return a;
+// Block holding token slot `off` of page `page`, and the token's index in it.
+struct BlockRef {
+  uint8_t* base;
+  int w;
+};
+__device__ __forceinline__ BlockRef block_ref(const hkv_int4_store& s, int64_t page, int off) {
+  BlockRef r;
+  r.base = static_cast<uint8_t*>(s.pages) + page * s.page_stride +
+           (int64_t)(off / HKV_BLOCK_TOKENS) * block_bytes(s.format, s.group);
+  r.w = off % HKV_BLOCK_TOKENS;
+  return r;
 }

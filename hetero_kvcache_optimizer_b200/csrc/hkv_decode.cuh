@@ -41,13 +41,14 @@ constexpr int kGroupWarps = 4;                      // warps per consumer group
 constexpr int kConsumerWarps = 2 * kGroupWarps;     // two groups take alternate tiles
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kIssueWarp = kConsumerWarps;          // TMA issue
-constexpr int kExpandWarp = kConsumerWarps + 1;     // metadata expansion
-constexpr int kDecodeThreads = (kConsumerWarps + 2) * 32;
+constexpr int kExpandWarp = kConsumerWarps + 1;     // metadata expansion, first of kExpandWarps
+constexpr int kExpandWarps = 2;                     // take alternate tiles
+constexpr int kDecodeThreads = (kConsumerWarps + 1 + kExpandWarps) * 32;
 constexpr int kTileI4 = 128;  // tokens per INT4 tile (32 per consumer warp)
 constexpr int kTileD = 32;    // tokens per dense tile (8 per consumer warp)
 constexpr int kMaxSlots = 8;
-constexpr int kSlotBytes = 24 * 1024;   // INT4: K codes 8 KB | V codes 8 KB | metadata 8 KB
-constexpr int kMetaOff = 16 * 1024;
+constexpr int kSlotBytes = 24 * 1024;   // INT4: one page block (K codes | V codes | metadata) + expansion room
+constexpr int kMetaOff = HKV_META_OFF;
 constexpr float kLazyRescale = 8.0f;
 constexpr int kDenseHalf = kTileD * 128;  // bytes of one 64-dim half of 32 dense rows (swizzled)
 
@@ -85,16 +86,19 @@ struct DecodeParams {
   float* out_ml;   // [B][Hq][2]
 };
 
-// Raw metadata of one INT4 tile as copied: fp16min: K (s,min) f16x2 [128][NG] | V ...;
-// ref: K scales f32 [128][NG] | V scales | K zps u8 [128][NG] | V zps. Expanded in
-// place (floats): K scale [128][NG] | K bias [128][NG] | V scale pairs f16x2 [64][NG]
-// (tokens 2p, 2p+1) | V bias [128][NG].
-__host__ __device__ constexpr int meta_raw_bytes(int fmt, int group) {
-  return 2 * kTileI4 * 4 * (HKV_D / group) + (fmt == HKV_FMT_REF ? 2 * kTileI4 * (HKV_D / group) : 0);
-}
+// An INT4 tile is one 128-token page block, copied as is: K codes | V codes |
+// metadata (fp16min: K (s,min) f16x2 [128][NG] | V; ref: K scales f32 [128][NG] |
+// V scales | K zps u8 [128][NG] | V zps). With N = 128 NG entries, the metadata
+// is expanded in place into byte ranges of the metadata area
+//   [0, 4N) K scale f32 | [4N, 8N) K bias f32 | [10N, 14N) V bias f32 |
+//   [14N, 16N) V scale pairs f16x2 [64][NG] (tokens 2p, 2p+1)
+// so that every expanded entry lands either on the raw entry of the same index
+// (read by the same lane just before) or past all raw data: a lane never
+// overwrites raw bytes another lane has yet to read.
 __host__ __device__ constexpr int dense_slot_bytes() { return 4 * kDenseHalf; }
-static_assert(kMetaOff + 14 * kTileI4 * 4 <= kSlotBytes, "expanded metadata (g32) must fit its slot");
+static_assert(kMetaOff + 16 * kTileI4 * 4 <= kSlotBytes, "expanded metadata (g32) must fit its slot");
 static_assert(2 * kTileI4 * HKV_CODE_BYTES == kMetaOff && dense_slot_bytes() <= kSlotBytes, "slot layout");
+static_assert(kTileI4 == HKV_BLOCK_TOKENS && block_bytes(HKV_FMT_REF, 32) <= kSlotBytes, "a tile is one page block");
 
 // ---------------------------------------------------------------- schedule arithmetic (per piece, not per tile)
 __device__ __forceinline__ int64_t cta_begin(const Sched& s, int c) { return (int64_t)c * s.Btot / s.C; }
@@ -511,21 +515,22 @@ __device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// ---------------------------------------------------------------- metadata expansion (warp kExpandWarp)
-// Expands one INT4 tile's metadata in place (all raw values are read into
-// registers before the first write). Entries are [token][group]; lane L holds
-// entries 128 it + 4 L + {0..3}. Tokens at or past `valid` (beyond the sequence
-// length) may hold uninitialised pool bytes: their scale and bias become 0, so
-// a masked token (P = 0) contributes exactly 0 and never NaN. The K scale is
-// multiplied by qs (sm_scale * log2 e) so scores come out as base-2 logits.
+// ---------------------------------------------------------------- metadata expansion (warps kExpandWarp..)
+// Expands one INT4 tile's metadata in place (layout above), streaming: lane L
+// handles entries 128 it + 4 L + {0..3} ([token][group] order) one iteration
+// at a time. Tokens at or past `valid` (beyond the sequence length) may hold
+// uninitialised pool bytes: their scale and bias become 0, so a masked token
+// (P = 0) contributes exactly 0 and never NaN. The K scale is multiplied by qs
+// (sm_scale * log2 e) so scores come out as base-2 logits.
 template <int FMT, int NG>
 __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, float qs) {
   constexpr int N = kTileI4 * NG;
   constexpr int IT = N / 128;
-  float sk[IT][4], bk[IT][4], sv[IT][4], bv[IT][4];
+  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + 14 * N);  // [64 pairs][NG] f16x2
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
     const int e = 128 * it + 4 * lane;
+    float sk[4], bk[4], sv[4], bv[4];
     if (FMT == HKV_FMT_REF) {
       const float4 a = *reinterpret_cast<const float4*>(meta + 4 * e);
       const float4 c = *reinterpret_cast<const float4*>(meta + 4 * N + 4 * e);
@@ -534,10 +539,10 @@ __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, 
       const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        sk[it][i] = av[i];
-        sv[it][i] = cv[i];
-        bk[it][i] = -static_cast<float>((zk >> (8 * i)) & 0xffu) * av[i];
-        bv[it][i] = -static_cast<float>((zv >> (8 * i)) & 0xffu) * cv[i];
+        sk[i] = av[i];
+        sv[i] = cv[i];
+        bk[i] = -static_cast<float>((zk >> (8 * i)) & 0xffu) * av[i];
+        bv[i] = -static_cast<float>((zv >> (8 * i)) & 0xffu) * cv[i];
       }
     } else {
       const uint4 a = *reinterpret_cast<const uint4*>(meta + 4 * e);
@@ -547,46 +552,39 @@ __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, 
       for (int i = 0; i < 4; ++i) {
         const float2 fk = __half22float2(*reinterpret_cast<const __half2*>(&av[i]));
         const float2 fv = __half22float2(*reinterpret_cast<const __half2*>(&cv[i]));
-        sk[it][i] = fk.x;
-        bk[it][i] = fk.y;
-        sv[it][i] = fv.x;
-        bv[it][i] = fv.y;
+        sk[i] = fk.x;
+        bk[i] = fk.y;
+        sv[i] = fv.x;
+        bv[i] = fv.y;
       }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      if ((e + i) / NG >= valid) sk[it][i] = bk[it][i] = sv[it][i] = bv[it][i] = 0.f;
+      if ((e + i) / NG >= valid) sk[i] = bk[i] = sv[i] = bv[i] = 0.f;
     }
-  }
-  __syncwarp();
-  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + 8 * N);  // [N/NG/2 pairs][NG] f16x2
-#pragma unroll
-  for (int it = 0; it < IT; ++it) {
-    const int e = 128 * it + 4 * lane;
-    *reinterpret_cast<float4*>(meta + 4 * e) =
-        make_float4(sk[it][0] * qs, sk[it][1] * qs, sk[it][2] * qs, sk[it][3] * qs);
-    *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[it][0], bk[it][1], bk[it][2], bk[it][3]);
-    *reinterpret_cast<float4*>(meta + 10 * N + 4 * e) = make_float4(bv[it][0], bv[it][1], bv[it][2], bv[it][3]);
+    *reinterpret_cast<float4*>(meta + 4 * e) = make_float4(sk[0] * qs, sk[1] * qs, sk[2] * qs, sk[3] * qs);
+    *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[0], bk[1], bk[2], bk[3]);
+    *reinterpret_cast<float4*>(meta + 10 * N + 4 * e) = make_float4(bv[0], bv[1], bv[2], bv[3]);
     if constexpr (NG == 4) {
       // lane holds token 32 it + lane; its pair partner is lane ^ 1
       float o[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, sv[it][i], 1);
+      for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, sv[i], 1);
       if ((lane & 1) == 0) {
         const int pair = 16 * it + (lane >> 1);
         *reinterpret_cast<uint4*>(vsp + pair * 4) =
-            make_uint4(pack2<__half>(sv[it][0], o[0]), pack2<__half>(sv[it][1], o[1]),
-                       pack2<__half>(sv[it][2], o[2]), pack2<__half>(sv[it][3], o[3]));
+            make_uint4(pack2<__half>(sv[0], o[0]), pack2<__half>(sv[1], o[1]), pack2<__half>(sv[2], o[2]),
+                       pack2<__half>(sv[3], o[3]));
       }
     } else if constexpr (NG == 2) {
       // entries: (t, g0), (t, g1), (t+1, g0), (t+1, g1) with t = 64 it + 2 lane
       const int pair = 32 * it + lane;
       *reinterpret_cast<uint2*>(vsp + pair * 2) =
-          make_uint2(pack2<__half>(sv[it][0], sv[it][2]), pack2<__half>(sv[it][1], sv[it][3]));
+          make_uint2(pack2<__half>(sv[0], sv[2]), pack2<__half>(sv[1], sv[3]));
     } else {
       // tokens 4 lane .. 4 lane + 3: pairs 2 lane, 2 lane + 1
       *reinterpret_cast<uint2*>(vsp + 2 * lane) =
-          make_uint2(pack2<__half>(sv[it][0], sv[it][1]), pack2<__half>(sv[it][2], sv[it][3]));
+          make_uint2(pack2<__half>(sv[0], sv[1]), pack2<__half>(sv[2], sv[3]));
     }
   }
   // order these generic-proxy writes before later TMA (async-proxy) writes to the slot
@@ -668,9 +666,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     int n = 0;
     // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
     int pg_u = -1, pg0 = 0, pg_lane = -1;
-    const uint32_t codes_b = kTileI4 * HKV_CODE_BYTES;
-    const uint32_t sc_b = kTileI4 * 4 * NG;
-    const uint32_t zp_b = FMT == HKV_FMT_REF ? kTileI4 * NG : 0;
+    constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
     while (cu.valid) {
       if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
       uint8_t* sb = ring + ri.slot * kSlotBytes;
@@ -695,17 +691,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
             mbar_arrive(fb);
           } else {
             const int off = p.page_shift >= 0 ? t & ((1 << p.page_shift) - 1) : t % p.body.page_tokens;
-            const SideAddr ka = side_addr(p.body.k, p.body, page, off);
-            const SideAddr va = side_addr(p.body.v, p.body, page, off);
-            mbar_arrive_expect_tx(fb, 2 * (codes_b + sc_b + zp_b));
-            bulk_g2s(sb, ka.codes, codes_b, fb);
-            bulk_g2s(sb + codes_b, va.codes, codes_b, fb);
-            bulk_g2s(sb + kMetaOff, ka.scales, sc_b, fb);
-            bulk_g2s(sb + kMetaOff + sc_b, va.scales, sc_b, fb);
-            if (FMT == HKV_FMT_REF) {
-              bulk_g2s(sb + kMetaOff + 2 * sc_b, ka.zps, zp_b, fb);
-              bulk_g2s(sb + kMetaOff + 2 * sc_b + zp_b, va.zps, zp_b, fb);
-            }
+            const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + (int64_t)page * p.body.page_stride +
+                                 (int64_t)(off / kTileI4) * kTileBytes;
+            mbar_arrive_expect_tx(fb, kTileBytes);
+            bulk_g2s(sb, src, kTileBytes, fb);
           }
         }
       } else if (lane == 0) {
@@ -728,12 +717,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     return;
   }
 
-  if (warp == kExpandWarp) {
-    // ================================================================ metadata expansion warp
+  if (warp >= kExpandWarp) {
+    // ================================================================ metadata expansion warps
+    // expansion warp x takes the loads n with n % kExpandWarps == x
+    const int x = warp - kExpandWarp;
     Cursor cu;
     cursor_start(p, c, end, cu);
     Ring re{0, 0u};
-    while (cu.valid) {
+    for (int n = 0; cu.valid; ++n) {
+      if (n % kExpandWarps != x) {
+        re.advance(nsl);
+        cursor_next(p, end, cu);
+        continue;
+      }
       if (!warp_wait(&full_bar[re.slot], re.phase)) break;
       uint8_t* sb = ring + re.slot * kSlotBytes;
       if (cu.pc.seg == 0) {
@@ -765,7 +761,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   int n_base = 0;    // index of the current piece's first load
   const int t0 = wg * 32;
   const int kc_off = (t0 + r) * HKV_CODE_BYTES + 16 * j;
-  const int vc_off = kTileI4 * HKV_CODE_BYTES + (t0 + 2 * j) * HKV_CODE_BYTES + 16 * r;
+  // chunk r of pair t0/2 + j (and of pair t0/2 + 8 + j): the block rotates pair q's chunks by 2q
+  const int vc_off = HKV_V_CODES_OFF + v_chunk_off(t0 / 2 + j, r);
   const int ks_off = (t0 + r) * NG;  // floats
   const int vs_off = (t0 / 2) * NG;  // f16x2 words
 
@@ -816,7 +813,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         const float* mk = reinterpret_cast<const float*>(stg + kMetaOff);
         const float* ks = mk + ks_off;
         const float* kb = mk + NM + ks_off;
-        const uint32_t* vsp = reinterpret_cast<const uint32_t*>(mk + 2 * NM) + vs_off;
+        const uint32_t* vsp = reinterpret_cast<const uint32_t*>(mk + 3 * NM + NM / 2) + vs_off;
         const float* vb = mk + 2 * NM + NM / 2 + ks_off;
         float xa[4], xb[4], x[8], P[8];
         k_scores<NG>(stg + kc_off, ks, kb, qf, nbias, qsum, xa);
@@ -956,14 +953,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
               L = fmaf(wk, __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2 + 1), L);
             }
             const int kn = min(32, n - k0);
-            for (int kk = 0; kk < kn; ++kk) {
-              const float w = __shfl_sync(0xffffffffu, wk, kk);
-              if (w == 0.f) continue;
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(o_u + ((k0 + kk) * p.G + h) * HKV_D) + lane);
-              acc.x = fmaf(w, v.x, acc.x);
-              acc.y = fmaf(w, v.y, acc.y);
-              acc.z = fmaf(w, v.z, acc.z);
-              acc.w = fmaf(w, v.w, acc.w);
+            // 8 partials per batch: all loads in flight before the first use
+            for (int kb = 0; kb < kn; kb += 8) {
+              float4 v[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                v[i] = kb + i < kn ? __ldcg(reinterpret_cast<const float4*>(o_u + ((k0 + kb + i) * p.G + h) * HKV_D) + lane)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float w = __shfl_sync(0xffffffffu, wk, (kb + i) & 31);
+                acc.x = fmaf(w, v[i].x, acc.x);
+                acc.y = fmaf(w, v[i].y, acc.y);
+                acc.z = fmaf(w, v[i].z, acc.z);
+                acc.w = fmaf(w, v[i].w, acc.w);
+              }
             }
           }
 #pragma unroll

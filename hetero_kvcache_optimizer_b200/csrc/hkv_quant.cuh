@@ -48,12 +48,12 @@ __device__ __forceinline__ uint32_t min_code(float x, const MinParams& p) {
 // A token of 128 values is held by 16 consecutive lanes (a half-warp), lane p
 // holding dims [8p, 8p+8) in v[0..7]. quantise_token() computes the group
 // statistics with xor-shuffles inside the half-warp, quantises, and writes the
-// packed codes + metadata of the token into store slot (page, off) of `sd`.
+// packed codes + metadata of the token into the K or V half (role) of store
+// slot (page, off).
 // All 32 lanes of the warp must call it (the shuffles use the full mask);
 // lanes with active == false only take part in the shuffles.
 __device__ __forceinline__ void quantise_token(const float (&v)[8], bool active, int role, int fmt, int group,
-                                               const hkv_int4_store& st, const hkv_int4_side& sd,
-                                               int64_t page, int off) {
+                                               const hkv_int4_store& st, int64_t page, int off) {
   const int lane = threadIdx.x & 31;
   const int p = lane & 15;
   float mn = v[0], mx = v[0];
@@ -90,28 +90,28 @@ __device__ __forceinline__ void quantise_token(const float (&v)[8], bool active,
     hi |= (by >> 4) << (4 * m);
   }
   if (!active) return;
-  const SideAddr a = side_addr(sd, st, page, off);
-  uint8_t* codes = const_cast<uint8_t*>(a.codes);
+  const BlockRef br = block_ref(st, page, off);
   if (role == HKV_ROLE_K) {
-    reinterpret_cast<uint32_t*>(codes)[4 * j + w] = lo | (hi << 16);
+    reinterpret_cast<uint32_t*>(br.base + br.w * HKV_CODE_BYTES)[4 * j + w] = lo | (hi << 16);
   } else {
-    // V token pairs: pair block at the even slot, token parity selects the half-word.
-    uint8_t* pair = codes - (off & 1) * HKV_CODE_BYTES;
-    const int tau = off & 1;
-    *reinterpret_cast<uint16_t*>(pair + 16 * (2 * j) + 4 * w + 2 * tau) = static_cast<uint16_t>(lo);
-    *reinterpret_cast<uint16_t*>(pair + 16 * (2 * j + 1) + 4 * w + 2 * tau) = static_cast<uint16_t>(hi);
+    // V token pairs: token parity selects the half-word of each word of the pair's chunks.
+    uint8_t* vc = br.base + HKV_V_CODES_OFF;
+    const int q = br.w >> 1, tau = br.w & 1;
+    *reinterpret_cast<uint16_t*>(vc + v_chunk_off(q, 2 * j) + 4 * w + 2 * tau) = static_cast<uint16_t>(lo);
+    *reinterpret_cast<uint16_t*>(vc + v_chunk_off(q, 2 * j + 1) + 4 * w + 2 * tau) = static_cast<uint16_t>(hi);
   }
   if ((p % lanes_per_group) == 0) {
+    const int ng = HKV_D / group;
     const int gi = p / lanes_per_group;
-    uint8_t* scales = const_cast<uint8_t*>(a.scales);
+    uint8_t* meta = br.base + meta_off(role, ng) + 4 * (br.w * ng + gi);
     if (fmt == HKV_FMT_REF) {
-      reinterpret_cast<float*>(scales)[gi] = rp.scale;
-      const_cast<uint8_t*>(a.zps)[gi] = static_cast<uint8_t>(rp.zpf);
+      *reinterpret_cast<float*>(meta) = rp.scale;
+      br.base[zps_off(role, ng) + br.w * ng + gi] = static_cast<uint8_t>(rp.zpf);
     } else {
       __half2 sm;
       sm.x = mp.sh;
       sm.y = mp.mh;
-      reinterpret_cast<__half2*>(scales)[gi] = sm;
+      *reinterpret_cast<__half2*>(meta) = sm;
     }
   }
 }
@@ -170,8 +170,7 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict_
       }
     }
   }
-  const hkv_int4_side& sd = role == HKV_ROLE_K ? store.k : store.v;
-  quantise_token(v, ok, role, store.format, store.group, store, sd, page, pos % store.page_tokens);
+  quantise_token(v, ok, role, store.format, store.group, store, page, pos % store.page_tokens);
 }
 
 // ------------------------------------------------------------------ decode-step append
@@ -220,8 +219,8 @@ __global__ void __launch_bounds__(1024) append_kv_kernel(const T* __restrict__ k
         if (lane == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
       }
     }
-    quantise_token(ev, ok, side ? HKV_ROLE_V : HKV_ROLE_K, body.format, body.group, body,
-                   side ? body.v : body.k, page, bl % body.page_tokens);
+    quantise_token(ev, ok, side ? HKV_ROLE_V : HKV_ROLE_K, body.format, body.group, body, page,
+                   bl % body.page_tokens);
   }
   if (!direct) store8(rowp, nv);
   __syncthreads();
@@ -282,19 +281,20 @@ __global__ void dequantize_flat_kernel(const uint8_t* __restrict__ codes, const 
 }
 
 // ------------------------------------------------------------------ packed -> dense
-// Nibble position of (token slot off, dim d) in a page of one side.
-__device__ __forceinline__ uint32_t packed_code(const uint8_t* codes_tok, int role, int off, int d) {
+// Code of (token br.w of block br, dim d) in the K or V half of the block.
+__device__ __forceinline__ uint32_t packed_code(const BlockRef& br, int role, int d) {
   if (role == HKV_ROLE_K) {
     const int w = d >> 5, rem = d & 31;
     const int a = rem >> 4, c = (rem >> 3) & 1, j = (rem & 7) >> 1, e = rem & 1;
     const int k = 2 * a + c + 4 * e;
-    const uint32_t word = reinterpret_cast<const uint32_t*>(codes_tok)[4 * j + w];
+    const uint32_t word = reinterpret_cast<const uint32_t*>(br.base + br.w * HKV_CODE_BYTES)[4 * j + w];
     return (word >> (4 * k)) & 0xFu;
   }
-  const uint8_t* pair = codes_tok - (off & 1) * HKV_CODE_BYTES;
+  // word 4i + k of a V pair = word k of its chunk i
   const int i = d & 7, e = d >> 3, k = e >> 2, m = e & 3;
-  const uint32_t word = reinterpret_cast<const uint32_t*>(pair)[4 * i + k];
-  return (word >> (4 * m + 16 * (off & 1))) & 0xFu;
+  const int q = br.w >> 1, tau = br.w & 1;
+  const uint32_t word = *reinterpret_cast<const uint32_t*>(br.base + HKV_V_CODES_OFF + v_chunk_off(q, i) + 4 * k);
+  return (word >> (4 * m + 16 * tau)) & 0xFu;
 }
 
 template <typename OT>
@@ -310,15 +310,17 @@ __global__ void dequantize_pack_kernel(hkv_int4_store st, int role, int H, int t
     if (d == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
     return;
   }
-  const int off = t % st.page_tokens;
-  const SideAddr a = side_addr(role == HKV_ROLE_K ? st.k : st.v, st, page, off);
-  const uint32_t c = packed_code(a.codes, role, off, d);
+  const BlockRef br = block_ref(st, page, t % st.page_tokens);
+  const uint32_t c = packed_code(br, role, d);
+  const int ng = HKV_D / st.group;
   const int gi = d / st.group;
+  const uint8_t* meta = br.base + meta_off(role, ng) + 4 * (br.w * ng + gi);
   float v;
   if (st.format == HKV_FMT_REF) {
-    v = (static_cast<float>(c) - static_cast<float>(a.zps[gi])) * reinterpret_cast<const float*>(a.scales)[gi];
+    const float zp = static_cast<float>(br.base[zps_off(role, ng) + br.w * ng + gi]);
+    v = (static_cast<float>(c) - zp) * *reinterpret_cast<const float*>(meta);
   } else {
-    const __half2 sm = reinterpret_cast<const __half2*>(a.scales)[gi];
+    const __half2 sm = *reinterpret_cast<const __half2*>(meta);
     v = static_cast<float>(c) * __half2float(sm.x) + __half2float(sm.y);
   }
   out[tok * HKV_D + d] = from_f32<OT>(v);
@@ -339,8 +341,7 @@ __global__ void repack_ref_kernel(const uint8_t* __restrict__ codes, const float
     if (hx == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
     return;
   }
-  const int off = t % st.page_tokens;
-  const SideAddr a = side_addr(role == HKV_ROLE_K ? st.k : st.v, st, page, off);
+  const BlockRef br = block_ref(st, page, t % st.page_tokens);
   const uint8_t* src = codes + tok * HKV_D;
   uint32_t half = 0;
   if (role == HKV_ROLE_K) {
@@ -352,7 +353,7 @@ __global__ void repack_ref_kernel(const uint8_t* __restrict__ codes, const float
       const int dim = 16 * (2 * w + (k % 4) / 2) + 8 * ((k % 4) % 2) + 2 * j + k / 4;
       half |= (uint32_t)(src[dim] & 0xF) << (4 * m);
     }
-    reinterpret_cast<uint16_t*>(const_cast<uint8_t*>(a.codes))[hx] = (uint16_t)half;
+    reinterpret_cast<uint16_t*>(br.base + br.w * HKV_CODE_BYTES)[hx] = (uint16_t)half;
   } else {
     const int i = hx >> 2, k = hx & 3;
 #pragma unroll
@@ -361,14 +362,14 @@ __global__ void repack_ref_kernel(const uint8_t* __restrict__ codes, const float
       const int dim = 16 * (e / 2) + 8 * (e % 2) + i;
       half |= (uint32_t)(src[dim] & 0xF) << (4 * m);
     }
-    uint8_t* pair = const_cast<uint8_t*>(a.codes) - (off & 1) * HKV_CODE_BYTES;
-    *reinterpret_cast<uint16_t*>(pair + 16 * i + 4 * k + 2 * (off & 1)) = (uint16_t)half;
+    const int q = br.w >> 1, tau = br.w & 1;
+    *reinterpret_cast<uint16_t*>(br.base + HKV_V_CODES_OFF + v_chunk_off(q, i) + 4 * k + 2 * tau) = (uint16_t)half;
   }
   const int ng = HKV_D / group;
   if (hx < ng) {
     const int64_t gidx = tok * ng + hx;
-    reinterpret_cast<float*>(const_cast<uint8_t*>(a.scales))[hx] = scales[gidx];
-    const_cast<uint8_t*>(a.zps)[hx] = zps[gidx];
+    *reinterpret_cast<float*>(br.base + meta_off(role, ng) + 4 * (br.w * ng + hx)) = scales[gidx];
+    br.base[zps_off(role, ng) + br.w * ng + hx] = zps[gidx];
   }
 }
 

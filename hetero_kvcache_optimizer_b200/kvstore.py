@@ -40,8 +40,8 @@ def _require_cuda(*ts: torch.Tensor) -> None:
                 "there is no CPU fallback)")
 
 
-def side_page_bytes(fmt: str, group: int, page_tokens: int) -> int:
-    n = L.load().hkv_side_page_bytes(FORMATS[fmt], group, page_tokens)
+def page_bytes(fmt: str, group: int, page_tokens: int) -> int:
+    n = L.load().hkv_page_bytes(FORMATS[fmt], group, page_tokens)
     if n <= 0:
         raise ValueError(f"bad store geometry fmt={fmt} group={group} page_tokens={page_tokens}")
     return int(n)
@@ -50,9 +50,10 @@ def side_page_bytes(fmt: str, group: int, page_tokens: int) -> int:
 class Int4KVStore:
     """Packed INT4 body of a KV cache for B sequences x H KV heads.
 
-    Memory: one pool of pages, each page one contiguous blob [K side | V side]
-    (``2 * side_page_bytes`` bytes; 43,008 B for the reference format, group 32,
-    256-token pages), so that one host->device copy moves a whole page.
+    Memory: one pool of pages; a page is page_tokens/128 contiguous blocks of
+    128 tokens, each holding K and V codes and metadata together (21,504 B per
+    block for the reference format at group 32; 20,480 B for fp16min), so that
+    one copy moves a decode tile and one host->device copy moves a whole page.
 
     Dense mode (``num_pages=None``): unit u = b*H + h owns pages
     [u*max_pages, (u+1)*max_pages) and no page table is used. Paged mode: the
@@ -71,8 +72,7 @@ class Int4KVStore:
         self.page_tokens = page_tokens
         self.max_pages = max(1, math.ceil(capacity / page_tokens))
         self.capacity = self.max_pages * page_tokens
-        self.side_bytes = side_page_bytes(fmt, group, page_tokens)
-        self.page_bytes = 2 * self.side_bytes
+        self.page_bytes = page_bytes(fmt, group, page_tokens)
         units = batch * kv_heads
         self.paged = num_pages is not None
         self.num_pages = num_pages if self.paged else units * self.max_pages
@@ -84,10 +84,9 @@ class Int4KVStore:
         self.len_hint = 0  # host-side upper bound of lengths (sizes the split-KV grid)
 
     def struct(self, len_hint: Optional[int] = None) -> L.HkvInt4Store:
-        base = self.pool.data_ptr()
         s = L.HkvInt4Store()
-        s.k = L.HkvInt4Side(base, self.page_bytes)
-        s.v = L.HkvInt4Side(base + self.side_bytes, self.page_bytes)
+        s.pages = self.pool.data_ptr()
+        s.page_stride = self.page_bytes
         s.format = FORMATS[self.fmt]
         s.group = self.group
         s.page_tokens = self.page_tokens
@@ -104,11 +103,6 @@ class Int4KVStore:
         else:
             self.lengths.copy_(n.to(torch.int32))
             self.len_hint = int(n.max().item())
-
-    # raw views (tests / debugging)
-    def side_view(self, role: int) -> torch.Tensor:
-        off = 0 if role == L.ROLE_K else self.side_bytes
-        return self.pool[:, off:off + self.side_bytes]
 
 
 class DenseKV:
@@ -208,7 +202,7 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
            stream=None) -> torch.Tensor:
     """Decode attention of q [B, Hq, 128] (or [B, Hq, 1, 128]) over the INT4
     body and/or the dense segment. Returns [B, Hq, 128] in ``out_dtype``.
-    ``ctas`` sets the persistent grid (0: two CTAs per SM); ``body_len`` /
+    ``ctas`` sets the persistent grid (0: one CTA per SM); ``body_len`` /
     ``dense_len`` override the host-side length hints that size the schedule."""
     _require_cuda(q)
     squeeze = q.dim() == 4

@@ -25,14 +25,22 @@
  *  - Kernels never trap: a bounded wait that expires, or a page id outside the
  *    pool, sets a sticky device error word read back by hkv_device_error().
  *
- * Packed INT4 page layout (head_dim D = 128, G = D/group groups per token):
- *   one page of one side (K or V) holds P tokens:
- *     codes  [P][64]  u8   two 4-bit codes per byte, in the mma-fragment nibble
- *                          order documented in oracle/kv_oracle.py (K per token,
- *                          V per token pair)
- *     scales [P][G]   f32  (HKV_FMT_REF)  or  [P][G] {f16 scale, f16 min} (HKV_FMT_FP16MIN)
- *     zps    [P][G]   u8   (HKV_FMT_REF only)
- *   => 84*P bytes (ref, group 32) or 80*P bytes (fp16min, group 32) per side.
+ * Packed INT4 page layout (head_dim D = 128, G = D/group groups per token).
+ * A page of P tokens (P a multiple of 128) is P/128 contiguous 128-token blocks,
+ * each holding K and V together so that one bulk copy moves a decode tile:
+ *     offset 0        K codes [128][64]     u8, two 4-bit codes per byte, in the
+ *                                           mma-fragment nibble order documented
+ *                                           in oracle/kv_oracle.py (per token)
+ *     offset 8192     V codes [64][128]     u8, per token pair; the 16-byte chunk
+ *                                           c of pair q is stored at chunk position
+ *                                           (c + 2q) mod 8 of the pair's 128 bytes
+ *     offset 16384    K meta  [128][G]      f32 scale (HKV_FMT_REF) or
+ *                                           {f16 scale, f16 min} (HKV_FMT_FP16MIN)
+ *     +   512*G       V meta  [128][G]
+ *     +  1024*G       K zps   [128][G] u8   (HKV_FMT_REF only)
+ *     +  1152*G       V zps   [128][G] u8   (HKV_FMT_REF only)
+ *   => 168 B per token (ref, group 32) or 160 B per token (fp16min, group 32)
+ *      for K and V together; hkv_page_bytes() gives the page size.
  */
 #ifndef HETERO_KV_H_
 #define HETERO_KV_H_
@@ -75,18 +83,13 @@ typedef int hkv_status;
 typedef void* hkv_stream_t; /* cudaStream_t */
 typedef void* hkv_event_t;  /* cudaEvent_t */
 
-/* One side (K or V) of an INT4 page pool: page p starts at base + p*page_stride. */
-typedef struct hkv_int4_side {
-  void* base;
-  int64_t page_stride; /* bytes; multiple of 16 */
-} hkv_int4_side;
-
-/* Packed INT4 body of a KV cache. Token t of unit u = b*Hkv + h lives in page
+/* Packed INT4 body of a KV cache: a pool of pages, page p at
+ * pages + p*page_stride. Token t of unit u = b*Hkv + h lives in page
  *   page_table ? page_table[u*max_pages + t/P] : u*max_pages + t/P
  * at slot t % P. A dense per-unit buffer is the special case page_table == NULL. */
 typedef struct hkv_int4_store {
-  hkv_int4_side k;
-  hkv_int4_side v;
+  void* pages;               /* device page pool, 16-byte aligned */
+  int64_t page_stride;       /* bytes between pages: >= hkv_page_bytes(), multiple of 16 */
   int32_t format;            /* HKV_FMT_* */
   int32_t group;             /* 32, 64 or 128 */
   int32_t page_tokens;       /* P: multiple of 128 */
@@ -119,8 +122,8 @@ hkv_status hkv_device_error(uint32_t* bits, int clear);
 /* cudaError_t value behind the last HKV_ERR_CUDA returned to this host thread
  * (0 if none). No counterpart in the reference (it raises Python exceptions). */
 int32_t hkv_last_cuda_error(void);
-/* Bytes of one page of one side for a format/group/page size. */
-int64_t hkv_side_page_bytes(int32_t format, int32_t group, int32_t page_tokens);
+/* Bytes of one page (K and V) for a format/group/page size; -1 if invalid. */
+int64_t hkv_page_bytes(int32_t format, int32_t group, int32_t page_tokens);
 
 /* ---------------------------------------------------------------- 1. quantise
  * Legacy flat quantiser, bit-exact with KVCompressor.compress
@@ -137,8 +140,8 @@ hkv_status hkv_dequantize_flat(const uint8_t* codes, const float* scales, const 
                                int64_t n, int32_t group, void* out, int32_t out_dtype,
                                hkv_stream_t stream);
 
-/* Quantise x[B][H][T][128] (fp16/bf16, strides in elements) into one side of
- * `dst` (role K or V): token t of unit (b,h) is written at body slot
+/* Quantise x[B][H][T][128] (fp16/bf16, strides in elements) into the K or V
+ * half (role) of the blocks of `dst`: token t of unit (b,h) is written at body slot
  * (dst_start ? dst_start[b] : start) + t. Per-group min/max, scale and
  * zero-point are computed exactly as KVCompressor.compress does for a
  * [.., 128] tensor (HKV_FMT_REF, bit-exact) or as the fp16min spec says.
@@ -162,7 +165,7 @@ hkv_status hkv_append_kv(const void* k_new, const void* v_new, int32_t dtype, in
                          int32_t* ring_head, const hkv_int4_store* body, int32_t* body_len,
                          hkv_stream_t stream);
 
-/* Dequantise tokens [t0, t0+T) of every unit of a store side to a dense
+/* Dequantise tokens [t0, t0+T) of the K or V half (role) of every unit to a dense
  * [B][H][T][128] tensor (out_dtype, contiguous). Serves the BF16-returning
  * AsyncPrefetcher.fetch_if_ready contract (src/policy/prefetcher.py:81-84). */
 hkv_status hkv_dequantize_pack(const hkv_int4_store* src, int32_t role, int32_t B, int32_t H,
@@ -171,7 +174,7 @@ hkv_status hkv_dequantize_pack(const hkv_int4_store* src, int32_t role, int32_t 
 
 /* Convert the reference's unpacked representation (codes [B][H][S][128] u8
  * one code per byte, scales f32 and zps u8 flat over groups of `group`) into
- * tokens [0, S) of one side of an HKV_FMT_REF store. Used when the legacy
+ * tokens [0, S) of the K or V half (role) of an HKV_FMT_REF store. Used when the legacy
  * fused_dequant_attn_decode signature is called with KVCompressor outputs. */
 hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8_t* zps,
                           int32_t B, int32_t H, int32_t S, int32_t group, int32_t role,
@@ -180,7 +183,7 @@ hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8
 /* ---------------------------------------------------------------- 2. decode attention
  * One persistent launch: the (sequence, KV head) units' tile lists (128-token
  * INT4 tiles, 32-token dense tiles) are cut into equal-byte ranges, one per CTA
- * (`ctas` <= 0: two per SM); the last CTA to finish a unit merges its partials.
+ * (`ctas` <= 0: one per SM); the last CTA to finish a unit merges its partials.
  * The len fields of body/dense size the schedule; device lengths may exceed them
  * (tokens are never dropped) at the cost of balance.
  *

@@ -227,26 +227,66 @@ def unpack_v(packed: np.ndarray, T: int | None = None) -> np.ndarray:
     return out.reshape(packed.shape[:-2] + (Tp, HEAD_DIM))[..., :T, :]
 
 
-def side_page_bytes(page_tokens: int, fmt: int, group: int) -> int:
-    """Bytes of one page of one side (K or V): codes | scales | zps."""
-    ng = HEAD_DIM // group
-    per_tok = CODE_BYTES + 4 * ng + (ng if fmt == FMT_REF else 0)
-    return page_tokens * per_tok
+BLOCK_TOKENS = 128
 
 
-def split_side_page(page: np.ndarray, page_tokens: int, fmt: int, group: int):
-    """Split one raw page (uint8 bytes) of one side into (codes [P,64],
-    meta...) views. For FMT_REF meta is (scales fp32 [P,ng], zps u8 [P,ng]);
-    for FMT_FP16MIN it is (scale fp16 [P,ng], min fp16 [P,ng])."""
-    P = page_tokens
+def block_bytes(fmt: int, group: int) -> int:
+    """Bytes of one 128-token page block: K codes | V codes | K meta | V meta
+    (| K zps | V zps for FMT_REF)."""
     ng = HEAD_DIM // group
-    codes = page[: P * 64].reshape(P, 64)
-    if fmt == FMT_REF:
-        sc = page[P * 64: P * 64 + P * 4 * ng].view(np.float32).reshape(P, ng)
-        zp = page[P * 64 + P * 4 * ng: P * 64 + P * 5 * ng].reshape(P, ng)
-        return codes, sc, zp
-    hm = page[P * 64: P * 64 + P * 4 * ng].view(np.float16).reshape(P, ng, 2)
-    return codes, hm[..., 0], hm[..., 1]
+    return BLOCK_TOKENS * (2 * CODE_BYTES + 8 * ng + (2 * ng if fmt == FMT_REF else 0))
+
+
+def page_bytes(page_tokens: int, fmt: int, group: int) -> int:
+    assert page_tokens % BLOCK_TOKENS == 0
+    return page_tokens // BLOCK_TOKENS * block_bytes(fmt, group)
+
+
+def v_chunk_pos(pair: int, chunk: int) -> int:
+    """Stored 16-byte chunk position of logical chunk `chunk` of token pair `pair`
+    inside the pair's 128 bytes of a block (rotated by 2*pair)."""
+    return (chunk + 2 * pair) % 8
+
+
+def _v_perm() -> np.ndarray:
+    """[64 pairs * 128 bytes] stored byte index -> logical byte index for one block."""
+    perm = np.zeros(64 * 128, np.int64)
+    for q in range(64):
+        for c in range(8):
+            pos = v_chunk_pos(q, c)
+            perm[q * 128 + pos * 16: q * 128 + pos * 16 + 16] = np.arange(q * 128 + c * 16, q * 128 + c * 16 + 16)
+    return perm
+
+
+_VPERM = _v_perm()
+
+
+def split_page(page: np.ndarray, page_tokens: int, fmt: int, group: int, role: int):
+    """Split one raw page (uint8 bytes) into the K (role 0) or V (role 1) half:
+    (codes [P, 64] in the pack_k / pack_v byte order, meta0 [P, ng], meta1 [P, ng]).
+    For FMT_REF the meta are (scales fp32, zps u8); for FMT_FP16MIN (scale fp16,
+    min fp16)."""
+    ng = HEAD_DIM // group
+    bb = block_bytes(fmt, group)
+    codes, m0, m1 = [], [], []
+    for blk in range(page_tokens // BLOCK_TOKENS):
+        b = page[blk * bb:(blk + 1) * bb]
+        if role == 0:
+            codes.append(b[:8192].reshape(BLOCK_TOKENS, 64))
+        else:
+            logical = np.empty(8192, np.uint8)
+            logical[_VPERM] = b[8192:16384]
+            codes.append(logical.reshape(BLOCK_TOKENS, 64))
+        meta = b[16384 + role * 512 * ng: 16384 + (role + 1) * 512 * ng]
+        if fmt == FMT_REF:
+            m0.append(meta.view(np.float32).reshape(BLOCK_TOKENS, ng))
+            zo = 16384 + 1024 * ng + role * 128 * ng
+            m1.append(b[zo: zo + 128 * ng].reshape(BLOCK_TOKENS, ng))
+        else:
+            hm = meta.view(np.float16).reshape(BLOCK_TOKENS, ng, 2)
+            m0.append(hm[..., 0])
+            m1.append(hm[..., 1])
+    return np.concatenate(codes), np.concatenate(m0), np.concatenate(m1)
 
 
 # ---------------------------------------------------------------------------

@@ -15,15 +15,14 @@ def t16(x: np.ndarray, device="cuda", dtype=torch.float16) -> torch.Tensor:
 
 
 def read_side(store, role: int):
-    """Unpack one side of a dense-mode or paged store into numpy arrays over
-    body slots [0, capacity): codes [B,H,cap,128] and the two meta arrays
-    [B,H,cap,ng] (scale/zp for ref, scale/min for fp16min)."""
+    """Unpack the K (role 0) or V (role 1) half of a dense-mode or paged store
+    into numpy arrays over body slots [0, capacity): codes [B,H,cap,128] and the
+    two meta arrays [B,H,cap,ng] (scale/zp for ref, scale/min for fp16min)."""
     torch.cuda.synchronize()
     pool = store.pool.cpu().numpy()
     P = store.page_tokens
     fmt = 0 if store.fmt == "ref" else 1
     ng = HEAD_DIM // store.group
-    off = 0 if role == 0 else store.side_bytes
     B, H, mp = store.batch, store.kv_heads, store.max_pages
     table = store.page_table.cpu().numpy() if store.paged else None
     codes = np.zeros((B, H, mp * P, HEAD_DIM), np.uint8)
@@ -35,8 +34,7 @@ def read_side(store, role: int):
             page = table[u, pi] if table is not None else u * mp + pi
             if page < 0:
                 continue
-            raw = pool[page, off:off + store.side_bytes]
-            c, a, z = ko.split_side_page(raw, P, fmt, store.group)
+            c, a, z = ko.split_page(pool[page], P, fmt, store.group, role)
             codes[b, h, pi * P:(pi + 1) * P] = ko.unpack_k(c) if role == 0 else ko.unpack_v(c, P)
             m0[b, h, pi * P:(pi + 1) * P] = a
             m1[b, h, pi * P:(pi + 1) * P] = z

@@ -40,8 +40,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_struct_layouts_match_header(lib):
-    assert ctypes.sizeof(lib.HkvInt4Side) == 16
-    assert ctypes.sizeof(lib.HkvInt4Store) == 16 + 16 + 4 * 4 + 8 + 8 + 4 + 4
+    assert ctypes.sizeof(lib.HkvInt4Store) == 8 + 8 + 4 * 4 + 8 + 8 + 4 + 4
     assert ctypes.sizeof(lib.HkvDenseKV) == 8 + 8 + 4 + 4 + 3 * 8 + 8 + 4 + 4
 
 
@@ -50,11 +49,12 @@ def test_host_only_entry_points(lib):
     assert so.hkv_version() >= 100
     assert lib.status_str(0) == "HKV_OK"
     assert "CAPACITY" in lib.status_str(5)
-    # page geometry: 84 B/token (ref, group 32), 80 B/token (fp16min, group 32)
-    assert so.hkv_side_page_bytes(0, 32, 256) == 256 * 84
-    assert so.hkv_side_page_bytes(1, 32, 256) == 256 * 80
-    assert so.hkv_side_page_bytes(0, 128, 256) == 256 * 69
-    assert so.hkv_side_page_bytes(0, 48, 256) == -1
+    # page geometry (K and V): 168 B/token (ref, group 32), 160 B/token (fp16min, group 32)
+    assert so.hkv_page_bytes(0, 32, 256) == 256 * 168
+    assert so.hkv_page_bytes(1, 32, 256) == 256 * 160
+    assert so.hkv_page_bytes(0, 128, 256) == 256 * 138
+    assert so.hkv_page_bytes(0, 48, 256) == -1
+    assert so.hkv_page_bytes(0, 32, 200) == -1  # pages hold whole 128-token blocks
     # no body and no dense segment: nothing to plan
     assert so.hkv_decode_workspace_bytes(None, None, 8, 32, 8, 128, 0) == 0
 

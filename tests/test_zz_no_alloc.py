@@ -14,10 +14,8 @@ def test_static_rejects_oversized_request_on_host():
     """A request whose workspace exceeds the scratch fails before any CUDA call
     (the pointers below are never dereferenced)."""
     lib = L.load()
-    side = lib.hkv_side_page_bytes(L.FMT_FP16MIN, 32, 256)
     st = L.HkvInt4Store()
-    st.k = L.HkvInt4Side(0x100000, side)
-    st.v = L.HkvInt4Side(0x200000, side)
+    st.pages, st.page_stride = 0x100000, lib.hkv_page_bytes(L.FMT_FP16MIN, 32, 256)
     st.format, st.group, st.page_tokens, st.max_pages = L.FMT_FP16MIN, 32, 256, 4
     st.page_table, st.lengths, st.len = None, None, 1024
     B, Hq, Hkv = 8192, 64, 8  # 65536 units: the merge partials alone need ~1 GiB
