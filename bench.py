@@ -337,7 +337,7 @@ def main():
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "api": "TieredKVDecoder.step_host (pinned host q/k/v in, fp32 out)"},
-            "gpu_launches": args.steps * args.layers * 2,  # append_kv_kernel + decode_kernel per layer
+            "gpu_launches": world * args.steps * args.layers * 2,  # append_kv + decode per layer, all ranks
             "clocks": clocks,
         }
         if cpu is not None:
