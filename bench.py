@@ -11,6 +11,7 @@ outlier K channels per head, bf16 queries); the per-step working set (12 GB)
 is far larger than L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload cfg3 [--window PAGES]   # config 3: tiered offload + prefetch
 
 With N > 1 (torchrun, one rank per GPU) every rank decodes its own 8
 sequences (batch x KV-head sharding, no collective on the data path): weak
@@ -45,7 +46,12 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--fmt", default="fp16min", choices=["fp16min", "ref"])
     ap.add_argument("--layers", type=int, default=CFG1["layers"])
-    ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = two CTAs per SM)")
+    ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = one CTA per SM)")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg3"],
+                    help="cfg1: the headline decode benchmark (default); cfg3: tiered offload, layer-ahead "
+                         "host->device page prefetch (prints its own line)")
+    ap.add_argument("--window", type=int, default=0,
+                    help="cfg3: cold pages copied and attended per unit and layer (0 = all of them)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
@@ -160,9 +166,82 @@ def layer_bytes(batch, body_tokens, fmt, kv_heads=8, q_heads=32, sink=64, recent
     return attn + append
 
 
+# --------------------------------------------------------------------------- config 3
+def run_cfg3(args) -> None:
+    """InternLM2-7B-shaped tiered offload: 32 layers, B4, Hq32/Hkv8, 131,072-token
+    context of which 8,256 stay in HBM (64 sink + 1,024 recent fp16, 28 INT4 pages)
+    and 480 INT4 pages of 256 tokens per (sequence, KV head) live in pinned host
+    DRAM, copied one layer ahead of their attention."""
+    import torch
+    from hetero_kvcache_optimizer_b200 import _lib
+    from hetero_kvcache_optimizer_b200.offload import TieredOffloadDecoder
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    layers = args.layers
+    dec = TieredOffloadDecoder(layers, 4, 32, 8, resident_pages=28, cold_pages=480,
+                               window_pages=args.window or None, fmt=args.fmt, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    dec.fill(gen)
+    q = torch.randn(layers, 4, 32, 128, device=dev, generator=gen).bfloat16()
+    out = torch.empty(layers, 4, 32, 128, device=dev)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(transfer: bool) -> float:
+        for _ in range(args.warmup):
+            dec.step(q, out, transfer)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(args.steps):
+            dec.step(q, out, transfer)
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    ms_with = timed(True)
+    clocks = sampler.stop()
+    ms_without = timed(False)
+    # host link alone: the same per-layer copies back to back on the side stream
+    ps = dec.prefetcher.stream
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    c0.record(ps)
+    for l in range(layers):
+        dec.prefetcher.submit(dec.src_pages, dec.dst_slots[l % 2])
+    c1.record(ps)
+    torch.cuda.synchronize()
+    copy_ms = c0.elapsed_time(c1)
+    h2d = dec.h2d_bytes_per_step()
+    derr = _lib.device_error(clear=True)
+    if derr:
+        raise RuntimeError(f"device error bits {derr} during the benchmark")
+    line = {"metric": "config3 tiered offload: H2D GB/s and exposed transfer ms per decode step",
+            "value": round(h2d / (ms_with * 1e-3) / 1e9, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_with, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 mma (int4 storage, fp32 accum)",
+            "data": "synthetic",
+            "config": {"workload": "config3: InternLM2-7B-shaped tiered offload, 32 layers, B4, Hq32/Hkv8, "
+                                   "ctx 131072: 64 sink + 1024 recent fp16 + 28 INT4 pages in HBM, 480 INT4 "
+                                   "pages of 256 tokens per unit in pinned host DRAM",
+                       "layers": layers, "kv_format": args.fmt, "window_pages": dec.window,
+                       "attended_tokens": dec.tokens + dec.dense[0].len_hint},
+            "h2d_bytes_per_step": h2d, "exposed_ms_per_step": round(ms_with - ms_without, 4),
+            "decode_ms_per_step_without_transfer": round(ms_without, 4),
+            "h2d_copy_only_ms_per_step": round(copy_ms, 4),
+            "h2d_copy_only_gbs": round(h2d / (copy_ms * 1e-3) / 1e9, 2),
+            "attn_gbs_without_transfer": round(dec.attn_bytes_per_step() / (ms_without * 1e-3) / 1e9, 1),
+            "gpu_launches": args.steps * layers, "clocks": clocks}
+    print(json.dumps(line))
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main():
     args = parse_args()
+    if args.workload == "cfg3" and args.impl == "ours":
+        run_cfg3(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
