@@ -47,9 +47,12 @@ def parse_args():
     ap.add_argument("--fmt", default="fp16min", choices=["fp16min", "ref"])
     ap.add_argument("--layers", type=int, default=CFG1["layers"])
     ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = one CTA per SM)")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg3"],
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg3", "cfg4b"],
                     help="cfg1: the headline decode benchmark (default); cfg3: tiered offload, layer-ahead "
-                         "host->device page prefetch (prints its own line)")
+                         "host->device page prefetch; cfg4b: sequence split across ranks + NCCL all-gather "
+                         "of partials + LSE merge (each prints its own line)")
+    ap.add_argument("--ctx", type=int, default=131072, help="cfg4b: context per sequence")
+    ap.add_argument("--batch", type=int, default=64, help="cfg4b: sequences")
     ap.add_argument("--window", type=int, default=0,
                     help="cfg3: cold pages copied and attended per unit and layer (0 = all of them)")
     ap.add_argument("--e2e-steps", type=int, default=20)
@@ -236,11 +239,102 @@ def run_cfg3(args) -> None:
     print(json.dumps(line))
 
 
+# --------------------------------------------------------------------------- config 4, variant B
+def run_cfg4b(args, world: int, rank: int, local: int) -> None:
+    """Llama-3.1-8B shape, B sequences of `ctx` tokens, each sequence's INT4 body
+    split in contiguous page-aligned slices over the ranks (the last rank also
+    holds the 64 sink + 1024 recent fp16 tokens); per layer: partial attention on
+    every rank, one all-gather of the partials, LSE merge."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv, seqsplit
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    B, Hq, Hkv, layers = args.batch, 32, 8, args.layers
+    sink, recent = 64, 1024
+    body_pages = (args.ctx - sink - recent) // 256
+    p0, p1 = seqsplit.shard_range(body_pages, world, rank)
+    ntok = (p1 - p0) * 256
+    gen = torch.Generator(device=dev).manual_seed(40 + rank)
+    stores, denses = [], []
+    for l in range(layers):
+        st = kv.Int4KVStore(B, Hkv, max(ntok, 256), fmt=args.fmt, group=32, device=dev)
+        for t0 in range(0, ntok, 4096):
+            n = min(4096, ntok - t0)
+            x = torch.randn(B, Hkv, n, 128, device=dev, generator=gen).half()
+            kv.quantize_pack(x, st, 0, t0)
+            kv.quantize_pack(x, st, 1, t0)
+        st.set_lengths(ntok)
+        stores.append(st)
+        if rank == world - 1:
+            d = kv.DenseKV(B, Hkv, sink + recent, device=dev)
+            d.k.normal_(generator=gen)
+            d.v.normal_(generator=gen)
+            d.set_lengths(sink + recent)
+            denses.append(d)
+        else:
+            denses.append(None)
+    q = torch.randn(layers, B, Hq, 128, device=dev, generator=gen).bfloat16()
+    out = torch.empty(layers, B, Hq, 128, device=dev)
+
+    def step():
+        for l in range(layers):
+            seqsplit.decode(q[l], stores[l] if ntok else None, denses[l], out=out[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    st_ = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st_)
+    for _ in range(args.steps):
+        step()
+    e1.record(st_)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    derr = _lib.device_error(clear=True)
+    if derr:
+        raise RuntimeError(f"device error bits {derr} during the benchmark")
+    per_tok = 2 * (64 + 4 * 4 + (4 if args.fmt == "ref" else 0))
+    step_bytes = layers * (B * Hkv * (body_pages * 256 * per_tok + (sink + recent) * 512) + B * Hq * 128 * 6)
+    if rank == 0:
+        peak, _ = measured_peak()
+        gbs = step_bytes / (ms * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "config4 variant B: sequence-split INT4 decode attention, aggregate HBM GB/s and tokens/s",
+            "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 mma (int4 storage, fp32 accum)", "data": "synthetic",
+            "config": {"workload": f"config4 B: Llama-3.1-8B shape, B{B}, ctx {args.ctx} ({body_pages} INT4 "
+                                   f"pages + 64 sink + 1024 recent fp16 per unit), {layers} layers, sequence "
+                                   f"split over {world} GPU(s), NCCL all-gather of partials + LSE merge",
+                       "kv_format": args.fmt, "layers": layers, "parallelism": f"seqsplit{world}"},
+            "tokens_per_s": round(B / (ms * 1e-3), 1),
+            "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
+            "gpu_launches": world * args.steps * layers * 2}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main():
     args = parse_args()
     if args.workload == "cfg3" and args.impl == "ours":
         run_cfg3(args)
+        return
+    if args.workload == "cfg4b" and args.impl == "ours":
+        run_cfg4b(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+                  int(os.environ.get("LOCAL_RANK", "0")))
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

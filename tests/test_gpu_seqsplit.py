@@ -1,0 +1,70 @@
+"""Sequence-split decode over NCCL (config 4, variant B) on 2 GPUs: every rank
+holds one slice of each sequence's INT4 body (the last rank also the fp16
+segment); all-gathered partials merged by hkv_lse_merge equal the oracle's
+attention over the whole sequence. Skipped with fewer than 2 GPUs."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rank(rank, world, port, errs):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from hetero_kvcache_optimizer_b200 import kvstore as kv, seqsplit
+        from oracle import kv_oracle as ko
+        rng = np.random.default_rng(21)
+        B, Hq, Hkv, S, ND = 2, 16, 4, 1536, 96
+        k = rng.standard_normal((B, Hkv, S, 128)).astype(np.float16)
+        v = rng.standard_normal((B, Hkv, S, 128)).astype(np.float16)
+        kd = rng.standard_normal((B, Hkv, ND, 128)).astype(np.float16)
+        vd = rng.standard_normal((B, Hkv, ND, 128)).astype(np.float16)
+        q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
+        p0, p1 = seqsplit.shard_range(S // 256, world, rank)
+        t0, t1 = p0 * 256, p1 * 256
+        st = kv.Int4KVStore(B, Hkv, max(t1 - t0, 1), fmt="fp16min", group=32, device=dev)
+        kv.prefill(st, torch.from_numpy(k[:, :, t0:t1]).to(dev), torch.from_numpy(v[:, :, t0:t1]).to(dev))
+        dense = None
+        if rank == world - 1:
+            dense = kv.DenseKV(B, Hkv, ND, device=dev)
+            dense.k.copy_(torch.from_numpy(kd))
+            dense.v.copy_(torch.from_numpy(vd))
+            dense.set_lengths(ND)
+        qd = torch.from_numpy(q).to(dev).bfloat16()
+        out = seqsplit.decode(qd, st, dense)
+        torch.cuda.synchronize()
+        c, s, m = ko.quantize_fp16min(k.astype(np.float32), 32)
+        kq = ko.dequantize_fp16min(c, s, m, 32)
+        c, s, m = ko.quantize_fp16min(v.astype(np.float32), 32)
+        vq = ko.dequantize_fp16min(c, s, m, 32)
+        kall = np.concatenate([kq, kd.astype(np.float32)], axis=2)
+        vall = np.concatenate([vq, vd.astype(np.float32)], axis=2)
+        ref = ko.decode_attention(qd.float().cpu().numpy(), kall, vall)
+        err = np.abs(out.cpu().numpy() - ref).max(axis=-1) / np.linalg.norm(ref, axis=-1)
+        errs[rank] = float(err.max())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_seqsplit_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as man:
+        errs = man.dict()
+        port = 29100 + os.getpid() % 500
+        procs = [ctx.Process(target=_rank, args=(r, 2, port, errs)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(180)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert len(errs) == 2 and max(errs.values()) <= 2e-3, dict(errs)
