@@ -194,17 +194,23 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   }
   if (dense) sc.Td = dense->len > 0 ? cdiv(dense->len, hkv::kTileD) : (dense->lengths ? 1 : 0);
   if (sc.Tb + sc.Td == 0) sc.Td = 1;  // nothing to attend to: one empty tile yields zeros
-  const int ng = HKV_D / group;
-  sc.tb = (int64_t)hkv::kTileI4 * 2 * (HKV_CODE_BYTES + 4 * ng + (fmt == HKV_FMT_REF ? ng : 0));
-  sc.td = (int64_t)hkv::kTileD * 2 * HKV_D * 2;
-  sc.Ub = sc.Tb * sc.tb + sc.Td * sc.td;
-  sc.Btot = sc.Ub * sc.U;
-  const int64_t maxtile = std::max(sc.Tb ? sc.tb : 0, sc.Td ? sc.td : 0);
+  // tile weights in 128-byte steps (the kernel's schedule is 32-bit arithmetic)
+  const int64_t tb = block_bytes(fmt, group) / hkv::kSchedStep;
+  const int64_t td = (int64_t)hkv::kTileD * 2 * HKV_D * 2 / hkv::kSchedStep;
+  const int64_t Ub = sc.Tb * tb + sc.Td * td;
+  const int64_t Btot = Ub * sc.U;
+  if (Btot >= (int64_t(1) << 31)) return HKV_ERR_UNSUPPORTED;  // > 256 GiB in one call
+  const int64_t maxtile = std::max<int64_t>(sc.Tb ? tb : 0, sc.Td ? td : 0);
   int C = ctas > 0 ? ctas : device_sms();
-  C = (int)std::max<int64_t>(1, std::min<int64_t>(C, sc.Btot / maxtile));  // every CTA owns >= 1 tile
+  C = (int)std::max<int64_t>(1, std::min<int64_t>(std::min(C, 65535), Btot / maxtile));  // >= 1 tile per CTA
   sc.C = C;
-  const int64_t m = sc.Btot / C;
-  sc.S = (int)(sc.Ub / m) + 4;
+  sc.tb = (uint32_t)tb;
+  sc.td = (uint32_t)td;
+  sc.Ub = (uint32_t)Ub;
+  sc.Btot = (uint32_t)Btot;
+  sc.q = (uint32_t)(Btot / C);
+  sc.r = (uint32_t)(Btot % C);
+  sc.S = (int)(Ub / (Btot / C)) + 4;
   Plan pl;
   pl.sc = sc;
   pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4;

@@ -53,14 +53,18 @@ constexpr float kLazyRescale = 8.0f;
 constexpr int kDenseHalf = kTileD * 128;  // bytes of one 64-dim half of 32 dense rows (swizzled)
 
 // Equal-byte partition of the tile list over the persistent grid.
+// Positions are counted in 128-byte steps (every tile is a multiple of 128
+// bytes) so that the schedule is 32-bit arithmetic in every warp.
+constexpr int kSchedStep = 128;
 struct Sched {
-  int U;           // units (B * Hkv)
-  int Tb, Td;      // body / dense tiles per unit (from the host-side length hints)
-  int C;           // CTAs
-  int S;           // partial slots per unit in the workspace
-  int64_t tb, td;  // bytes per body / dense tile
-  int64_t Ub;      // bytes per unit
-  int64_t Btot;    // bytes in total
+  int U;            // units (B * Hkv)
+  int Tb, Td;       // body / dense tiles per unit (from the host-side length hints)
+  int C;            // CTAs
+  int S;            // partial slots per unit in the workspace
+  uint32_t tb, td;  // steps per body / dense tile
+  uint32_t Ub;      // steps per unit
+  uint32_t Btot;    // steps in total (< 2^31)
+  uint32_t q, r;    // Btot = q * C + r
 };
 
 struct DecodeParams {
@@ -101,13 +105,18 @@ static_assert(2 * kTileI4 * HKV_CODE_BYTES == kMetaOff && dense_slot_bytes() <= 
 static_assert(kTileI4 == HKV_BLOCK_TOKENS && block_bytes(HKV_FMT_REF, 32) <= kSlotBytes, "a tile is one page block");
 
 // ---------------------------------------------------------------- schedule arithmetic (per piece, not per tile)
-__device__ __forceinline__ int64_t cta_begin(const Sched& s, int c) { return (int64_t)c * s.Btot / s.C; }
-__device__ __forceinline__ int64_t tile_byte(const Sched& s, int u, int seg, int k) {
-  return (int64_t)u * s.Ub + (seg == 0 ? (int64_t)k * s.tb : (int64_t)s.Tb * s.tb + (int64_t)k * s.td);
+// CTA c owns steps [floor(c Btot / C), floor((c+1) Btot / C)); c*r < C^2 fits 32 bits.
+__device__ __forceinline__ uint32_t cta_begin(const Sched& s, int c) {
+  return (uint32_t)c * s.q + ((uint32_t)c * s.r) / (uint32_t)s.C;
 }
-__device__ __forceinline__ int owner_of(const Sched& s, int64_t x) {
-  int c = (int)(x * s.C / s.Btot);
-  if (c + 1 <= s.C && cta_begin(s, c + 1) <= x) ++c;
+__device__ __forceinline__ uint32_t tile_byte(const Sched& s, int u, int seg, int k) {
+  return (uint32_t)u * s.Ub + (seg == 0 ? (uint32_t)k * s.tb : (uint32_t)s.Tb * s.tb + (uint32_t)k * s.td);
+}
+// The CTA whose range holds step x: a float estimate, then exact corrections.
+__device__ __forceinline__ int owner_of(const Sched& s, uint32_t x) {
+  int c = min(s.C - 1, (int)((float)x * (float)s.C / (float)s.Btot));
+  while (c > 0 && cta_begin(s, c) > x) --c;
+  while (c + 1 < s.C && cta_begin(s, c + 1) <= x) ++c;
   return c;
 }
 
@@ -124,14 +133,14 @@ __device__ __forceinline__ int seg_len(const DecodeParams& p, int u, int seg) {
   return p.dense.lengths ? p.dense.lengths[b] : p.dense.len;
 }
 
-__device__ __forceinline__ void piece_fill(const DecodeParams& p, int64_t end, Piece& pc) {
+__device__ __forceinline__ void piece_fill(const DecodeParams& p, uint32_t end, Piece& pc) {
   const Sched& s = p.sc;
   const int T = pc.seg == 0 ? s.Tb : s.Td;
-  const int64_t ts = pc.seg == 0 ? s.tb : s.td;
+  const uint32_t ts = pc.seg == 0 ? s.tb : s.td;
   const int tile = pc.seg == 0 ? kTileI4 : kTileD;
-  const int64_t seg0 = tile_byte(s, pc.u, pc.seg, 0);
-  const int64_t kq = (end - 1 - seg0) / ts;
-  const int kl = kq < (int64_t)(T - 1) ? (int)kq : T - 1;  // last hinted tile starting in range
+  const uint32_t seg0 = tile_byte(s, pc.u, pc.seg, 0);
+  const uint32_t kq = (end - 1 - seg0) / ts;
+  const int kl = kq < (uint32_t)(T - 1) ? (int)kq : T - 1;  // last hinted tile starting in range
   pc.len = seg_len(p, pc.u, pc.seg);
   const int kneed = (pc.len + tile - 1) / tile;
   pc.k1 = kl + 1;
@@ -141,19 +150,20 @@ __device__ __forceinline__ void piece_fill(const DecodeParams& p, int64_t end, P
   pc.kd = min(pc.k1, kneed);
 }
 
-__device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, int64_t end) {
+__device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, uint32_t end) {
   const Sched& s = p.sc;
-  const int64_t x = cta_begin(s, c);
+  const uint32_t x = cta_begin(s, c);
   Piece pc;
   pc.u = (int)(x / s.Ub);
-  const int64_t r = x - (int64_t)pc.u * s.Ub;
-  if (s.Tb > 0 && r <= (int64_t)(s.Tb - 1) * s.tb) {
+  const uint32_t r = x - (uint32_t)pc.u * s.Ub;
+  if (s.Tb > 0 && r <= (uint32_t)(s.Tb - 1) * s.tb) {
     pc.seg = 0;
     pc.k0 = (int)((r + s.tb - 1) / s.tb);
-  } else if (s.Td > 0 && r <= (int64_t)s.Tb * s.tb + (int64_t)(s.Td - 1) * s.td) {
+  } else if (s.Td > 0 && r <= (uint32_t)s.Tb * s.tb + (uint32_t)(s.Td - 1) * s.td) {
     pc.seg = 1;
-    const int64_t rd = r - (int64_t)s.Tb * s.tb;
-    pc.k0 = rd > 0 ? (int)((rd + s.td - 1) / s.td) : 0;
+    // r may lie inside the last body tile (before the dense segment starts)
+    const uint32_t db = (uint32_t)s.Tb * s.tb;
+    pc.k0 = r > db ? (int)((r - db + s.td - 1) / s.td) : 0;
   } else {
     pc.u += 1;
     pc.seg = s.Tb > 0 ? 0 : 1;
@@ -164,7 +174,7 @@ __device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, int64
   return pc;
 }
 
-__device__ __forceinline__ void next_piece(const DecodeParams& p, int64_t end, Piece& pc) {
+__device__ __forceinline__ void next_piece(const DecodeParams& p, uint32_t end, Piece& pc) {
   const Sched& s = p.sc;
   const int T = pc.seg == 0 ? s.Tb : s.Td;
   if (pc.k1 < T) {  // the range ended inside this segment
@@ -483,6 +493,12 @@ __device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int h
   }
 }
 
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // Named barrier 1 over the consumer warps only (the TMA and expansion warps never join it).
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
 // Same barrier, returning whether v held on every consumer thread.
@@ -610,19 +626,19 @@ struct Cursor {
   int k;
   bool valid;
 };
-__device__ __forceinline__ void cursor_settle(const DecodeParams& p, int64_t end, Cursor& cu) {
+__device__ __forceinline__ void cursor_settle(const DecodeParams& p, uint32_t end, Cursor& cu) {
   while (cu.pc.valid && cu.k >= cu.pc.kd) {
     next_piece(p, end, cu.pc);
     cu.k = cu.pc.k0;
   }
   cu.valid = cu.pc.valid;
 }
-__device__ __forceinline__ void cursor_start(const DecodeParams& p, int c, int64_t end, Cursor& cu) {
+__device__ __forceinline__ void cursor_start(const DecodeParams& p, int c, uint32_t end, Cursor& cu) {
   cu.pc = first_piece(p, c, end);
   cu.k = cu.pc.k0;
   cursor_settle(p, end, cu);
 }
-__device__ __forceinline__ void cursor_next(const DecodeParams& p, int64_t end, Cursor& cu) {
+__device__ __forceinline__ void cursor_next(const DecodeParams& p, uint32_t end, Cursor& cu) {
   cu.k++;
   cursor_settle(p, end, cu);
 }
@@ -636,13 +652,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   __shared__ __align__(8) uint64_t full_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t ready_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t empty_bar[kMaxSlots];
+  __shared__ int2 s_info[kMaxSlots];  // per slot, written by the issue warp: (segment or -1 = done, valid tokens)
   __shared__ int s_last;
 
   // the 128-byte swizzle of the dense tiles repeats every 1024 bytes: align the ring
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const Sched& sc = p.sc;
   const int c = blockIdx.x;
-  const int64_t end = cta_begin(sc, c + 1);
+  const uint32_t end = cta_begin(sc, c + 1);
   const int nsl = p.nslots;
   uint8_t* ring = smem;
   float* comb = reinterpret_cast<float*>(ring + nsl * kSlotBytes);  // [8][G][128] + [8][8][2]
@@ -658,89 +675,97 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   }
   __syncthreads();
 
-  if (warp == kIssueWarp) {
-    // ================================================================ TMA issue warp
-    Cursor cu;
-    cursor_start(p, c, end, cu);
-    Ring ri{0, 0u};
-    int n = 0;
-    // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
-    int pg_u = -1, pg0 = 0, pg_lane = -1;
-    constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
-    while (cu.valid) {
-      if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
-      uint8_t* sb = ring + ri.slot * kSlotBytes;
-      uint64_t* fb = &full_bar[ri.slot];
-      const int u = cu.pc.u;
-      if (cu.pc.seg == 0) {
-        const int t = cu.k * kTileI4;
-        const int pi = p.page_shift >= 0 ? t >> p.page_shift : t / p.body.page_tokens;
-        if (u != pg_u || pi < pg0 || pi >= pg0 + 32) {
-          pg_u = u;
-          pg0 = pi;
-          const int pl = pi + lane;
-          pg_lane = -1;
-          if (pl < p.body.max_pages)
-            pg_lane = p.body.page_table ? p.body.page_table[(int64_t)u * p.body.max_pages + pl]
-                                        : (int)((int64_t)u * p.body.max_pages + pl);
-        }
-        const int page = __shfl_sync(0xffffffffu, pg_lane, pi - pg0);
-        if (lane == 0) {
-          if (page < 0) {
-            hkv_flag_error(HKV_DEVERR_BAD_PAGE);
-            mbar_arrive(fb);
-          } else {
-            const int off = p.page_shift >= 0 ? t & ((1 << p.page_shift) - 1) : t % p.body.page_tokens;
-            const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + (int64_t)page * p.body.page_stride +
-                                 (int64_t)(off / kTileI4) * kTileBytes;
-            mbar_arrive_expect_tx(fb, kTileBytes);
-            bulk_g2s(sb, src, kTileBytes, fb);
+  if (warp >= kConsumerWarps) {
+    if (warp == kIssueWarp) {
+      // ================================================================ TMA issue warp
+      Cursor cu;
+      cursor_start(p, c, end, cu);
+      Ring ri{0, 0u};
+      int n = 0;
+      // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
+      int pg_u = -1, pg0 = 0, pg_lane = -1;
+      constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
+      while (cu.valid) {
+        if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
+        uint8_t* sb = ring + ri.slot * kSlotBytes;
+        uint64_t* fb = &full_bar[ri.slot];
+        const int u = cu.pc.u;
+        // what the expansion warp needs to know about this load (published by the arrive below)
+        if (lane == 0)
+          s_info[ri.slot] = make_int2(cu.pc.seg, cu.pc.len - cu.k * (cu.pc.seg == 0 ? kTileI4 : kTileD));
+        if (cu.pc.seg == 0) {
+          const int t = cu.k * kTileI4;
+          const int pi = p.page_shift >= 0 ? t >> p.page_shift : t / p.body.page_tokens;
+          if (u != pg_u || pi < pg0 || pi >= pg0 + 32) {
+            pg_u = u;
+            pg0 = pi;
+            const int pl = pi + lane;
+            pg_lane = -1;
+            if (pl < p.body.max_pages)
+              pg_lane = p.body.page_table ? p.body.page_table[(int64_t)u * p.body.max_pages + pl]
+                                          : (int)((int64_t)u * p.body.max_pages + pl);
           }
+          const int page = __shfl_sync(0xffffffffu, pg_lane, pi - pg0);
+          if (lane == 0) {
+            if (page < 0) {
+              hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+              mbar_arrive(fb);
+            } else {
+              const int off = p.page_shift >= 0 ? t & ((1 << p.page_shift) - 1) : t % p.body.page_tokens;
+              const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + (int64_t)page * p.body.page_stride +
+                                   (int64_t)(off / kTileI4) * kTileBytes;
+              mbar_arrive_expect_tx(fb, kTileBytes);
+              bulk_g2s(sb, src, kTileBytes, fb);
+            }
+          }
+        } else if (lane == 0) {
+          const int b = u / p.Hkv, hk = u - b * p.Hkv, t = cu.k * kTileD;
+          const uint32_t d = smem_u32(sb);
+          mbar_arrive_expect_tx(fb, dense_slot_bytes());
+          tma_tile_4d(d, &p.tmk, 0, t, hk, b, fb);
+          tma_tile_4d(d + kDenseHalf, &p.tmk, 64, t, hk, b, fb);
+          tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
+          tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
         }
-      } else if (lane == 0) {
-        const int b = u / p.Hkv, hk = u - b * p.Hkv, t = cu.k * kTileD;
-        const uint32_t d = smem_u32(sb);
-        mbar_arrive_expect_tx(fb, dense_slot_bytes());
-        tma_tile_4d(d, &p.tmk, 0, t, hk, b, fb);
-        tma_tile_4d(d + kDenseHalf, &p.tmk, 64, t, hk, b, fb);
-        tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
-        tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
-      }
-      n++;
-      ri.advance(nsl);
-      cursor_next(p, end, cu);
-    }
-    // every issued copy must have landed before the CTA exits
-    if (lane == 0) {
-      for (int i = max(0, n - nsl); i < n; ++i) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
-    }
-    return;
-  }
-
-  if (warp >= kExpandWarp) {
-    // ================================================================ metadata expansion warps
-    // expansion warp x takes the loads n with n % kExpandWarps == x
-    const int x = warp - kExpandWarp;
-    Cursor cu;
-    cursor_start(p, c, end, cu);
-    Ring re{0, 0u};
-    for (int n = 0; cu.valid; ++n) {
-      if (n % kExpandWarps != x) {
-        re.advance(nsl);
+        n++;
+        ri.advance(nsl);
         cursor_next(p, end, cu);
-        continue;
       }
-      if (!warp_wait(&full_bar[re.slot], re.phase)) break;
-      uint8_t* sb = ring + re.slot * kSlotBytes;
-      if (cu.pc.seg == 0) {
-        expand_meta<FMT, NG>(sb + kMetaOff, lane, cu.pc.len - cu.k * kTileI4, p.qscale);
-      } else {
-        zero_dense_v_tail(sb, cu.pc.len - cu.k * kTileD, lane);
+      // one end-of-work load per expansion warp (a plain arrive, no copy)
+      for (int x = 0; x < kExpandWarps; ++x) {
+        if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
+        if (lane == 0) {
+          s_info[ri.slot] = make_int2(-1, 0);
+          mbar_arrive(&full_bar[ri.slot]);
+        }
+        n++;
+        ri.advance(nsl);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ready_bar[re.slot]);
-      re.advance(nsl);
-      cursor_next(p, end, cu);
+      // every issued copy must have landed before the CTA exits
+      if (lane == 0) {
+        for (int i = max(0, n - nsl); i < n; ++i) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
+      }
+    } else {
+      // ================================================================ metadata expansion warps
+      // expansion warp x takes the loads n with n % kExpandWarps == x, until the
+      // issue warp's end-of-work load
+      const int x = warp - kExpandWarp;
+      Ring re{0, 0u};
+      for (int i = 0; i < x; ++i) re.advance(nsl);
+      while (true) {
+        if (!warp_wait(&full_bar[re.slot], re.phase)) break;
+        const int2 info = s_info[re.slot];
+        if (info.x < 0) break;
+        uint8_t* sb = ring + re.slot * kSlotBytes;
+        if (info.x == 0) {
+          expand_meta<FMT, NG>(sb + kMetaOff, lane, info.y, p.qscale);
+        } else {
+          zero_dense_v_tail(sb, info.y, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready_bar[re.slot]);
+        for (int i = 0; i < kExpandWarps; ++i) re.advance(nsl);
+      }
     }
     return;
   }
@@ -929,13 +954,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
           pml[2 * h + 1] = L;
         }
       }
-      __threadfence();
+      // The barrier orders every consumer thread's partial stores before thread 0's
+      // acq_rel atomic, whose release makes them visible GPU-wide (cumulativity)
+      // and whose acquire, followed by the barrier, orders the merge's loads of the
+      // other CTAs' partials after their releases.
       consumer_sync();
-      if (threadIdx.x == 0) s_last = atomicAdd(&p.counters[u], 1) == nb + nd - 1;
+      if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.counters[u], 1) == nb + nd - 1;
       consumer_sync();
       if (s_last) {
         // last piece of the unit: merge all its partials (warp h: head h)
-        __threadfence();
         const int n = nb + nd;
         const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
         const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
