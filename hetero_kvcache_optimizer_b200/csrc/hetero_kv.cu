@@ -393,7 +393,9 @@ hkv_status hkv_quantize_pack(const void* x, int32_t dtype, int32_t B, int32_t H,
     return HKV_ERR_CAPACITY;
   if (T == 0) return HKV_OK;
   const int64_t ntok = (int64_t)B * H * T;
-  const int blocks = (int)((ntok + 15) / 16);
+  if (ntok >= (int64_t(1) << 31) - 64) return HKV_ERR_UNSUPPORTED;
+  const int per_block = 16 * hkv::kQuantTokens;
+  const int blocks = (int)((ntok + per_block - 1) / per_block);
   if (dtype == HKV_DT_F16) {
     hkv::quantize_pack_kernel<__half><<<blocks, 256, 0, S(stream)>>>(static_cast<const __half*>(x), B, H, T, stride_b,
                                                                      stride_h, stride_t, role, *dst, dst_start, start);

@@ -10,17 +10,31 @@ namespace hkv {
 //   q = clamp(rint(x / scale + zp), 0, 15)
 // Division is correctly rounded (the library is built without fast-math) and
 // the add is not contracted into an fma, so codes match torch bit for bit.
+// x / s correctly rounded, given r = RN(1/s): q0 = RN(x r); the remainder
+// e = x - q0 s is exact with an fma; RN(q0 + e r) is the correctly rounded
+// quotient (Markstein's correction step, IBM J. R&D 34(1), 1990; see Muller et
+// al., Handbook of Floating-Point Arithmetic, ch. on division with an FMA).
+// Holds away from underflow and overflow of the intermediates; the codes only
+// depend on quotients near x.5, far from both. Three operations per element
+// instead of a full division: the reciprocal is computed once per group.
+__device__ __forceinline__ float div_by(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-q0, s, x);
+  return __fmaf_rn(e, r, q0);
+}
+
 struct RefParams {
-  float scale, zpf;
+  float scale, zpf, rcp;
 };
 __device__ __forceinline__ RefParams ref_params(float mn, float mx) {
   RefParams p;
   p.scale = fmaxf((mx - mn) / 15.0f, 1e-8f);
   p.zpf = fminf(fmaxf(rintf(-mn / p.scale), 0.0f), 15.0f);
+  p.rcp = __frcp_rn(p.scale);
   return p;
 }
 __device__ __forceinline__ uint32_t ref_code(float x, const RefParams& p) {
-  const float t = __fadd_rn(__fdiv_rn(x, p.scale), p.zpf);
+  const float t = __fadd_rn(div_by(x, p.scale, p.rcp), p.zpf);
   return static_cast<uint32_t>(fminf(fmaxf(rintf(t), 0.0f), 15.0f));
 }
 
@@ -28,7 +42,7 @@ __device__ __forceinline__ uint32_t ref_code(float x, const RefParams& p) {
 // q = clamp(rint((x - min_h) / scale_h), 0, 15), or 0 when scale_h == 0.
 struct MinParams {
   __half sh, mh;
-  float sf, mf;
+  float sf, mf, rcp;
 };
 __device__ __forceinline__ MinParams min_params(float mn, float mx) {
   MinParams p;
@@ -36,11 +50,12 @@ __device__ __forceinline__ MinParams min_params(float mn, float mx) {
   p.mh = __float2half_rn(mn);
   p.sf = __half2float(p.sh);
   p.mf = __half2float(p.mh);
+  p.rcp = p.sf > 0.0f ? __frcp_rn(p.sf) : 0.0f;
   return p;
 }
 __device__ __forceinline__ uint32_t min_code(float x, const MinParams& p) {
   if (!(p.sf > 0.0f)) return 0u;
-  const float t = __fdiv_rn(__fsub_rn(x, p.mf), p.sf);
+  const float t = div_by(__fsub_rn(x, p.mf), p.sf, p.rcp);
   return static_cast<uint32_t>(fminf(fmaxf(rintf(t), 0.0f), 15.0f));
 }
 
@@ -133,44 +148,55 @@ __device__ __forceinline__ void store8(T* dst, const float (&v)[8]) {
 }
 
 // ------------------------------------------------------------------ quantise + pack
-// grid.x covers B*H*T tokens, 16 tokens per 256-thread block, 16 lanes per token.
+// Each half-warp quantises kQuantTokens consecutive tokens: their 16-byte loads
+// are all issued before the first token is processed (latency overlap), 16
+// lanes per token. grid.x covers ceil(B*H*T / (16 * kQuantTokens)) blocks of 256.
+constexpr int kQuantTokens = 1;
 template <typename T>
 __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict__ x, int B, int H, int T_,
                                                             int64_t sb, int64_t sh, int64_t st, int role,
                                                             hkv_int4_store store, const int32_t* dst_start,
                                                             int start) {
-  const int64_t tok = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
-  const int64_t ntok = (int64_t)B * H * T_;
-  const bool valid = tok < ntok;
-  const int64_t tt = valid ? tok : 0;
-  const int t = (int)(tt % T_);
-  const int u = (int)(tt / T_);
-  const int b = u / H, h = u % H;
+  const int ntok = B * H * T_;  // < 2^31 (checked by the host)
+  const int tok0 = (blockIdx.x * 16 + (threadIdx.x >> 4)) * kQuantTokens;
   const int p = threadIdx.x & 15;
-  float v[8];
-  if (valid) {
-    load8(x + b * sb + h * sh + (int64_t)t * st + 8 * p, v);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
-  }
-  const int pos = (dst_start ? dst_start[b] : start) + t;
   const int cap = store.max_pages * store.page_tokens;
-  bool ok = valid;
-  int64_t page = 0;
-  if (valid) {
-    if (pos < 0 || pos >= cap) {
-      if (p == 0) hkv_flag_error(HKV_DEVERR_CAPACITY);
-      ok = false;
+  float v[kQuantTokens][8];
+  int pos[kQuantTokens], unit[kQuantTokens];
+#pragma unroll
+  for (int i = 0; i < kQuantTokens; ++i) {
+    const int tok = tok0 + i;
+    const bool valid = tok < ntok;
+    const int tt = valid ? tok : 0;
+    const int u = tt / T_, t = tt - u * T_;
+    const int b = u / H, h = u - b * H;
+    unit[i] = valid ? u : -1;
+    pos[i] = (dst_start ? dst_start[b] : start) + t;
+    if (valid) {
+      load8(x + b * sb + h * sh + (int64_t)t * st + 8 * p, v[i]);
     } else {
-      page = store_page(store, u, pos);
-      if (page < 0) {
-        if (p == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
-        ok = false;
-      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
     }
   }
-  quantise_token(v, ok, role, store.format, store.group, store, page, pos % store.page_tokens);
+#pragma unroll
+  for (int i = 0; i < kQuantTokens; ++i) {
+    bool ok = unit[i] >= 0;
+    int64_t page = 0;
+    if (ok) {
+      if (pos[i] < 0 || pos[i] >= cap) {
+        if (p == 0) hkv_flag_error(HKV_DEVERR_CAPACITY);
+        ok = false;
+      } else {
+        page = store_page(store, unit[i], pos[i]);
+        if (page < 0) {
+          if (p == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+          ok = false;
+        }
+      }
+    }
+    quantise_token(v[i], ok, role, store.format, store.group, store, page, ok ? pos[i] % store.page_tokens : 0);
+  }
 }
 
 // ------------------------------------------------------------------ decode-step append

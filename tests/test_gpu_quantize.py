@@ -41,6 +41,33 @@ def test_quantize_flat_matches_reference_sweep(hkv, golden):
         assert ko.sha256(deq.cpu().numpy()) == d["decompress_f32"], name
 
 
+def test_quantize_rounding_boundaries(hkv):
+    """Values whose quotient x/scale + zp sits on, or one or two ulps either side
+    of, a .5 rounding boundary, over scales from 1e-6 to 1e3 (fp32 input): codes
+    must equal the IEEE-division oracle's exactly."""
+    rng = np.random.default_rng(123)
+    G, ngroups = 32, 4096
+    x = np.zeros((ngroups, G), np.float32)
+    for g in range(ngroups):
+        mag = np.float32(10.0 ** rng.uniform(-5, 4))
+        mn, mx = np.float32(-rng.uniform(0.05, 1.0) * mag), np.float32(rng.uniform(0.05, 1.0) * mag)
+        scale = np.maximum(np.float32((mx - mn) / np.float32(15.0)), np.float32(1e-8))
+        zp = np.clip(np.rint(np.float32(-mn / scale)), 0, 15).astype(np.float32)
+        vals = [mn, mx]
+        while len(vals) < G:
+            k = rng.integers(0, 16)
+            b = np.float32((np.float32(k) + np.float32(0.5) - zp) * scale)
+            for _ in range(int(rng.integers(-2, 3))):
+                b = np.nextafter(b, np.float32(np.inf), dtype=np.float32)
+            vals.append(np.float32(np.clip(b, mn, mx)))
+        x[g] = np.array(vals, np.float32)
+    q, s_, z = hkv.quantize_flat(torch.from_numpy(x).cuda(), G)
+    qc, qs, qz = ko.quantize_ref(x, G)
+    assert np.array_equal(s_.cpu().numpy().reshape(-1), qs)
+    assert np.array_equal(z.cpu().numpy().reshape(-1), qz)
+    assert np.array_equal(q.cpu().numpy().reshape(qc.shape), qc)
+
+
 @pytest.mark.parametrize("page_tokens", [256, 4096])
 def test_quantize_pack_cfg0_bit_exact(hkv, golden, page_tokens):
     """Config 0 K/V packed into pages, unpacked by the oracle: codes, scales and
