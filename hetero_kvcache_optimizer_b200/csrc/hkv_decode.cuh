@@ -93,14 +93,19 @@ struct DecodeParams {
 // An INT4 tile is one 128-token page block, copied as is: K codes | V codes |
 // metadata (fp16min: K (s,min) f16x2 [128][NG] | V; ref: K scales f32 [128][NG] |
 // V scales | K zps u8 [128][NG] | V zps). With N = 128 NG entries, the metadata
-// is expanded in place into byte ranges of the metadata area
-//   [0, 4N) K scale f32 | [4N, 8N) K bias f32 | [10N, 14N) V bias f32 |
-//   [14N, 16N) V scale pairs f16x2 [64][NG] (tokens 2p, 2p+1)
-// so that every expanded entry lands either on the raw entry of the same index
-// (read by the same lane just before) or past all raw data: a lane never
-// overwrites raw bytes another lane has yet to read.
+// is expanded in place into these byte ranges of the metadata area:
+//   both:    [0, 4N) K scale * qs, f32 [128][NG]
+//   ref:     [4N, 8N) K bias -z*s f32 [128][NG] | [10N, 14N) V zero-point
+//            constants [64 pairs][NG][2] f16x2 | [14N, 16N) V scale pairs
+//   fp16min: [8N, 10N) V scale pairs f16x2 [64][NG] (tokens 2p, 2p+1) |
+//            [10N, 12N) V min pairs f16x2 [64][NG] | [12N, 12N + 1 KB) K mins as
+//            the bias MMA's A columns, f16x2 [128][2]
+// Every expanded entry lands either on the raw entry of the same index (read
+// by the same lane just before) or past all raw data: a lane never overwrites
+// raw bytes another lane has yet to read.
 __host__ __device__ constexpr int dense_slot_bytes() { return 4 * kDenseHalf; }
-static_assert(kMetaOff + 16 * kTileI4 * 4 <= kSlotBytes, "expanded metadata (g32) must fit its slot");
+static_assert(kMetaOff + 16 * kTileI4 * 4 <= kSlotBytes && 12 * kTileI4 * 4 + 1024 <= 16 * kTileI4 * 4,
+              "expanded metadata (g32) must fit its slot");
 static_assert(2 * kTileI4 * HKV_CODE_BYTES == kMetaOff && dense_slot_bytes() <= kSlotBytes, "slot layout");
 static_assert(kTileI4 == HKV_BLOCK_TOKENS && block_bytes(HKV_FMT_REF, 32) <= kSlotBytes, "a tile is one page block");
 
@@ -227,7 +232,7 @@ constexpr float kNoMax = -1.0e30f;
 template <int NG>
 struct WarpState {
   float o[8][4];      // O^T, m-tile mt: (dim 16mt+r | 16mt+r+8) x (head 2j | 2j+1)
-  float zacc[NG][2];  // sum_t b_g(t) * P(t)/16   (INT4 only)
+  float zc[4];        // fp16min INT4: sum_t min_r(t) P(t)/16 for group r (lanes r < NG), heads 2j, 2j+1
   float m[2];         // running max (base-2 logits)
   float mo[2];        // m + log2 of the P pre-scale (4 for INT4: P/16; 0 for dense)
   float l[2];         // sum of the pre-scaled P
@@ -238,7 +243,7 @@ __device__ __forceinline__ void ws_reset(WarpState<NG>& ws) {
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) ws.o[mt][0] = ws.o[mt][1] = ws.o[mt][2] = ws.o[mt][3] = 0.f;
 #pragma unroll
-  for (int g = 0; g < NG; ++g) ws.zacc[g][0] = ws.zacc[g][1] = 0.f;
+  for (int i = 0; i < 4; ++i) ws.zc[i] = 0.f;
   ws.m[0] = ws.m[1] = ws.mo[0] = ws.mo[1] = kNoMax;
   ws.l[0] = ws.l[1] = 0.f;
 }
@@ -278,11 +283,10 @@ __device__ __forceinline__ void softmax_step(WarpState<NG>& ws, const float (&x)
       ws.o[mt][2] *= a0;
       ws.o[mt][3] *= a1;
     }
-#pragma unroll
-    for (int g = 0; g < NG; ++g) {
-      ws.zacc[g][0] *= a0;
-      ws.zacc[g][1] *= a1;
-    }
+    ws.zc[0] *= a0;
+    ws.zc[1] *= a1;
+    ws.zc[2] *= a0;
+    ws.zc[3] *= a1;
     ws.l[0] *= a0;
     ws.l[1] *= a1;
   }
@@ -330,13 +334,20 @@ __device__ __forceinline__ void ld_row_u(const uint32_t* base, int row, uint32_t
 }
 
 // Scores of 16 tokens x 8 heads: x = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)},
-// already in base-2 logits (the expanded K scale and qsum carry sm_scale*log2 e).
-// kc / ks / kb point at this thread's row r of the tile's K codes / K scale / K bias.
-template <int NG>
+// already in base-2 logits (the expanded K scale and the bias terms carry
+// sm_scale*log2 e). kc / ks point at this thread's row r of the tile's K codes /
+// K scales. The group bias term sum_g b_g * sum(Q_g):
+//   ref:     b = -z*s in fp32 (kb, row r), one FMA per group;
+//   fp16min: b = min (exact f16), one extra MMA of A = mins [token][group, twice]
+//            against B = qs*sum(Q_g) split into f16 hi + lo parts (qbias), so
+//            every product is exact and the sum is fp32.
+template <int FMT, int NG>
 __device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, const float* kb,
-                                         const uint32_t (&qf)[8][2], const float (&nbias)[NG][2],
-                                         const float (&qsum)[NG][2], float (&x)[4]) {
+                                         const uint32_t* kmin, const uint32_t (&qf)[8][2],
+                                         const float (&nbias)[NG][2], const float (&qsum)[NG][2],
+                                         uint32_t qbias, float (&x)[4]) {
   constexpr int WPG = 4 / NG;  // packed words per group
+  const int lane = threadIdx.x & 31, r = lane >> 2, j = lane & 3;
   const uint4 kA = *reinterpret_cast<const uint4*>(kc);
   const uint4 kB = *reinterpret_cast<const uint4*>(kc + 8 * HKV_CODE_BYTES);
   const uint32_t kwa[4] = {kA.x, kA.y, kA.z, kA.w};
@@ -344,9 +355,16 @@ __device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, con
   float sA[NG], sB[NG], bA[NG], bB[NG];
   ld_row<NG>(ks, 0, sA);
   ld_row<NG>(ks, 8, sB);
-  ld_row<NG>(kb, 0, bA);
-  ld_row<NG>(kb, 8, bB);
   x[0] = x[1] = x[2] = x[3] = 0.f;
+  if constexpr (FMT == HKV_FMT_REF) {
+    ld_row<NG>(kb, 0, bA);
+    ld_row<NG>(kb, 8, bB);
+  } else {
+    constexpr int JB = NG == 4 ? 4 : (NG == 2 ? 2 : 1);  // lanes j < JB carry the A columns
+    const uint32_t ab[4] = {j < JB ? kmin[2 * r + (j & 1)] : 0u, j < JB ? kmin[2 * (r + 8) + (j & 1)] : 0u, 0u,
+                            0u};
+    mma16816<__half>(x, ab, qbias, 0u);
+  }
   float c[4];
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
@@ -362,10 +380,17 @@ __device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, con
     }
     mma16816<__half>(c, a1, qf[2 * w + 1][0], qf[2 * w + 1][1]);
     if (w % WPG == WPG - 1) {
-      x[0] = fmaf(sA[g], c[0], fmaf(bA[g], qsum[g][0], x[0]));
-      x[1] = fmaf(sA[g], c[1], fmaf(bA[g], qsum[g][1], x[1]));
-      x[2] = fmaf(sB[g], c[2], fmaf(bB[g], qsum[g][0], x[2]));
-      x[3] = fmaf(sB[g], c[3], fmaf(bB[g], qsum[g][1], x[3]));
+      if constexpr (FMT == HKV_FMT_REF) {
+        x[0] = fmaf(sA[g], c[0], fmaf(bA[g], qsum[g][0], x[0]));
+        x[1] = fmaf(sA[g], c[1], fmaf(bA[g], qsum[g][1], x[1]));
+        x[2] = fmaf(sB[g], c[2], fmaf(bB[g], qsum[g][0], x[2]));
+        x[3] = fmaf(sB[g], c[3], fmaf(bB[g], qsum[g][1], x[3]));
+      } else {
+        x[0] = fmaf(sA[g], c[0], x[0]);
+        x[1] = fmaf(sA[g], c[1], x[1]);
+        x[2] = fmaf(sB[g], c[2], x[2]);
+        x[3] = fmaf(sB[g], c[3], x[3]);
+      }
     }
   }
 }
@@ -376,22 +401,39 @@ __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   return d;
 }
 
+// 8 nibbles of x -> 4 f16x2 of the exact integers n - z, with per-half zero
+// points: zlo = (1024 + z_lo, 1024 + z_hi) and zhi = (-64 - z_lo, -64 - z_hi)
+// (as nib8_to_h2, whose constants are the z = 0 case).
+__device__ __forceinline__ void nib8_to_h2_z(uint32_t x, uint32_t zlo, uint32_t zhi, uint32_t (&h)[4]) {
+  constexpr uint32_t kMagic = 0x64006400u;  // (1024, 1024)
+  constexpr uint32_t kInv16 = 0x2C002C00u;  // (1/16, 1/16)
+  const uint32_t e0 = lop3<0xEA>(x, 0x000F000Fu, kMagic);
+  const uint32_t e1 = lop3<0xEA>(x, 0x00F000F0u, kMagic);
+  const uint32_t x8 = x >> 8;
+  const uint32_t e2 = lop3<0xEA>(x8, 0x000F000Fu, kMagic);
+  const uint32_t e3 = lop3<0xEA>(x8, 0x00F000F0u, kMagic);
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(h[0]) : "r"(e0), "r"(zlo));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[1]) : "r"(e1), "r"(kInv16), "r"(zhi));
+  asm("sub.f16x2 %0, %1, %2;" : "=r"(h[2]) : "r"(e2), "r"(zlo));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(e3), "r"(kInv16), "r"(zhi));
+}
+
 // O^T += V^T . (s P/16)^T for 16 tokens; P = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)}
 // pre-scaled by 1/16. vc points at this thread's V chunk (pair j, chunk r), vsp
-// at the subtile's V scale pairs (pair 0 = its tokens 0, 1), vb at row r of the
-// V bias. P is transposed once into the B layout (token pair 2j, 2j+1 of head
-// r) and multiplied by the pair's per-group scales there.
-template <int NG>
+// at the subtile's V scale pairs (pair 0 = its tokens 0, 1). P is transposed
+// once into the B layout (token pair 2j, 2j+1 of head r) and multiplied by the
+// pair's per-group scales there. The group bias:
+//   ref:     codes enter as exact n - z (vz: per pair and group the two
+//            zero-point constants of nib8_to_h2_z), so no bias term remains;
+//   fp16min: zc += mins [group][token] . P^T, one extra MMA (vz: min pairs).
+template <int FMT, int NG>
 __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* vc, const uint32_t* vsp,
-                                             const float* vb, const float (&P)[4]) {
+                                             const uint32_t* vz, const float (&P)[4]) {
   constexpr int WPG = 4 / NG;
-  const int j = threadIdx.x & 3;
+  const int lane = threadIdx.x & 31, r = lane >> 2, j = lane & 3;
   uint32_t sA[NG], sB[NG];
-  float bA[NG], bB[NG];
   ld_row_u<NG>(vsp, j, sA);
   ld_row_u<NG>(vsp, 4 + j, sB);
-  ld_row<NG>(vb, 0, bA);
-  ld_row<NG>(vb, 8, bB);
   const uint32_t tA = movmatrix_t(pack2<__half>(P[0], P[1]));
   const uint32_t tB = movmatrix_t(pack2<__half>(P[2], P[3]));
   uint32_t pb[NG][2];
@@ -399,8 +441,10 @@ __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* v
   for (int g = 0; g < NG; ++g) {
     pb[g][0] = hmul2(tA, sA[g]);
     pb[g][1] = hmul2(tB, sB[g]);
-    ws.zacc[g][0] = fmaf(bA[g], P[0], fmaf(bB[g], P[2], ws.zacc[g][0]));
-    ws.zacc[g][1] = fmaf(bA[g], P[1], fmaf(bB[g], P[3], ws.zacc[g][1]));
+  }
+  if constexpr (FMT == HKV_FMT_FP16MIN) {
+    const uint32_t ab[4] = {r < NG ? vz[j * NG + r] : 0u, 0u, r < NG ? vz[(4 + j) * NG + r] : 0u, 0u};
+    mma16816<__half>(ws.zc, ab, tA, tB);
   }
   const uint4 vA = *reinterpret_cast<const uint4*>(vc);
   const uint4 vB = *reinterpret_cast<const uint4*>(vc + 8 * HKV_CODE_BYTES);
@@ -412,8 +456,15 @@ __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* v
   for (int k = 0; k < 4; ++k) {
     const int g = k / WPG;
     uint32_t ha[4], hb[4];
-    nib8_to_h2(vwa[k], ha);
-    nib8_to_h2(vwb[k], hb);
+    if constexpr (FMT == HKV_FMT_REF) {
+      const uint2 za = *reinterpret_cast<const uint2*>(vz + 2 * (j * NG + g));
+      const uint2 zb = *reinterpret_cast<const uint2*>(vz + 2 * ((4 + j) * NG + g));
+      nib8_to_h2_z(vwa[k], za.x, za.y, ha);
+      nib8_to_h2_z(vwb[k], zb.x, zb.y, hb);
+    } else {
+      nib8_to_h2(vwa[k], ha);
+      nib8_to_h2(vwb[k], hb);
+    }
     const uint32_t a0[4] = {ha[0], ha[1], hb[0], hb[1]};
     const uint32_t a1[4] = {ha[2], ha[3], hb[2], hb[3]};
     mma16816<__half>(ws.o[2 * k], a0, pb[g][0], pb[g][1]);
@@ -542,23 +593,28 @@ template <int FMT, int NG>
 __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, float qs) {
   constexpr int N = kTileI4 * NG;
   constexpr int IT = N / 128;
-  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + 14 * N);  // [64 pairs][NG] f16x2
+  constexpr int VSP = FMT == HKV_FMT_REF ? 14 * N : 8 * N;
+  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + VSP);      // [64 pairs][NG] f16x2 scales
+  uint32_t* vmn = reinterpret_cast<uint32_t*>(meta + 10 * N);   // fp16min: [64][NG] min pairs
+  uint32_t* vzc = reinterpret_cast<uint32_t*>(meta + 10 * N);   // ref: [64][NG][2] zero-point constants
+  uint32_t* kmn = reinterpret_cast<uint32_t*>(meta + 12 * N);   // fp16min: [128][2] K mins, A columns
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
     const int e = 128 * it + 4 * lane;
     float sk[4], bk[4], sv[4], bv[4];
+    uint32_t zv = 0;
     if (FMT == HKV_FMT_REF) {
       const float4 a = *reinterpret_cast<const float4*>(meta + 4 * e);
       const float4 c = *reinterpret_cast<const float4*>(meta + 4 * N + 4 * e);
       const uint32_t zk = *reinterpret_cast<const uint32_t*>(meta + 8 * N + e);
-      const uint32_t zv = *reinterpret_cast<const uint32_t*>(meta + 9 * N + e);
+      zv = *reinterpret_cast<const uint32_t*>(meta + 9 * N + e);
       const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         sk[i] = av[i];
         sv[i] = cv[i];
         bk[i] = -static_cast<float>((zk >> (8 * i)) & 0xffu) * av[i];
-        bv[i] = -static_cast<float>((zv >> (8 * i)) & 0xffu) * cv[i];
+        bv[i] = 0.f;
       }
     } else {
       const uint4 a = *reinterpret_cast<const uint4*>(meta + 4 * e);
@@ -574,33 +630,75 @@ __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, 
         bv[i] = fv.y;
       }
     }
+    float zf[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      if ((e + i) / NG >= valid) sk[i] = bk[i] = sv[i] = bv[i] = 0.f;
+      zf[i] = static_cast<float>((zv >> (8 * i)) & 0xffu);
+      if ((e + i) / NG >= valid) sk[i] = bk[i] = sv[i] = bv[i] = zf[i] = 0.f;
     }
     *reinterpret_cast<float4*>(meta + 4 * e) = make_float4(sk[0] * qs, sk[1] * qs, sk[2] * qs, sk[3] * qs);
-    *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[0], bk[1], bk[2], bk[3]);
-    *reinterpret_cast<float4*>(meta + 10 * N + 4 * e) = make_float4(bv[0], bv[1], bv[2], bv[3]);
+    if (FMT == HKV_FMT_REF) *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[0], bk[1], bk[2], bk[3]);
+    // pairs (tokens 2p, 2p+1): scales and (fp16min) mins or (ref) zero-point constants
     if constexpr (NG == 4) {
-      // lane holds token 32 it + lane; its pair partner is lane ^ 1
-      float o[4];
+      // lane holds token t = 32 it + lane, groups 0..3; its pair partner is lane ^ 1
+      float os[4], ob[4], oz[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, sv[i], 1);
-      if ((lane & 1) == 0) {
-        const int pair = 16 * it + (lane >> 1);
-        *reinterpret_cast<uint4*>(vsp + pair * 4) =
-            make_uint4(pack2<__half>(sv[0], o[0]), pack2<__half>(sv[1], o[1]), pack2<__half>(sv[2], o[2]),
-                       pack2<__half>(sv[3], o[3]));
+      for (int i = 0; i < 4; ++i) {
+        os[i] = __shfl_xor_sync(0xffffffffu, sv[i], 1);
+        ob[i] = __shfl_xor_sync(0xffffffffu, bv[i], 1);
+        oz[i] = __shfl_xor_sync(0xffffffffu, zf[i], 1);
       }
+      const int t = 32 * it + lane;
+      if ((lane & 1) == 0) {
+        const int pair = t >> 1;
+        *reinterpret_cast<uint4*>(vsp + pair * 4) =
+            make_uint4(pack2<__half>(sv[0], os[0]), pack2<__half>(sv[1], os[1]), pack2<__half>(sv[2], os[2]),
+                       pack2<__half>(sv[3], os[3]));
+        if (FMT == HKV_FMT_REF) {
+          uint32_t w[8];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            w[2 * g] = pack2<__half>(1024.f + zf[g], 1024.f + oz[g]);
+            w[2 * g + 1] = pack2<__half>(-64.f - zf[g], -64.f - oz[g]);
+          }
+          *reinterpret_cast<uint4*>(vzc + pair * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(vzc + pair * 8 + 4) = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+          *reinterpret_cast<uint4*>(vmn + pair * 4) =
+              make_uint4(pack2<__half>(bv[0], ob[0]), pack2<__half>(bv[1], ob[1]), pack2<__half>(bv[2], ob[2]),
+                         pack2<__half>(bv[3], ob[3]));
+        }
+      }
+      if (FMT == HKV_FMT_FP16MIN)
+        *reinterpret_cast<uint2*>(kmn + 2 * t) = make_uint2(pack2<__half>(bk[0], bk[1]), pack2<__half>(bk[2], bk[3]));
     } else if constexpr (NG == 2) {
       // entries: (t, g0), (t, g1), (t+1, g0), (t+1, g1) with t = 64 it + 2 lane
-      const int pair = 32 * it + lane;
-      *reinterpret_cast<uint2*>(vsp + pair * 2) =
-          make_uint2(pack2<__half>(sv[0], sv[2]), pack2<__half>(sv[1], sv[3]));
+      const int pair = 32 * it + lane, t = 2 * pair;
+      *reinterpret_cast<uint2*>(vsp + pair * 2) = make_uint2(pack2<__half>(sv[0], sv[2]), pack2<__half>(sv[1], sv[3]));
+      if (FMT == HKV_FMT_REF) {
+        *reinterpret_cast<uint4*>(vzc + pair * 4) =
+            make_uint4(pack2<__half>(1024.f + zf[0], 1024.f + zf[2]), pack2<__half>(-64.f - zf[0], -64.f - zf[2]),
+                       pack2<__half>(1024.f + zf[1], 1024.f + zf[3]), pack2<__half>(-64.f - zf[1], -64.f - zf[3]));
+      } else {
+        *reinterpret_cast<uint2*>(vmn + pair * 2) = make_uint2(pack2<__half>(bv[0], bv[2]), pack2<__half>(bv[1], bv[3]));
+        const uint32_t m0 = pack2<__half>(bk[0], bk[1]), m1 = pack2<__half>(bk[2], bk[3]);
+        *reinterpret_cast<uint4*>(kmn + 2 * t) = make_uint4(m0, m0, m1, m1);
+      }
     } else {
-      // tokens 4 lane .. 4 lane + 3: pairs 2 lane, 2 lane + 1
-      *reinterpret_cast<uint2*>(vsp + 2 * lane) =
-          make_uint2(pack2<__half>(sv[0], sv[1]), pack2<__half>(sv[2], sv[3]));
+      // tokens 4 lane .. 4 lane + 3 (t = 4 lane): pairs 2 lane, 2 lane + 1
+      const int t = 4 * lane;
+      *reinterpret_cast<uint2*>(vsp + 2 * lane) = make_uint2(pack2<__half>(sv[0], sv[1]), pack2<__half>(sv[2], sv[3]));
+      if (FMT == HKV_FMT_REF) {
+        *reinterpret_cast<uint4*>(vzc + 4 * lane) =
+            make_uint4(pack2<__half>(1024.f + zf[0], 1024.f + zf[1]), pack2<__half>(-64.f - zf[0], -64.f - zf[1]),
+                       pack2<__half>(1024.f + zf[2], 1024.f + zf[3]), pack2<__half>(-64.f - zf[2], -64.f - zf[3]));
+      } else {
+        *reinterpret_cast<uint2*>(vmn + 2 * lane) = make_uint2(pack2<__half>(bv[0], bv[1]), pack2<__half>(bv[2], bv[3]));
+        *reinterpret_cast<uint4*>(kmn + 2 * t) =
+            make_uint4(pack2<__half>(bk[0], bk[0]), 0u, pack2<__half>(bk[1], bk[1]), 0u);
+        *reinterpret_cast<uint4*>(kmn + 2 * t + 4) =
+            make_uint4(pack2<__half>(bk[2], bk[2]), 0u, pack2<__half>(bk[3], bk[3]), 0u);
+      }
     }
   }
   // order these generic-proxy writes before later TMA (async-proxy) writes to the slot
@@ -776,7 +874,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   // [8 wg, 8 wg + 8) of a dense tile.
   WarpState<NG> ws;
   uint32_t qf[8][2];
-  float qsum[NG][2], nbias[NG][2];
+  float qsum[NG][2], nbias[NG][2];  // qsum: ref only
+  uint32_t qbias = 0;                // fp16min: B fragment of the K bias MMA
   const int r = lane >> 2, j = lane & 3;
   const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
   const bool h0 = 2 * j < p.G, h1 = 2 * j + 1 < p.G;
@@ -818,6 +917,27 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
           nbias[g][0] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j) * 4);
           nbias[g][1] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j + 1) * 4);
         }
+        if constexpr (FMT == HKV_FMT_FP16MIN) {
+          // B of the K bias MMA, head r: rows 0..NG-1 = f16 hi parts of qs*sum(Q_g),
+          // rows NG..2NG-1 = the lo parts (this lane holds rows 2j, 2j+1)
+          __half hi[NG], lo[NG];
+#pragma unroll
+          for (int g = 0; g < NG; ++g) {
+            const float v = qs * ps[g];
+            hi[g] = __float2half_rn(v);
+            lo[g] = __float2half_rn(v - __half2float(hi[g]));
+          }
+          auto h2 = [](__half a, __half b) {
+            return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+          };
+          if constexpr (NG == 4) {
+            qbias = j == 0 ? h2(hi[0], hi[1]) : j == 1 ? h2(hi[2], hi[3]) : j == 2 ? h2(lo[0], lo[1]) : h2(lo[2], lo[3]);
+          } else if constexpr (NG == 2) {
+            qbias = j == 0 ? h2(hi[0], hi[1]) : j == 1 ? h2(lo[0], lo[1]) : 0u;
+          } else {
+            qbias = j == 0 ? h2(hi[0], lo[0]) : 0u;
+          }
+        }
       } else {
         load_q_frags<DTy>(p, b, hk, false, qf, qa, qb);
       }
@@ -835,14 +955,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
           break;
         }
         const uint8_t* stg = ring + rc.slot * kSlotBytes;
-        const float* mk = reinterpret_cast<const float*>(stg + kMetaOff);
-        const float* ks = mk + ks_off;
-        const float* kb = mk + NM + ks_off;
-        const uint32_t* vsp = reinterpret_cast<const uint32_t*>(mk + 3 * NM + NM / 2) + vs_off;
-        const float* vb = mk + 2 * NM + NM / 2 + ks_off;
+        const uint8_t* mb = stg + kMetaOff;  // expanded metadata (layout above)
+        const float* ks = reinterpret_cast<const float*>(mb) + ks_off;
+        const float* kb = reinterpret_cast<const float*>(mb + 4 * NM) + ks_off;
+        const uint32_t* kmn = reinterpret_cast<const uint32_t*>(mb + 12 * NM) + 2 * t0;
+        const uint32_t* vsp =
+            reinterpret_cast<const uint32_t*>(mb + (FMT == HKV_FMT_REF ? 14 : 8) * NM) + vs_off;
+        const uint32_t* vz = reinterpret_cast<const uint32_t*>(mb + 10 * NM) + (FMT == HKV_FMT_REF ? 2 : 1) * vs_off;
         float xa[4], xb[4], x[8], P[8];
-        k_scores<NG>(stg + kc_off, ks, kb, qf, nbias, qsum, xa);
-        k_scores<NG>(stg + kc_off + 16 * HKV_CODE_BYTES, ks + 16 * NG, kb + 16 * NG, qf, nbias, qsum, xb);
+        k_scores<FMT, NG>(stg + kc_off, ks, kb, kmn, qf, nbias, qsum, qbias, xa);
+        k_scores<FMT, NG>(stg + kc_off + 16 * HKV_CODE_BYTES, ks + 16 * NG, kb + 16 * NG, kmn + 32, qf, nbias, qsum,
+                          qbias, xb);
         const int tok = k * kTileI4 + t0;
         x[0] = xa[0];
         x[1] = xa[1];
@@ -861,8 +984,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         softmax_step<NG, 8>(ws, x, P, 4.f);
         const float pa[4] = {P[0], P[1], P[2], P[3]};
         const float pc4[4] = {P[4], P[5], P[6], P[7]};
-        v_accumulate<NG>(ws, stg + vc_off, vsp, vb, pa);
-        v_accumulate<NG>(ws, stg + vc_off + 16 * HKV_CODE_BYTES, vsp + 8 * NG, vb + 16 * NG, pc4);
+        v_accumulate<FMT, NG>(ws, stg + vc_off, vsp, vz, pa);
+        v_accumulate<FMT, NG>(ws, stg + vc_off + 16 * HKV_CODE_BYTES, vsp + 8 * NG,
+                              vz + (FMT == HKV_FMT_REF ? 2 : 1) * 8 * NG, pc4);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);
         rc.advance(nsl);
@@ -895,16 +1019,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         l0 += __shfl_xor_sync(0xffffffffu, l0, sft);
         l1 += __shfl_xor_sync(0xffffffffu, l1, sft);
       }
+      // fp16min V bias of group g, heads 2j, 2j+1: row g of the bias MMA (lane 4g + j)
       float z[NG][2];
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
-        z[g][0] = body ? ws.zacc[g][0] : 0.f;
-        z[g][1] = body ? ws.zacc[g][1] : 0.f;
-#pragma unroll
-        for (int sft = 4; sft < 32; sft <<= 1) {
-          z[g][0] += __shfl_xor_sync(0xffffffffu, z[g][0], sft);
-          z[g][1] += __shfl_xor_sync(0xffffffffu, z[g][1], sft);
-        }
+        z[g][0] = __shfl_sync(0xffffffffu, ws.zc[0], 4 * g + j);
+        z[g][1] = __shfl_sync(0xffffffffu, ws.zc[1], 4 * g + j);
+        if (FMT == HKV_FMT_REF || !body) z[g][0] = z[g][1] = 0.f;
       }
       float* wo = comb + warp * p.G * HKV_D;
       float* cml = comb + kConsumerWarps * p.G * HKV_D;  // [8 warps][8 heads][2]
