@@ -141,11 +141,12 @@ __device__ __forceinline__ void nib8_to_h2(uint32_t x, uint32_t (&h)[4]) {
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(h[3]) : "r"(e3), "r"(kInv16), "r"(kM64));
 }
 
-// D = A(16x16, row) * B(16x8, col) + D, fp32 accumulate.
+// D = A(16x16, row) * B(16x8, col) + D, fp32 accumulate. Register-only, so not
+// volatile: the compiler may interleave independent MMAs with other work.
 template <typename T> __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
 template <>
 __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -154,7 +155,7 @@ __device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (
 template <>
 __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                                         uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -164,7 +165,7 @@ __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uin
 // D = A * B + C with separate C (used to seed an accumulator with a bias).
 __device__ __forceinline__ void mma16816_c(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
                                            const float (&c)[4]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -182,7 +183,7 @@ __device__ __forceinline__ uint32_t biased1(uint32_t x) { return lop3<0xEA>(x, 0
 // 8x8 b16 matrix transpose across the warp (fragment layout in and out).
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
 }
 
