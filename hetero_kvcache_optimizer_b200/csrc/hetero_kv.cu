@@ -213,7 +213,8 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   sc.S = (int)(Ub / (Btot / C)) + 4;
   Plan pl;
   pl.sc = sc;
-  pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4;
+  // the piece-end combine area, then the prefetched query rows of the next piece (f16/bf16)
+  pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4 + G * HKV_D * 2;
   const int avail = kDynSmemBudget - 1024 - pl.comb_bytes;
   pl.nslots = std::min(hkv::kMaxSlots, avail / hkv::kSlotBytes);
   if (pl.nslots < 2) return HKV_ERR_UNSUPPORTED;
@@ -254,6 +255,8 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
   p.q_dtype = q_dtype;
   p.q_sb = q_sb;
   p.q_sh = q_sh;
+  // 16-byte aligned query rows are prefetched a piece ahead with cp.async
+  p.q_async = aligned16(q) && (q_sb * 2) % 16 == 0 && (q_sh * 2) % 16 == 0;
   if (body) p.body = *body;
   if (dense) p.dense = *dense;
   p.B = B;

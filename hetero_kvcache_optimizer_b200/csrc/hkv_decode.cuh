@@ -73,6 +73,7 @@ struct DecodeParams {
   const void* q;
   int q_dtype;
   int64_t q_sb, q_sh;
+  int q_async;  // q rows 16-byte aligned: consumers prefetch the next piece's rows with cp.async
   hkv_int4_store body;
   hkv_dense_kv dense;
   int B, Hq, Hkv, G;
@@ -138,7 +139,7 @@ __device__ __forceinline__ int seg_len(const DecodeParams& p, int u, int seg) {
   return p.dense.lengths ? p.dense.lengths[b] : p.dense.len;
 }
 
-__device__ __forceinline__ void piece_fill(const DecodeParams& p, uint32_t end, Piece& pc) {
+__device__ __forceinline__ void piece_fill_len(const DecodeParams& p, uint32_t end, Piece& pc, int len) {
   const Sched& s = p.sc;
   const int T = pc.seg == 0 ? s.Tb : s.Td;
   const uint32_t ts = pc.seg == 0 ? s.tb : s.td;
@@ -146,13 +147,16 @@ __device__ __forceinline__ void piece_fill(const DecodeParams& p, uint32_t end, 
   const uint32_t seg0 = tile_byte(s, pc.u, pc.seg, 0);
   const uint32_t kq = (end - 1 - seg0) / ts;
   const int kl = kq < (uint32_t)(T - 1) ? (int)kq : T - 1;  // last hinted tile starting in range
-  pc.len = seg_len(p, pc.u, pc.seg);
+  pc.len = len;
   const int kneed = (pc.len + tile - 1) / tile;
   pc.k1 = kl + 1;
   // past its last hinted tile a segment continues while the true length needs it
   // (a stale hint can unbalance the grid, never drop tokens)
   if (kl == T - 1 && kneed > pc.k1) pc.k1 = kneed;
   pc.kd = min(pc.k1, kneed);
+}
+__device__ __forceinline__ void piece_fill(const DecodeParams& p, uint32_t end, Piece& pc) {
+  piece_fill_len(p, end, pc, seg_len(p, pc.u, pc.seg));
 }
 
 __device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, uint32_t end) {
@@ -179,7 +183,8 @@ __device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, uint3
   return pc;
 }
 
-__device__ __forceinline__ void next_piece(const DecodeParams& p, uint32_t end, Piece& pc) {
+// The piece after pc without its length-dependent fields (u, seg, k0, valid only).
+__device__ __forceinline__ void next_piece_head(const DecodeParams& p, uint32_t end, Piece& pc) {
   const Sched& s = p.sc;
   const int T = pc.seg == 0 ? s.Tb : s.Td;
   if (pc.k1 < T) {  // the range ended inside this segment
@@ -194,6 +199,9 @@ __device__ __forceinline__ void next_piece(const DecodeParams& p, uint32_t end, 
   }
   pc.k0 = 0;
   pc.valid = pc.u < s.U && tile_byte(s, pc.u, pc.seg, 0) < end;
+}
+__device__ __forceinline__ void next_piece(const DecodeParams& p, uint32_t end, Piece& pc) {
+  next_piece_head(p, end, pc);
   if (pc.valid) piece_fill(p, end, pc);
 }
 
@@ -513,24 +521,27 @@ __device__ __forceinline__ void dense_subtile(WarpState<NG>& ws, uint32_t slot, 
 // qf[kt][0] and 16kt + 2j + {8,9} in qf[kt][1] (divided by 16 when hi_div16).
 // qa/qb return the values exactly as the tensor core sees them. Heads r >= G
 // get Q = 0: their scores are finite and their results are never stored.
+// The rows come from global memory, or (qs != nullptr) from the G x 128 copy of
+// them in shared memory that the consumers prefetched.
 template <typename T>
-__device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int hk, bool hi_div16,
+__device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int hk, bool hi_div16, const void* qs,
                                              uint32_t (&qf)[8][2], float (&qa)[8][2], float (&qb)[8][2]) {
   const int lane = threadIdx.x & 31;
   const int r = lane >> 2, j = lane & 3;
   const bool live = r < p.G;
   const int hq = hk * p.G + (live ? r : 0);
-  const int64_t base = (int64_t)b * p.q_sb + (int64_t)hq * p.q_sh;
+  const void* src = qs ? qs : p.q;
+  const int64_t base = qs ? (int64_t)(live ? r : 0) * HKV_D : (int64_t)b * p.q_sb + (int64_t)hq * p.q_sh;
   const float sc = hi_div16 ? 0.0625f : 1.0f;
 #pragma unroll
   for (int kt = 0; kt < 8; ++kt) {
     const int d = 16 * kt + 2 * j;
     float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;
     if (live) {
-      v0 = load_any(p.q, p.q_dtype, base + d);
-      v1 = load_any(p.q, p.q_dtype, base + d + 1);
-      v2 = load_any(p.q, p.q_dtype, base + d + 8);
-      v3 = load_any(p.q, p.q_dtype, base + d + 9);
+      v0 = load_any(src, p.q_dtype, base + d);
+      v1 = load_any(src, p.q_dtype, base + d + 1);
+      v2 = load_any(src, p.q_dtype, base + d + 8);
+      v3 = load_any(src, p.q_dtype, base + d + 9);
     }
     const float r0 = to_f32(from_f32<T>(v0)), r1 = to_f32(from_f32<T>(v1));
     const float r2 = to_f32(from_f32<T>(to_f32(from_f32<T>(v2)) * sc));
@@ -543,6 +554,28 @@ __device__ __forceinline__ void load_q_frags(const DecodeParams& p, int b, int h
     qb[kt][1] = r3;
   }
 }
+
+__device__ __forceinline__ int q_elem_bytes(int dtype) { return dtype == HKV_DT_F32 ? 4 : 2; }
+
+// Consumer threads copy unit u's G query rows (G x 128 elements) into qbuf with
+// cp.async, 16 bytes per thread; the caller waits (cp.async.wait_all + a consumer
+// barrier) before reading them. Requires p.q_async (16-byte aligned rows).
+__device__ __forceinline__ void q_prefetch(const DecodeParams& p, int u, uint8_t* qbuf) {
+  const int b = u / p.Hkv, hk = u - b * p.Hkv;
+  const int es = q_elem_bytes(p.q_dtype);
+  const int chunks = (HKV_D * es) / 16;  // per row
+  const int t = threadIdx.x;
+  if (t < p.G * chunks) {
+    const int row = t / chunks, ch = t - row * chunks;
+    const uint8_t* src = static_cast<const uint8_t*>(p.q) +
+                         ((int64_t)b * p.q_sb + (int64_t)(hk * p.G + row) * p.q_sh) * es + ch * 16;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(qbuf + row * HKV_D * es + ch * 16)),
+                 "l"(src)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
   int old;
@@ -889,14 +922,24 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   const int vc_off = HKV_V_CODES_OFF + v_chunk_off(t0 / 2 + j, r);
   const int ks_off = (t0 + r) * NG;  // floats
   const int vs_off = (t0 / 2) * NG;  // f16x2 words
+  // the query rows of the current piece's unit, prefetched during the previous piece
+  uint8_t* qbuf = reinterpret_cast<uint8_t*>(comb + kConsumerWarps * p.G * HKV_D + kConsumerWarps * 16);
 
-  for (Piece pc = first_piece(p, c, end); pc.valid; next_piece(p, end, pc)) {
+  Piece pc = first_piece(p, c, end);
+  if (p.q_async && pc.valid) q_prefetch(p, pc.u, qbuf);
+  while (pc.valid) {
     const int u = pc.u, b = u / p.Hkv, hk = u - b * p.Hkv;
     // ---- begin piece: query fragments for this unit
+    const void* qsrc = nullptr;
+    if (p.q_async) {
+      cp_async_wait_all();
+      consumer_sync();
+      qsrc = qbuf;
+    }
     {
       float qa[8][2], qb[8][2];
       if (pc.seg == 0) {
-        load_q_frags<__half>(p, b, hk, true, qf, qa, qb);
+        load_q_frags<__half>(p, b, hk, true, qsrc, qf, qa, qb);
         float ps[NG], pbias[NG];
 #pragma unroll
         for (int g = 0; g < NG; ++g) ps[g] = pbias[g] = 0.f;
@@ -939,8 +982,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
           }
         }
       } else {
-        load_q_frags<DTy>(p, b, hk, false, qf, qa, qb);
+        load_q_frags<DTy>(p, b, hk, false, qsrc, qf, qa, qb);
       }
+    }
+    // the next piece: its length and its query rows load while this piece runs
+    Piece nx = pc;
+    next_piece_head(p, end, nx);
+    const int nlen = nx.valid ? seg_len(p, nx.u, nx.seg) : 0;
+    if (p.q_async && nx.valid) {
+      consumer_sync();  // every consumer has read qbuf
+      q_prefetch(p, nx.u, qbuf);
     }
     ws_reset<NG>(ws);
 
@@ -1088,34 +1139,47 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
         const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
         for (int h = warp; h < p.G; h += kConsumerWarps) {
-          float M = kNoMax;
-          for (int k = lane; k < n; k += 32) M = fmaxf(M, __ldcg(ml_u + (k * p.G + h) * 2));
+          // partial k's (m, l) in lane k; the first 8 partials' o rows load in
+          // the same round trip (the usual unit has at most 8 partials)
+          const float2* mlp = reinterpret_cast<const float2*>(ml_u) + h;
+          const float4* op = reinterpret_cast<const float4*>(o_u + h * HKV_D) + lane;
+          const int ostep = p.G * HKV_D / 4;  // float4s per partial
+          const float2 ml0 = lane < n ? __ldcg(mlp + lane * p.G) : make_float2(kNoMax, 0.f);
+          float4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = i < n ? __ldcg(op + i * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
+          float M = ml0.x;
+          for (int k = lane + 32; k < n; k += 32) M = fmaxf(M, __ldcg(mlp + k * p.G).x);
 #pragma unroll
           for (int sft = 16; sft > 0; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
-          float L = 0.f;
+          float wk = lane < n ? fast_exp2(ml0.x - M) : 0.f;
+          float L = wk * ml0.y;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int k0 = 0; k0 < n; k0 += 32) {
-            float wk = 0.f;
-            if (k0 + lane < n) {
-              wk = fast_exp2(__ldcg(ml_u + ((k0 + lane) * p.G + h) * 2) - M);
-              L = fmaf(wk, __ldcg(ml_u + ((k0 + lane) * p.G + h) * 2 + 1), L);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float w = __shfl_sync(0xffffffffu, wk, i);
+            acc.x = fmaf(w, v[i].x, acc.x);
+            acc.y = fmaf(w, v[i].y, acc.y);
+            acc.z = fmaf(w, v[i].z, acc.z);
+            acc.w = fmaf(w, v[i].w, acc.w);
+          }
+          // partials 8.. (8 per batch, all loads in flight before the first use)
+          for (int k0 = 8; k0 < n; k0 += 8) {
+            if (k0 % 32 == 0) {
+              const float2 mlk = k0 + lane < n ? __ldcg(mlp + (k0 + lane) * p.G) : make_float2(kNoMax, 0.f);
+              wk = k0 + lane < n ? fast_exp2(mlk.x - M) : 0.f;
+              L = fmaf(wk, mlk.y, L);
             }
-            const int kn = min(32, n - k0);
-            // 8 partials per batch: all loads in flight before the first use
-            for (int kb = 0; kb < kn; kb += 8) {
-              float4 v[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                v[i] = kb + i < kn ? __ldcg(reinterpret_cast<const float4*>(o_u + ((k0 + kb + i) * p.G + h) * HKV_D) + lane)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < 8; ++i)
+              v[i] = k0 + i < n ? __ldcg(op + (k0 + i) * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float w = __shfl_sync(0xffffffffu, wk, (kb + i) & 31);
-                acc.x = fmaf(w, v[i].x, acc.x);
-                acc.y = fmaf(w, v[i].y, acc.y);
-                acc.z = fmaf(w, v[i].z, acc.z);
-                acc.w = fmaf(w, v[i].w, acc.w);
-              }
+            for (int i = 0; i < 8; ++i) {
+              const float w = __shfl_sync(0xffffffffu, wk, (k0 + i) & 31);
+              acc.x = fmaf(w, v[i].x, acc.x);
+              acc.y = fmaf(w, v[i].y, acc.y);
+              acc.z = fmaf(w, v[i].z, acc.z);
+              acc.w = fmaf(w, v[i].w, acc.w);
             }
           }
 #pragma unroll
@@ -1143,7 +1207,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
       consumer_sync();  // the combine area is free again
     }
     if (!alive) break;
+    pc = nx;
+    if (pc.valid) piece_fill_len(p, end, pc, nlen);
   }
+  cp_async_wait_all();
 }
 
 // ---------------------------------------------------------------- log-sum-exp merge (cross-GPU partials)
