@@ -150,7 +150,7 @@ hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemBudget);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
-  hkv::decode_kernel<FMT, GROUP, DTy><<<p.sc.C, hkv::kDecodeThreads, smem, st>>>(p);
+  hkv::decode_kernel<FMT, GROUP, DTy><<<p.sc.C, hkv::decode_threads(FMT), smem, st>>>(p);
   return launch_status();
 }
 
@@ -216,10 +216,11 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   // the piece-end combine area, then the prefetched query rows of the next piece (f16/bf16)
   pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4 + G * HKV_D * 2;
   const int avail = kDynSmemBudget - 1024 - pl.comb_bytes;
-  pl.nslots = std::min(hkv::kMaxSlots, avail / hkv::kSlotBytes);
+  const int slot = hkv::slot_bytes(fmt, group);
+  pl.nslots = std::min(hkv::kMaxSlots, avail / slot);
   if (pl.nslots < 2) return HKV_ERR_UNSUPPORTED;
   // + 1 KiB so the kernel can align the ring to 1024 bytes
-  pl.smem = 1024 + pl.nslots * hkv::kSlotBytes + pl.comb_bytes;
+  pl.smem = 1024 + pl.nslots * slot + pl.comb_bytes;
   pl.ws_bytes = kCounterBytes + (size_t)sc.U * sc.S * G * (HKV_D + 2) * sizeof(float);
   *out = pl;
   return HKV_OK;

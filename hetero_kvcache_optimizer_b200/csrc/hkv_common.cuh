@@ -206,8 +206,11 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // ------------------------------------------------------------------ store addressing
 // A page is page_tokens/128 blocks of 128 tokens; a block holds, at these byte
-// offsets: K codes [128][64] | V codes [64 pairs][128] | K meta [128][ng] x 4 B |
-// V meta | K zps [128][ng] u8 | V zps (the zps only for HKV_FMT_REF).
+// offsets: K codes [128][64] | V codes [64 pairs][128] | metadata (ng groups):
+//   HKV_FMT_REF:     K scales f32 [128][ng] | V scales | K zps u8 [128][ng] | V zps
+//   HKV_FMT_FP16MIN: K scales f16 [128][ng] | K mins | V scales f16 [64 pairs][ng][2]
+//                    | V mins  (the V entries of a token pair side by side, the
+//                    layout the decode kernel's fragments read without a rewrite)
 #define HKV_BLOCK_TOKENS 128
 #define HKV_V_CODES_OFF 8192
 #define HKV_META_OFF 16384
@@ -215,9 +218,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __host__ __device__ constexpr int block_bytes(int fmt, int group) {
   return HKV_BLOCK_TOKENS * (2 * HKV_CODE_BYTES + 8 * (HKV_D / group) + (fmt == HKV_FMT_REF ? 2 * (HKV_D / group) : 0));
 }
-// Byte offset of K (role 0) or V (role 1) meta / zps inside a block.
+// HKV_FMT_REF: byte offset of the K (role 0) or V (role 1) scales / zps inside a block.
 __host__ __device__ constexpr int meta_off(int role, int ng) { return HKV_META_OFF + role * 512 * ng; }
 __host__ __device__ constexpr int zps_off(int role, int ng) { return HKV_META_OFF + 1024 * ng + role * 128 * ng; }
+// HKV_FMT_FP16MIN: byte offsets of the f16 scale and min of token w (0..127),
+// group g of role K (0) or V (1) inside a block.
+__host__ __device__ constexpr int mn_index(int role, int w, int ng, int g) {
+  return role == 0 ? w * ng + g : ((w >> 1) * ng + g) * 2 + (w & 1);
+}
+__host__ __device__ constexpr int mn_scale_off(int role, int w, int ng, int g) {
+  return HKV_META_OFF + role * 512 * ng + 2 * mn_index(role, w, ng, g);
+}
+__host__ __device__ constexpr int mn_min_off(int role, int w, int ng, int g) {
+  return mn_scale_off(role, w, ng, g) + 256 * ng;
+}
 // Byte offset, inside the V code area of a block, of the 16-byte chunk c of
 // token pair q. Rotating the chunks by 2q makes the decode kernel's fragment
 // loads (chunk r of pairs j = 0..3 in one quarter-warp) hit 8 distinct bank groups.

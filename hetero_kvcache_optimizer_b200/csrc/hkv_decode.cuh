@@ -41,13 +41,15 @@ constexpr int kGroupWarps = 4;                      // warps per consumer group
 constexpr int kConsumerWarps = 2 * kGroupWarps;     // two groups take alternate tiles
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kIssueWarp = kConsumerWarps;          // TMA issue
-constexpr int kExpandWarp = kConsumerWarps + 1;     // metadata expansion, first of kExpandWarps
-constexpr int kExpandWarps = 2;                     // take alternate tiles
-constexpr int kDecodeThreads = (kConsumerWarps + 1 + kExpandWarps) * 32;
+constexpr int kExpandWarp = kConsumerWarps + 1;     // HKV_FMT_REF metadata expansion, first of 2
+// HKV_FMT_REF tiles get their metadata rewritten by two expansion warps (alternate
+// tiles); HKV_FMT_FP16MIN blocks are stored in the layout the consumers read.
+__host__ __device__ constexpr int expand_warps(int fmt) { return fmt == HKV_FMT_REF ? 2 : 0; }
+__host__ __device__ constexpr int decode_threads(int fmt) { return (kConsumerWarps + 1 + expand_warps(fmt)) * 32; }
 constexpr int kTileI4 = 128;  // tokens per INT4 tile (32 per consumer warp)
 constexpr int kTileD = 32;    // tokens per dense tile (8 per consumer warp)
-constexpr int kMaxSlots = 8;
-constexpr int kSlotBytes = 24 * 1024;   // INT4: one page block (K codes | V codes | metadata) + expansion room
+constexpr int kMaxSlots = 12;
+constexpr int kSlotBytes = 24 * 1024;   // HKV_FMT_REF: one page block + expansion room
 constexpr int kMetaOff = HKV_META_OFF;
 constexpr float kLazyRescale = 8.0f;
 constexpr int kDenseHalf = kTileD * 128;  // bytes of one 64-dim half of 32 dense rows (swizzled)
@@ -92,19 +94,25 @@ struct DecodeParams {
 };
 
 // An INT4 tile is one 128-token page block, copied as is: K codes | V codes |
-// metadata (fp16min: K (s,min) f16x2 [128][NG] | V; ref: K scales f32 [128][NG] |
-// V scales | K zps u8 [128][NG] | V zps). With N = 128 NG entries, the metadata
-// is expanded in place into these byte ranges of the metadata area:
-//   both:    [0, 4N) K scale * qs, f32 [128][NG]
-//   ref:     [4N, 8N) K bias -z*s f32 [128][NG] | [10N, 14N) V zero-point
-//            constants [64 pairs][NG][2] f16x2 | [14N, 16N) V scale pairs
-//   fp16min: [8N, 10N) V scale pairs f16x2 [64][NG] (tokens 2p, 2p+1) |
-//            [10N, 12N) V min pairs f16x2 [64][NG] | [12N, 12N + 1 KB) K mins as
-//            the bias MMA's A columns, f16x2 [128][2]
+// metadata. The consumers read fp16min metadata as stored (f16: K scales
+// [128][NG] | K mins | V scales [64 pairs][NG][2] | V mins). Ref metadata (K
+// scales f32 [128][NG] | V scales | K zps u8 [128][NG] | V zps) is first expanded
+// in place, with N = 128 NG entries, into these byte ranges:
+//   [0, 4N) K scale * qs, f32 [128][NG] | [4N, 8N) K bias -z*s f32 [128][NG] |
+//   [10N, 14N) V zero-point constants [64 pairs][NG][2] f16x2 |
+//   [14N, 16N) V scale pairs f16x2 [64][NG] (tokens 2p, 2p+1)
 // Every expanded entry lands either on the raw entry of the same index (read
 // by the same lane just before) or past all raw data: a lane never overwrites
 // raw bytes another lane has yet to read.
 __host__ __device__ constexpr int dense_slot_bytes() { return 4 * kDenseHalf; }
+// Ring slot size: a page block (HKV_FMT_FP16MIN: as stored; HKV_FMT_REF: with room
+// for the expanded metadata) or a dense tile, in whole KiB (the dense tiles'
+// 128-byte swizzle repeats every 1024 bytes).
+__host__ __device__ constexpr int slot_bytes(int fmt, int group) {
+  return fmt == HKV_FMT_REF ? kSlotBytes
+                            : ((block_bytes(fmt, group) > dense_slot_bytes() ? block_bytes(fmt, group)
+                                                                              : dense_slot_bytes()) + 1023) / 1024 * 1024;
+}
 static_assert(kMetaOff + 16 * kTileI4 * 4 <= kSlotBytes && 12 * kTileI4 * 4 + 1024 <= 16 * kTileI4 * 4,
               "expanded metadata (g32) must fit its slot");
 static_assert(2 * kTileI4 * HKV_CODE_BYTES == kMetaOff && dense_slot_bytes() <= kSlotBytes, "slot layout");
@@ -341,19 +349,39 @@ __device__ __forceinline__ void ld_row_u(const uint32_t* base, int row, uint32_t
   }
 }
 
-// Scores of 16 tokens x 8 heads: x = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)},
-// already in base-2 logits (the expanded K scale and the bias terms carry
-// sm_scale*log2 e). kc / ks point at this thread's row r of the tile's K codes /
-// K scales. The group bias term sum_g b_g * sum(Q_g):
-//   ref:     b = -z*s in fp32 (kb, row r), one FMA per group;
-//   fp16min: b = min (exact f16), one extra MMA of A = mins [token][group, twice]
-//            against B = qs*sum(Q_g) split into f16 hi + lo parts (qbias), so
-//            every product is exact and the sum is fp32.
+template <int NG>
+__device__ __forceinline__ void ld_row_h(const __half* base, int row, float (&v)[NG]) {
+  if constexpr (NG == 4) {
+    const uint2 t = *reinterpret_cast<const uint2*>(base + row * 4);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&t.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&t.y));
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = b.x;
+    v[3] = b.y;
+  } else if constexpr (NG == 2) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(base + row * 2));
+    v[0] = a.x;
+    v[1] = a.y;
+  } else {
+    v[0] = __half2float(base[row]);
+  }
+}
+
+// Scores of 16 tokens x 8 heads: x = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)}
+// in base-2 logits. kc points at this thread's row r of the tile's K codes, mb at
+// the tile's metadata, t at the subtile's first token in the tile. The group
+// bias term sum_g b_g * sum(Q_g):
+//   ref:     expanded metadata, K scale * qs and b = -z*s in fp32, one FMA per
+//            group (qsum carries qs);
+//   fp16min: the block's own f16 metadata; b = min, one extra MMA of A = mins
+//            [token][group, twice] against B = sum(Q_g) split into f16 hi + lo
+//            parts (qbias), so every product is exact and the sum is fp32;
+//            qs is applied once at the end.
 template <int FMT, int NG>
-__device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, const float* kb,
-                                         const uint32_t* kmin, const uint32_t (&qf)[8][2],
+__device__ __forceinline__ void k_scores(const uint8_t* kc, const uint8_t* mb, int t, const uint32_t (&qf)[8][2],
                                          const float (&nbias)[NG][2], const float (&qsum)[NG][2],
-                                         uint32_t qbias, float (&x)[4]) {
+                                         uint32_t qbias, float qs, float (&x)[4]) {
   constexpr int WPG = 4 / NG;  // packed words per group
   const int lane = threadIdx.x & 31, r = lane >> 2, j = lane & 3;
   const uint4 kA = *reinterpret_cast<const uint4*>(kc);
@@ -361,16 +389,39 @@ __device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, con
   const uint32_t kwa[4] = {kA.x, kA.y, kA.z, kA.w};
   const uint32_t kwb[4] = {kB.x, kB.y, kB.z, kB.w};
   float sA[NG], sB[NG], bA[NG], bB[NG];
-  ld_row<NG>(ks, 0, sA);
-  ld_row<NG>(ks, 8, sB);
   x[0] = x[1] = x[2] = x[3] = 0.f;
   if constexpr (FMT == HKV_FMT_REF) {
+    const float* ks = reinterpret_cast<const float*>(mb) + (t + r) * NG;
+    const float* kb = reinterpret_cast<const float*>(mb + 4 * kTileI4 * NG) + (t + r) * NG;
+    ld_row<NG>(ks, 0, sA);
+    ld_row<NG>(ks, 8, sB);
     ld_row<NG>(kb, 0, bA);
     ld_row<NG>(kb, 8, bB);
   } else {
-    constexpr int JB = NG == 4 ? 4 : (NG == 2 ? 2 : 1);  // lanes j < JB carry the A columns
-    const uint32_t ab[4] = {j < JB ? kmin[2 * r + (j & 1)] : 0u, j < JB ? kmin[2 * (r + 8) + (j & 1)] : 0u, 0u,
-                            0u};
+    const __half* ks = reinterpret_cast<const __half*>(mb) + (t + r) * NG;
+    ld_row_h<NG>(ks, 0, sA);
+    ld_row_h<NG>(ks, 8, sB);
+    // A columns 2j, 2j+1 of the bias MMA (rows r and r + 8) meet qbias rows 2j,
+    // 2j+1 (f16 hi parts of sum(Q_g) in rows 0..NG-1, lo parts in NG..2NG-1):
+    // NG 4: (min_g0, min_g1), (min_g2, min_g3), twice; NG 2: (min_g0, min_g1)
+    // twice; NG 1: (min, min)
+    const uint8_t* kmin = mb + 256 * NG + t * NG * 2;
+    uint32_t m0 = 0u, m1 = 0u;
+    if constexpr (NG == 4) {
+      m0 = reinterpret_cast<const uint32_t*>(kmin)[2 * r + (j & 1)];
+      m1 = reinterpret_cast<const uint32_t*>(kmin)[2 * (r + 8) + (j & 1)];
+    } else if constexpr (NG == 2) {
+      if (j < 2) {
+        m0 = reinterpret_cast<const uint32_t*>(kmin)[r];
+        m1 = reinterpret_cast<const uint32_t*>(kmin)[r + 8];
+      }
+    } else {
+      if (j == 0) {
+        m0 = reinterpret_cast<const uint16_t*>(kmin)[r] * 0x10001u;
+        m1 = reinterpret_cast<const uint16_t*>(kmin)[r + 8] * 0x10001u;
+      }
+    }
+    const uint32_t ab[4] = {m0, m1, 0u, 0u};
     mma16816<__half>(x, ab, qbias, 0u);
   }
   float c[4];
@@ -401,6 +452,12 @@ __device__ __forceinline__ void k_scores(const uint8_t* kc, const float* ks, con
       }
     }
   }
+  if constexpr (FMT == HKV_FMT_FP16MIN) {
+    x[0] *= qs;
+    x[1] *= qs;
+    x[2] *= qs;
+    x[3] *= qs;
+  }
 }
 
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
@@ -428,15 +485,17 @@ __device__ __forceinline__ void nib8_to_h2_z(uint32_t x, uint32_t zlo, uint32_t 
 
 // O^T += V^T . (s P/16)^T for 16 tokens; P = {(r,2j), (r,2j+1), (r+8,2j), (r+8,2j+1)}
 // pre-scaled by 1/16. vc points at this thread's V chunk (pair j, chunk r), vsp
-// at the subtile's V scale pairs (pair 0 = its tokens 0, 1). P is transposed
-// once into the B layout (token pair 2j, 2j+1 of head r) and multiplied by the
-// pair's per-group scales there. The group bias:
+// at the subtile's V scale pairs (pair 0 = its tokens 0, 1), [pair][NG] f16x2.
+// P is transposed once into the B layout (token pair 2j, 2j+1 of head r) and
+// multiplied by the pair's per-group scales there. The group bias:
 //   ref:     codes enter as exact n - z (vz: per pair and group the two
 //            zero-point constants of nib8_to_h2_z), so no bias term remains;
 //   fp16min: zc += mins [group][token] . P^T, one extra MMA (vz: min pairs).
+// fp16min metadata of tokens at or past nv (< 16: the sequence ends inside the
+// subtile) may hold any bits and is zeroed, so that P = 0 meets 0, never NaN.
 template <int FMT, int NG>
 __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* vc, const uint32_t* vsp,
-                                             const uint32_t* vz, const float (&P)[4]) {
+                                             const uint32_t* vz, const float (&P)[4], int nv) {
   constexpr int WPG = 4 / NG;
   const int lane = threadIdx.x & 31, r = lane >> 2, j = lane & 3;
   uint32_t sA[NG], sB[NG];
@@ -444,15 +503,29 @@ __device__ __forceinline__ void v_accumulate(WarpState<NG>& ws, const uint8_t* v
   ld_row_u<NG>(vsp, 4 + j, sB);
   const uint32_t tA = movmatrix_t(pack2<__half>(P[0], P[1]));
   const uint32_t tB = movmatrix_t(pack2<__half>(P[2], P[3]));
+  if constexpr (FMT == HKV_FMT_FP16MIN) {
+    uint32_t zA = r < NG ? vz[j * NG + r] : 0u, zB = r < NG ? vz[(4 + j) * NG + r] : 0u;
+    if (nv < 16) {
+      // keep the halves of tokens t, t + 1 of a pair that lie before nv
+      auto keep = [nv](uint32_t w, int t) {
+        return w & ((t < nv ? 0x0000FFFFu : 0u) | (t + 1 < nv ? 0xFFFF0000u : 0u));
+      };
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        sA[g] = keep(sA[g], 2 * j);
+        sB[g] = keep(sB[g], 8 + 2 * j);
+      }
+      zA = keep(zA, 2 * j);
+      zB = keep(zB, 8 + 2 * j);
+    }
+    const uint32_t ab[4] = {zA, 0u, zB, 0u};
+    mma16816<__half>(ws.zc, ab, tA, tB);
+  }
   uint32_t pb[NG][2];
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
     pb[g][0] = hmul2(tA, sA[g]);
     pb[g][1] = hmul2(tB, sB[g]);
-  }
-  if constexpr (FMT == HKV_FMT_FP16MIN) {
-    const uint32_t ab[4] = {r < NG ? vz[j * NG + r] : 0u, 0u, r < NG ? vz[(4 + j) * NG + r] : 0u, 0u};
-    mma16816<__half>(ws.zc, ab, tA, tB);
   }
   const uint4 vA = *reinterpret_cast<const uint4*>(vc);
   const uint4 vB = *reinterpret_cast<const uint4*>(vc + 8 * HKV_CODE_BYTES);
@@ -616,69 +689,46 @@ __device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map
 }
 
 // ---------------------------------------------------------------- metadata expansion (warps kExpandWarp..)
-// Expands one INT4 tile's metadata in place (layout above), streaming: lane L
-// handles entries 128 it + 4 L + {0..3} ([token][group] order) one iteration
-// at a time. Tokens at or past `valid` (beyond the sequence length) may hold
-// uninitialised pool bytes: their scale and bias become 0, so a masked token
-// (P = 0) contributes exactly 0 and never NaN. The K scale is multiplied by qs
-// (sm_scale * log2 e) so scores come out as base-2 logits.
-template <int FMT, int NG>
+// Expands one HKV_FMT_REF tile's metadata in place (layout above), streaming:
+// lane L handles entries 128 it + 4 L + {0..3} ([token][group] order) one
+// iteration at a time. Tokens at or past `valid` (beyond the sequence length)
+// may hold uninitialised pool bytes: their scale and bias become 0, so a masked
+// token (P = 0) contributes exactly 0 and never NaN. The K scale is multiplied
+// by qs (sm_scale * log2 e) so scores come out as base-2 logits.
+template <int NG>
 __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, float qs) {
   constexpr int N = kTileI4 * NG;
   constexpr int IT = N / 128;
-  constexpr int VSP = FMT == HKV_FMT_REF ? 14 * N : 8 * N;
-  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + VSP);      // [64 pairs][NG] f16x2 scales
-  uint32_t* vmn = reinterpret_cast<uint32_t*>(meta + 10 * N);   // fp16min: [64][NG] min pairs
-  uint32_t* vzc = reinterpret_cast<uint32_t*>(meta + 10 * N);   // ref: [64][NG][2] zero-point constants
-  uint32_t* kmn = reinterpret_cast<uint32_t*>(meta + 12 * N);   // fp16min: [128][2] K mins, A columns
+  uint32_t* vsp = reinterpret_cast<uint32_t*>(meta + 14 * N);  // [64 pairs][NG] f16x2 scales
+  uint32_t* vzc = reinterpret_cast<uint32_t*>(meta + 10 * N);  // [64][NG][2] zero-point constants
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
     const int e = 128 * it + 4 * lane;
-    float sk[4], bk[4], sv[4], bv[4];
-    uint32_t zv = 0;
-    if (FMT == HKV_FMT_REF) {
+    float sk[4], bk[4], sv[4], zf[4];
+    {
       const float4 a = *reinterpret_cast<const float4*>(meta + 4 * e);
       const float4 c = *reinterpret_cast<const float4*>(meta + 4 * N + 4 * e);
       const uint32_t zk = *reinterpret_cast<const uint32_t*>(meta + 8 * N + e);
-      zv = *reinterpret_cast<const uint32_t*>(meta + 9 * N + e);
+      const uint32_t zv = *reinterpret_cast<const uint32_t*>(meta + 9 * N + e);
       const float av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         sk[i] = av[i];
         sv[i] = cv[i];
         bk[i] = -static_cast<float>((zk >> (8 * i)) & 0xffu) * av[i];
-        bv[i] = 0.f;
+        zf[i] = static_cast<float>((zv >> (8 * i)) & 0xffu);
+        if ((e + i) / NG >= valid) sk[i] = bk[i] = sv[i] = zf[i] = 0.f;
       }
-    } else {
-      const uint4 a = *reinterpret_cast<const uint4*>(meta + 4 * e);
-      const uint4 c = *reinterpret_cast<const uint4*>(meta + 4 * N + 4 * e);
-      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, cv[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 fk = __half22float2(*reinterpret_cast<const __half2*>(&av[i]));
-        const float2 fv = __half22float2(*reinterpret_cast<const __half2*>(&cv[i]));
-        sk[i] = fk.x;
-        bk[i] = fk.y;
-        sv[i] = fv.x;
-        bv[i] = fv.y;
-      }
-    }
-    float zf[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      zf[i] = static_cast<float>((zv >> (8 * i)) & 0xffu);
-      if ((e + i) / NG >= valid) sk[i] = bk[i] = sv[i] = bv[i] = zf[i] = 0.f;
     }
     *reinterpret_cast<float4*>(meta + 4 * e) = make_float4(sk[0] * qs, sk[1] * qs, sk[2] * qs, sk[3] * qs);
-    if (FMT == HKV_FMT_REF) *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[0], bk[1], bk[2], bk[3]);
-    // pairs (tokens 2p, 2p+1): scales and (fp16min) mins or (ref) zero-point constants
+    *reinterpret_cast<float4*>(meta + 4 * N + 4 * e) = make_float4(bk[0], bk[1], bk[2], bk[3]);
+    // pairs (tokens 2p, 2p+1): scales and zero-point constants
     if constexpr (NG == 4) {
       // lane holds token t = 32 it + lane, groups 0..3; its pair partner is lane ^ 1
-      float os[4], ob[4], oz[4];
+      float os[4], oz[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         os[i] = __shfl_xor_sync(0xffffffffu, sv[i], 1);
-        ob[i] = __shfl_xor_sync(0xffffffffu, bv[i], 1);
         oz[i] = __shfl_xor_sync(0xffffffffu, zf[i], 1);
       }
       const int t = 32 * it + lane;
@@ -687,68 +737,47 @@ __device__ __forceinline__ void expand_meta(uint8_t* meta, int lane, int valid, 
         *reinterpret_cast<uint4*>(vsp + pair * 4) =
             make_uint4(pack2<__half>(sv[0], os[0]), pack2<__half>(sv[1], os[1]), pack2<__half>(sv[2], os[2]),
                        pack2<__half>(sv[3], os[3]));
-        if (FMT == HKV_FMT_REF) {
-          uint32_t w[8];
+        uint32_t w[8];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            w[2 * g] = pack2<__half>(1024.f + zf[g], 1024.f + oz[g]);
-            w[2 * g + 1] = pack2<__half>(-64.f - zf[g], -64.f - oz[g]);
-          }
-          *reinterpret_cast<uint4*>(vzc + pair * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-          *reinterpret_cast<uint4*>(vzc + pair * 8 + 4) = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {
-          *reinterpret_cast<uint4*>(vmn + pair * 4) =
-              make_uint4(pack2<__half>(bv[0], ob[0]), pack2<__half>(bv[1], ob[1]), pack2<__half>(bv[2], ob[2]),
-                         pack2<__half>(bv[3], ob[3]));
+        for (int g = 0; g < 4; ++g) {
+          w[2 * g] = pack2<__half>(1024.f + zf[g], 1024.f + oz[g]);
+          w[2 * g + 1] = pack2<__half>(-64.f - zf[g], -64.f - oz[g]);
         }
+        *reinterpret_cast<uint4*>(vzc + pair * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(vzc + pair * 8 + 4) = make_uint4(w[4], w[5], w[6], w[7]);
       }
-      if (FMT == HKV_FMT_FP16MIN)
-        *reinterpret_cast<uint2*>(kmn + 2 * t) = make_uint2(pack2<__half>(bk[0], bk[1]), pack2<__half>(bk[2], bk[3]));
     } else if constexpr (NG == 2) {
       // entries: (t, g0), (t, g1), (t+1, g0), (t+1, g1) with t = 64 it + 2 lane
-      const int pair = 32 * it + lane, t = 2 * pair;
+      const int pair = 32 * it + lane;
       *reinterpret_cast<uint2*>(vsp + pair * 2) = make_uint2(pack2<__half>(sv[0], sv[2]), pack2<__half>(sv[1], sv[3]));
-      if (FMT == HKV_FMT_REF) {
-        *reinterpret_cast<uint4*>(vzc + pair * 4) =
-            make_uint4(pack2<__half>(1024.f + zf[0], 1024.f + zf[2]), pack2<__half>(-64.f - zf[0], -64.f - zf[2]),
-                       pack2<__half>(1024.f + zf[1], 1024.f + zf[3]), pack2<__half>(-64.f - zf[1], -64.f - zf[3]));
-      } else {
-        *reinterpret_cast<uint2*>(vmn + pair * 2) = make_uint2(pack2<__half>(bv[0], bv[2]), pack2<__half>(bv[1], bv[3]));
-        const uint32_t m0 = pack2<__half>(bk[0], bk[1]), m1 = pack2<__half>(bk[2], bk[3]);
-        *reinterpret_cast<uint4*>(kmn + 2 * t) = make_uint4(m0, m0, m1, m1);
-      }
+      *reinterpret_cast<uint4*>(vzc + pair * 4) =
+          make_uint4(pack2<__half>(1024.f + zf[0], 1024.f + zf[2]), pack2<__half>(-64.f - zf[0], -64.f - zf[2]),
+                     pack2<__half>(1024.f + zf[1], 1024.f + zf[3]), pack2<__half>(-64.f - zf[1], -64.f - zf[3]));
     } else {
-      // tokens 4 lane .. 4 lane + 3 (t = 4 lane): pairs 2 lane, 2 lane + 1
-      const int t = 4 * lane;
+      // tokens 4 lane .. 4 lane + 3: pairs 2 lane, 2 lane + 1
       *reinterpret_cast<uint2*>(vsp + 2 * lane) = make_uint2(pack2<__half>(sv[0], sv[1]), pack2<__half>(sv[2], sv[3]));
-      if (FMT == HKV_FMT_REF) {
-        *reinterpret_cast<uint4*>(vzc + 4 * lane) =
-            make_uint4(pack2<__half>(1024.f + zf[0], 1024.f + zf[1]), pack2<__half>(-64.f - zf[0], -64.f - zf[1]),
-                       pack2<__half>(1024.f + zf[2], 1024.f + zf[3]), pack2<__half>(-64.f - zf[2], -64.f - zf[3]));
-      } else {
-        *reinterpret_cast<uint2*>(vmn + 2 * lane) = make_uint2(pack2<__half>(bv[0], bv[1]), pack2<__half>(bv[2], bv[3]));
-        *reinterpret_cast<uint4*>(kmn + 2 * t) =
-            make_uint4(pack2<__half>(bk[0], bk[0]), 0u, pack2<__half>(bk[1], bk[1]), 0u);
-        *reinterpret_cast<uint4*>(kmn + 2 * t + 4) =
-            make_uint4(pack2<__half>(bk[2], bk[2]), 0u, pack2<__half>(bk[3], bk[3]), 0u);
-      }
+      *reinterpret_cast<uint4*>(vzc + 4 * lane) =
+          make_uint4(pack2<__half>(1024.f + zf[0], 1024.f + zf[1]), pack2<__half>(-64.f - zf[0], -64.f - zf[1]),
+                     pack2<__half>(1024.f + zf[2], 1024.f + zf[3]), pack2<__half>(-64.f - zf[2], -64.f - zf[3]));
     }
   }
   // order these generic-proxy writes before later TMA (async-proxy) writes to the slot
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Zero dense V rows [valid, 32) of a swizzled slot (whole 128-byte rows, so the
+// Zero dense V rows [r0, r1) of a swizzled slot (whole 128-byte rows, so the
 // swizzle does not matter); rows past the sequence length may hold any bits.
-__device__ __forceinline__ void zero_dense_v_tail(uint8_t* slot, int valid, int lane) {
-  if (valid >= kTileD) return;
+// The fence orders these generic-proxy writes before later TMA writes to the slot.
+__device__ __forceinline__ void zero_dense_v_rows(uint8_t* slot, int r0, int r1, int lane) {
   uint8_t* v = slot + 2 * kDenseHalf;
-  const int rows = kTileD - valid;
-  for (int i = lane; i < rows * 16; i += 32) {  // 2 halves x 8 chunks of 16 B per row
-    const int rr = valid + i / 16, h = (i >> 3) & 1, ch = i & 7;
+  for (int i = lane; i < (r1 - r0) * 16; i += 32) {  // 2 halves x 8 chunks of 16 B per row
+    const int rr = r0 + i / 16, h = (i >> 3) & 1, ch = i & 7;
     *reinterpret_cast<uint4*>(v + h * kDenseHalf + rr * 128 + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void zero_dense_v_tail(uint8_t* slot, int valid, int lane) {
+  if (valid < kTileD) zero_dense_v_rows(slot, valid, kTileD, lane);
 }
 
 // Cursor over the CTA's tiles that hold tokens (the loads, in ring order).
@@ -776,9 +805,11 @@ __device__ __forceinline__ void cursor_next(const DecodeParams& p, uint32_t end,
 
 // ---------------------------------------------------------------- the persistent kernel
 template <int FMT, int GROUP, typename DTy>
-__global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __grid_constant__ DecodeParams p) {
   constexpr int NG = HKV_D / GROUP;
   constexpr int NM = kTileI4 * NG;  // metadata entries per array of a tile
+  constexpr int kSlot = slot_bytes(FMT, GROUP);
+  constexpr int kExp = expand_warps(FMT);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t ready_bar[kMaxSlots];
@@ -793,7 +824,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   const uint32_t end = cta_begin(sc, c + 1);
   const int nsl = p.nslots;
   uint8_t* ring = smem;
-  float* comb = reinterpret_cast<float*>(ring + nsl * kSlotBytes);  // [8][G][128] + [8][8][2]
+  float* comb = reinterpret_cast<float*>(ring + nsl * kSlot);  // [8][G][128] + [8][8][2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -818,7 +849,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
       constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
       while (cu.valid) {
         if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
-        uint8_t* sb = ring + ri.slot * kSlotBytes;
+        uint8_t* sb = ring + ri.slot * kSlot;
         uint64_t* fb = &full_bar[ri.slot];
         const int u = cu.pc.u;
         // what the expansion warp needs to know about this load (published by the arrive below)
@@ -863,7 +894,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         cursor_next(p, end, cu);
       }
       // one end-of-work load per expansion warp (a plain arrive, no copy)
-      for (int x = 0; x < kExpandWarps; ++x) {
+      for (int x = 0; x < kExp; ++x) {
         if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
         if (lane == 0) {
           s_info[ri.slot] = make_int2(-1, 0);
@@ -876,10 +907,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
       if (lane == 0) {
         for (int i = max(0, n - nsl); i < n; ++i) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
       }
-    } else {
-      // ================================================================ metadata expansion warps
-      // expansion warp x takes the loads n with n % kExpandWarps == x, until the
-      // issue warp's end-of-work load
+    } else if constexpr (kExp > 0) {
+      // ================================================================ metadata expansion warps (ref)
+      // expansion warp x takes the loads n with n % kExp == x, until the issue
+      // warp's end-of-work load
       const int x = warp - kExpandWarp;
       Ring re{0, 0u};
       for (int i = 0; i < x; ++i) re.advance(nsl);
@@ -887,15 +918,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         if (!warp_wait(&full_bar[re.slot], re.phase)) break;
         const int2 info = s_info[re.slot];
         if (info.x < 0) break;
-        uint8_t* sb = ring + re.slot * kSlotBytes;
+        uint8_t* sb = ring + re.slot * kSlot;
         if (info.x == 0) {
-          expand_meta<FMT, NG>(sb + kMetaOff, lane, info.y, p.qscale);
+          expand_meta<NG>(sb + kMetaOff, lane, info.y, p.qscale);
         } else {
           zero_dense_v_tail(sb, info.y, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready_bar[re.slot]);
-        for (int i = 0; i < kExpandWarps; ++i) re.advance(nsl);
+        for (int i = 0; i < kExp; ++i) re.advance(nsl);
       }
     }
     return;
@@ -905,6 +936,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   // Group grp (warps 4 grp .. 4 grp + 3) takes the loads n with n % 2 == grp;
   // warp wg of the group computes tokens [32 wg, 32 wg + 32) of an INT4 tile and
   // [8 wg, 8 wg + 8) of a dense tile.
+  // a tile is ready for the consumers once expanded (ref) or once landed (fp16min)
+  uint64_t* cons_bar = kExp > 0 ? ready_bar : full_bar;
   WarpState<NG> ws;
   uint32_t qf[8][2];
   float qsum[NG][2], nbias[NG][2];  // qsum: ref only
@@ -920,7 +953,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
   const int kc_off = (t0 + r) * HKV_CODE_BYTES + 16 * j;
   // chunk r of pair t0/2 + j (and of pair t0/2 + 8 + j): the block rotates pair q's chunks by 2q
   const int vc_off = HKV_V_CODES_OFF + v_chunk_off(t0 / 2 + j, r);
-  const int ks_off = (t0 + r) * NG;  // floats
   const int vs_off = (t0 / 2) * NG;  // f16x2 words
   // the query rows of the current piece's unit, prefetched during the previous piece
   uint8_t* qbuf = reinterpret_cast<uint8_t*>(comb + kConsumerWarps * p.G * HKV_D + kConsumerWarps * 16);
@@ -961,12 +993,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
           nbias[g][1] = -1024.f * __shfl_sync(0xffffffffu, pbias[g], (2 * j + 1) * 4);
         }
         if constexpr (FMT == HKV_FMT_FP16MIN) {
-          // B of the K bias MMA, head r: rows 0..NG-1 = f16 hi parts of qs*sum(Q_g),
+          // B of the K bias MMA, head r: rows 0..NG-1 = f16 hi parts of sum(Q_g),
           // rows NG..2NG-1 = the lo parts (this lane holds rows 2j, 2j+1)
           __half hi[NG], lo[NG];
 #pragma unroll
           for (int g = 0; g < NG; ++g) {
-            const float v = qs * ps[g];
+            const float v = ps[g];
             hi[g] = __float2half_rn(v);
             lo[g] = __float2half_rn(v - __half2float(hi[g]));
           }
@@ -1001,22 +1033,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
     if (pc.seg == 0) {
       for (; n_next < n_end; n_next += 2) {
         const int k = pc.k0 + (n_next - n_base);
-        if (!warp_wait(&ready_bar[rc.slot], rc.phase)) {
+        if (!warp_wait(&cons_bar[rc.slot], rc.phase)) {
           alive = false;
           break;
         }
-        const uint8_t* stg = ring + rc.slot * kSlotBytes;
-        const uint8_t* mb = stg + kMetaOff;  // expanded metadata (layout above)
-        const float* ks = reinterpret_cast<const float*>(mb) + ks_off;
-        const float* kb = reinterpret_cast<const float*>(mb + 4 * NM) + ks_off;
-        const uint32_t* kmn = reinterpret_cast<const uint32_t*>(mb + 12 * NM) + 2 * t0;
+        const uint8_t* stg = ring + rc.slot * kSlot;
+        // metadata: ref expanded in place (layout above); fp16min as stored
+        const uint8_t* mb = stg + kMetaOff;
         const uint32_t* vsp =
-            reinterpret_cast<const uint32_t*>(mb + (FMT == HKV_FMT_REF ? 14 : 8) * NM) + vs_off;
-        const uint32_t* vz = reinterpret_cast<const uint32_t*>(mb + 10 * NM) + (FMT == HKV_FMT_REF ? 2 : 1) * vs_off;
+            reinterpret_cast<const uint32_t*>(mb + (FMT == HKV_FMT_REF ? 14 * NM : 512 * NG)) + vs_off;
+        const uint32_t* vz =
+            reinterpret_cast<const uint32_t*>(mb + (FMT == HKV_FMT_REF ? 10 * NM : 768 * NG)) +
+            (FMT == HKV_FMT_REF ? 2 : 1) * vs_off;
         float xa[4], xb[4], x[8], P[8];
-        k_scores<FMT, NG>(stg + kc_off, ks, kb, kmn, qf, nbias, qsum, qbias, xa);
-        k_scores<FMT, NG>(stg + kc_off + 16 * HKV_CODE_BYTES, ks + 16 * NG, kb + 16 * NG, kmn + 32, qf, nbias, qsum,
-                          qbias, xb);
+        k_scores<FMT, NG>(stg + kc_off, mb, t0, qf, nbias, qsum, qbias, qs, xa);
+        k_scores<FMT, NG>(stg + kc_off + 16 * HKV_CODE_BYTES, mb, t0 + 16, qf, nbias, qsum, qbias, qs, xb);
         const int tok = k * kTileI4 + t0;
         x[0] = xa[0];
         x[1] = xa[1];
@@ -1035,9 +1066,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
         softmax_step<NG, 8>(ws, x, P, 4.f);
         const float pa[4] = {P[0], P[1], P[2], P[3]};
         const float pc4[4] = {P[4], P[5], P[6], P[7]};
-        v_accumulate<FMT, NG>(ws, stg + vc_off, vsp, vz, pa);
+        const int nv = pc.len - tok;  // tokens of this warp's 32 that lie in the sequence
+        v_accumulate<FMT, NG>(ws, stg + vc_off, vsp, vz, pa, nv);
         v_accumulate<FMT, NG>(ws, stg + vc_off + 16 * HKV_CODE_BYTES, vsp + 8 * NG,
-                              vz + (FMT == HKV_FMT_REF ? 2 : 1) * 8 * NG, pc4);
+                              vz + (FMT == HKV_FMT_REF ? 2 : 1) * 8 * NG, pc4, nv - 16);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);
         rc.advance(nsl);
@@ -1047,11 +1079,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const __grid_
       const int dt0 = wg * 8;
       for (; n_next < n_end; n_next += 2) {
         const int k = pc.k0 + (n_next - n_base);
-        if (!warp_wait(&ready_bar[rc.slot], rc.phase)) {
+        if (!warp_wait(&cons_bar[rc.slot], rc.phase)) {
           alive = false;
           break;
         }
-        const uint32_t slot = smem_u32(ring + rc.slot * kSlotBytes);
+        uint8_t* sl = ring + rc.slot * kSlot;
+        if constexpr (kExp == 0) {
+          // no expansion warp zeroes the V rows past the sequence end: this
+          // warp zeroes its own rows [dt0, dt0 + 8) that lie there
+          const int valid = pc.len - k * kTileD;
+          if (dt0 + 8 > valid) {
+            zero_dense_v_rows(sl, max(dt0, valid), dt0 + 8, lane);
+            __syncwarp();
+          }
+        }
+        const uint32_t slot = smem_u32(sl);
         dense_subtile<DTy, NG>(ws, slot, dt0, k * kTileD + dt0 + r < pc.len, qf, qs);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);

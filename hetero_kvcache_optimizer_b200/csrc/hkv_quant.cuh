@@ -118,15 +118,12 @@ __device__ __forceinline__ void quantise_token(const float (&v)[8], bool active,
   if ((p % lanes_per_group) == 0) {
     const int ng = HKV_D / group;
     const int gi = p / lanes_per_group;
-    uint8_t* meta = br.base + meta_off(role, ng) + 4 * (br.w * ng + gi);
     if (fmt == HKV_FMT_REF) {
-      *reinterpret_cast<float*>(meta) = rp.scale;
+      *reinterpret_cast<float*>(br.base + meta_off(role, ng) + 4 * (br.w * ng + gi)) = rp.scale;
       br.base[zps_off(role, ng) + br.w * ng + gi] = static_cast<uint8_t>(rp.zpf);
     } else {
-      __half2 sm;
-      sm.x = mp.sh;
-      sm.y = mp.mh;
-      *reinterpret_cast<__half2*>(meta) = sm;
+      *reinterpret_cast<__half*>(br.base + mn_scale_off(role, br.w, ng, gi)) = mp.sh;
+      *reinterpret_cast<__half*>(br.base + mn_min_off(role, br.w, ng, gi)) = mp.mh;
     }
   }
 }
@@ -340,14 +337,14 @@ __global__ void dequantize_pack_kernel(hkv_int4_store st, int role, int H, int t
   const uint32_t c = packed_code(br, role, d);
   const int ng = HKV_D / st.group;
   const int gi = d / st.group;
-  const uint8_t* meta = br.base + meta_off(role, ng) + 4 * (br.w * ng + gi);
   float v;
   if (st.format == HKV_FMT_REF) {
     const float zp = static_cast<float>(br.base[zps_off(role, ng) + br.w * ng + gi]);
-    v = (static_cast<float>(c) - zp) * *reinterpret_cast<const float*>(meta);
+    v = (static_cast<float>(c) - zp) * *reinterpret_cast<const float*>(br.base + meta_off(role, ng) + 4 * (br.w * ng + gi));
   } else {
-    const __half2 sm = *reinterpret_cast<const __half2*>(meta);
-    v = static_cast<float>(c) * __half2float(sm.x) + __half2float(sm.y);
+    const float sc = __half2float(*reinterpret_cast<const __half*>(br.base + mn_scale_off(role, br.w, ng, gi)));
+    const float mn = __half2float(*reinterpret_cast<const __half*>(br.base + mn_min_off(role, br.w, ng, gi)));
+    v = static_cast<float>(c) * sc + mn;
   }
   out[tok * HKV_D + d] = from_f32<OT>(v);
 }

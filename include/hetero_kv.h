@@ -34,11 +34,16 @@
  *     offset 8192     V codes [64][128]     u8, per token pair; the 16-byte chunk
  *                                           c of pair q is stored at chunk position
  *                                           (c + 2q) mod 8 of the pair's 128 bytes
- *     offset 16384    K meta  [128][G]      f32 scale (HKV_FMT_REF) or
- *                                           {f16 scale, f16 min} (HKV_FMT_FP16MIN)
- *     +   512*G       V meta  [128][G]
- *     +  1024*G       K zps   [128][G] u8   (HKV_FMT_REF only)
- *     +  1152*G       V zps   [128][G] u8   (HKV_FMT_REF only)
+ *   HKV_FMT_REF metadata:
+ *     offset 16384    K scales [128][G]     f32
+ *     +   512*G       V scales [128][G]     f32
+ *     +  1024*G       K zps    [128][G]     u8
+ *     +  1152*G       V zps    [128][G]     u8
+ *   HKV_FMT_FP16MIN metadata (f16; V entries of a token pair side by side):
+ *     offset 16384    K scales [128][G]
+ *     +   256*G       K mins   [128][G]
+ *     +   512*G       V scales [64 pairs][G][2]
+ *     +   768*G       V mins   [64 pairs][G][2]
  *   => 168 B per token (ref, group 32) or 160 B per token (fp16min, group 32)
  *      for K and V together; hkv_page_bytes() gives the page size.
  */

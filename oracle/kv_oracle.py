@@ -265,7 +265,8 @@ def split_page(page: np.ndarray, page_tokens: int, fmt: int, group: int, role: i
     """Split one raw page (uint8 bytes) into the K (role 0) or V (role 1) half:
     (codes [P, 64] in the pack_k / pack_v byte order, meta0 [P, ng], meta1 [P, ng]).
     For FMT_REF the meta are (scales fp32, zps u8); for FMT_FP16MIN (scale fp16,
-    min fp16)."""
+    min fp16), stored as four f16 arrays: K scales [128][ng], K mins, V scales
+    [64 token pairs][ng][2], V mins."""
     ng = HEAD_DIM // group
     bb = block_bytes(fmt, group)
     codes, m0, m1 = [], [], []
@@ -283,9 +284,13 @@ def split_page(page: np.ndarray, page_tokens: int, fmt: int, group: int, role: i
             zo = 16384 + 1024 * ng + role * 128 * ng
             m1.append(b[zo: zo + 128 * ng].reshape(BLOCK_TOKENS, ng))
         else:
-            hm = meta.view(np.float16).reshape(BLOCK_TOKENS, ng, 2)
-            m0.append(hm[..., 0])
-            m1.append(hm[..., 1])
+            hm = meta.view(np.float16).reshape(2, BLOCK_TOKENS * ng)   # scales | mins
+            if role == 0:
+                m0.append(hm[0].reshape(BLOCK_TOKENS, ng))
+                m1.append(hm[1].reshape(BLOCK_TOKENS, ng))
+            else:  # [pair][group][token parity] -> [token][group]
+                m0.append(hm[0].reshape(BLOCK_TOKENS // 2, ng, 2).transpose(0, 2, 1).reshape(BLOCK_TOKENS, ng))
+                m1.append(hm[1].reshape(BLOCK_TOKENS // 2, ng, 2).transpose(0, 2, 1).reshape(BLOCK_TOKENS, ng))
     return np.concatenate(codes), np.concatenate(m0), np.concatenate(m1)
 
 
