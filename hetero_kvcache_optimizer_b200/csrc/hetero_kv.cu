@@ -103,7 +103,11 @@ hkv_status static_scratch(void** out) {
 }
 
 // --------------------------------------------------------------------------- decode plan
-constexpr int kDynSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in, static barriers aside)
+constexpr int kDynSmemBudget = 226 * 1024;
+#ifndef HKV_PIECE_STEPS
+#define HKV_PIECE_STEPS 1280
+#endif
+constexpr int64_t kPieceSteps = HKV_PIECE_STEPS;  // 160 KiB, about 8 fp16min g32 tiles (tuned on config 1)  // one CTA per SM (227 KB opt-in, static barriers aside)
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime (no link
 // dependency on libcuda).
@@ -197,7 +201,11 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   // tile weights in 128-byte steps (the kernel's schedule is 32-bit arithmetic)
   const int64_t tb = block_bytes(fmt, group) / hkv::kSchedStep;
   const int64_t td = (int64_t)hkv::kTileD * 2 * HKV_D * 2 / hkv::kSchedStep;
-  const int64_t Ub = sc.Tb * tb + sc.Td * td;
+  // a segment also costs its piece start and end (query rows, partial, merge):
+  // charged as steps before it, so that CTAs whose range holds more segment
+  // starts get fewer tiles
+  const int64_t wb = sc.Tb > 0 ? kPieceSteps : 0, wd = sc.Td > 0 ? kPieceSteps : 0;
+  const int64_t Ub = wb + sc.Tb * tb + wd + sc.Td * td;
   const int64_t Btot = Ub * sc.U;
   if (Btot >= (int64_t(1) << 31)) return HKV_ERR_UNSUPPORTED;  // > 256 GiB in one call
   const int64_t maxtile = std::max<int64_t>(sc.Tb ? tb : 0, sc.Td ? td : 0);
@@ -206,6 +214,8 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   sc.C = C;
   sc.tb = (uint32_t)tb;
   sc.td = (uint32_t)td;
+  sc.wb = (uint32_t)wb;
+  sc.wd = (uint32_t)wd;
   sc.Ub = (uint32_t)Ub;
   sc.Btot = (uint32_t)Btot;
   sc.q = (uint32_t)(Btot / C);

@@ -64,6 +64,7 @@ struct Sched {
   int C;            // CTAs
   int S;            // partial slots per unit in the workspace
   uint32_t tb, td;  // steps per body / dense tile
+  uint32_t wb, wd;  // steps charged before a unit's body / dense segment (piece start and end work)
   uint32_t Ub;      // steps per unit
   uint32_t Btot;    // steps in total (< 2^31)
   uint32_t q, r;    // Btot = q * C + r
@@ -123,8 +124,10 @@ static_assert(kTileI4 == HKV_BLOCK_TOKENS && block_bytes(HKV_FMT_REF, 32) <= kSl
 __device__ __forceinline__ uint32_t cta_begin(const Sched& s, int c) {
   return (uint32_t)c * s.q + ((uint32_t)c * s.r) / (uint32_t)s.C;
 }
+// First step of tile k of segment seg of unit u. A unit is [wb | Tb body tiles | wd | Td dense tiles].
 __device__ __forceinline__ uint32_t tile_byte(const Sched& s, int u, int seg, int k) {
-  return (uint32_t)u * s.Ub + (seg == 0 ? (uint32_t)k * s.tb : (uint32_t)s.Tb * s.tb + (uint32_t)k * s.td);
+  return (uint32_t)u * s.Ub + s.wb +
+         (seg == 0 ? (uint32_t)k * s.tb : (uint32_t)s.Tb * s.tb + s.wd + (uint32_t)k * s.td);
 }
 // The CTA whose range holds step x: a float estimate, then exact corrections.
 __device__ __forceinline__ int owner_of(const Sched& s, uint32_t x) {
@@ -173,13 +176,14 @@ __device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, uint3
   Piece pc;
   pc.u = (int)(x / s.Ub);
   const uint32_t r = x - (uint32_t)pc.u * s.Ub;
-  if (s.Tb > 0 && r <= (uint32_t)(s.Tb - 1) * s.tb) {
+  const uint32_t db = s.wb + (uint32_t)s.Tb * s.tb + s.wd;  // first dense step of the unit
+  if (s.Tb > 0 && r <= s.wb + (uint32_t)(s.Tb - 1) * s.tb) {
     pc.seg = 0;
-    pc.k0 = (int)((r + s.tb - 1) / s.tb);
-  } else if (s.Td > 0 && r <= (uint32_t)s.Tb * s.tb + (uint32_t)(s.Td - 1) * s.td) {
+    // r may lie inside the charge before the body
+    pc.k0 = r > s.wb ? (int)((r - s.wb + s.tb - 1) / s.tb) : 0;
+  } else if (s.Td > 0 && r <= db + (uint32_t)(s.Td - 1) * s.td) {
     pc.seg = 1;
-    // r may lie inside the last body tile (before the dense segment starts)
-    const uint32_t db = (uint32_t)s.Tb * s.tb;
+    // r may lie inside the last body tile or the charge before the dense segment
     pc.k0 = r > db ? (int)((r - db + s.td - 1) / s.td) : 0;
   } else {
     pc.u += 1;

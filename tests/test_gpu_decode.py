@@ -253,3 +253,29 @@ def test_workspace_reuse_across_shapes(hkv):
         for store, q, ref, splits in cases:
             out = hkv.decode(t16(q), store, None, ctas=splits).cpu().numpy()
             assert ko.rel_err(out, ref) < TOL
+
+
+@pytest.mark.parametrize("fmt,group", [("ref", 32), ("fp16min", 32), ("fp16min", 64), ("fp16min", 128)])
+@pytest.mark.parametrize("S", [129, 200, 511])
+def test_poisoned_tails_stay_finite(hkv, fmt, group, S):
+    """Pool bytes past the sequence end and dense rows past the dense length hold
+    NaN bit patterns (0xFF bytes): the masked tokens must contribute exactly 0."""
+    B, Hkv, G, Sd = 2, 2, 4, 45
+    k, v = ko.make_kv(S + group, B, Hkv, S + Sd)
+    store = hkv.Int4KVStore(B, Hkv, S, fmt=fmt, group=group)
+    store.pool.fill_(255)
+    hkv.prefill(store, t16(k[:, :, :S]), t16(v[:, :, :S]))
+    dense = hkv.DenseKV(B, Hkv, 64)
+    dense.k.fill_(float("nan"))
+    dense.v.fill_(float("nan"))
+    dense.k[:, :, :Sd] = t16(k[:, :, S:])
+    dense.v[:, :, :Sd] = t16(v[:, :, S:])
+    dense.set_lengths(Sd)
+    q = ko.make_q(S, B, Hkv * G).astype(np.float16).astype(np.float32)
+    kd = np.concatenate([dequant_side(store, K, S), dense.k[:, :, :Sd].float().cpu().numpy()], axis=2)
+    vd = np.concatenate([dequant_side(store, V, S), dense.v[:, :, :Sd].float().cpu().numpy()], axis=2)
+    ref = ko.decode_attention(q, kd, vd)
+    for ctas in (0, 3):
+        out = hkv.decode(t16(q), store, dense, ctas=ctas).cpu().numpy()
+        assert np.isfinite(out).all(), (fmt, group, S, ctas)
+        assert ko.rel_err(out, ref) < TOL, (fmt, group, S, ctas)
