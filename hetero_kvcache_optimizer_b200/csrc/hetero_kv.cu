@@ -103,11 +103,13 @@ hkv_status static_scratch(void** out) {
 }
 
 // --------------------------------------------------------------------------- decode plan
-constexpr int kDynSmemBudget = 226 * 1024;
+constexpr int kDynSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in, static barriers aside)
+// Schedule charge per segment start, in 128-byte steps: 160 KiB, about 8 fp16min
+// group-32 tiles (tuned on config 1; overridable at build time for sweeps).
 #ifndef HKV_PIECE_STEPS
 #define HKV_PIECE_STEPS 1280
 #endif
-constexpr int64_t kPieceSteps = HKV_PIECE_STEPS;  // 160 KiB, about 8 fp16min g32 tiles (tuned on config 1)  // one CTA per SM (227 KB opt-in, static barriers aside)
+constexpr int64_t kPieceSteps = HKV_PIECE_STEPS;
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime (no link
 // dependency on libcuda).
