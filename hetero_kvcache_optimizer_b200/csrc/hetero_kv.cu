@@ -229,7 +229,10 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   pl.comb_bytes = (hkv::kConsumerWarps * G * HKV_D + hkv::kConsumerWarps * 8 * 2) * 4 + G * HKV_D * 2;
   const int avail = kDynSmemBudget - 1024 - pl.comb_bytes;
   const int slot = hkv::slot_bytes(fmt, group);
-  pl.nslots = std::min(hkv::kMaxSlots, avail / slot);
+  // even, so that every slot always serves the same consumer group (loads n and
+  // n + nslots have the same parity): a group's parity wait on a slot can then
+  // never match a phase that belongs to the other group's load
+  pl.nslots = std::min(hkv::kMaxSlots, avail / slot) & ~1;
   if (pl.nslots < 2) return HKV_ERR_UNSUPPORTED;
   // + 1 KiB so the kernel can align the ring to 1024 bytes
   pl.smem = 1024 + pl.nslots * slot + pl.comb_bytes;

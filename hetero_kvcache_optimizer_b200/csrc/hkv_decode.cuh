@@ -40,12 +40,15 @@ namespace hkv {
 constexpr int kGroupWarps = 4;                      // warps per consumer group
 constexpr int kConsumerWarps = 2 * kGroupWarps;     // two groups take alternate tiles
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kIssueWarp = kConsumerWarps;          // TMA issue
-constexpr int kExpandWarp = kConsumerWarps + 1;     // HKV_FMT_REF metadata expansion, first of 2
+constexpr int kIssueWarp = kConsumerWarps;          // TMA issue, first of kIssueWarps
+constexpr int kIssueWarps = 2;                      // issue warp w feeds the loads n with n % 2 == w
+constexpr int kExpandWarp = kIssueWarp + kIssueWarps;  // HKV_FMT_REF metadata expansion, first of 2
 // HKV_FMT_REF tiles get their metadata rewritten by two expansion warps (alternate
 // tiles); HKV_FMT_FP16MIN blocks are stored in the layout the consumers read.
 __host__ __device__ constexpr int expand_warps(int fmt) { return fmt == HKV_FMT_REF ? 2 : 0; }
-__host__ __device__ constexpr int decode_threads(int fmt) { return (kConsumerWarps + 1 + expand_warps(fmt)) * 32; }
+__host__ __device__ constexpr int decode_threads(int fmt) {
+  return (kConsumerWarps + kIssueWarps + expand_warps(fmt)) * 32;
+}
 constexpr int kTileI4 = 128;  // tokens per INT4 tile (32 per consumer warp)
 constexpr int kTileD = 32;    // tokens per dense tile (8 per consumer warp)
 constexpr int kMaxSlots = 12;
@@ -842,12 +845,18 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   __syncthreads();
 
   if (warp >= kConsumerWarps) {
-    if (warp == kIssueWarp) {
-      // ================================================================ TMA issue warp
+    if (warp < kIssueWarp + kIssueWarps) {
+      // ================================================================ TMA issue warps
+      // Issue warp w takes the loads n with n % 2 == w: one bulk copy in flight per
+      // warp is accepted at a time, so two warps keep more of the ring moving. With
+      // an even slot count a slot always belongs to one issue warp (and one
+      // consumer group), whose waits on it therefore never alias.
+      const int w = warp - kIssueWarp;
       Cursor cu;
       cursor_start(p, c, end, cu);
-      Ring ri{0, 0u};
-      int n = 0;
+      if (w == 1 && cu.valid) cursor_next(p, end, cu);
+      Ring ri{w, 0u};
+      int n = w;
       // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
       int pg_u = -1, pg0 = 0, pg_lane = -1;
       constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
@@ -893,28 +902,30 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
           tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
           tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
         }
-        n++;
+        n += 2;
+        ri.advance(nsl);
         ri.advance(nsl);
         cursor_next(p, end, cu);
+        if (cu.valid) cursor_next(p, end, cu);
       }
-      // one end-of-work load per expansion warp (a plain arrive, no copy)
-      for (int x = 0; x < kExp; ++x) {
-        if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
+      // an end-of-work load (a plain arrive, no copy) for expansion warp w, which
+      // takes the loads of this warp's parity
+      if (kExp > 0 && (n < nsl || warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u))) {
         if (lane == 0) {
           s_info[ri.slot] = make_int2(-1, 0);
           mbar_arrive(&full_bar[ri.slot]);
         }
-        n++;
-        ri.advance(nsl);
+        n += 2;
       }
-      // every issued copy must have landed before the CTA exits
+      // every copy this warp issued must have landed before the CTA exits
       if (lane == 0) {
-        for (int i = max(0, n - nsl); i < n; ++i) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
+        for (int i = max(w, n - nsl); i < n; i += 2) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
       }
     } else if constexpr (kExp > 0) {
       // ================================================================ metadata expansion warps (ref)
-      // expansion warp x takes the loads n with n % kExp == x, until the issue
-      // warp's end-of-work load
+      // expansion warp x takes the loads n with n % 2 == x (those of issue warp x),
+      // until that warp's end-of-work load
+      static_assert(expand_warps(HKV_FMT_REF) == kIssueWarps, "one expansion warp per issue warp");
       const int x = warp - kExpandWarp;
       Ring re{0, 0u};
       for (int i = 0; i < x; ++i) re.advance(nsl);
