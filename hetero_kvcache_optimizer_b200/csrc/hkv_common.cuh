@@ -83,20 +83,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// As mbar_try_wait, but a thread whose phase is not complete may sleep up to
+// `ns` nanoseconds (woken early when the phase completes) instead of returning
+// after the hardware's default limit: fewer spin iterations for long waits.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 // Bounded wait on an mbarrier phase. Returns false (and flags the device error
-// word) if the phase has not completed within HKV_WAIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// word) if the phase has not completed within HKV_WAIT_NS. With sleep_ns > 0 a
+// pending try_wait may sleep that long (woken by the phase completion).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+      if (sleep_ns ? mbar_try_wait_sleep(bar, parity, sleep_ns) : mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > HKV_WAIT_NS) {
       hkv_flag_error(HKV_DEVERR_TIMEOUT);
       return false;

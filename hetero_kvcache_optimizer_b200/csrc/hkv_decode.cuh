@@ -55,6 +55,15 @@ constexpr int kMaxSlots = 12;
 constexpr int kSlotBytes = 24 * 1024;   // HKV_FMT_REF: one page block + expansion room
 constexpr int kMetaOff = HKV_META_OFF;
 constexpr float kLazyRescale = 8.0f;
+// Longest sleep (ns) of one pending mbarrier try_wait: issue warps (waiting for a
+// free slot) and consumer warps (waiting for a tile). A sleeping warp is woken by
+// the phase completion, so the sleep only saves the spin loop's issue slots.
+#ifndef HKV_ISSUE_SLEEP_NS
+#define HKV_ISSUE_SLEEP_NS 2000
+#endif
+#ifndef HKV_CONS_SLEEP_NS
+#define HKV_CONS_SLEEP_NS 0
+#endif
 constexpr int kDenseHalf = kTileD * 128;  // bytes of one 64-dim half of 32 dense rows (swizzled)
 
 // Equal-byte partition of the tile list over the persistent grid.
@@ -682,8 +691,8 @@ __device__ __forceinline__ bool consumer_sync_and(bool v) {
 // Bounded mbarrier wait with a warp-uniform outcome: lanes that reach the
 // timeout at different moments must not split the warp before the next
 // warp-synchronous instruction (mma.sync, shuffles, movmatrix).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns = 0) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, sleep_ns));
 }
 
 __device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
@@ -861,7 +870,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       int pg_u = -1, pg0 = 0, pg_lane = -1;
       constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
       while (cu.valid) {
-        if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u)) break;
+        if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u, HKV_ISSUE_SLEEP_NS)) break;
         uint8_t* sb = ring + ri.slot * kSlot;
         uint64_t* fb = &full_bar[ri.slot];
         const int u = cu.pc.u;
@@ -1048,7 +1057,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
     if (pc.seg == 0) {
       for (; n_next < n_end; n_next += 2) {
         const int k = pc.k0 + (n_next - n_base);
-        if (!warp_wait(&cons_bar[rc.slot], rc.phase)) {
+        if (!warp_wait(&cons_bar[rc.slot], rc.phase, HKV_CONS_SLEEP_NS)) {
           alive = false;
           break;
         }
@@ -1094,7 +1103,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       const int dt0 = wg * 8;
       for (; n_next < n_end; n_next += 2) {
         const int k = pc.k0 + (n_next - n_base);
-        if (!warp_wait(&cons_bar[rc.slot], rc.phase)) {
+        if (!warp_wait(&cons_bar[rc.slot], rc.phase, HKV_CONS_SLEEP_NS)) {
           alive = false;
           break;
         }
