@@ -129,19 +129,21 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-// Dense K or V [B][Hkv][capacity][128] as a 4-D tensor (dim, token, head, batch);
-// boxes of 64 dims x 32 tokens land in shared memory with the 128-byte swizzle.
+// Dense K or V [B][Hkv][capacity][128] as a 5-D tensor (dim within a 64-dim
+// half, token, half, head, batch): one box of 64 dims x 32 tokens x 2 halves is a
+// whole 32-token tile side (8 KiB, one copy), landing in shared memory as
+// [half][32 rows][128 B] with the 128-byte swizzle.
 hkv_status dense_map(CUtensorMap* m, const void* base, const hkv_dense_kv* d, int B, int Hkv) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return HKV_ERR_CUDA;
   const cuuint64_t es = 2;
-  const cuuint64_t dims[4] = {HKV_D, (cuuint64_t)std::max(1, d->capacity), (cuuint64_t)Hkv, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)d->stride_t * es, (cuuint64_t)d->stride_h * es,
+  const cuuint64_t dims[5] = {64, (cuuint64_t)std::max(1, d->capacity), 2, (cuuint64_t)Hkv, (cuuint64_t)B};
+  const cuuint64_t strides[4] = {(cuuint64_t)d->stride_t * es, 64 * es, (cuuint64_t)d->stride_h * es,
                                  (cuuint64_t)d->stride_b * es};
-  const cuuint32_t box[4] = {64, (cuuint32_t)hkv::kTileD, 1, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const cuuint32_t box[5] = {64, (cuuint32_t)hkv::kTileD, 2, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUresult r = enc(m, d->dtype == HKV_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                         4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         5, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? HKV_OK : HKV_ERR_ARG;

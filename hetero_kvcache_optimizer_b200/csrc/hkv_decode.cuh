@@ -83,7 +83,7 @@ struct Sched {
 };
 
 struct DecodeParams {
-  CUtensorMap tmk;  // dense K [B][Hkv][cap][128] as 4-D (dim, token, head, batch), box 64 x 32
+  CUtensorMap tmk;  // dense K [B][Hkv][cap][128] as 5-D (dim in half, token, half, head, batch), box 64 x 32 x 2
   CUtensorMap tmv;
   const void* q;
   int q_dtype;
@@ -695,12 +695,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, sleep_ns));
 }
 
-__device__ __forceinline__ void tma_tile_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+// One tiled TMA load of a 5-D box (coordinates innermost first; x = 0 here, so
+// the 16-byte rule on the innermost coordinate holds). No multicast.
+__device__ __forceinline__ void tma_tile_5d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w, int v,
                                             uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, %6}], "
+      "[%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -906,10 +908,9 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
           const int b = u / p.Hkv, hk = u - b * p.Hkv, t = cu.k * kTileD;
           const uint32_t d = smem_u32(sb);
           mbar_arrive_expect_tx(fb, dense_slot_bytes());
-          tma_tile_4d(d, &p.tmk, 0, t, hk, b, fb);
-          tma_tile_4d(d + kDenseHalf, &p.tmk, 64, t, hk, b, fb);
-          tma_tile_4d(d + 2 * kDenseHalf, &p.tmv, 0, t, hk, b, fb);
-          tma_tile_4d(d + 3 * kDenseHalf, &p.tmv, 64, t, hk, b, fb);
+          // K then V: one box each, both 64-dim halves of 32 rows
+          tma_tile_5d(d, &p.tmk, 0, t, 0, hk, b, fb);
+          tma_tile_5d(d + 2 * kDenseHalf, &p.tmv, 0, t, 0, hk, b, fb);
         }
         n += 2;
         ri.advance(nsl);
