@@ -182,7 +182,8 @@ __device__ __forceinline__ void piece_fill(const DecodeParams& p, uint32_t end, 
   piece_fill_len(p, end, pc, seg_len(p, pc.u, pc.seg));
 }
 
-__device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, uint32_t end) {
+// The CTA's first piece without its length-dependent fields (see piece_fill_len).
+__device__ __forceinline__ Piece first_piece_head(const DecodeParams& p, int c, uint32_t end) {
   const Sched& s = p.sc;
   const uint32_t x = cta_begin(s, c);
   Piece pc;
@@ -203,7 +204,6 @@ __device__ __forceinline__ Piece first_piece(const DecodeParams& p, int c, uint3
     pc.k0 = 0;
   }
   pc.valid = pc.u < s.U && tile_byte(s, pc.u, pc.seg, pc.k0) < end;
-  if (pc.valid) piece_fill(p, end, pc);
   return pc;
 }
 
@@ -811,8 +811,8 @@ __device__ __forceinline__ void cursor_settle(const DecodeParams& p, uint32_t en
   }
   cu.valid = cu.pc.valid;
 }
-__device__ __forceinline__ void cursor_start(const DecodeParams& p, int c, uint32_t end, Cursor& cu) {
-  cu.pc = first_piece(p, c, end);
+__device__ __forceinline__ void cursor_start(const DecodeParams& p, uint32_t end, const Piece& first, Cursor& cu) {
+  cu.pc = first;
   cu.k = cu.pc.k0;
   cursor_settle(p, end, cu);
 }
@@ -845,15 +845,20 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   float* comb = reinterpret_cast<float*>(ring + nsl * kSlot);  // [8][G][128] + [8][8][2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < nsl; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&ready_bar[i], 1);
-      mbar_init(&empty_bar[i], kGroupWarps);
-    }
+  // The first piece: its sequence length (and, for the consumers, its query rows)
+  // load while the barriers are set up.
+  Piece first = first_piece_head(p, c, end);
+  const int first_len = first.valid ? seg_len(p, first.u, first.seg) : 0;
+  uint8_t* qbuf = reinterpret_cast<uint8_t*>(comb + kConsumerWarps * p.G * HKV_D + kConsumerWarps * 16);
+  if (warp < kConsumerWarps && p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
+  if (warp == kConsumerWarps - 1 && lane < nsl) {  // a warp whose first work waits anyway
+    mbar_init(&full_bar[lane], 1);
+    mbar_init(&ready_bar[lane], 1);
+    mbar_init(&empty_bar[lane], kGroupWarps);
     fence_barrier_init();
   }
   __syncthreads();
+  if (first.valid) piece_fill_len(p, end, first, first_len);
 
   if (warp >= kConsumerWarps) {
     if (warp < kIssueWarp + kIssueWarps) {
@@ -864,7 +869,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       // consumer group), whose waits on it therefore never alias.
       const int w = warp - kIssueWarp;
       Cursor cu;
-      cursor_start(p, c, end, cu);
+      cursor_start(p, end, first, cu);
       if (w == 1 && cu.valid) cursor_next(p, end, cu);
       Ring ri{w, 0u};
       int n = w;
@@ -979,11 +984,9 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   // chunk r of pair t0/2 + j (and of pair t0/2 + 8 + j): the block rotates pair q's chunks by 2q
   const int vc_off = HKV_V_CODES_OFF + v_chunk_off(t0 / 2 + j, r);
   const int vs_off = (t0 / 2) * NG;  // f16x2 words
-  // the query rows of the current piece's unit, prefetched during the previous piece
-  uint8_t* qbuf = reinterpret_cast<uint8_t*>(comb + kConsumerWarps * p.G * HKV_D + kConsumerWarps * 16);
-
-  Piece pc = first_piece(p, c, end);
-  if (p.q_async && pc.valid) q_prefetch(p, pc.u, qbuf);
+  // the query rows of the current piece's unit (qbuf) are prefetched during the
+  // previous piece (the first piece's before the barrier setup)
+  Piece pc = first;
   while (pc.valid) {
     const int u = pc.u, b = u / p.Hkv, hk = u - b * p.Hkv;
     // ---- begin piece: query fragments for this unit
