@@ -3,21 +3,23 @@
 //
 // Schedule. The work of every (sequence, KV head) unit is a list of tiles:
 // 128-token INT4 body tiles, then 32-token dense tiles. Tiles are weighted by
-// their HBM bytes and the whole list (all units) is cut into one contiguous,
-// equal-byte range per CTA of a persistent grid (one CTA per SM). A CTA's
-// range is a short sequence of pieces: runs of tiles of one (unit, segment).
-// Each piece ends in an un-normalised partial (m, l, O) for the unit's G query
-// heads; the CTA that delivers a unit's last partial merges them.
+// their HBM bytes, each segment start adds a fixed charge for its piece start and
+// end, and the whole list (all units) is cut into one contiguous, equal-weight
+// range per CTA of a persistent grid (one CTA per SM). A CTA's range is a short
+// sequence of pieces: runs of tiles of one (unit, segment). Each piece ends in
+// an un-normalised partial (m, l, O) for the unit's G query heads; the CTA that
+// delivers a unit's last partial merges them.
 //
-// Pipeline (320 threads). The loaded HBM latency on B200 is ~2.6 us, so an SM
-// needs ~128 KB of reads in flight to stream at full bandwidth: the ring has
-// eight 24 KB slots. Warp 8 issues the TMA copies (no multicast): INT4 tiles as
-// 1-D bulk copies of their code and metadata blocks, dense tiles as 2-D tensor
-// copies with 128-byte swizzle. Warp 9 expands each INT4 tile's group metadata
-// (f16 or u8) in place into fp32 / f16x2 and zeroes what lies past the sequence
-// length. Warps 0-7 are two consumer groups that take alternate tiles; each
-// warp computes 32 tokens of a tile with m16n8k16 tensor-core MMAs (N = 8
-// query heads, G <= 8 used):
+// Pipeline. The loaded HBM latency on B200 is several microseconds, so an SM
+// needs ~200 KB of reads in flight: the ring has an even number (up to 12) of
+// slots, ten 20 KiB slots for fp16min group 32. Warps 8-9 issue the TMA copies
+// (no multicast), each the loads of one parity: INT4 tiles as one 1-D bulk copy
+// of their page block, dense tiles as one 5-D tensor copy per side with 128-byte
+// swizzle. fp16min blocks are consumed as stored; for ref blocks warps 10-11
+// first expand the group metadata in place into fp32 / f16x2 and zero what lies
+// past the sequence length. Warps 0-7 are two consumer groups that take
+// alternate tiles; each warp computes 32 tokens of a tile with m16n8k16
+// tensor-core MMAs (N = 8 query heads, G <= 8 used):
 //   S^T[tok][head] = K[tok][:] . Q^T      (M = 16 tokens, K = dims)
 //   O^T[dim][head] += V^T[dim][tok] . P^T (M = 16 dims,   K = tokens)
 // INT4 K and V fragments come straight from the packed nibbles (the page
