@@ -37,6 +37,37 @@ inline hkv_status launch_status() {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launch with programmatic stream serialization (programmatic dependent launch):
+// the kernel may start while the previous kernel in the stream finishes, and
+// waits for it (griddep_wait) before its first global access. Used for the
+// decode kernel (its barrier setup then overlaps the tail of the kernel before
+// it: 2.586 -> 2.561 ms per config-1 step); the append kernel, whose blocks
+// would wait resident beside the decode kernel's, measured slower with it
+// (2.608 ms) and launches normally. HKV_PDL (bit mask: 1 decode, 2 append;
+// default 1) overrides this for experiments.
+bool pdl_enabled(int which) {
+  static const int mask = [] {
+    const char* e = std::getenv("HKV_PDL");
+    return e ? std::atoi(e) : 1;
+  }();
+  return (mask & which) != 0;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(int which, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled(which) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
 // The workspace starts with a region reserved for the per-unit merge counters
@@ -158,7 +189,9 @@ hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemBudget);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
-  hkv::decode_kernel<FMT, GROUP, DTy><<<p.sc.C, hkv::decode_threads(FMT), smem, st>>>(p);
+  const cudaError_t e =
+      launch_pdl(1, hkv::decode_kernel<FMT, GROUP, DTy>, dim3(p.sc.C), dim3(hkv::decode_threads(FMT)), smem, st, p);
+  if (e != cudaSuccess) return cuda_fail(e);
   return launch_status();
 }
 
@@ -443,14 +476,16 @@ hkv_status hkv_append_kv(const void* k_new, const void* v_new, int32_t dtype, in
   if (sink < 0 || sink > dense->capacity) return HKV_ERR_ARG;
   if (!aligned16(k_new) || !aligned16(v_new) || stride_b % 8 || stride_h % 8) return HKV_ERR_ARG;
   if (dtype == HKV_DT_F16) {
-    hkv::append_kv_kernel<__half><<<B, 32 * H, 0, S(stream)>>>(static_cast<const __half*>(k_new),
-                                                              static_cast<const __half*>(v_new), H, stride_b,
-                                                              stride_h, *dense, sink, dense_len, ring_head, *body,
-                                                              body_len);
+    const cudaError_t e = launch_pdl(2, hkv::append_kv_kernel<__half>, dim3(B), dim3(32 * H), 0, S(stream),
+                                     static_cast<const __half*>(k_new), static_cast<const __half*>(v_new), H,
+                                     stride_b, stride_h, *dense, sink, dense_len, ring_head, *body, body_len);
+    if (e != cudaSuccess) return cuda_fail(e);
   } else if (dtype == HKV_DT_BF16) {
-    hkv::append_kv_kernel<__nv_bfloat16><<<B, 32 * H, 0, S(stream)>>>(
-        static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new), H, stride_b, stride_h,
-        *dense, sink, dense_len, ring_head, *body, body_len);
+    const cudaError_t e =
+        launch_pdl(2, hkv::append_kv_kernel<__nv_bfloat16>, dim3(B), dim3(32 * H), 0, S(stream),
+                   static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new), H, stride_b,
+                   stride_h, *dense, sink, dense_len, ring_head, *body, body_len);
+    if (e != cudaSuccess) return cuda_fail(e);
   } else {
     return HKV_ERR_ARG;
   }

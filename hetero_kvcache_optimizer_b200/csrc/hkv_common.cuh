@@ -97,6 +97,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
       : "memory");
   return ok != 0;
 }
+// Programmatic dependent launch (kernels launched with the programmatic stream
+// serialization attribute): griddep_wait blocks until the preceding grid has
+// completed and its memory operations are visible, so it goes before the first
+// global access; griddep_launch_dependents lets the next grid in the stream
+// start its own prologue early (that grid then waits for this one the same way).
+// Both are no-ops for a normal launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

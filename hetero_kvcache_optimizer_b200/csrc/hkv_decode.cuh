@@ -847,18 +847,22 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   float* comb = reinterpret_cast<float*>(ring + nsl * kSlot);  // [8][G][128] + [8][8][2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // The first piece: its sequence length (and, for the consumers, its query rows)
-  // load while the barriers are set up.
-  Piece first = first_piece_head(p, c, end);
-  const int first_len = first.valid ? seg_len(p, first.u, first.seg) : 0;
+  // The next grid in the stream may start its prologue now (it waits for this one
+  // before touching global memory, as this one does below).
+  griddep_launch_dependents();
+  Piece first = first_piece_head(p, c, end);  // parameters only
   uint8_t* qbuf = reinterpret_cast<uint8_t*>(comb + kConsumerWarps * p.G * HKV_D + kConsumerWarps * 16);
-  if (warp < kConsumerWarps && p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
   if (warp == kConsumerWarps - 1 && lane < nsl) {  // a warp whose first work waits anyway
     mbar_init(&full_bar[lane], 1);
     mbar_init(&ready_bar[lane], 1);
     mbar_init(&empty_bar[lane], kGroupWarps);
     fence_barrier_init();
   }
+  // Global memory from here on. The first piece's sequence length (and, for the
+  // consumers, its query rows) load across the barrier.
+  griddep_wait();
+  const int first_len = first.valid ? seg_len(p, first.u, first.seg) : 0;
+  if (warp < kConsumerWarps && p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
   __syncthreads();
   if (first.valid) piece_fill_len(p, end, first, first_len);
 
