@@ -834,7 +834,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   __shared__ __align__(8) uint64_t full_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t ready_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t empty_bar[kMaxSlots];
-  __shared__ int2 s_info[kMaxSlots];  // per slot, written by the issue warp: (segment or -1 = done, valid tokens)
+  __shared__ int2 s_info[kMaxSlots];  // ref: per slot, from the issue warp: (segment or -1 = done, valid tokens)
   __shared__ int s_last;
 
   // the 128-byte swizzle of the dense tiles repeats every 1024 bytes: align the ring
@@ -887,8 +887,8 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
         uint8_t* sb = ring + ri.slot * kSlot;
         uint64_t* fb = &full_bar[ri.slot];
         const int u = cu.pc.u;
-        // what the expansion warp needs to know about this load (published by the arrive below)
-        if (lane == 0)
+        // ref: what the expansion warp needs to know about this load (published by the arrive below)
+        if (kExp > 0 && lane == 0)
           s_info[ri.slot] = make_int2(cu.pc.seg, cu.pc.len - cu.k * (cu.pc.seg == 0 ? kTileI4 : kTileD));
         if (cu.pc.seg == 0) {
           const int t = cu.k * kTileI4;
