@@ -99,6 +99,12 @@ class FusedHeteroCache(DynamicCache):
         out = m.attend(layer_idx, q, sm_scale=sm_scale, out_dtype=out_dtype or q.dtype)
         return out if out.dim() == 4 else out[:, :, None, :]
 
+    def holds_layer(self, layer_idx: int) -> bool:
+        """Whether ``attend`` can serve this layer (it holds cached tokens)."""
+        m = self._manager
+        return (m is not None and layer_idx < len(m._dense) and m._dense[layer_idx] is not None
+                and m._dense_len[layer_idx] > 0)
+
     def get_seq_length(self, layer_idx: int = 0) -> int:
         if self._manager is None or self._manager._dense[layer_idx] is None:
             return 0
@@ -108,8 +114,9 @@ class FusedHeteroCache(DynamicCache):
     def seen_tokens(self) -> int:
         return self.real_seq_len
 
-    def get_mask_sizes(self, cache_position: torch.Tensor, layer_idx: int = 0, *args, **kwargs) -> Tuple[int, int]:
-        q = cache_position.shape[0]
+    def get_mask_sizes(self, cache_position, layer_idx: int = 0, *args, **kwargs) -> Tuple[int, int]:
+        # transformers >= 5 passes the query length, earlier versions the cache positions
+        q = cache_position if isinstance(cache_position, int) else cache_position.shape[0]
         if self._manager is None or self._manager._dense[layer_idx] is None:
             return q, 0
         m = self._manager
