@@ -180,25 +180,29 @@ hkv_status dense_map(CUtensorMap* m, const void* base, const hkv_dense_kv* d, in
   return r == CUDA_SUCCESS ? HKV_OK : HKV_ERR_ARG;
 }
 
-template <int FMT, int GROUP, typename DTy>
+template <int FMT, int GROUP, typename DTy, bool STATS>
 hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(hkv::decode_kernel<FMT, GROUP, DTy>,
+    attr_err = cudaFuncSetAttribute(hkv::decode_kernel<FMT, GROUP, DTy, STATS>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemBudget);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
   const cudaError_t e =
-      launch_pdl(1, hkv::decode_kernel<FMT, GROUP, DTy>, dim3(p.sc.C), dim3(hkv::decode_threads(FMT)), smem, st, p);
+      launch_pdl(1, hkv::decode_kernel<FMT, GROUP, DTy, STATS>, dim3(p.sc.C), dim3(hkv::decode_threads(FMT)), smem, st, p);
   if (e != cudaSuccess) return cuda_fail(e);
   return launch_status();
 }
 
 template <int FMT, int GROUP>
 hkv_status launch_decode_g(const hkv::DecodeParams& p, int ddt, int smem, cudaStream_t st) {
-  if (ddt == HKV_DT_BF16) return launch_decode_t<FMT, GROUP, __nv_bfloat16>(p, smem, st);
-  return launch_decode_t<FMT, GROUP, __half>(p, smem, st);
+  const bool stats = p.tile_stats != nullptr;
+  if (ddt == HKV_DT_BF16)
+    return stats ? launch_decode_t<FMT, GROUP, __nv_bfloat16, true>(p, smem, st)
+                 : launch_decode_t<FMT, GROUP, __nv_bfloat16, false>(p, smem, st);
+  return stats ? launch_decode_t<FMT, GROUP, __half, true>(p, smem, st)
+               : launch_decode_t<FMT, GROUP, __half, false>(p, smem, st);
 }
 
 template <int FMT>
@@ -293,7 +297,8 @@ hkv_status check_decode_args(const void* q, int q_dtype, const hkv_int4_store* b
 hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, const hkv_int4_store* body,
                       const hkv_dense_kv* dense, int B, int Hq, int Hkv, int D, float sm_scale, int ctas,
                       void* workspace, size_t workspace_bytes, void* out, int out_dtype, int64_t out_sb,
-                      int64_t out_sh, float* out_o, float* out_ml, cudaStream_t st) {
+                      int64_t out_sh, float* out_o, float* out_ml, cudaStream_t st, float* tile_stats = nullptr,
+                      int stat_tiles = 0, float* unit_ml = nullptr) {
   hkv_status rc = check_decode_args(q, q_dtype, body, dense, B, Hq, Hkv, D);
   if (rc != HKV_OK) return rc;
   if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
@@ -336,6 +341,9 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
   p.out_sh = out_sh;
   p.out_o = out_o;
   p.out_ml = out_ml;
+  p.tile_stats = tile_stats;
+  p.stat_tiles = stat_tiles;
+  p.unit_ml = unit_ml;
   const int fmt = body ? body->format : HKV_FMT_REF;
   const int group = body ? body->group : 32;
   const int ddt = dense ? dense->dtype : HKV_DT_F16;
@@ -564,6 +572,29 @@ hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, i
   if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
   return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
                     workspace_bytes, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr, S(stream));
+}
+
+hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                                  const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B, int32_t Hq,
+                                  int32_t Hkv, int32_t D, float sm_scale, int32_t ctas, void* workspace,
+                                  size_t workspace_bytes, void* out, int32_t out_dtype, int64_t out_stride_b,
+                                  int64_t out_stride_h, float* tile_stats, int32_t stat_tiles, float* unit_ml,
+                                  hkv_stream_t stream) {
+  if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
+  if (!tile_stats || !unit_ml || stat_tiles <= 0 || !aligned16(tile_stats)) return HKV_ERR_ARG;
+  return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
+                    workspace_bytes, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr, S(stream),
+                    tile_stats, stat_tiles, unit_ml);
+}
+
+hkv_status hkv_tile_scores(const float* tile_stats, const float* unit_ml, const hkv_int4_store* body, int32_t B,
+                           int32_t Hkv, int32_t G, int32_t stat_tiles, float* mass, hkv_stream_t stream) {
+  if (!tile_stats || !unit_ml || !mass || !body || B <= 0 || Hkv <= 0 || G <= 0 || G > 8 || stat_tiles <= 0)
+    return HKV_ERR_ARG;
+  if ((int64_t)B * Hkv > kMaxUnits) return HKV_ERR_UNSUPPORTED;
+  hkv::tile_scores_kernel<<<B * Hkv, 128, 0, S(stream)>>>(tile_stats, unit_ml, body->lengths, body->len, Hkv, G,
+                                                         stat_tiles, mass);
+  return launch_status();
 }
 
 hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,

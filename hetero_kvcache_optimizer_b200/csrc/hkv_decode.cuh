@@ -106,7 +106,31 @@ struct DecodeParams {
   int64_t out_sb, out_sh;
   float* out_o;    // [B][Hq][128] f32 (partial mode, when non-null)
   float* out_ml;   // [B][Hq][2]
+  // where the attention mass fell (optional, normalised mode): per INT4 body tile
+  // k < stat_tiles of unit u, per consumer warp and head, (sum of the warp's
+  // softmax numerators, running max) in tile_stats[u][k][warp][head][2]; the
+  // unit's final (max, sum) per head in unit_ml[u][head][2]
+  float* tile_stats;
+  int stat_tiles;
+  float* unit_ml;
 };
+
+// Records one body tile's share of the attention for the unit's heads (see
+// DecodeParams::tile_stats). P: this thread's numerators (heads 2j + (i & 1)),
+// pre-scaled by 1/16 as INT4 tiles carry them; m: the warp's running max.
+__device__ __forceinline__ void record_tile_stats(const DecodeParams& p, int u, int k, int wg,
+                                                  const float (&m)[2], const float (&P)[8]) {
+  const int lane = threadIdx.x & 31, r = lane >> 2, j = lane & 3;
+  float s0 = (P[0] + P[2]) + (P[4] + P[6]), s1 = (P[1] + P[3]) + (P[5] + P[7]);
+#pragma unroll
+  for (int sft = 4; sft < 32; sft <<= 1) {
+    s0 += __shfl_xor_sync(0xffffffffu, s0, sft);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, sft);
+  }
+  if (r == 0)
+    *reinterpret_cast<float4*>(p.tile_stats + ((((int64_t)u * p.stat_tiles + k) * 4 + wg) * 8 + 2 * j) * 2) =
+        make_float4(16.f * s0, m[0], 16.f * s1, m[1]);
+}
 
 // An INT4 tile is one 128-token page block, copied as is: K codes | V codes |
 // metadata. The consumers read fp16min metadata as stored (f16: K scales
@@ -824,7 +848,9 @@ __device__ __forceinline__ void cursor_next(const DecodeParams& p, uint32_t end,
 }
 
 // ---------------------------------------------------------------- the persistent kernel
-template <int FMT, int GROUP, typename DTy>
+// STATS: record where the attention mass falls (DecodeParams::tile_stats); a
+// separate instantiation so that the plain kernel's tile loop stays unchanged.
+template <int FMT, int GROUP, typename DTy, bool STATS>
 __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __grid_constant__ DecodeParams p) {
   constexpr int NG = HKV_D / GROUP;
   constexpr int NM = kTileI4 * NG;  // metadata entries per array of a tile
@@ -1098,6 +1124,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
           if (tok + r + 24 >= pc.len) x[6] = x[7] = -INFINITY;
         }
         softmax_step<NG, 8>(ws, x, P, 4.f);
+        if (STATS && k < p.stat_tiles) record_tile_stats(p, u, k, wg, ws.m, P);
         const float pa[4] = {P[0], P[1], P[2], P[3]};
         const float pc4[4] = {P[4], P[5], P[6], P[7]};
         const int nv = pc.len - tok;  // tokens of this warp's 32 that lie in the sequence
@@ -1260,6 +1287,10 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
           }
 #pragma unroll
           for (int sft = 16; sft > 0; sft >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sft);
+          if (STATS && lane == 0) {
+            p.unit_ml[((int64_t)u * 8 + h) * 2] = M;
+            p.unit_ml[((int64_t)u * 8 + h) * 2 + 1] = L;
+          }
           const int hq = hk * p.G + h;
           if (p.out_o) {
             reinterpret_cast<float4*>(p.out_o + ((int64_t)b * p.Hq + hq) * HKV_D)[lane] = acc;
@@ -1322,6 +1353,36 @@ __global__ void __launch_bounds__(128) lse_merge_kernel(const MergeParams mp) {
   }
   const float v = L > 0.f ? acc / L : 0.f;
   store_any(mp.out, mp.out_dtype, (int64_t)b * mp.out_sb + (int64_t)hq * mp.out_sh + d, v);
+}
+
+// ---------------------------------------------------------------- attention mass per body tile
+// One block of 128 threads per unit u: mass[u][k] = mean over the unit's G heads
+// of sum_warps s * 2^(m - M) / L, the softmax probability on tile k's tokens
+// (0 for tiles past the body length). Inputs as recorded by decode_kernel.
+__global__ void __launch_bounds__(128) tile_scores_kernel(const float* __restrict__ stats,
+                                                          const float* __restrict__ unit_ml,
+                                                          const int32_t* __restrict__ lengths, int len, int Hkv,
+                                                          int G, int stat_tiles, float* __restrict__ mass) {
+  const int u = blockIdx.x;
+  const int b = u / Hkv;
+  const int n = lengths ? lengths[b] : len;
+  const int tiles = min(stat_tiles, (n + kTileI4 - 1) / kTileI4);
+  for (int k = threadIdx.x; k < stat_tiles; k += blockDim.x) {
+    float acc = 0.f;
+    if (k < tiles) {
+      const float* st = stats + ((int64_t)u * stat_tiles + k) * 4 * 8 * 2;
+      for (int h = 0; h < G; ++h) {
+        const float M = unit_ml[((int64_t)u * 8 + h) * 2], L = unit_ml[((int64_t)u * 8 + h) * 2 + 1];
+        if (!(L > 0.f)) continue;
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) t += st[(w * 8 + h) * 2] * exp2f(st[(w * 8 + h) * 2 + 1] - M);
+        acc += t / L;
+      }
+      acc /= (float)G;
+    }
+    mass[(int64_t)u * stat_tiles + k] = acc;
+  }
 }
 
 }  // namespace hkv

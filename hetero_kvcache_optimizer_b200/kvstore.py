@@ -230,6 +230,49 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
     return out[:, :, None, :] if squeeze else out
 
 
+def decode_scored(q: torch.Tensor, store: Int4KVStore, dense: Optional[DenseKV],
+                  sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
+                  ctas: int = 0, out: Optional[torch.Tensor] = None,
+                  body_len: Optional[int] = None, dense_len: Optional[int] = None,
+                  stat_tiles: Optional[int] = None, stream=None):
+    """``decode`` plus where the attention fell: returns (out, mass) with mass
+    [B, Hkv, stat_tiles] f32 the mean over each KV head's query heads of the
+    softmax probability on every 128-token INT4 body tile (0 past the body
+    length). Stays on the device (no host sync). ``stat_tiles`` defaults to the
+    store's capacity in tiles."""
+    _require_cuda(q)
+    squeeze = q.dim() == 4
+    if squeeze:
+        q = q[:, :, 0]
+    B, Hq, D = q.shape
+    Hkv = store.kv_heads
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=out_dtype, device=q.device)
+    if stat_tiles is None:
+        stat_tiles = store.max_pages * store.page_tokens // 128
+    st = store.struct(body_len)
+    ds = dense.struct(dense_len) if dense is not None else None
+    pds = ctypes.byref(ds) if ds is not None else None
+    lib = L.load()
+    nbytes = lib.hkv_decode_workspace_bytes(ctypes.byref(st), pds, B, Hq, Hkv, D, ctas)
+    if nbytes == 0:
+        raise RuntimeError("hkv_decode_workspace_bytes: unsupported decode configuration")
+    ws = workspace(nbytes, q.device, stream)
+    stats = torch.empty(B * Hkv * stat_tiles * 4 * 8 * 2, dtype=torch.float32, device=q.device)
+    unit_ml = torch.empty(B * Hkv * 8 * 2, dtype=torch.float32, device=q.device)
+    mass = torch.empty(B, Hkv, stat_tiles, dtype=torch.float32, device=q.device)
+    L.check(lib.hkv_decode_attn_scored(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), ctypes.byref(st), pds,
+        B, Hq, Hkv, D, float(sm_scale), ctas, ws.data_ptr(), ws.numel(), out.data_ptr(),
+        dtype_code(out.dtype), out.stride(0), out.stride(1), stats.data_ptr(), stat_tiles,
+        unit_ml.data_ptr(), _stream(stream)), "hkv_decode_attn_scored")
+    L.check(lib.hkv_tile_scores(stats.data_ptr(), unit_ml.data_ptr(), ctypes.byref(st), B, Hkv, Hq // Hkv,
+                                stat_tiles, mass.data_ptr(), _stream(stream)), "hkv_tile_scores")
+    return (out[:, :, None, :] if squeeze else out), mass
+
+
 def decode_static(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
                   sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
                   ctas: int = 0, out: Optional[torch.Tensor] = None,

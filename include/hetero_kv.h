@@ -216,6 +216,31 @@ hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b,
                            size_t workspace_bytes, void* out, int32_t out_dtype,
                            int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream);
 
+/* hkv_decode_attn, plus where the attention mass fell, for the prefetch policy
+ * (the reference aggregates accumulated token scores into block means on the
+ * host side of a sync, oracle_triton.py:16-79 and manager.py:931-1056).
+ * tile_stats [B*Hkv][stat_tiles][4][8][2] f32 (16-byte aligned) receives, for
+ * every INT4 body tile k < stat_tiles (128 tokens) of every (sequence, KV head)
+ * unit, per consumer warp and query head of the unit, the sum of the warp's
+ * softmax numerators and its running max (base-2 logits); unit_ml
+ * [B*Hkv][8][2] f32 the unit's final (max, sum) per head. hkv_tile_scores turns
+ * them into attention mass per tile. */
+hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stride_b,
+                                  int64_t q_stride_h, const hkv_int4_store* body,
+                                  const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
+                                  int32_t D, float sm_scale, int32_t ctas, void* workspace,
+                                  size_t workspace_bytes, void* out, int32_t out_dtype,
+                                  int64_t out_stride_b, int64_t out_stride_h, float* tile_stats,
+                                  int32_t stat_tiles, float* unit_ml, hkv_stream_t stream);
+
+/* mass [B*Hkv][stat_tiles] f32: for each unit, the mean over its G query heads
+ * of the softmax probability on tile k's 128 body tokens (0 past the body
+ * length, read from body->lengths or body->len), from the buffers of
+ * hkv_decode_attn_scored over the same store. Stream-ordered, no host sync. */
+hkv_status hkv_tile_scores(const float* tile_stats, const float* unit_ml, const hkv_int4_store* body,
+                           int32_t B, int32_t Hkv, int32_t G, int32_t stat_tiles, float* mass,
+                           hkv_stream_t stream);
+
 /* Same attention, but stops at one un-normalised partial per (b, hq):
  * part_o [B][Hq][128] f32 = sum_t 2^(x_t - m) v_t, part_ml [B][Hq][2] f32 =
  * (m, l) with x = score * sm_scale * log2(e) and l = sum_t 2^(x_t - m).
