@@ -11,6 +11,7 @@
 #include "hkv_common.cuh"
 #include "hkv_decode.cuh"
 #include "hkv_quant.cuh"
+#include "hkv_prefill.cuh"
 
 #define HKV_VERSION 100
 
@@ -351,6 +352,32 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
   return launch_decode_f<HKV_FMT_FP16MIN>(p, group, ddt, pl.smem, st);
 }
 
+
+// --------------------------------------------------------------------------- prefill
+template <int FMT, int GROUP>
+hkv_status launch_prefill_t(const hkv::PrefillParams& p, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(hkv::prefill_kernel<FMT, GROUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    hkv::kPfSmem);
+  });
+  if (attr_err != cudaSuccess) return cuda_fail(attr_err);
+  const dim3 grid((unsigned)cdiv((int64_t)p.Sq * p.G, hkv::kPfRows), (unsigned)(p.B * p.Hkv));
+  hkv::prefill_kernel<FMT, GROUP><<<grid, hkv::kPfRows, hkv::kPfSmem, st>>>(p);
+  return launch_status();
+}
+
+template <int FMT>
+hkv_status launch_prefill_f(const hkv::PrefillParams& p, int group, cudaStream_t st) {
+  switch (group) {
+    case 32: return launch_prefill_t<FMT, 32>(p, st);
+    case 64: return launch_prefill_t<FMT, 64>(p, st);
+    case 128: return launch_prefill_t<FMT, 128>(p, st);
+  }
+  return HKV_ERR_UNSUPPORTED;
+}
+
 }  // namespace
 
 // =========================================================================== C ABI
@@ -585,6 +612,42 @@ hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stri
   return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
                     workspace_bytes, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr, S(stream),
                     tile_stats, stat_tiles, unit_ml);
+}
+
+hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                            int64_t q_stride_s, const hkv_int4_store* body, int32_t B, int32_t Hq, int32_t Hkv,
+                            int32_t Sq, int32_t D, float sm_scale, void* out, int32_t out_dtype, int64_t out_stride_b,
+                            int64_t out_stride_h, int64_t out_stride_s, hkv_stream_t stream) {
+  if (!q || !out || (q_dtype != HKV_DT_F16 && q_dtype != HKV_DT_BF16)) return HKV_ERR_ARG;
+  if (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32) return HKV_ERR_ARG;
+  if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Sq < 0) return HKV_ERR_ARG;
+  if ((int64_t)B * Hkv > 65535) return HKV_ERR_UNSUPPORTED;
+  if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
+  hkv_status rc = check_store(body);
+  if (rc != HKV_OK) return rc;
+  if (Sq == 0) return HKV_OK;
+  hkv::PrefillParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.q_dtype = q_dtype;
+  p.q_sb = q_stride_b;
+  p.q_sh = q_stride_h;
+  p.q_ss = q_stride_s;
+  p.body = *body;
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = Hq / Hkv;
+  p.Sq = Sq;
+  p.qscale = static_cast<float>(static_cast<double>(sm_scale) * 1.4426950408889634);
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.out_sb = out_stride_b;
+  p.out_sh = out_stride_h;
+  p.out_ss = out_stride_s;
+  if (body->format == HKV_FMT_REF) return launch_prefill_f<HKV_FMT_REF>(p, body->group, S(stream));
+  return launch_prefill_f<HKV_FMT_FP16MIN>(p, body->group, S(stream));
 }
 
 hkv_status hkv_tile_scores(const float* tile_stats, const float* unit_ml, const hkv_int4_store* body, int32_t B,

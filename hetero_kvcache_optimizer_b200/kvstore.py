@@ -273,6 +273,25 @@ def decode_scored(q: torch.Tensor, store: Int4KVStore, dense: Optional[DenseKV],
     return (out[:, :, None, :] if squeeze else out), mass
 
 
+def prefill_attn(q: torch.Tensor, store: Int4KVStore, sm_scale: Optional[float] = None,
+                 out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None,
+                 body_len: Optional[int] = None, stream=None) -> torch.Tensor:
+    """Multi-query attention of q [B, Hq, Sq, 128] over every INT4 body token of
+    each sequence (no mask), on the tcgen05 tensor cores. Returns [B, Hq, Sq, 128]."""
+    _require_cuda(q)
+    B, Hq, Sq, D = q.shape
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, Sq, D, dtype=out_dtype, device=q.device)
+    st = store.struct(body_len)
+    L.check(L.load().hkv_prefill_attn(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), q.stride(2), ctypes.byref(st), B, Hq,
+        store.kv_heads, Sq, D, float(sm_scale), out.data_ptr(), dtype_code(out.dtype), out.stride(0),
+        out.stride(1), out.stride(2), _stream(stream)), "hkv_prefill_attn")
+    return out
+
+
 def decode_static(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
                   sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
                   ctas: int = 0, out: Optional[torch.Tensor] = None,

@@ -57,11 +57,18 @@ def decode(q, store: kv.Int4KVStore, sm_scale: Optional[float], out_dtype) -> to
     return kv.decode(q, store, None, sm_scale=sm_scale, out_dtype=out_dtype)
 
 
+# (query, head) rows per KV head from which the tensor-core prefill kernel
+# takes over from the split-KV decode kernel
+PREFILL_MIN_ROWS = 16
+
+
 def forward(q, store: kv.Int4KVStore, sm_scale: Optional[float], out_dtype) -> torch.Tensor:
     """Multi-query (prefill-shaped) attention without a causal mask, as the
-    reference computes it (fused_dequant_attn.py:158-247). The Sq query rows of
-    each head are folded into GQA query heads (at most 8 per KV head per
-    launch), so the same split-KV kernel serves it."""
+    reference computes it (fused_dequant_attn.py:158-247). f16/bf16 queries
+    with at least PREFILL_MIN_ROWS (query, head) rows per KV head run the
+    tcgen05 prefill kernel (kvstore.prefill_attn); otherwise the Sq query rows
+    of each head are folded into GQA query heads (at most 8 per KV head per
+    launch) of the split-KV decode kernel."""
     if q.dim() != 4:
         raise ValueError(f"Forward expects [B,H,S,D], got {tuple(q.shape)}")
     B, Hq, Sq, D = q.shape
@@ -69,6 +76,8 @@ def forward(q, store: kv.Int4KVStore, sm_scale: Optional[float], out_dtype) -> t
         sm_scale = 1.0 / math.sqrt(D)
     Hkv = store.kv_heads
     G = Hq // Hkv
+    if q.dtype in (torch.float16, torch.bfloat16) and Sq * G >= PREFILL_MIN_ROWS:
+        return kv.prefill_attn(q, store, sm_scale=sm_scale, out_dtype=out_dtype)
     out = torch.empty(B, Hq, Sq, D, dtype=out_dtype, device=q.device)
     step = max(1, 8 // G)
     for s0 in range(0, Sq, step):

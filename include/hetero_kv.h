@@ -241,6 +241,20 @@ hkv_status hkv_tile_scores(const float* tile_stats, const float* unit_ml, const 
                            int32_t B, int32_t Hkv, int32_t G, int32_t stat_tiles, float* mass,
                            hkv_stream_t stream);
 
+/* Multi-query attention over the INT4 body (chunked prefill against offloaded
+ * context; replaces fused_dequant_attn_forward,
+ * src/quantization/fused_dequant_attn.py:158-247 and its twin
+ * kernels/fused_dequant_attn.py:371-435): out[b][hq][s] = softmax(q[b][hq][s] .
+ * K^T * sm_scale) V over every body token of unit (b, hq / (Hq/Hkv)), no mask.
+ * q and out [B][Hq][Sq][128] with element strides; q f16/bf16 (computed in f16),
+ * out f16/bf16/f32. Runs on the tcgen05 tensor cores: 128 (query, head) rows of
+ * one KV head per CTA, the body dequantised tile by tile into shared memory. */
+hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                            int64_t q_stride_s, const hkv_int4_store* body, int32_t B, int32_t Hq,
+                            int32_t Hkv, int32_t Sq, int32_t D, float sm_scale, void* out,
+                            int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                            int64_t out_stride_s, hkv_stream_t stream);
+
 /* Same attention, but stops at one un-normalised partial per (b, hq):
  * part_o [B][Hq][128] f32 = sum_t 2^(x_t - m) v_t, part_ml [B][Hq][2] f32 =
  * (m, l) with x = score * sm_scale * log2(e) and l = sum_t 2^(x_t - m).

@@ -325,6 +325,26 @@ def decode_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray,
     return np.matmul(p[:, :, None, :], vv)[:, :, 0, :]
 
 
+def prefill_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray,
+                      sm_scale: float | None = None) -> np.ndarray:
+    """Multi-query attention without a mask, restating the reference's
+    decompress-then-matmul path of fused_dequant_attn_forward
+    (src/quantization/fused_dequant_attn.py:241-246): ``softmax(Q K^T *
+    sm_scale) V`` in fp32 over every key, for q [B, Hq, Sq, D] against
+    dequantised k, v [B, Hkv, S, D] (GQA as in ``decode_attention``)."""
+    B, Hq, Sq, D = q.shape
+    G = Hq // k.shape[1]
+    if sm_scale is None:
+        sm_scale = 1.0 / (D ** 0.5)
+    kk = np.repeat(k.astype(np.float32), G, axis=1)
+    vv = np.repeat(v.astype(np.float32), G, axis=1)
+    s = np.matmul(q.astype(np.float32), np.swapaxes(kk, -1, -2)) * np.float32(sm_scale)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p = p / p.sum(axis=-1, keepdims=True)
+    return np.matmul(p, vv)
+
+
 def lse_merge(parts_o: np.ndarray, parts_m: np.ndarray, parts_l: np.ndarray) -> np.ndarray:
     """Merge split-KV partials: parts_o [n, ..., D] (unnormalised), parts_m /
     parts_l [n, ...] in the natural-log domain. Returns the normalised output."""

@@ -1,0 +1,144 @@
+"""GPU parity of the tcgen05 multi-query (prefill) attention over the INT4 body
+against the CPU oracle's restatement of the reference's decompress-then-matmul
+forward (fused_dequant_attn.py:241-246).
+
+Tolerance (benchmark spec): max |out - ref| <= 2e-3 * ||ref||_2 per (b, head, query).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import kv_oracle as ko
+from tests.hkv_testutil import dequant_side, t16
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+K, V = 0, 1
+
+
+@pytest.fixture(scope="module")
+def hkv():
+    from hetero_kvcache_optimizer_b200 import kvstore
+    return kvstore
+
+
+def _store(hkv, k, v, fmt="ref", group=32, page_tokens=256):
+    B, H, S, _ = k.shape
+    store = hkv.Int4KVStore(B, H, max(S, 1), fmt=fmt, group=group, page_tokens=page_tokens)
+    if S:
+        hkv.prefill(store, t16(k), t16(v))
+    return store
+
+
+def _make_q(seed, B, Hq, Sq, dtype=torch.float16):
+    q = ko.rng_for(seed + 31).standard_normal((B, Hq, Sq, 128), dtype=np.float32)
+    qt = t16(q, dtype=dtype)
+    return qt, qt.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("fmt,group", [("ref", 32), ("ref", 64), ("ref", 128), ("fp16min", 32),
+                                       ("fp16min", 64), ("fp16min", 128)])
+@pytest.mark.parametrize("G,Sq", [(1, 37), (4, 37), (7, 19), (8, 64), (4, 1)])
+def test_formats_gqa_vs_oracle(hkv, fmt, group, G, Sq):
+    B, Hkv, S = 2, 2, 517
+    k, v = ko.make_kv(200 + G, B, Hkv, S)
+    store = _store(hkv, k, v, fmt=fmt, group=group)
+    qt, q = _make_q(G + Sq, B, Hkv * G, Sq)
+    ref = ko.prefill_attention(q, dequant_side(store, K, S), dequant_side(store, V, S))
+    out = hkv.prefill_attn(qt, store).cpu().numpy()
+    assert np.isfinite(out).all()
+    assert ko.rel_err(out, ref) < TOL, (fmt, group, G, Sq)
+
+
+@pytest.mark.parametrize("S", [1, 2, 127, 128, 129, 255, 256, 1000])
+def test_body_lengths_and_ragged(hkv, S):
+    """Per-sequence device lengths (one of them empty); tails of every residue."""
+    B, Hkv, G, Sq = 3, 2, 4, 40
+    k, v = ko.make_kv(S, B, Hkv, S)
+    store = _store(hkv, k, v, fmt="fp16min")
+    lens = [S, max(1, S // 2), 0]
+    store.set_lengths(torch.tensor(lens, dtype=torch.int32, device="cuda"))
+    qt, q = _make_q(S, B, Hkv * G, Sq)
+    kd, vd = dequant_side(store, K, S), dequant_side(store, V, S)
+    out = hkv.prefill_attn(qt, store).cpu().numpy()
+    for b, L_ in enumerate(lens):
+        if L_ == 0:
+            assert np.count_nonzero(out[b]) == 0
+            continue
+        ref = ko.prefill_attention(q[b:b + 1], kd[b:b + 1, :, :L_], vd[b:b + 1, :, :L_])
+        assert ko.rel_err(out[b:b + 1], ref) < TOL, (b, L_)
+
+
+@pytest.mark.parametrize("qdt,odt", [(torch.bfloat16, torch.float32), (torch.float16, torch.float16),
+                                     (torch.bfloat16, torch.bfloat16)])
+def test_dtypes_and_strided_views(hkv, qdt, odt):
+    """q as the transposed view of a [B, Sq, Hq, D] projection; out written into
+    a strided view too; sm_scale other than 1/sqrt(D)."""
+    B, Hkv, G, Sq, S = 2, 4, 2, 150, 700
+    k, v = ko.make_kv(21, B, Hkv, S)
+    store = _store(hkv, k, v, fmt="ref", group=64)
+    qbs = torch.from_numpy(ko.rng_for(5).standard_normal((B, Sq, Hkv * G, 128), dtype=np.float32))
+    qbs = qbs.to("cuda", qdt)
+    qt = qbs.transpose(1, 2)  # [B, Hq, Sq, D], not contiguous
+    out_bs = torch.zeros(B, Sq, Hkv * G, 128, dtype=odt, device="cuda")
+    res = hkv.prefill_attn(qt, store, sm_scale=0.05, out=out_bs.transpose(1, 2))
+    assert res.data_ptr() == out_bs.data_ptr()
+    ref = ko.prefill_attention(qt.float().cpu().numpy(), dequant_side(store, K, S),
+                               dequant_side(store, V, S), sm_scale=0.05)
+    tol = TOL if odt == torch.float32 else TOL + 4e-3  # half-precision output rounding
+    assert ko.rel_err(out_bs.transpose(1, 2).float().cpu().numpy(), ref) < tol
+
+
+def test_paged_store_shuffled_pages(hkv):
+    B, Hkv, G, Sq, S = 2, 2, 4, 33, 900
+    k, v = ko.make_kv(12, B, Hkv, S)
+    mp = 4
+    npages = 3 * B * Hkv * mp
+    store = hkv.Int4KVStore(B, Hkv, S, fmt="fp16min", group=32, page_tokens=256, num_pages=npages)
+    perm = np.random.default_rng(2).permutation(npages)[: B * Hkv * mp].reshape(B * Hkv, mp)
+    store.page_table.copy_(torch.from_numpy(perm.astype(np.int32)))
+    hkv.prefill(store, t16(k), t16(v))
+    qt, q = _make_q(12, B, Hkv * G, Sq)
+    ref = ko.prefill_attention(q, dequant_side(store, K, S), dequant_side(store, V, S))
+    out = hkv.prefill_attn(qt, store).cpu().numpy()
+    assert ko.rel_err(out, ref) < TOL
+
+
+def test_matches_decode_kernel_row_by_row(hkv):
+    """Each query row of the prefill equals a one-query decode over the same body."""
+    B, Hkv, G, Sq, S = 1, 2, 4, 9, 1500
+    k, v = ko.make_kv(44, B, Hkv, S)
+    store = _store(hkv, k, v)
+    qt, _ = _make_q(44, B, Hkv * G, Sq)
+    out = hkv.prefill_attn(qt, store)
+    for s in range(Sq):
+        d = hkv.decode(qt[:, :, s].contiguous(), store, None)
+        assert ko.rel_err(out[:, :, s].cpu().numpy(), d.cpu().numpy()) < TOL, s
+
+
+def test_legacy_forward_routes_to_prefill(hkv):
+    """fused_dequant_attn_forward with per-token KVCompressor metadata (group 128)."""
+    from hetero_kvcache_optimizer_b200.quantization.fused_dequant_attn import fused_dequant_attn_forward
+    B, H, S, Sq = 1, 4, 300, 24
+    k, v = ko.make_kv(9, B, H, S, outlier_channels=0)
+    kq, ks, kz = hkv.quantize_flat(t16(k), 128)
+    vq, vs, vz = hkv.quantize_flat(t16(v), 128)
+    qt, q = _make_q(9, B, H, Sq)
+    out = fused_dequant_attn_forward(qt, kq, ks.view(B, H, S), kz.view(B, H, S), vq, vs.view(B, H, S),
+                                     vz.view(B, H, S))
+    assert out.dtype == torch.float32 and out.shape == (B, H, Sq, 128)
+    kd = ko.dequantize_ref(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(), 128)
+    vd = ko.dequantize_ref(vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), 128)
+    ref = ko.prefill_attention(q, kd, vd)
+    assert ko.rel_err(out.cpu().numpy(), ref) < TOL
+
+
+def test_deterministic_and_no_error_flag(hkv):
+    from hetero_kvcache_optimizer_b200 import _lib as L
+    k, v = ko.make_kv(8, 2, 2, 2000)
+    store = _store(hkv, k, v, fmt="fp16min", group=64)
+    qt, _ = _make_q(8, 2, 16, 300)
+    a = hkv.prefill_attn(qt, store).clone()
+    b = hkv.prefill_attn(qt, store)
+    assert torch.equal(a, b)
+    assert L.device_error() == 0
