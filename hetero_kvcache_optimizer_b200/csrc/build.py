@@ -19,7 +19,7 @@ PKG = os.path.dirname(HERE)
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libhetero_kv.so")
 SOURCES = ["hetero_kv.cu"]
-DEPS = ["hetero_kv.cu", "hkv_common.cuh", "hkv_decode.cuh", "hkv_quant.cuh",
+DEPS = ["hetero_kv.cu", "hkv_common.cuh", "hkv_decode.cuh", "hkv_prefill.cuh", "hkv_quant.cuh",
         os.path.join("..", "..", "include", "hetero_kv.h")]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

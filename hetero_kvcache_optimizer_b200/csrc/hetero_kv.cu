@@ -364,7 +364,7 @@ hkv_status launch_prefill_t(const hkv::PrefillParams& p, cudaStream_t st) {
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
   const dim3 grid((unsigned)cdiv((int64_t)p.Sq * p.G, hkv::kPfRows), (unsigned)(p.B * p.Hkv));
-  hkv::prefill_kernel<FMT, GROUP><<<grid, hkv::kPfRows, hkv::kPfSmem, st>>>(p);
+  hkv::prefill_kernel<FMT, GROUP><<<grid, hkv::kPfThreads, hkv::kPfSmem, st>>>(p);
   return launch_status();
 }
 
@@ -616,8 +616,9 @@ hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stri
 
 hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                             int64_t q_stride_s, const hkv_int4_store* body, int32_t B, int32_t Hq, int32_t Hkv,
-                            int32_t Sq, int32_t D, float sm_scale, void* out, int32_t out_dtype, int64_t out_stride_b,
-                            int64_t out_stride_h, int64_t out_stride_s, hkv_stream_t stream) {
+                            int32_t Sq, int32_t D, float sm_scale, int32_t causal, void* out, int32_t out_dtype,
+                            int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, float* lse,
+                            hkv_stream_t stream) {
   if (!q || !out || (q_dtype != HKV_DT_F16 && q_dtype != HKV_DT_BF16)) return HKV_ERR_ARG;
   if (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32) return HKV_ERR_ARG;
   if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
@@ -646,6 +647,13 @@ hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, 
   p.out_sb = out_stride_b;
   p.out_sh = out_stride_h;
   p.out_ss = out_stride_s;
+  p.causal = causal ? 1 : 0;
+  p.lse = lse;
+  {
+    const int64_t e = out_dtype == HKV_DT_F32 ? 4 : 8;  // elements per 16 bytes
+    p.out_vec = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && out_stride_b % e == 0 && out_stride_h % e == 0 &&
+                out_stride_s % e == 0;
+  }
   if (body->format == HKV_FMT_REF) return launch_prefill_f<HKV_FMT_REF>(p, body->group, S(stream));
   return launch_prefill_f<HKV_FMT_FP16MIN>(p, body->group, S(stream));
 }

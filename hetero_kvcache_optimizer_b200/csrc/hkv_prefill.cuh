@@ -1,25 +1,29 @@
 // Multi-query (prefill) attention over a packed INT4 body on the 5th-generation
 // tensor cores (tcgen05). Included by hetero_kv.cu.
 //
-// One CTA of 128 threads per (sequence, KV head) unit and 128-row query tile;
-// rows are (query position, head of the unit's G) pairs, row = s * G + g. Per
-// 128-token body tile, in order:
-//   1. the raw page block lands in one of two ring slots (1-D bulk copy, issued
-//      two tiles ahead by thread 0);
-//   2. the 128 threads dequantise it into f16 operand tiles in shared memory
-//      (128-byte swizzled, the canonical UMMA layouts): K as [token][dim]
-//      (K-major B of S = Q K^T) and V transposed, [dim][token] (K-major B of
-//      O = P V); K by thread = token, V by thread = 8 tokens x 16 dims;
-//   3. thread 0 issues S = Q K^T (M = 128 rows, N = 128 tokens, 8 x K = 16) into
-//      TMEM columns [0, 128) and commits to an mbarrier;
-//   4. thread t reads its row of S from TMEM lane t (tcgen05.ld), masks tokens
-//      past the body length, runs the online softmax in fp32 (base 2; the
-//      running max moves only when a score beats it by more than 2^8, then the
-//      thread rescales its own row of O in TMEM) and writes P (f16) as the
-//      K-major A operand of the second product;
-//   5. thread 0 issues O += P V (N = 128 dims) into TMEM columns [128, 256).
-// Finally thread t reads its row of O, divides by the row sum and stores it.
-// Every wait is bounded (HKV_WAIT_NS) and sets the device error word on expiry.
+// One CTA per (sequence, KV head) unit and 128-row query tile; rows are
+// (query position, head of the unit's G) pairs, row = s * G + g. Eight warps in
+// two roles of 128 threads run a software pipeline over the body's 128-token tiles:
+//   warps 4-7 (converters) copy raw page block j into ring slot j & 1 with
+//     16-byte cp.async (two tiles ahead; completion on an mbarrier), dequantise
+//     it into f16 operand tiles K[j & 1] ([token][dim], K-major B of S = Q K^T)
+//     and Vt[j & 1] ([dim][token], K-major B of O = P V), 128-byte swizzled,
+//     meet on a named barrier, and their first thread issues S(j) = Q K(j)^T
+//     into TMEM buffer S[j & 1] (M = 128 rows, N = 128 tokens);
+//   warps 0-3 (softmax; thread = query row = TMEM lane) read S(j), mask it, run
+//     the online softmax in fp32 (base 2) and write P(j) as packed f16 over the
+//     first 64 columns of S[j & 1]; after a named barrier their first thread
+//     issues O += P(j) V(j) with P read from TMEM (the TS form). The running max
+//     moves only when a score beats it by more than 2^8; only then does a warp
+//     wait for O(j-1) and rescale its rows of O in TMEM, so softmax(j) normally
+//     overlaps the O(j-1) product.
+// S(j) is issued only after O(j-2) has completed (the converters wait for it
+// before they overwrite K/Vt[j & 1]), which also frees S[j & 1].
+// Then warps 0-3 read their rows of O, divide by the row sum, store them, and
+// optionally the natural-log sum of exponentials per row.
+// Every wait is bounded (HKV_WAIT_NS) and sets the device error word on expiry;
+// each role decides to stop together (barrier AND), and an aborted CTA waits
+// (bounded) for its copies and products before it frees TMEM.
 #pragma once
 #include "hkv_common.cuh"
 
@@ -28,7 +32,8 @@ namespace hkv {
 constexpr int kPfRows = 128;                   // query rows per CTA (the MMA's M)
 constexpr int kPfTileBytes = 128 * 128 * 2;    // one f16 [128][128] operand tile (two 64-column atoms)
 constexpr int kPfRawBytes = 24 * 1024;         // one raw page block (ref g32: 21,504 B)
-constexpr int kPfSmem = 4 * kPfTileBytes + 2 * kPfRawBytes + 1024;  // Q | K | Vt | P | 2 raw | alignment
+constexpr int kPfThreads = 256;                // softmax warps 0-3 | converter warps 4-7
+constexpr int kPfSmem = 5 * kPfTileBytes + 2 * kPfRawBytes + 1024;  // Q | K[2] | Vt[2] | raw[2] | alignment
 constexpr float kPfLazy = 8.0f;
 
 struct PrefillParams {
@@ -37,10 +42,13 @@ struct PrefillParams {
   int64_t q_sb, q_sh, q_ss;  // elements
   hkv_int4_store body;
   int B, Hq, Hkv, G, Sq;
+  int causal;         // query s sees body tokens t <= len - Sq + s
   float qscale;       // sm_scale * log2(e)
   void* out;          // [B][Hq][Sq][128]
   int out_dtype;
+  int out_vec;        // out 16-byte aligned with strides in 16-byte units
   int64_t out_sb, out_sh, out_ss;
+  float* lse;         // optional [B][Hq][Sq]: ln sum_t exp(sm_scale q.k_t)
 };
 
 // Byte offset of the 16-byte chunk (8 columns) c of a row of a [128][128]
@@ -65,6 +73,14 @@ __device__ __forceinline__ void pf_mma(uint32_t tmem, uint64_t a, uint64_t b, ui
       "l"(a), "l"(b), "r"(kPfIdesc), "r"(accumulate)
       : "memory");
 }
+// O += P V with A (P, packed f16 pairs along K) read from TMEM columns [a_tmem, a_tmem + 8)
+__device__ __forceinline__ void pf_mma_ts(uint32_t tmem, uint32_t a_tmem, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem),
+      "r"(a_tmem), "l"(b), "r"(kPfIdesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void pf_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -87,6 +103,39 @@ __device__ __forceinline__ void tm_ld32(uint32_t addr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 32 consecutive columns of this thread's lane, without waiting (tm_wait_ld after a batch).
+__device__ __forceinline__ void tm_ld32_nw(uint32_t addr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(addr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tm_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tm_st32u(uint32_t addr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tm_st16u(uint32_t addr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tm_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tm_st32(uint32_t addr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -105,16 +154,55 @@ __device__ __forceinline__ void tm_st32(uint32_t addr, const float (&v)[32]) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Named barrier over `n` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// arrive on `bar` once this thread's earlier cp.async copies have landed
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// Dequantises K of token t (thread t) of the raw block rb into sK ([token][dim]).
+// Ring layout of a raw block: the page block as stored, except that the four
+// 16-byte chunks of each K token are XOR-swizzled as they are copied in (chunk
+// c of token t at t * 64 + 16 * (c ^ ((t >> 1) & 3))), so that the K
+// converter's 16-byte reads (thread = token) hit 8 distinct bank groups per phase.
+__device__ __forceinline__ uint32_t pf_ring_off(int gc) {  // ring offset of 16-byte chunk gc of a block
+  if (gc < 512) {
+    const int t = gc >> 2, c = gc & 3;
+    return t * 64 + ((c ^ ((t >> 1) & 3)) << 4);
+  }
+  return gc * 16;
+}
+
+// Dequantises K of token t (thread t) of the ring block rb into sK ([token][dim]).
 // Word 4j + w of a K token holds dims 32w + 8c + 16a + 2j + e at nibble 2a + c + 4e,
 // so nib8_to_h2 of a word gives the dim pairs (2j, 2j+1) + 32w + {0, 8, 16, 24}.
 template <int FMT, int GROUP>
 __device__ __forceinline__ void pf_convert_k(const uint8_t* rb, uint8_t* sK, int t, bool valid) {
   constexpr int NG = HKV_D / GROUP;
-  const uint32_t* kw = reinterpret_cast<const uint32_t*>(rb + t * HKV_CODE_BYTES);
+  uint32_t kw[16];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 c = *reinterpret_cast<const uint4*>(rb + t * 64 + ((j ^ ((t >> 1) & 3)) << 4));
+    kw[4 * j] = c.x;
+    kw[4 * j + 1] = c.y;
+    kw[4 * j + 2] = c.z;
+    kw[4 * j + 3] = c.w;
+  }
   const uint8_t* meta = rb + HKV_META_OFF;
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
@@ -131,9 +219,8 @@ __device__ __forceinline__ void pf_convert_k(const uint8_t* rb, uint8_t* sK, int
       const uint32_t z = meta[1024 * NG + t * NG + g];
       s2 = __float2half2_rn(s);
       m2 = __float2half2_rn(0.f);
-      const uint32_t zl = h2u(__float2half2_rn(1024.f + (float)z)), zh = h2u(__float2half2_rn(-64.f - (float)z));
-      zlo = zl;
-      zhi = zh;
+      zlo = h2u(__float2half2_rn(1024.f + (float)z));
+      zhi = h2u(__float2half2_rn(-64.f - (float)z));
     }
     if (!valid) s2 = m2 = __float2half2_rn(0.f);
     uint32_t h[4][4];  // [j][nibble pair]
@@ -143,7 +230,7 @@ __device__ __forceinline__ void pf_convert_k(const uint8_t* rb, uint8_t* sK, int
       else nib8_to_h2_z(kw[4 * j + w], zlo, zhi, h[j]);
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {  // dims 32w + 8c' .. + 7 with c' = {0: +0, 1: +8, 2: +16, 3: +24}
+    for (int c = 0; c < 4; ++c) {  // dims 32w + 8c .. + 7
       uint32_t o[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) o[j] = h2u(__hfma2(u2h(h[j][c]), s2, m2));
@@ -154,47 +241,52 @@ __device__ __forceinline__ void pf_convert_k(const uint8_t* rb, uint8_t* sK, int
 }
 
 // Dequantises V into sVt ([dim][token]): thread t handles tokens 8o .. 8o + 7
-// (o = t % 16: pairs 4o .. 4o + 3), word k = t / 32 of the chunks i in
-// [4 * ((t / 16) & 1), + 4). Word k of chunk i of a pair holds dims i + 32k + 8m
-// (nibble m) of its two tokens (low / high half-word), so nib8_to_h2 of it gives
-// the token pairs of dims i + 32k + {0, 8, 16, 24}. `valid` tokens hold data;
-// the rest become zero (their P is zero and their bytes may be any bits).
+// (o = t / 8: pairs 4o .. 4o + 3) and chunk i = t % 8 of each pair, so the 8
+// threads of a load phase read the 8 chunks of one pair (distinct bank groups)
+// and share its metadata (broadcast). Word k of
+// chunk i of a pair holds dims i + 32k + 8m (nibble m) of its two tokens (low /
+// high half-word), so nib8_to_h2 of it gives the token pairs of dims
+// i + 32k + {0, 8, 16, 24}. `valid` tokens hold data; the rest become zero
+// (their P is zero and their bytes may be any bits).
 template <int FMT, int GROUP>
 __device__ __forceinline__ void pf_convert_v(const uint8_t* rb, uint8_t* sVt, int t, int valid) {
   constexpr int NG = HKV_D / GROUP;
-  const int o = t & 15, k = t >> 5, i0 = 4 * ((t >> 4) & 1);
-  const int g = (32 * k) / GROUP;
+  const int o = t >> 3, i = t & 7;
   const uint8_t* meta = rb + HKV_META_OFF;
-  __half2 s2[4], m2[4];
-  uint32_t zlo[4], zhi[4];
+  uint4 cw[4];
 #pragma unroll
-  for (int pp = 0; pp < 4; ++pp) {
-    const int p = 4 * o + pp;  // pair: tokens 2p, 2p+1
-    if constexpr (FMT == HKV_FMT_FP16MIN) {
-      s2[pp] = reinterpret_cast<const __half2*>(meta + 512 * NG)[p * NG + g];
-      m2[pp] = reinterpret_cast<const __half2*>(meta + 768 * NG)[p * NG + g];
-      zlo[pp] = zhi[pp] = 0;
-    } else {
-      const float* vs = reinterpret_cast<const float*>(meta + 512 * NG);
-      const uint8_t* vz = meta + 1152 * NG;
-      const float za = (float)vz[(2 * p) * NG + g], zb = (float)vz[(2 * p + 1) * NG + g];
-      s2[pp] = __floats2half2_rn(vs[(2 * p) * NG + g], vs[(2 * p + 1) * NG + g]);
-      m2[pp] = __float2half2_rn(0.f);
-      zlo[pp] = h2u(__floats2half2_rn(1024.f + za, 1024.f + zb));
-      zhi[pp] = h2u(__floats2half2_rn(-64.f - za, -64.f - zb));
+  for (int pp = 0; pp < 4; ++pp)
+    cw[pp] = *reinterpret_cast<const uint4*>(rb + HKV_V_CODES_OFF + v_chunk_off(4 * o + pp, i));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int g = (32 * k) / GROUP;
+    __half2 s2[4], m2[4];
+    uint32_t zlo[4], zhi[4];
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      const int p = 4 * o + pp;  // pair: tokens 2p, 2p+1
+      if constexpr (FMT == HKV_FMT_FP16MIN) {
+        s2[pp] = reinterpret_cast<const __half2*>(meta + 512 * NG)[p * NG + g];
+        m2[pp] = reinterpret_cast<const __half2*>(meta + 768 * NG)[p * NG + g];
+        zlo[pp] = zhi[pp] = 0;
+      } else {
+        const float* vs = reinterpret_cast<const float*>(meta + 512 * NG);
+        const uint8_t* vz = meta + 1152 * NG;
+        const float za = (float)vz[(2 * p) * NG + g], zb = (float)vz[(2 * p + 1) * NG + g];
+        s2[pp] = __floats2half2_rn(vs[(2 * p) * NG + g], vs[(2 * p + 1) * NG + g]);
+        m2[pp] = __float2half2_rn(0.f);
+        zlo[pp] = h2u(__floats2half2_rn(1024.f + za, 1024.f + zb));
+        zhi[pp] = h2u(__floats2half2_rn(-64.f - za, -64.f - zb));
+      }
+      // zero the scale and offset of tokens at or past `valid`
+      const uint32_t keep = (2 * p < valid ? 0x0000FFFFu : 0u) | (2 * p + 1 < valid ? 0xFFFF0000u : 0u);
+      s2[pp] = u2h(h2u(s2[pp]) & keep);
+      m2[pp] = u2h(h2u(m2[pp]) & keep);
     }
-    // zero the scale and offset of tokens at or past `valid`
-    const uint32_t keep = (2 * p < valid ? 0x0000FFFFu : 0u) | (2 * p + 1 < valid ? 0xFFFF0000u : 0u);
-    s2[pp] = u2h(h2u(s2[pp]) & keep);
-    m2[pp] = u2h(h2u(m2[pp]) & keep);
-  }
-#pragma unroll
-  for (int ii = 0; ii < 4; ++ii) {
-    const int i = i0 + ii;
     uint32_t h[4][4];  // [pair][nibble m]
 #pragma unroll
     for (int pp = 0; pp < 4; ++pp) {
-      const uint32_t wd = *reinterpret_cast<const uint32_t*>(rb + HKV_V_CODES_OFF + v_chunk_off(4 * o + pp, i) + 4 * k);
+      const uint32_t wd = k == 0 ? cw[pp].x : k == 1 ? cw[pp].y : k == 2 ? cw[pp].z : cw[pp].w;
       if constexpr (FMT == HKV_FMT_FP16MIN) nib8_to_h2(wd, h[pp]);
       else nib8_to_h2_z(wd, zlo[pp], zhi[pp], h[pp]);
     }
@@ -210,199 +302,262 @@ __device__ __forceinline__ void pf_convert_v(const uint8_t* rb, uint8_t* sVt, in
 }
 
 template <int FMT, int GROUP>
-__global__ void __launch_bounds__(128, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t pf_raw[];
-  __shared__ __align__(8) uint64_t full_bar[2];
-  __shared__ __align__(8) uint64_t s_bar, o_bar;
+  __shared__ __align__(8) uint64_t raw_full[2], op_empty[2], s_full[2], vt_full[2], o_done[2], drain_bar[2];
   __shared__ uint32_t s_tmem;
   uint8_t* sm = pf_raw + ((1024u - (smem_u32(pf_raw) & 1023u)) & 1023u);  // swizzle atoms need 1 KiB alignment
   uint8_t* sQ = sm;
-  uint8_t* sK = sm + kPfTileBytes;
-  uint8_t* sVt = sm + 2 * kPfTileBytes;
-  uint8_t* sP = sm + 3 * kPfTileBytes;
-  uint8_t* ring = sm + 4 * kPfTileBytes;
+  uint8_t* sK = sm + kPfTileBytes;      // K[0], K[1]
+  uint8_t* sV = sm + 3 * kPfTileBytes;  // Vt[0], Vt[1]
+  uint8_t* ring = sm + 5 * kPfTileBytes;
   const int t = threadIdx.x, warp = t >> 5;
   const int u = blockIdx.y, b = u / p.Hkv, hk = u - b * p.Hkv;
-  const int row = blockIdx.x * kPfRows + t;  // this thread's query row
-  const bool row_ok = row < p.Sq * p.G;
-  const int qs = row_ok ? row / p.G : 0, qg = row_ok ? row % p.G : 0;
+  const int row0 = blockIdx.x * kPfRows, nrows = p.Sq * p.G;
   constexpr uint32_t kBlock = block_bytes(FMT, GROUP);
 
+  const int len = max(0, p.body.lengths ? p.body.lengths[b] : p.body.len);
+  // tokens the CTA's rows can see: all of the body, or up to the last row's causal limit
+  int span = len;
+  if (p.causal) span = min(len, len - p.Sq + 1 + (min(row0 + kPfRows, nrows) - 1) / p.G);
+  const int ntiles = span > 0 ? (span + HKV_BLOCK_TOKENS - 1) / HKV_BLOCK_TOKENS : 0;
+
   if (t == 0) {
-    mbar_init(&full_bar[0], 1);
-    mbar_init(&full_bar[1], 1);
-    mbar_init(&s_bar, 1);
-    mbar_init(&o_bar, 1);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&raw_full[i], 128);  // one cp.async arrival per converter thread
+      mbar_init(&op_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&vt_full[i], 1);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&drain_bar[i], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&s_tmem)));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&s_tmem)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  const int len = p.body.lengths ? p.body.lengths[b] : p.body.len;
-  const int ntiles = (len + HKV_BLOCK_TOKENS - 1) / HKV_BLOCK_TOKENS;
-
-  // query row -> Q tile (f16, K-major A operand); rows past the end stay zero
-  {
-    const int64_t base = (int64_t)b * p.q_sb + (int64_t)(hk * p.G + qg) * p.q_sh + (int64_t)qs * p.q_ss;
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      uint32_t o[4];
+  // query rows -> Q tile (f16, K-major A operand), 16-byte chunk c of row i per
+  // step so that neighbouring threads read neighbouring bytes; missing rows are zero
+  for (int c = t; c < kPfRows * 16; c += kPfThreads) {
+    const int i = c >> 4, ch = c & 15, r = row0 + i;
+    uint32_t o[4] = {0u, 0u, 0u, 0u};
+    if (r < nrows) {
+      const int qs = r / p.G, qg = r - qs * p.G;
+      const int64_t base =
+          (int64_t)b * p.q_sb + (int64_t)(hk * p.G + qg) * p.q_sh + (int64_t)qs * p.q_ss + 8 * ch;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a = row_ok ? load_any(p.q, p.q_dtype, base + 8 * c + 2 * e) : 0.f;
-        const float bb = row_ok ? load_any(p.q, p.q_dtype, base + 8 * c + 2 * e + 1) : 0.f;
-        o[e] = h2u(__floats2half2_rn(a, bb));
-      }
-      *reinterpret_cast<uint4*>(sQ + pf_chunk(t, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int e = 0; e < 4; ++e)
+        o[e] = h2u(__floats2half2_rn(load_any(p.q, p.q_dtype, base + 2 * e),
+                                     load_any(p.q, p.q_dtype, base + 2 * e + 1)));
     }
+    *reinterpret_cast<uint4*>(sQ + pf_chunk(i, ch)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = s_tmem, tS = tmem, tO = tmem + 128;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t tmem = s_tmem, tO = tmem + 256;
 
-  // raw block of tile k -> ring slot k & 1 (thread 0, which also counts its
-  // copies and commits so that an abnormal exit can wait for them)
-  int n_issued = 0, n_s = 0, n_o = 0;
-  auto issue = [&](int k) {
-    ++n_issued;
-    const int tok = k * HKV_BLOCK_TOKENS;
-    const int64_t page = store_page(p.body, u, tok);
-    uint64_t* fb = &full_bar[k & 1];
-    if (page < 0) {
-      hkv_flag_error(HKV_DEVERR_BAD_PAGE);
-      mbar_arrive(fb);
-      return;
+  if (warp >= 4) {
+    // ------------- converters: raw block -> ring -> K[j & 1], Vt[j & 1]; issue S(j) -------------
+    const int ct = t - 128;
+    auto load = [&](int j) {  // this thread's 16-byte chunks of raw block j into slot j & 1
+      const int tok = j * HKV_BLOCK_TOKENS;
+      const int64_t page = store_page(p.body, u, tok);
+      if (page >= 0) {
+        const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + page * p.body.page_stride +
+                             (int64_t)((tok % p.body.page_tokens) / HKV_BLOCK_TOKENS) * kBlock;
+        uint8_t* dst = ring + (j & 1) * kPfRawBytes;
+#pragma unroll
+        for (int n = 0; n < (int)(kBlock / 16 + 127) / 128; ++n) {
+          const int gc = ct + 128 * n;
+          if (gc < (int)(kBlock / 16)) cp_async16(dst + pf_ring_off(gc), src + 16 * gc);
+        }
+      } else if (ct == 0) {
+        hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+      }
+      cp_async_arrive(&raw_full[j & 1]);
+    };
+    if (ntiles > 0) load(0);
+    if (ntiles > 1) load(1);
+    bool ok = true;
+    int n_s = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      ok = mbar_wait(&raw_full[j & 1], (j >> 1) & 1);
+      if (j >= 2) ok = mbar_wait(&op_empty[j & 1], ((j >> 1) - 1) & 1) && ok;
+      const int valid = min(HKV_BLOCK_TOKENS, len - j * HKV_BLOCK_TOKENS);
+      const uint8_t* rb = ring + (j & 1) * kPfRawBytes;
+      pf_convert_k<FMT, GROUP>(rb, sK + (j & 1) * kPfTileBytes, ct, ct < valid);
+      pf_convert_v<FMT, GROUP>(rb, sV + (j & 1) * kPfTileBytes, ct, valid);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      ok = bar_and(2, 128, ok);  // operands written, slot j & 1 read, by all 128 converters
+      if (!ok) break;
+      if (ct == 0) {
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + (j & 1) * kPfTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          pf_mma(tmem + 128 * (j & 1), pf_desc(q0 + off), pf_desc(k0 + off), kk > 0);
+        }
+        pf_commit(&s_full[j & 1]);
+        mbar_arrive(&vt_full[j & 1]);  // Vt(j) is written: hand it to the thread that issues O(j)
+        ++n_s;
+      }
+      if (j + 2 < ntiles) load(j + 2);
     }
-    const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + page * p.body.page_stride +
-                         (int64_t)((tok % p.body.page_tokens) / HKV_BLOCK_TOKENS) * kBlock;
-    mbar_arrive_expect_tx(fb, kBlock);
-    bulk_g2s(ring + (k & 1) * kPfRawBytes, src, kBlock, fb);
-  };
-  if (t == 0) {
-    if (ntiles > 0) issue(0);
-    if (ntiles > 1) issue(1);
-  }
-
-  float m_run = -1.0e30f, l_run = 0.f;
-  bool alive = true;
-  for (int k = 0; k < ntiles; ++k) {
-    const int valid = min(HKV_BLOCK_TOKENS, len - k * HKV_BLOCK_TOKENS);
-    // the previous tile's P V product must be done before K, Vt and P are rewritten
-    if (k > 0 && !mbar_wait(&o_bar, (k - 1) & 1)) alive = false;
-    if (!mbar_wait(&full_bar[k & 1], (k >> 1) & 1)) alive = false;
-    if (!__syncthreads_and(alive)) break;
-    const uint8_t* rb = ring + (k & 1) * kPfRawBytes;
-    pf_convert_k<FMT, GROUP>(rb, sK, t, t < valid);
-    pf_convert_v<FMT, GROUP>(rb, sVt, t, valid);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    __syncthreads();  // operands written; the raw slot is free
-    if (t == 0) {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (!ok && ct == 0 && n_s > 0) {  // the products already issued finish before TMEM is freed
+      pf_commit(&drain_bar[1]);
+      mbar_wait(&drain_bar[1], 0);
+    }
+  } else {
+    // ---------------- softmax: thread = query row = TMEM lane; issue O(j) ----------------
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int r = row0 + t;
+    const bool row_ok = r < nrows;
+    const int qs = row_ok ? r / p.G : 0, qg = row_ok ? r - qs * p.G : 0;
+    const int lim_row = p.causal ? min(len, len - p.Sq + 1 + qs) : len;  // tokens this row sees
+    const float qscale = p.qscale;
+    float m_run = -1.0e30f, l_run = 0.f;
+    bool ok = true;
+    int n_o = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1) && ok;
       tc_fence_after();
-      if (k + 2 < ntiles) issue(k + 2);
-      const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK);
+      const uint32_t ts = tmem + 128 * (j & 1) + lane_base;
+      float s[128];
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-        pf_mma(tS, pf_desc(q0 + off), pf_desc(k0 + off), kk > 0);
+      for (int c = 0; c < 4; ++c) tm_ld32_nw(ts + 32 * c, s + 32 * c);
+      tm_wait_ld();
+      const int lim = lim_row - j * HKV_BLOCK_TOKENS;
+      if (lim < HKV_BLOCK_TOKENS) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= lim) s[i] = -INFINITY;
       }
-      pf_commit(&s_bar);
-      ++n_s;
-    }
-    // softmax of this thread's row
-    if (!mbar_wait(&s_bar, k & 1)) alive = false;
-    tc_fence_after();
-    float s[4][32];
+      float mx4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-    for (int c = 0; c < 4; ++c) tm_ld32(tS + lane_base + 32 * c, s[c]);
-    float mx = -1.0e30f;
+      for (int i = 4; i < 128; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], s[i]);
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * qscale;
+      // the running max moves only when a score beats it by more than 2^8; the
+      // warp then waits for O(j-1) and rescales its rows (ld/st are warp-collective)
+      const bool move = mx > m_run + kPfLazy;
+      if (__any_sync(0xffffffffu, move)) {
+        const float nm = move ? mx : m_run;
+        const float a = fast_exp2(m_run - nm);
+        if (j > 0) {
+          ok = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1) && ok;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tm_ld32(tO + lane_base + 32 * c, o);
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        s[c][i] = 32 * c + i < valid ? s[c][i] * p.qscale : -INFINITY;
-        mx = fmaxf(mx, s[c][i]);
+            for (int i = 0; i < 32; ++i) o[i] *= a;
+            tm_st32(tO + lane_base + 32 * c, o);
+          }
+        }
+        l_run *= a;
+        m_run = nm;
       }
-    // The row max moves only when a score beats it by more than 2^8; then the
-    // row's O is rescaled in TMEM (tcgen05.ld/st are warp-collective: the whole
-    // warp takes part, with factor 1 for rows that keep their max).
-    const bool move = mx > m_run + kPfLazy;
-    if (__any_sync(0xffffffffu, move)) {
-      const float nm = move ? mx : m_run;
-      const float a = fast_exp2(m_run - nm);
-      if (k > 0) {
+      // x = s * qscale - m two lanes at a time (packed f32x2 FMA / add)
+      const float2 qs2 = make_float2(qscale, qscale), nm2 = make_float2(-m_run, -m_run);
+      float2 lsum = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float o[32];
-          tm_ld32(tO + lane_base + 32 * c, o);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= a;
-          tm_st32(tO + lane_base + 32 * c, o);
+        for (int i = 0; i < 16; ++i) {
+          float2 x = __ffma2_rn(make_float2(s[32 * c + 2 * i], s[32 * c + 2 * i + 1]), qs2, nm2);
+          x.x = fast_exp2(x.x);
+          x.y = fast_exp2(x.y);
+          lsum = __fadd2_rn(lsum, x);
+          pk[i] = h2u(__floats2half2_rn(x.x, x.y));
+        }
+        tm_st16u(ts + 16 * c, pk);
+      }
+      l_run += lsum.x + lsum.y;
+      tm_wait_st();
+      tc_fence_before();
+      ok = bar_and(1, 128, ok);  // P(j) (and any rescale of O) written by all 128 rows
+      if (!ok) break;
+      if (t == 0) {
+        // a failed wait skips the product; the next barrier (or the one below) stops the role
+        ok = mbar_wait(&vt_full[j & 1], (j >> 1) & 1);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t v0 = smem_u32(sV + (j & 1) * kPfTileBytes), pa = tmem + 128 * (j & 1);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            pf_mma_ts(tO, pa + 8 * kk, pf_desc(v0 + off), (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          pf_commit(&op_empty[j & 1]);
+          pf_commit(&o_done[j & 1]);
+          ++n_o;
         }
       }
-      l_run *= a;
-      m_run = nm;
     }
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint32_t o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float x0 = s[c >> 2][8 * (c & 3) + 2 * e], x1 = s[c >> 2][8 * (c & 3) + 2 * e + 1];
-        const __half2 pv = __floats2half2_rn(fast_exp2(x0 - m_run), fast_exp2(x1 - m_run));
-        const float2 pf = __half22float2(pv);
-        l_run += pf.x + pf.y;
-        o[e] = h2u(pv);
-      }
-      *reinterpret_cast<uint4*>(sP + pf_chunk(t, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+    ok = bar_and(1, 128, ok);
+    if (!ok && t == 0 && n_o > 0) {  // the products already issued finish before TMEM is freed
+      pf_commit(&drain_bar[0]);
+      mbar_wait(&drain_bar[0], 0);
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    __syncthreads();
-    if (t == 0) {
+    // epilogue: O row / l
+    bool have = ok && ntiles > 0;
+    if (have) {
+      const bool w = mbar_wait(&o_done[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1);
+      have = __all_sync(0xffffffffu, w);
       tc_fence_after();
-      const uint32_t p0 = smem_u32(sP), v0 = smem_u32(sVt);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-        pf_mma(tO, pf_desc(p0 + off), pf_desc(v0 + off), (k > 0 || kk > 0) ? 1u : 0u);
-      }
-      pf_commit(&o_bar);
-      ++n_o;
     }
-  }
-  // every thread leaves the loop at the same tile; a wait that ran out anywhere
-  // ends the CTA after thread 0 has waited (bounded) for its copies and products
-  alive = __syncthreads_and(alive);
-  if (!alive && t == 0) {
-    for (int j = max(0, n_issued - 2); j < n_issued; ++j) mbar_wait(&full_bar[j & 1], (j >> 1) & 1);
-    if (n_s > 0) mbar_wait(&s_bar, (n_s - 1) & 1);
-    if (n_o > 0) mbar_wait(&o_bar, (n_o - 1) & 1);
-  }
-  // epilogue: O row / l
-  if (alive && ntiles > 0 && !mbar_wait(&o_bar, (ntiles - 1) & 1)) alive = false;
-  tc_fence_after();
-  {
-    // tcgen05.ld is warp-collective: every lane reads, lanes with a query row store
+    const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
     const int64_t ob = (int64_t)b * p.out_sb + (int64_t)(hk * p.G + qg) * p.out_sh + (int64_t)qs * p.out_ss;
-    const float inv = (alive && ntiles > 0 && l_run > 0.f) ? 1.f / l_run : 0.f;
+#pragma unroll 1
     for (int c0 = 0; c0 < 128; c0 += 32) {
       float o[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = 0.f;
-      if (ntiles > 0) tm_ld32(tO + lane_base + c0, o);
-      if (row_ok) {
+      if (have) tm_ld32(tO + lane_base + c0, o);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) store_any(p.out, p.out_dtype, ob + c0 + i, o[i] * inv);
+      for (int i = 0; i < 32; ++i) o[i] *= inv;
+      if (!row_ok) continue;
+      if (p.out_vec && p.out_dtype == HKV_DT_F32) {
+        float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.out) + ob + c0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      } else if (p.out_vec && p.out_dtype == HKV_DT_F16) {
+        uint4* d = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + ob + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d[i] = make_uint4(pack2<__half>(o[8 * i], o[8 * i + 1]), pack2<__half>(o[8 * i + 2], o[8 * i + 3]),
+                            pack2<__half>(o[8 * i + 4], o[8 * i + 5]), pack2<__half>(o[8 * i + 6], o[8 * i + 7]));
+      } else if (p.out_vec && p.out_dtype == HKV_DT_BF16) {
+        uint4* d = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + ob + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d[i] = make_uint4(pack2<__nv_bfloat16>(o[8 * i], o[8 * i + 1]),
+                            pack2<__nv_bfloat16>(o[8 * i + 2], o[8 * i + 3]),
+                            pack2<__nv_bfloat16>(o[8 * i + 4], o[8 * i + 5]),
+                            pack2<__nv_bfloat16>(o[8 * i + 6], o[8 * i + 7]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) store_any(p.out, p.out_dtype, ob + c0 + i, o[i]);
       }
     }
+    if (p.lse && row_ok)
+      p.lse[((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs] =
+          (have && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
 }
 
 }  // namespace hkv

@@ -275,20 +275,33 @@ def decode_scored(q: torch.Tensor, store: Int4KVStore, dense: Optional[DenseKV],
 
 def prefill_attn(q: torch.Tensor, store: Int4KVStore, sm_scale: Optional[float] = None,
                  out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None,
-                 body_len: Optional[int] = None, stream=None) -> torch.Tensor:
-    """Multi-query attention of q [B, Hq, Sq, 128] over every INT4 body token of
-    each sequence (no mask), on the tcgen05 tensor cores. Returns [B, Hq, Sq, 128]."""
+                 body_len: Optional[int] = None, causal: bool = False, lse: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+    """Multi-query attention of q [B, Hq, Sq, 128] over the INT4 body of each
+    sequence on the tcgen05 tensor cores. Returns [B, Hq, Sq, 128].
+
+    causal: the queries are the last Sq positions of the body, so query s sees
+    tokens t <= len - Sq + s. lse: optional contiguous f32 [B, Hq, Sq] that
+    receives ln sum_t exp(sm_scale q.k_t) per row (-inf for a row that sees no
+    token), for merging with attention over other segments."""
     _require_cuda(q)
     B, Hq, Sq, D = q.shape
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty(B, Hq, Sq, D, dtype=out_dtype, device=q.device)
+    if out.stride(3) != 1 or q.stride(3) != 1:
+        raise ValueError("q and out need a contiguous head dimension")
+    lse_ptr = None
+    if lse is not None:
+        if lse.dtype != torch.float32 or tuple(lse.shape) != (B, Hq, Sq) or not lse.is_contiguous():
+            raise ValueError("lse must be a contiguous float32 [B, Hq, Sq] tensor")
+        lse_ptr = lse.data_ptr()
     st = store.struct(body_len)
     L.check(L.load().hkv_prefill_attn(
         q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), q.stride(2), ctypes.byref(st), B, Hq,
-        store.kv_heads, Sq, D, float(sm_scale), out.data_ptr(), dtype_code(out.dtype), out.stride(0),
-        out.stride(1), out.stride(2), _stream(stream)), "hkv_prefill_attn")
+        store.kv_heads, Sq, D, float(sm_scale), int(bool(causal)), out.data_ptr(), dtype_code(out.dtype),
+        out.stride(0), out.stride(1), out.stride(2), lse_ptr, _stream(stream)), "hkv_prefill_attn")
     return out
 
 

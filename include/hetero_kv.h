@@ -245,15 +245,19 @@ hkv_status hkv_tile_scores(const float* tile_stats, const float* unit_ml, const 
  * context; replaces fused_dequant_attn_forward,
  * src/quantization/fused_dequant_attn.py:158-247 and its twin
  * kernels/fused_dequant_attn.py:371-435): out[b][hq][s] = softmax(q[b][hq][s] .
- * K^T * sm_scale) V over every body token of unit (b, hq / (Hq/Hkv)), no mask.
- * q and out [B][Hq][Sq][128] with element strides; q f16/bf16 (computed in f16),
- * out f16/bf16/f32. Runs on the tcgen05 tensor cores: 128 (query, head) rows of
+ * K^T * sm_scale) V over the body tokens of unit (b, hq / (Hq/Hkv)); with
+ * causal != 0 query s sees only tokens t <= len - Sq + s (the queries are the
+ * last Sq positions), and a query that sees none gets zeros. q and out
+ * [B][Hq][Sq][128] with element strides; q f16/bf16 (computed in f16), out
+ * f16/bf16/f32. lse (optional, [B][Hq][Sq] f32) receives ln sum_t
+ * exp(sm_scale q.k_t) (-inf for an empty row), for merging with attention over
+ * other segments. Runs on the tcgen05 tensor cores: 128 (query, head) rows of
  * one KV head per CTA, the body dequantised tile by tile into shared memory. */
 hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                             int64_t q_stride_s, const hkv_int4_store* body, int32_t B, int32_t Hq,
-                            int32_t Hkv, int32_t Sq, int32_t D, float sm_scale, void* out,
+                            int32_t Hkv, int32_t Sq, int32_t D, float sm_scale, int32_t causal, void* out,
                             int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
-                            int64_t out_stride_s, hkv_stream_t stream);
+                            int64_t out_stride_s, float* lse, hkv_stream_t stream);
 
 /* Same attention, but stops at one un-normalised partial per (b, hq):
  * part_o [B][Hq][128] f32 = sum_t 2^(x_t - m) v_t, part_ml [B][Hq][2] f32 =

@@ -326,23 +326,40 @@ def decode_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray,
 
 
 def prefill_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray,
-                      sm_scale: float | None = None) -> np.ndarray:
-    """Multi-query attention without a mask, restating the reference's
-    decompress-then-matmul path of fused_dequant_attn_forward
-    (src/quantization/fused_dequant_attn.py:241-246): ``softmax(Q K^T *
-    sm_scale) V`` in fp32 over every key, for q [B, Hq, Sq, D] against
-    dequantised k, v [B, Hkv, S, D] (GQA as in ``decode_attention``)."""
+                      sm_scale: float | None = None, causal: bool = False,
+                      lengths=None, return_lse: bool = False):
+    """Multi-query attention, restating the reference's decompress-then-matmul
+    path of fused_dequant_attn_forward (src/quantization/fused_dequant_attn.py:
+    241-246): ``softmax(Q K^T * sm_scale) V`` in fp32, for q [B, Hq, Sq, D]
+    against dequantised k, v [B, Hkv, S, D] (GQA as in ``decode_attention``).
+
+    Extensions of this build (the reference has no mask): ``lengths`` [B] keys
+    per sequence (default S); ``causal`` lets query s see keys t <= len - Sq + s
+    (the queries are the last Sq positions); a query that sees no key gets
+    zeros and an lse of -inf. ``return_lse`` also returns ln sum exp(scores)."""
     B, Hq, Sq, D = q.shape
+    S = k.shape[2]
     G = Hq // k.shape[1]
     if sm_scale is None:
         sm_scale = 1.0 / (D ** 0.5)
     kk = np.repeat(k.astype(np.float32), G, axis=1)
     vv = np.repeat(v.astype(np.float32), G, axis=1)
     s = np.matmul(q.astype(np.float32), np.swapaxes(kk, -1, -2)) * np.float32(sm_scale)
-    s = s - s.max(axis=-1, keepdims=True)
-    p = np.exp(s)
-    p = p / p.sum(axis=-1, keepdims=True)
-    return np.matmul(p, vv)
+    lens = np.full(B, S) if lengths is None else np.asarray(lengths)
+    tok = np.arange(S)[None, None, :]
+    lim = lens[:, None, None] - Sq + 1 + np.arange(Sq)[None, :, None] if causal else lens[:, None, None]
+    vis = np.broadcast_to(tok < np.minimum(lim, lens[:, None, None]), (B, Sq, S))[:, None]  # [B,1,Sq,S]
+    s = np.where(vis, s, -np.inf)
+    mx = s.max(axis=-1, keepdims=True)
+    mx = np.where(np.isfinite(mx), mx, 0.0)
+    e = np.where(vis, np.exp(s - mx), 0.0)
+    den = e.sum(axis=-1, keepdims=True)
+    out = np.matmul(e / np.where(den > 0, den, 1.0), vv)
+    if not return_lse:
+        return out
+    with np.errstate(divide="ignore"):
+        lse = np.where(den[..., 0] > 0, np.log(den[..., 0]) + mx[..., 0], -np.inf)
+    return out, lse
 
 
 def lse_merge(parts_o: np.ndarray, parts_m: np.ndarray, parts_l: np.ndarray) -> np.ndarray:

@@ -5,8 +5,9 @@ Run in the build container, where the reference package is importable:
     python tests/golden/make_golden.py [path-to-reference-checkout]
 
 It imports ``src.quantization.kv_compressor.KVCompressor`` and the PyTorch
-fallback of ``src.quantization.fused_dequant_attn.fused_dequant_attn_decode``
-(which is what runs on CPU tensors, fused_dequant_attn.py:326-331) from the
+fallbacks of ``src.quantization.fused_dequant_attn.fused_dequant_attn_decode``
+and ``fused_dequant_attn_forward`` (what runs on CPU tensors,
+fused_dequant_attn.py:326-331 and :241-246) from the
 reference checkout, feeds them seeded inputs from ``oracle.kv_oracle`` and
 writes ``tests/golden/golden.npz`` (small arrays) and ``golden.json`` (SHA-256
 digests of full-size outputs, so configuration-0-sized results are pinned
@@ -28,7 +29,7 @@ from oracle import kv_oracle as ko  # noqa: E402
 REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HKV_REFERENCE", "/root/reference")
 sys.path.insert(0, REF)
 from src.quantization.kv_compressor import KVCompressor  # noqa: E402
-from src.quantization.fused_dequant_attn import fused_dequant_attn_decode  # noqa: E402
+from src.quantization.fused_dequant_attn import fused_dequant_attn_decode, fused_dequant_attn_forward  # noqa: E402
 
 torch.set_num_threads(max(1, os.cpu_count() or 1))
 
@@ -131,6 +132,18 @@ def main():
     arrays["legacy_q"] = q
     arrays["legacy_out"] = out[:, :, 0, :].numpy()
     digests["legacy"] = {"seed": 21, "B": B, "H": H, "S": S, "group": 128}
+
+    # 5. Legacy multi-query forward (prefill), same per-token metadata, Sq = 24.
+    B, H, S, Sq = 1, 4, 300, 24
+    k, v = ko.make_kv(22, B, H, S, outlier_channels=0)
+    kq, ks, kz = comp128.compress(torch.from_numpy(k))
+    vq, vs, vz = comp128.compress(torch.from_numpy(v))
+    q = ko.rng_for(22).standard_normal((B, H, Sq, 128), dtype=np.float32).astype(np.float16)
+    out = fused_dequant_attn_forward(torch.from_numpy(q), kq, ks.reshape(B, H, S), kz.reshape(B, H, S).float(),
+                                     vq, vs.reshape(B, H, S), vz.reshape(B, H, S).float())
+    arrays["legacy_fwd_q"] = q
+    arrays["legacy_fwd_out"] = out.numpy()
+    digests["legacy_fwd"] = {"seed": 22, "B": B, "H": H, "S": S, "Sq": Sq, "group": 128}
 
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)
     with open(os.path.join(HERE, "golden.json"), "w") as f:

@@ -116,21 +116,51 @@ def test_matches_decode_kernel_row_by_row(hkv):
         assert ko.rel_err(out[:, :, s].cpu().numpy(), d.cpu().numpy()) < TOL, s
 
 
-def test_legacy_forward_routes_to_prefill(hkv):
-    """fused_dequant_attn_forward with per-token KVCompressor metadata (group 128)."""
+def test_legacy_forward_matches_reference_golden(hkv, golden):
+    """fused_dequant_attn_forward with per-token KVCompressor metadata (group 128)
+    against the reference's own forward (golden outputs)."""
     from hetero_kvcache_optimizer_b200.quantization.fused_dequant_attn import fused_dequant_attn_forward
-    B, H, S, Sq = 1, 4, 300, 24
-    k, v = ko.make_kv(9, B, H, S, outlier_channels=0)
+    from hetero_kvcache_optimizer_b200.quantization.kernels.fused_dequant_attn import \
+        fused_dequant_attn_forward as twin_forward
+    digests, arrays = golden
+    d = digests["legacy_fwd"]
+    B, H, S = d["B"], d["H"], d["S"]
+    k, v = ko.make_kv(d["seed"], B, H, S, outlier_channels=0)
     kq, ks, kz = hkv.quantize_flat(t16(k), 128)
     vq, vs, vz = hkv.quantize_flat(t16(v), 128)
-    qt, q = _make_q(9, B, H, Sq)
-    out = fused_dequant_attn_forward(qt, kq, ks.view(B, H, S), kz.view(B, H, S), vq, vs.view(B, H, S),
-                                     vz.view(B, H, S))
-    assert out.dtype == torch.float32 and out.shape == (B, H, Sq, 128)
-    kd = ko.dequantize_ref(kq.cpu().numpy(), ks.cpu().numpy(), kz.cpu().numpy(), 128)
-    vd = ko.dequantize_ref(vq.cpu().numpy(), vs.cpu().numpy(), vz.cpu().numpy(), 128)
-    ref = ko.prefill_attention(q, kd, vd)
-    assert ko.rel_err(out.cpu().numpy(), ref) < TOL
+    qt = t16(arrays["legacy_fwd_q"].astype(np.float32))
+    args = (kq, ks.view(B, H, S), kz.view(B, H, S), vq, vs.view(B, H, S), vz.view(B, H, S))
+    out = fused_dequant_attn_forward(qt, *args)
+    assert out.dtype == torch.float32 and out.shape == (B, H, d["Sq"], 128)
+    assert ko.rel_err(out.cpu().numpy(), arrays["legacy_fwd_out"]) < TOL
+    out2 = twin_forward(qt, *args)  # the kernels-directory twin returns q.dtype
+    assert out2.dtype == torch.float16
+    assert ko.rel_err(out2.float().cpu().numpy(), arrays["legacy_fwd_out"]) < TOL + 4e-3
+
+
+@pytest.mark.parametrize("Sq,G,S", [(37, 4, 517), (200, 1, 300), (64, 7, 64), (300, 2, 150)])
+def test_causal_and_lse(hkv, Sq, G, S):
+    """Bottom-right causal mask (queries are the last Sq positions; with Sq > S
+    the first rows see nothing) and the per-row log-sum-exp."""
+    B, Hkv = 2, 2
+    k, v = ko.make_kv(70 + Sq, B, Hkv, S)
+    store = _store(hkv, k, v, fmt="fp16min", group=32)
+    lens = [S, max(1, S - 50)]
+    store.set_lengths(torch.tensor(lens, dtype=torch.int32, device="cuda"))
+    qt, q = _make_q(Sq, B, Hkv * G, Sq)
+    lse = torch.empty(B, Hkv * G, Sq, dtype=torch.float32, device="cuda")
+    out = hkv.prefill_attn(qt, store, causal=True, lse=lse).cpu().numpy()
+    ref, ref_lse = ko.prefill_attention(q, dequant_side(store, K, S), dequant_side(store, V, S), causal=True,
+                                        lengths=lens, return_lse=True)
+    empty = np.isneginf(ref_lse)
+    assert np.all(out[empty] == 0)
+    full = ~empty
+    diff = np.abs(out - ref).max(-1)[full]
+    nrm = np.linalg.norm(ref, axis=-1)[full]
+    assert (diff / nrm).max() < TOL
+    got = lse.cpu().numpy()
+    assert np.all(np.isneginf(got[empty]))
+    np.testing.assert_allclose(got[full], ref_lse[full], atol=2e-3, rtol=1e-4)
 
 
 def test_deterministic_and_no_error_flag(hkv):
