@@ -12,6 +12,7 @@ is far larger than L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload cfg3 [--window PAGES]   # config 3: tiered offload + prefetch
+  python bench.py --workload prefill [--sq N]          # multi-query attention over the INT4 body
 
 With N > 1 (torchrun, one rank per GPU) every rank decodes its own 8
 sequences (batch x KV-head sharding, no collective on the data path): weak
@@ -47,11 +48,13 @@ def parse_args():
     ap.add_argument("--fmt", default="fp16min", choices=["fp16min", "ref"])
     ap.add_argument("--layers", type=int, default=CFG1["layers"])
     ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = one CTA per SM)")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4b"],
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4b", "prefill"],
                     help="cfg1: the headline decode benchmark (default); cfg2: long multimodal context "
                          "(chunked prefill quantise + decode); cfg3: tiered offload, layer-ahead "
                          "host->device page prefetch; cfg4b: sequence split across ranks + NCCL all-gather "
-                         "of partials + LSE merge (each prints its own line)")
+                         "of partials + LSE merge; prefill: tcgen05 multi-query attention over a "
+                         "32K INT4 body (each prints its own line)")
+    ap.add_argument("--sq", type=int, default=2048, help="prefill: query positions per sequence")
     ap.add_argument("--ctx", type=int, default=131072, help="cfg4b: context per sequence")
     ap.add_argument("--batch", type=int, default=64, help="cfg4b: sequences")
     ap.add_argument("--window", type=int, default=0,
@@ -60,6 +63,15 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
+
+
+def measured_tensor_peak(sustained: bool = False):
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops_sustained" if sustained else "bf16_tflops"]), "measured"
+    except Exception:
+        return (1400.0 if sustained else 1590.0), "fallback"
 
 
 def measured_peak():
@@ -275,6 +287,114 @@ def run_cfg2(args) -> None:
         "gpu_launches": args.steps * layers * 2, "clocks": clocks}))
 
 
+# --------------------------------------------------------------------------- prefill
+def run_prefill(args) -> None:
+    """Chunked-prefill attention against an offloaded INT4 context: Sq query
+    positions x 32 query heads (GQA 4 over 8 KV heads) of one sequence attend a
+    32,768-token INT4 body (fp16min, group 32; Llama-3.1-8B attention shape),
+    one launch of the tcgen05 prefill kernel per step (fused_dequant_attn_forward's
+    path). FLOPs = 4 * Hq * Sq * S * 128 (QK^T and PV). The body (8 heads x
+    32,768 tokens x 160 B = 42 MB) fits in L2, so L2 is flushed before every
+    timed launch; the launch then reads it from HBM once and from L2 after."""
+    import numpy as np
+    import torch
+    from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    B, Hq, Hkv, S, Sq = 1, 32, 8, 32768, args.sq
+    gen = torch.Generator(device=dev).manual_seed(5)
+    store = kv.Int4KVStore(B, Hkv, S, fmt=args.fmt, group=32, device=dev)
+    k = torch.randn(B, Hkv, S, 128, device=dev, generator=gen)
+    for h in range(Hkv):
+        ch = torch.randperm(128, device=dev, generator=gen)[:4]
+        k[:, h, :, ch] *= 10.0
+    kv.prefill(store, k.half(), torch.randn(B, Hkv, S, 128, device=dev, generator=gen).half())
+    del k
+    q = torch.randn(B, Hq, Sq, 128, device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty(B, Hq, Sq, 128, device=dev, dtype=torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 256 MB > L2
+    st_ = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        kv.prefill_attn(q, store, out=out)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.2)
+    for i in range(args.steps):
+        flush.fill_(i & 255)
+        starts[i].record(st_)
+        kv.prefill_attn(q, store, out=out)
+        ends[i].record(st_)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
+    flops = 4.0 * B * Hq * Sq * S * 128
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak, kind = measured_tensor_peak(sustained=False)
+
+    # end to end through the public API: q from pinned host, out back to pinned host
+    qh = q.cpu().pin_memory()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    qd = torch.empty_like(q)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        qd.copy_(qh, non_blocking=True)
+        kv.prefill_attn(qd, store, out=out)
+        oh.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e0.record(st_)
+    for _ in range(args.steps):
+        qd.copy_(qh, non_blocking=True)
+        kv.prefill_attn(qd, store, out=out)
+        oh.copy_(out, non_blocking=True)
+    e1.record(st_)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    derr = _lib.device_error(clear=True)
+    if derr:
+        raise RuntimeError(f"device error bits {derr} during the benchmark")
+
+    cpu = None
+    if not args.no_cpu:  # the oracle's numpy restatement on a bounded sample: one KV head, 64 query rows
+        from oracle import kv_oracle as ko
+        rng = ko.rng_for(5)
+        kk = rng.standard_normal((1, 1, S, 128), dtype=np.float32)
+        vv = rng.standard_normal((1, 1, S, 128), dtype=np.float32)
+        qq = rng.standard_normal((1, 4, 16, 128), dtype=np.float32)
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 3 or time.perf_counter() - t0 < 2.0:
+            ko.prefill_attention(qq, kk, vv)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        cpu = {"value": round(4.0 * 64 * S * 128 / dt / 1e12, 5), "unit": "TFLOP/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"numpy restatement (dequantised fp32 K/V given), 1 KV head x 64 query rows x {S} keys"}
+    line = {
+        "metric": "INT4 prefill attention TFLOP/s (tcgen05, fused dequant)", "value": round(tflops, 1),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 tcgen05 mma (int4 storage, fp32 accum)", "data": "synthetic",
+        "config": {"workload": f"prefill: B1, Hq32/Hkv8, D128, {Sq} query positions vs a {S}-token INT4 body "
+                               f"({args.fmt}, g32), no mask", "kv_format": args.fmt, "sq": Sq, "body": S,
+                   "l2": "flushed (256 MB write) before every timed launch"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4), "traffic": None,
+                     "kernel": "prefill_kernel (one launch per step)", "flops_per_launch": flops,
+                     "peak_kind": f"{kind} (cuBLAS bf16 burst)"},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": qh.numel() * qh.element_size(),
+                "d2h_bytes_per_step": oh.numel() * oh.element_size(), "ms_per_step": round(e2e_ms, 4),
+                "api": "kvstore.prefill_attn (pinned host q in, bf16 out back to pinned host)"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line))
+
+
 # --------------------------------------------------------------------------- config 3
 def run_cfg3(args) -> None:
     """InternLM2-7B-shaped tiered offload: 32 layers, B4, Hq32/Hkv8, 131,072-token
@@ -440,6 +560,9 @@ def main():
         return
     if args.workload == "cfg3" and args.impl == "ours":
         run_cfg3(args)
+        return
+    if args.workload == "prefill" and args.impl == "ours":
+        run_prefill(args)
         return
     if args.workload == "cfg4b" and args.impl == "ours":
         run_cfg4b(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),

@@ -173,8 +173,37 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ __half2 u2h_(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// N consecutive f16 / f16x2 values from shared memory in one vector load
+// (N * 2 resp. N * 4 bytes, naturally aligned in the page block's metadata).
+template <int N>
+__device__ __forceinline__ void vload_h(const uint8_t* p, __half (&v)[N]) {
+  if constexpr (N == 4) {
+    const uint2 r = *reinterpret_cast<const uint2*>(p);
+    const __half2 a = u2h_(r.x), b = u2h_(r.y);
+    v[0] = __low2half(a), v[1] = __high2half(a), v[2] = __low2half(b), v[3] = __high2half(b);
+  } else if constexpr (N == 2) {
+    const __half2 a = u2h_(*reinterpret_cast<const uint32_t*>(p));
+    v[0] = __low2half(a), v[1] = __high2half(a);
+  } else {
+    v[0] = *reinterpret_cast<const __half*>(p);
+  }
+}
+template <int N>
+__device__ __forceinline__ void vload_h2(const uint8_t* p, __half2 (&v)[N]) {
+  if constexpr (N == 4) {
+    const uint4 r = *reinterpret_cast<const uint4*>(p);
+    v[0] = u2h_(r.x), v[1] = u2h_(r.y), v[2] = u2h_(r.z), v[3] = u2h_(r.w);
+  } else if constexpr (N == 2) {
+    const uint2 r = *reinterpret_cast<const uint2*>(p);
+    v[0] = u2h_(r.x), v[1] = u2h_(r.y);
+  } else {
+    v[0] = u2h_(*reinterpret_cast<const uint32_t*>(p));
+  }
+}
 
 // Ring layout of a raw block: the page block as stored, except that the four
 // 16-byte chunks of each K token are XOR-swizzled as they are copied in (chunk
@@ -204,16 +233,16 @@ __device__ __forceinline__ void pf_convert_k(const uint8_t* rb, uint8_t* sK, int
     kw[4 * j + 3] = c.w;
   }
   const uint8_t* meta = rb + HKV_META_OFF;
+  __half ks[NG], km[NG];  // fp16min: this token's scales and mins, one vector load each
+  if constexpr (FMT == HKV_FMT_FP16MIN) vload_h<NG>(meta + 2 * NG * t, ks), vload_h<NG>(meta + 256 * NG + 2 * NG * t, km);
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
     const int g = (32 * w) / GROUP;
     __half2 s2, m2;
     uint32_t zlo = 0, zhi = 0;
     if constexpr (FMT == HKV_FMT_FP16MIN) {
-      const __half s = reinterpret_cast<const __half*>(meta)[t * NG + g];
-      const __half m = reinterpret_cast<const __half*>(meta + 256 * NG)[t * NG + g];
-      s2 = __half2half2(s);
-      m2 = __half2half2(m);
+      s2 = __half2half2(ks[g]);
+      m2 = __half2half2(km[g]);
     } else {
       const float s = reinterpret_cast<const float*>(meta)[t * NG + g];
       const uint32_t z = meta[1024 * NG + t * NG + g];
@@ -257,6 +286,14 @@ __device__ __forceinline__ void pf_convert_v(const uint8_t* rb, uint8_t* sVt, in
 #pragma unroll
   for (int pp = 0; pp < 4; ++pp)
     cw[pp] = *reinterpret_cast<const uint4*>(rb + HKV_V_CODES_OFF + v_chunk_off(4 * o + pp, i));
+  __half2 vs2[4][NG], vm2[4][NG];  // fp16min: each pair's NG scales and mins, one vector load each
+  if constexpr (FMT == HKV_FMT_FP16MIN) {
+#pragma unroll
+    for (int pp = 0; pp < 4; ++pp) {
+      vload_h2<NG>(meta + 512 * NG + 4 * NG * (4 * o + pp), vs2[pp]);
+      vload_h2<NG>(meta + 768 * NG + 4 * NG * (4 * o + pp), vm2[pp]);
+    }
+  }
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int g = (32 * k) / GROUP;
@@ -266,8 +303,8 @@ __device__ __forceinline__ void pf_convert_v(const uint8_t* rb, uint8_t* sVt, in
     for (int pp = 0; pp < 4; ++pp) {
       const int p = 4 * o + pp;  // pair: tokens 2p, 2p+1
       if constexpr (FMT == HKV_FMT_FP16MIN) {
-        s2[pp] = reinterpret_cast<const __half2*>(meta + 512 * NG)[p * NG + g];
-        m2[pp] = reinterpret_cast<const __half2*>(meta + 768 * NG)[p * NG + g];
+        s2[pp] = vs2[pp][g];
+        m2[pp] = vm2[pp][g];
         zlo[pp] = zhi[pp] = 0;
       } else {
         const float* vs = reinterpret_cast<const float*>(meta + 512 * NG);
