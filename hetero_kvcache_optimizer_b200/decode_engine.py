@@ -42,7 +42,9 @@ class TieredKVDecoder:
                                          device=self.device))
         self.body_len = 0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.host_graph: Optional[torch.cuda.CUDAGraph] = None
         self._static = None
+        self._host = None
 
     # ------------------------------------------------------------------ prefill
     def prefill_layer(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -112,6 +114,7 @@ class TieredKVDecoder:
         vn = torch.zeros_like(kn)
         out = torch.empty(Lyr, B, self.q_heads, 128, dtype=self.out_dtype, device=self.device)
         hint = self.body_len + max_steps
+        self._hint = hint
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         g = torch.cuda.CUDAGraph()
@@ -129,6 +132,74 @@ class TieredKVDecoder:
         torch.cuda.current_stream(self.device).wait_stream(s)
         self.graph = g
         self._static = (q, kn, vn, out)
+
+    def capture_host(self) -> None:
+        """Capture the end-to-end step over engine-owned pinned host buffers
+        (``host_buffers``: q, new K, new V in; out back), after ``capture``.
+        Layer l's inputs go in on a side stream and gate only layer l's kernels;
+        outputs go back on another side stream in chunks that halve towards the
+        end (8, 8, 8, 4, 2, 1, 1 layers for 32), each started when its last layer
+        is done, so only layer 0's inputs and the last layer's output are not
+        overlapped with the step's kernels."""
+        assert self._static is not None, "capture() first"
+        q, kn, vn, out = self._static
+        hq = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+        hk = torch.empty(kn.shape, dtype=kn.dtype, pin_memory=True)
+        hv = torch.empty(vn.shape, dtype=vn.dtype, pin_memory=True)
+        ho = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        hint = self._hint
+        Lyr = self.num_layers
+        # output chunk boundaries: [start, end) layer ranges
+        ends, left = [], Lyr
+        while left > 0:
+            n = max(1, min(8, left // 2)) if left > 1 else 1
+            ends.append(Lyr - left + n)
+            left -= n
+        chunks = list(zip([0] + ends[:-1], ends))
+        s = torch.cuda.Stream(device=self.device)
+        s_in = torch.cuda.Stream(device=self.device)
+        s_out = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        ev_in = [torch.cuda.Event() for _ in range(Lyr)]
+        ev_out = [torch.cuda.Event() for _ in chunks]
+        # warm the capture stream's decode workspace outside capture (state restored)
+        snap = self._snapshot()
+        with torch.cuda.stream(s):
+            for l in range(Lyr):
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+        s.synchronize()
+        self._restore(snap)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            s_in.wait_stream(s)
+            s_out.wait_stream(s)
+            with torch.cuda.stream(s_in):
+                for l in range(Lyr):
+                    q[l].copy_(hq[l], non_blocking=True)
+                    kn[l].copy_(hk[l], non_blocking=True)
+                    vn[l].copy_(hv[l], non_blocking=True)
+                    ev_in[l].record(s_in)
+            ci = 0
+            for l in range(Lyr):
+                s.wait_event(ev_in[l])
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+                a, b = chunks[ci]
+                if l == b - 1:
+                    ev_out[ci].record(s)
+                    with torch.cuda.stream(s_out):
+                        s_out.wait_event(ev_out[ci])
+                        ho[a:b].copy_(out[a:b], non_blocking=True)
+                    ci += 1
+            s.wait_stream(s_in)
+            s.wait_stream(s_out)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.host_graph = g
+        self._host = (hq, hk, hv, ho)
+
+    @property
+    def host_buffers(self):
+        """Pinned host (q, new K, new V, out) of the pipelined end-to-end step."""
+        return self._host
 
     def _snapshot(self):
         return [(st.lengths.clone(), d.lengths.clone(), d.ring_head.clone(),
@@ -153,7 +224,15 @@ class TieredKVDecoder:
     def step_host(self, q_host: torch.Tensor, k_host: torch.Tensor, v_host: torch.Tensor,
                   out_host: torch.Tensor) -> None:
         """End-to-end step from (pinned) host buffers: H2D of the step's queries
-        and new K/V, the captured step, D2H of the attention outputs."""
+        and new K/V, the captured step, D2H of the attention outputs. Given the
+        engine's own ``host_buffers`` (after ``capture_host``) it replays the
+        pipelined graph (per-layer copies overlapping the kernels); otherwise it
+        copies everything in, replays the step and copies everything out."""
+        if self._host is not None and all(a.data_ptr() == b.data_ptr() for a, b in
+                                          zip((q_host, k_host, v_host, out_host), self._host)):
+            self.host_graph.replay()
+            self.body_len += 1
+            return
         q, kn, vn, out = self._static
         q.copy_(q_host, non_blocking=True)
         kn.copy_(k_host, non_blocking=True)
