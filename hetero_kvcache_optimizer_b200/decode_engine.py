@@ -136,11 +136,16 @@ class TieredKVDecoder:
     def capture_host(self) -> None:
         """Capture the end-to-end step over engine-owned pinned host buffers
         (``host_buffers``: q, new K, new V in; out back), after ``capture``.
-        Layer l's inputs go in on a side stream and gate only layer l's kernels;
-        outputs go back on another side stream in chunks that halve towards the
-        end (8, 8, 8, 4, 2, 1, 1 layers for 32), each started when its last layer
-        is done, so only layer 0's inputs and the last layer's output are not
-        overlapped with the step's kernels."""
+        Inputs go in on a side stream as three copies, each gating the first
+        layer that reads it: layer 0's, layers 1-3's (small, lands while layer 0
+        computes) and the rest (lands while layers 0-3 compute; the host link
+        moves ~26 GB/s, so one copy of all later layers would hold layer 1 up).
+        Outputs go back on another side stream
+        as two copies: layers [0, L-2) once layer L-3 is done, and the last two
+        layers at the end. Every dependency of a kernel on a copy, and every
+        copy, costs microseconds of the step even when the data is ready, hence
+        as few of them as the overlap allows (measured on the 32-layer config-1
+        step: per-layer copies +138 us over the device-only step, this ~+55 us)."""
         assert self._static is not None, "capture() first"
         q, kn, vn, out = self._static
         hq = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
@@ -149,18 +154,15 @@ class TieredKVDecoder:
         ho = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
         hint = self._hint
         Lyr = self.num_layers
-        # output chunk boundaries: [start, end) layer ranges
-        ends, left = [], Lyr
-        while left > 0:
-            n = max(1, min(8, left // 2)) if left > 1 else 1
-            ends.append(Lyr - left + n)
-            left -= n
-        chunks = list(zip([0] + ends[:-1], ends))
+        cuts = sorted({c for c in (Lyr - 2,) if 0 < c < Lyr}) + [Lyr]
+        chunks = list(zip([0] + cuts[:-1], cuts))
         s = torch.cuda.Stream(device=self.device)
         s_in = torch.cuda.Stream(device=self.device)
         s_out = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
-        ev_in = [torch.cuda.Event() for _ in range(Lyr)]
+        bounds = sorted({b for b in (1, 4) if b < Lyr}) + [Lyr]
+        in_chunks = list(zip([0] + bounds[:-1], bounds))  # [0,1), [1,4), [4,L)
+        ev_in = [torch.cuda.Event() for _ in in_chunks]
         ev_out = [torch.cuda.Event() for _ in chunks]
         # warm the capture stream's decode workspace outside capture (state restored)
         snap = self._snapshot()
@@ -174,14 +176,16 @@ class TieredKVDecoder:
             s_in.wait_stream(s)
             s_out.wait_stream(s)
             with torch.cuda.stream(s_in):
-                for l in range(Lyr):
-                    q[l].copy_(hq[l], non_blocking=True)
-                    kn[l].copy_(hk[l], non_blocking=True)
-                    vn[l].copy_(hv[l], non_blocking=True)
-                    ev_in[l].record(s_in)
+                for i, (a, b) in enumerate(in_chunks):
+                    q[a:b].copy_(hq[a:b], non_blocking=True)
+                    kn[a:b].copy_(hk[a:b], non_blocking=True)
+                    vn[a:b].copy_(hv[a:b], non_blocking=True)
+                    ev_in[i].record(s_in)
             ci = 0
             for l in range(Lyr):
-                s.wait_event(ev_in[l])
+                for i, (a, _) in enumerate(in_chunks):
+                    if l == a:  # the first layer that reads input copy i
+                        s.wait_event(ev_in[i])
                 self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
                 a, b = chunks[ci]
                 if l == b - 1:
@@ -198,7 +202,10 @@ class TieredKVDecoder:
 
     @property
     def host_buffers(self):
-        """Pinned host (q, new K, new V, out) of the pipelined end-to-end step."""
+        """Pinned host (q, new K, new V, out) of the pipelined end-to-end step.
+        The step's copies read and write them asynchronously: write the next
+        step's inputs, and read ``out``, only after the step has finished on
+        the device (e.g. after a stream or event synchronisation)."""
         return self._host
 
     def _snapshot(self):
