@@ -27,7 +27,7 @@ DT_F16, DT_BF16, DT_F32 = 0, 1, 2
 FMT_REF, FMT_FP16MIN = 0, 1
 ROLE_K, ROLE_V = 0, 1
 
-DEVERR_TIMEOUT, DEVERR_BAD_PAGE, DEVERR_CAPACITY, DEVERR_STABLE_LEN = 1, 2, 4, 8
+DEVERR_TIMEOUT, DEVERR_BAD_PAGE, DEVERR_CAPACITY = 1, 2, 4
 
 c_i32, c_i64, c_u32, c_f32, c_vp, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
                                           ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t)
@@ -37,7 +37,7 @@ P_i32 = ctypes.POINTER(ctypes.c_int32)
 class HkvInt4Store(ctypes.Structure):
     _fields_ = [("pages", c_vp), ("page_stride", c_i64), ("format", c_i32), ("group", c_i32),
                 ("page_tokens", c_i32), ("max_pages", c_i32), ("page_table", c_vp),
-                ("lengths", c_vp), ("len", c_i32), ("stable_len", c_i32)]
+                ("lengths", c_vp), ("len", c_i32), ("reserved", c_i32)]
 
 
 class HkvDenseKV(ctypes.Structure):

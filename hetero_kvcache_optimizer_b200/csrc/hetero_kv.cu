@@ -103,7 +103,6 @@ hkv_status check_store(const hkv_int4_store* s) {
   const int64_t pb = hkv_page_bytes(s->format, s->group, s->page_tokens);
   if (s->page_stride < pb || s->page_stride % 16) return HKV_ERR_ARG;
   if (s->len < 0) return HKV_ERR_ARG;
-  if (s->stable_len < 0 || s->stable_len > s->len) return HKV_ERR_ARG;  // a floor cannot exceed the bound
   return HKV_OK;
 }
 

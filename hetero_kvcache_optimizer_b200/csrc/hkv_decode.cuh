@@ -847,38 +847,6 @@ __device__ __forceinline__ void cursor_next(const DecodeParams& p, uint32_t end,
   cursor_settle(p, end, cu);
 }
 
-// One INT4 tile (page block) of unit u, tile k, into ring slot sb on full barrier
-// fb: the issue warp looks page ids up 32 at a time (one per lane, cached in
-// pg_u / pg0 / pg_lane), lane 0 issues the bulk copy (a missing page arrives
-// without data and sets the device error word).
-__device__ __forceinline__ void issue_int4_tile(const DecodeParams& p, int u, int k, uint8_t* sb, uint64_t* fb,
-                                                uint32_t tile_bytes, int lane, int& pg_u, int& pg0, int& pg_lane) {
-  const int t = k * kTileI4;
-  const int pi = p.page_shift >= 0 ? t >> p.page_shift : t / p.body.page_tokens;
-  if (u != pg_u || pi < pg0 || pi >= pg0 + 32) {
-    pg_u = u;
-    pg0 = pi;
-    const int pl = pi + lane;
-    pg_lane = -1;
-    if (pl < p.body.max_pages)
-      pg_lane = p.body.page_table ? p.body.page_table[(int64_t)u * p.body.max_pages + pl]
-                                  : (int)((int64_t)u * p.body.max_pages + pl);
-  }
-  const int page = __shfl_sync(0xffffffffu, pg_lane, pi - pg0);
-  if (lane == 0) {
-    if (page < 0) {
-      hkv_flag_error(HKV_DEVERR_BAD_PAGE);
-      mbar_arrive(fb);
-    } else {
-      const int off = p.page_shift >= 0 ? t & ((1 << p.page_shift) - 1) : t % p.body.page_tokens;
-      const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + (int64_t)page * p.body.page_stride +
-                           (int64_t)(off / kTileI4) * tile_bytes;
-      mbar_arrive_expect_tx(fb, tile_bytes);
-      bulk_g2s(sb, src, tile_bytes, fb);
-    }
-  }
-}
-
 // ---------------------------------------------------------------- the persistent kernel
 // STATS: record where the attention mass falls (DecodeParams::tile_stats); a
 // separate instantiation so that the plain kernel's tile loop stays unchanged.
@@ -916,10 +884,13 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
     mbar_init(&empty_bar[lane], kGroupWarps);
     fence_barrier_init();
   }
-  __syncthreads();  // the barriers are initialised (while the previous grid may still run)
-  // Each role waits for the previous grid (griddepcontrol.wait) before it touches
-  // global memory that grid may write; the issue warps may load body tiles below
-  // the store's stable_len first.
+  // Global memory from here on. The first piece's sequence length (and, for the
+  // consumers, its query rows) load across the barrier.
+  griddep_wait();
+  const int first_len = first.valid ? seg_len(p, first.u, first.seg) : 0;
+  if (warp < kConsumerWarps && p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
+  __syncthreads();
+  if (first.valid) piece_fill_len(p, end, first, first_len);
 
   if (warp >= kConsumerWarps) {
     if (warp < kIssueWarp + kIssueWarps) {
@@ -929,40 +900,14 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       // an even slot count a slot always belongs to one issue warp (and one
       // consumer group), whose waits on it therefore never alias.
       const int w = warp - kIssueWarp;
-      constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
-      int pg_u = -1, pg0 = 0, pg_lane = -1;  // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane
-      // With a stable_len promise, the first piece's INT4 tiles that lie wholly
-      // below it go into the free ring slots before the wait; the loop skips them.
-      int n_early = 0;
-      if (p.body.stable_len >= kTileI4 && first.valid && first.seg == 0) {
-        const uint32_t seg0 = tile_byte(sc, first.u, 0, 0);
-        const int kl = min((int)((end - 1 - seg0) / sc.tb), sc.Tb - 1);  // last tile starting in range
-        const int kmax = min(kl + 1, p.body.stable_len / kTileI4);        // tiles [k0, kmax) are safe
-        for (int n = w; n < nsl && first.k0 + n < kmax; n += 2) {
-          if (kExp > 0 && lane == 0) s_info[n] = make_int2(0, kTileI4);
-          issue_int4_tile(p, first.u, first.k0 + n, ring + n * kSlot, &full_bar[n], kTileBytes, lane, pg_u, pg0,
-                          pg_lane);
-          ++n_early;
-        }
-      }
-      griddep_wait();
-      if (first.valid) piece_fill_len(p, end, first, seg_len(p, first.u, first.seg));
       Cursor cu;
       cursor_start(p, end, first, cu);
       if (w == 1 && cu.valid) cursor_next(p, end, cu);
       Ring ri{w, 0u};
       int n = w;
-      // the loads issued before the wait are the cursor's first ones; a sequence
-      // shorter than stable_len breaks that (flagged; its results are invalid)
-      for (int i = 0; i < n_early; ++i) {
-        if (!(cu.valid && cu.pc.seg == 0 && cu.pc.u == first.u && cu.k == first.k0 + n) && lane == 0)
-          hkv_flag_error(HKV_DEVERR_STABLE_LEN);
-        n += 2;
-        ri.advance(nsl);
-        ri.advance(nsl);
-        if (cu.valid) cursor_next(p, end, cu);
-        if (cu.valid) cursor_next(p, end, cu);
-      }
+      // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
+      int pg_u = -1, pg0 = 0, pg_lane = -1;
+      constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
       while (cu.valid) {
         if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u, HKV_ISSUE_SLEEP_NS)) break;
         uint8_t* sb = ring + ri.slot * kSlot;
@@ -972,7 +917,30 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
         if (kExp > 0 && lane == 0)
           s_info[ri.slot] = make_int2(cu.pc.seg, cu.pc.len - cu.k * (cu.pc.seg == 0 ? kTileI4 : kTileD));
         if (cu.pc.seg == 0) {
-          issue_int4_tile(p, u, cu.k, sb, fb, kTileBytes, lane, pg_u, pg0, pg_lane);
+          const int t = cu.k * kTileI4;
+          const int pi = p.page_shift >= 0 ? t >> p.page_shift : t / p.body.page_tokens;
+          if (u != pg_u || pi < pg0 || pi >= pg0 + 32) {
+            pg_u = u;
+            pg0 = pi;
+            const int pl = pi + lane;
+            pg_lane = -1;
+            if (pl < p.body.max_pages)
+              pg_lane = p.body.page_table ? p.body.page_table[(int64_t)u * p.body.max_pages + pl]
+                                          : (int)((int64_t)u * p.body.max_pages + pl);
+          }
+          const int page = __shfl_sync(0xffffffffu, pg_lane, pi - pg0);
+          if (lane == 0) {
+            if (page < 0) {
+              hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+              mbar_arrive(fb);
+            } else {
+              const int off = p.page_shift >= 0 ? t & ((1 << p.page_shift) - 1) : t % p.body.page_tokens;
+              const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + (int64_t)page * p.body.page_stride +
+                                   (int64_t)(off / kTileI4) * kTileBytes;
+              mbar_arrive_expect_tx(fb, kTileBytes);
+              bulk_g2s(sb, src, kTileBytes, fb);
+            }
+          }
         } else if (lane == 0) {
           const int b = u / p.Hkv, hk = u - b * p.Hkv, t = cu.k * kTileD;
           const uint32_t d = smem_u32(sb);
@@ -1006,7 +974,6 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       // until that warp's end-of-work load
       static_assert(expand_warps(HKV_FMT_REF) == kIssueWarps, "one expansion warp per issue warp");
       const int x = warp - kExpandWarp;
-      griddep_wait();
       Ring re{0, 0u};
       for (int i = 0; i < x; ++i) re.advance(nsl);
       while (true) {
@@ -1028,9 +995,6 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   }
 
   // ================================================================== consumer warps
-  griddep_wait();
-  if (p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
-  if (first.valid) piece_fill_len(p, end, first, seg_len(p, first.u, first.seg));
   // Group grp (warps 4 grp .. 4 grp + 3) takes the loads n with n % 2 == grp;
   // warp wg of the group computes tokens [32 wg, 32 wg + 32) of an INT4 tile and
   // [8 wg, 8 wg + 8) of a dense tile.

@@ -208,10 +208,6 @@ __global__ void __launch_bounds__(1024) append_kv_kernel(const T* __restrict__ k
   const int lane = threadIdx.x & 31;
   const int side = lane >> 4;  // 0 = K, 1 = V
   const int p = lane & 15;
-  // The decode that follows may start at once: it waits (griddepcontrol.wait)
-  // before reading anything this kernel writes, and before that touches only
-  // body tokens below its stable_len, which this kernel does not write.
-  griddep_launch_dependents();
   griddep_wait();  // all global accesses below
   const int dl = dense_len[b];
   const int head = ring_head[b];
@@ -260,6 +256,7 @@ __global__ void __launch_bounds__(1024) append_kv_kernel(const T* __restrict__ k
       if (!direct) ring_head[b] = (head + 1) % cap_r;
     }
   }
+  griddep_launch_dependents();  // after this block's work: the next grid may start its prologue
 }
 
 // ------------------------------------------------------------------ legacy flat path

@@ -47,18 +47,9 @@ class TieredKVDecoder:
         self._host = None
 
     # ------------------------------------------------------------------ prefill
-    def _drop_graphs(self) -> None:
-        """The cache was rewritten: captured steps (whose stable_len promise
-        assumed a body that only grows) must be captured again."""
-        self.graph = self.host_graph = None
-        self._host = None
-        for st in self.stores:
-            st.stable_len = 0
-
     def prefill_layer(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
         """k, v [B, Hkv, S, 128]: the first ``sink`` tokens and the last
         ``recent`` stay dense, the rest is quantised into the INT4 body."""
-        self._drop_graphs()
         S = k.shape[2]
         d, st = self.dense[layer], self.stores[layer]
         ns = min(self.sink, S)
@@ -79,7 +70,6 @@ class TieredKVDecoder:
 
     def set_state(self, body_len: int) -> None:
         """Declare that every layer holds ``body_len`` INT4 tokens and a full sink + ring."""
-        self._drop_graphs()
         for st, d in zip(self.stores, self.dense):
             st.set_lengths(body_len)
             d.set_lengths(self.sink + self.recent)
@@ -117,10 +107,7 @@ class TieredKVDecoder:
     def capture(self, max_steps: int) -> None:
         """Capture one decode step over static input/output buffers. The split
         grid is sized for a body of ``body_len + max_steps`` tokens; device-side
-        lengths keep replays exact as the body grows. Each layer's append writes
-        only the body token at the current length, and the body only grows from
-        here, so the current length is a stable_len for every replay: the decode
-        starts loading the INT4 tiles below it while the append still runs."""
+        lengths keep replays exact as the body grows."""
         Lyr, B = self.num_layers, self.batch
         q = torch.zeros(Lyr, B, self.q_heads, 128, dtype=torch.bfloat16, device=self.device)
         kn = torch.zeros(Lyr, B, self.kv_heads, 128, dtype=self.kv_dtype, device=self.device)
@@ -128,8 +115,6 @@ class TieredKVDecoder:
         out = torch.empty(Lyr, B, self.q_heads, 128, dtype=self.out_dtype, device=self.device)
         hint = self.body_len + max_steps
         self._hint = hint
-        for st in self.stores:
-            st.stable_len = self.body_len
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         g = torch.cuda.CUDAGraph()
@@ -240,8 +225,6 @@ class TieredKVDecoder:
         return self._static
 
     def replay(self) -> None:
-        if self.graph is None:
-            raise RuntimeError("no captured step: call capture() (again after set_state / prefill_layer)")
         self.graph.replay()
         self.body_len += 1
 

@@ -82,10 +82,6 @@ class Int4KVStore:
                            if self.paged else None)
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=self.device)
         self.len_hint = 0  # host-side upper bound of lengths (sizes the split-KV grid)
-        # 0, or a floor of every sequence's length whose tokens the kernel launched
-        # just before a decode does not write (hkv_int4_store.stable_len): the
-        # decode may then start loading them before that kernel has finished
-        self.stable_len = 0
 
     def struct(self, len_hint: Optional[int] = None) -> L.HkvInt4Store:
         s = L.HkvInt4Store()
@@ -98,7 +94,6 @@ class Int4KVStore:
         s.page_table = self.page_table.data_ptr() if self.paged else None
         s.lengths = self.lengths.data_ptr()
         s.len = int(self.len_hint if len_hint is None else len_hint)
-        s.stable_len = min(int(self.stable_len), s.len)
         return s
 
     def set_lengths(self, n: Union[int, torch.Tensor]) -> None:

@@ -84,7 +84,6 @@ typedef int hkv_status;
 #define HKV_DEVERR_TIMEOUT 1u
 #define HKV_DEVERR_BAD_PAGE 2u
 #define HKV_DEVERR_CAPACITY 4u
-#define HKV_DEVERR_STABLE_LEN 8u  /* a sequence was shorter than its store's stable_len */
 
 typedef void* hkv_stream_t; /* cudaStream_t */
 typedef void* hkv_event_t;  /* cudaEvent_t */
@@ -103,14 +102,7 @@ typedef struct hkv_int4_store {
   const int32_t* page_table; /* [units][max_pages] int32 on device, or NULL */
   const int32_t* lengths;    /* [B] int32 on device (tokens per sequence), or NULL */
   int32_t len;               /* tokens when lengths == NULL; else an upper bound */
-  /* 0, or a promise for the decode entry points: every sequence holds at least
-   * stable_len tokens, and neither those tokens' page blocks nor their page-table
-   * entries are written by the kernel launched just before the decode on its
-   * stream. The decode then loads its first INT4 tiles below stable_len before
-   * waiting for that kernel (programmatic dependent launch): a decode step's own
-   * append writes only token `length`, so the length before the append is a valid
-   * value. A sequence found shorter sets HKV_DEVERR_STABLE_LEN (results invalid). */
-  int32_t stable_len;
+  int32_t reserved;
 } hkv_int4_store;
 
 /* Dense fp16/bf16 K/V segment [B][Hkv][capacity][D] (e.g. sink + recent ring). */

@@ -279,51 +279,3 @@ def test_poisoned_tails_stay_finite(hkv, fmt, group, S):
         out = hkv.decode(t16(q), store, dense, ctas=ctas).cpu().numpy()
         assert np.isfinite(out).all(), (fmt, group, S, ctas)
         assert ko.rel_err(out, ref) < TOL, (fmt, group, S, ctas)
-
-
-@pytest.mark.parametrize("fmt", ["fp16min", "ref"])
-def test_stable_len_promise(hkv, fmt):
-    """hkv_int4_store.stable_len: with a kept promise the decode loads its first
-    INT4 tiles before waiting for the previous kernel and gives bit-identical
-    output; a sequence shorter than stable_len sets HKV_DEVERR_STABLE_LEN
-    (every read stays inside the pool, the results are simply invalid)."""
-    from hetero_kvcache_optimizer_b200 import _lib as L
-    B, Hkv, G, S = 2, 4, 4, 1500
-    k, v = ko.make_kv(31, B, Hkv, S)
-    store = _body_store(hkv, k, v, fmt=fmt, capacity=2048)
-    dense = hkv.DenseKV(B, Hkv, 96)  # 64 sink rows + a ring of 32, full
-    dense.k[:, :, :96] = t16(k[:, :, :96])
-    dense.v[:, :, :96] = t16(v[:, :, :96])
-    dense.set_lengths(96)
-    q = t16(ko.make_q(31, B, Hkv * G))
-    L.device_error()
-    ref = hkv.decode(q, store, dense, ctas=5).clone()
-    for stable in (S, 1000, 128):
-        store.stable_len = stable
-        for ctas in (5, 0):
-            out = hkv.decode(q, store, dense, ctas=ctas)
-            assert torch.equal(out, hkv.decode(q, store, dense, ctas=ctas)), (stable, ctas)
-            store.stable_len = 0
-            assert torch.equal(out, hkv.decode(q, store, dense, ctas=ctas)), (stable, ctas)
-            store.stable_len = stable
-    assert L.device_error() == 0
-    # an append right before the decode on the same stream (the case the promise is
-    # for): the full ring evicts its oldest row into body token S, above the floor
-    store.stable_len = S
-    kn = t16(ko.make_kv(32, B, Hkv, 1)[0][:, :, 0])
-    vn = t16(ko.make_kv(33, B, Hkv, 1)[0][:, :, 0])
-    hkv.append_kv(kn, vn, dense, 64, store)
-    out = hkv.decode(q, store, dense, ctas=5, body_len=S + 1)
-    assert int(store.lengths[0].item()) == S + 1
-    store.stable_len = 0
-    assert torch.equal(out, hkv.decode(q, store, dense, ctas=5, body_len=S + 1))
-    assert not torch.equal(out, ref)  # the evicted row and the new token changed the context
-    assert L.device_error() == 0
-    # broken promise: one sequence shorter than stable_len
-    store.set_lengths(torch.tensor([S, 300], dtype=torch.int32, device="cuda"))
-    store.len_hint = S
-    store.stable_len = 1200
-    hkv.decode(q, store, dense, ctas=5)
-    torch.cuda.synchronize()
-    assert L.device_error() & L.DEVERR_STABLE_LEN
-    store.stable_len = 0
