@@ -46,7 +46,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--fmt", default="fp16min", choices=["fp16min", "ref"])
-    ap.add_argument("--layers", type=int, default=CFG1["layers"])
+    ap.add_argument("--layers", type=int, default=None,
+                    help="layers (default: the workload's own, 32 for cfg1/cfg3, 28 for cfg2)")
     ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = one CTA per SM)")
     ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4b", "prefill"],
                     help="cfg1: the headline decode benchmark (default); cfg2: long multimodal context "
@@ -555,6 +556,8 @@ def run_cfg4b(args, world: int, rank: int, local: int) -> None:
 # --------------------------------------------------------------------------- GPU arm
 def main():
     args = parse_args()
+    if args.layers is None:
+        args.layers = 28 if args.workload == "cfg2" else CFG1["layers"]
     if args.workload == "cfg2" and args.impl == "ours":
         run_cfg2(args)
         return
