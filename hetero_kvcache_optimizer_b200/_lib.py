@@ -72,8 +72,9 @@ SIGNATURES = {
                                        c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_i32, c_i64, c_i64, c_vp,
                                        c_i32, c_vp, c_vp]),
     "hkv_tile_scores": (c_i32, [c_vp, c_vp, P_store, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "hkv_prefill_workspace_bytes": (c_sz, [P_store, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32]),
     "hkv_prefill_attn": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, P_store, c_i32, c_i32, c_i32, c_i32, c_i32,
-                                 c_f32, c_i32, c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp]),
+                                 c_f32, c_i32, c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_i32, c_vp, c_sz, c_vp]),
     "hkv_decode_attn_partial": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32,
                                         c_i32, c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_vp, c_vp]),
     "hkv_decode_attn_static": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32, c_i32,

@@ -363,9 +363,40 @@ hkv_status launch_prefill_t(const hkv::PrefillParams& p, cudaStream_t st) {
                                     hkv::kPfSmem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
-  const dim3 grid((unsigned)cdiv((int64_t)p.Sq * p.G, hkv::kPfRows), (unsigned)(p.B * p.Hkv));
+  const dim3 grid((unsigned)cdiv((int64_t)p.Sq * p.G, hkv::kPfRows), (unsigned)(p.B * p.Hkv), (unsigned)p.nsplit);
   hkv::prefill_kernel<FMT, GROUP><<<grid, hkv::kPfThreads, hkv::kPfSmem, st>>>(p);
+  hkv_status rc = launch_status();
+  if (rc != HKV_OK || p.nsplit == 1) return rc;
+  const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+  hkv::prefill_merge_kernel<<<(unsigned)cdiv(rows, 8), 256, 0, st>>>(p);
   return launch_status();
+}
+
+// Splits of the body per query tile for a prefill: the smallest count that
+// fills the SMs' waves best, by a model in units of one tile's time (~1.9 us):
+// waves x (tiles per split + 5 for a CTA's fixed start and end, measured) + the
+// merge's traffic (each split's partial, 520 B per row, read once at ~6.5 TB/s).
+// `forced` > 0 asks for that count (still at most one split per tile, 16 in all).
+int prefill_splits(int64_t base_ctas, int tiles, int64_t rows, int forced) {
+  if (tiles <= 1) return 1;
+  if (forced > 0) return std::min(std::min(forced, tiles), 16);
+  const int sms = device_sms();
+  double best = 0.0;
+  int bs = 1;
+  for (int sp = 1; sp <= 16; ++sp) {
+    if (sp > 1 && tiles / sp < 8) break;
+    const double waves = (double)((base_ctas * sp + sms - 1) / sms);
+    double t = waves * ((double)tiles / sp + 5.0);
+    if (sp > 1) t += (double)rows * sp * 520.0 / 6.5e12 / 1.9e-6 + 2.0;
+    if (sp == 1 || t < 0.98 * best) {
+      best = t;
+      bs = sp;
+    }
+  }
+  return bs;
+}
+inline size_t prefill_ws_bytes(int splits, int64_t rows) {
+  return splits > 1 ? (size_t)splits * (size_t)rows * (HKV_D + 2) * sizeof(float) : 0;
 }
 
 template <int FMT>
@@ -614,17 +645,27 @@ hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stri
                     tile_stats, stat_tiles, unit_ml);
 }
 
+size_t hkv_prefill_workspace_bytes(const hkv_int4_store* body, int32_t B, int32_t Hq, int32_t Hkv, int32_t Sq,
+                                   int32_t D, int32_t splits) {
+  if (check_store(body) != HKV_OK || B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Sq <= 0 || D != HKV_D) return 0;
+  const int64_t base = cdiv((int64_t)Sq * (Hq / Hkv), hkv::kPfRows) * B * Hkv;
+  const int64_t rows = (int64_t)B * Hq * Sq;
+  const int tiles = (int)cdiv((int64_t)body->len, hkv::kTileI4);
+  return prefill_ws_bytes(prefill_splits(base, tiles, rows, splits), rows);
+}
+
 hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                             int64_t q_stride_s, const hkv_int4_store* body, int32_t B, int32_t Hq, int32_t Hkv,
                             int32_t Sq, int32_t D, float sm_scale, int32_t causal, void* out, int32_t out_dtype,
                             int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, float* lse,
-                            hkv_stream_t stream) {
+                            int32_t splits, void* workspace, size_t workspace_bytes, hkv_stream_t stream) {
   if (!q || !out || (q_dtype != HKV_DT_F16 && q_dtype != HKV_DT_BF16)) return HKV_ERR_ARG;
   if (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32) return HKV_ERR_ARG;
   if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
-  if (B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Sq < 0) return HKV_ERR_ARG;
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Sq < 0 || splits < 0) return HKV_ERR_ARG;
   if ((int64_t)B * Hkv > 65535) return HKV_ERR_UNSUPPORTED;
   if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
+  if (workspace && !aligned16(workspace)) return HKV_ERR_ARG;
   hkv_status rc = check_store(body);
   if (rc != HKV_OK) return rc;
   if (Sq == 0) return HKV_OK;
@@ -649,6 +690,18 @@ hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, 
   p.out_ss = out_stride_s;
   p.causal = causal ? 1 : 0;
   p.lse = lse;
+  {
+    // body splits (wave quantisation): as many as the workspace holds, up to the model's choice
+    const int64_t base = cdiv((int64_t)Sq * p.G, hkv::kPfRows) * B * Hkv;
+    const int64_t rows = (int64_t)B * Hq * Sq;
+    int sp = prefill_splits(base, (int)cdiv((int64_t)body->len, hkv::kTileI4), rows, splits);
+    while (sp > 1 && (!workspace || prefill_ws_bytes(sp, rows) > workspace_bytes)) --sp;
+    p.nsplit = sp;
+    if (sp > 1) {
+      p.part_o = static_cast<float*>(workspace);
+      p.part_ml = p.part_o + (size_t)sp * rows * HKV_D;
+    }
+  }
   {
     const int64_t e = out_dtype == HKV_DT_F32 ? 4 : 8;  // elements per 16 bytes
     p.out_vec = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && out_stride_b % e == 0 && out_stride_h % e == 0 &&

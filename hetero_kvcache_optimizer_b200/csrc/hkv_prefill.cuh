@@ -49,6 +49,12 @@ struct PrefillParams {
   int out_vec;        // out 16-byte aligned with strides in 16-byte units
   int64_t out_sb, out_sh, out_ss;
   float* lse;         // optional [B][Hq][Sq]: ln sum_t exp(sm_scale q.k_t)
+  // split of the body over gridDim.z CTAs per query tile (nsplit > 1): each
+  // writes an un-normalised partial, row r = (b Hq + hq) Sq + s, and
+  // prefill_merge_kernel combines them
+  int nsplit;
+  float* part_o;      // [nsplit][rows][128]  sum_t 2^(x_t - m) v_t
+  float* part_ml;     // [nsplit][rows][2]    (m, l), x = score * sm_scale * log2(e)
 };
 
 // Byte offset of the 16-byte chunk (8 columns) c of a row of a [128][128]
@@ -357,7 +363,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   // tokens the CTA's rows can see: all of the body, or up to the last row's causal limit
   int span = len;
   if (p.causal) span = min(len, len - p.Sq + 1 + (min(row0 + kPfRows, nrows) - 1) / p.G);
-  const int ntiles = span > 0 ? (span + HKV_BLOCK_TOKENS - 1) / HKV_BLOCK_TOKENS : 0;
+  // this CTA's share of the tiles: [t0, t0 + ntiles) of split blockIdx.z; loop
+  // indices (ring slots, barrier phases) count from 0, token positions from t0
+  const int tiles_all = span > 0 ? (span + HKV_BLOCK_TOKENS - 1) / HKV_BLOCK_TOKENS : 0;
+  const int t0 = (int)(((int64_t)blockIdx.z * tiles_all) / p.nsplit);
+  const int ntiles = (int)(((int64_t)(blockIdx.z + 1) * tiles_all) / p.nsplit) - t0;
 
   if (t == 0) {
 #pragma unroll
@@ -400,8 +410,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
   if (warp >= 4) {
     // ------------- converters: raw block -> ring -> K[j & 1], Vt[j & 1]; issue S(j) -------------
     const int ct = t - 128;
-    auto load = [&](int j) {  // this thread's 16-byte chunks of raw block j into slot j & 1
-      const int tok = j * HKV_BLOCK_TOKENS;
+    auto load = [&](int j) {  // this thread's 16-byte chunks of raw block t0 + j into slot j & 1
+      const int tok = (t0 + j) * HKV_BLOCK_TOKENS;
       const int64_t page = store_page(p.body, u, tok);
       if (page >= 0) {
         const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + page * p.body.page_stride +
@@ -424,7 +434,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     for (int j = 0; j < ntiles; ++j) {
       ok = mbar_wait(&raw_full[j & 1], (j >> 1) & 1);
       if (j >= 2) ok = mbar_wait(&op_empty[j & 1], ((j >> 1) - 1) & 1) && ok;
-      const int valid = min(HKV_BLOCK_TOKENS, len - j * HKV_BLOCK_TOKENS);
+      const int valid = min(HKV_BLOCK_TOKENS, len - (t0 + j) * HKV_BLOCK_TOKENS);
       const uint8_t* rb = ring + (j & 1) * kPfRawBytes;
       pf_convert_k<FMT, GROUP>(rb, sK + (j & 1) * kPfTileBytes, ct, ct < valid);
       pf_convert_v<FMT, GROUP>(rb, sV + (j & 1) * kPfTileBytes, ct, valid);
@@ -470,7 +480,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
 #pragma unroll
       for (int c = 0; c < 4; ++c) tm_ld32_nw(ts + 32 * c, s + 32 * c);
       tm_wait_ld();
-      const int lim = lim_row - j * HKV_BLOCK_TOKENS;
+      const int lim = lim_row - (t0 + j) * HKV_BLOCK_TOKENS;
       if (lim < HKV_BLOCK_TOKENS) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
@@ -551,6 +561,25 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       have = __all_sync(0xffffffffu, w);
       tc_fence_after();
     }
+    if (p.part_o) {  // split: the un-normalised partial of this CTA's tiles
+      const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+      const int64_t row = ((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs;
+      float4* po = reinterpret_cast<float4*>(p.part_o + ((int64_t)blockIdx.z * rows + row) * HKV_D);
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        if (have) tm_ld32(tO + lane_base + c0, o);
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) po[c0 / 4 + i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        }
+      }
+      if (row_ok)
+        *reinterpret_cast<float2*>(p.part_ml + ((int64_t)blockIdx.z * rows + row) * 2) =
+            have ? make_float2(m_run, l_run) : make_float2(-1.0e30f, 0.f);
+    } else {
     const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
     const int64_t ob = (int64_t)b * p.out_sb + (int64_t)(hk * p.G + qg) * p.out_sh + (int64_t)qs * p.out_ss;
 #pragma unroll 1
@@ -588,6 +617,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     if (p.lse && row_ok)
       p.lse[((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs] =
           (have && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -595,6 +625,35 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
   }
+}
+
+// Combines the nsplit partials of each prefill row (one warp per row, lane =
+// dims 4 lane .. 4 lane + 3): O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+__global__ void __launch_bounds__(256) prefill_merge_kernel(const __grid_constant__ PrefillParams p) {
+  const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float M = -1.0e30f;
+  for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, p.part_ml[((int64_t)s * rows + row) * 2]);
+  float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < p.nsplit; ++s) {
+    const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + ((int64_t)s * rows + row) * 2);
+    const float w = ml.y > 0.f ? fast_exp2(ml.x - M) : 0.f;
+    L += w * ml.y;
+    const float4 o = *reinterpret_cast<const float4*>(p.part_o + ((int64_t)s * rows + row) * HKV_D + 4 * lane);
+    acc[0] += w * o.x;
+    acc[1] += w * o.y;
+    acc[2] += w * o.z;
+    acc[3] += w * o.w;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int64_t hs = (int64_t)p.Hq * p.Sq;
+  const int b = (int)(row / hs), hq = (int)((row - (int64_t)b * hs) / p.Sq), qs = (int)(row % p.Sq);
+  const int64_t ob = (int64_t)b * p.out_sb + (int64_t)hq * p.out_sh + (int64_t)qs * p.out_ss + 4 * lane;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) store_any(p.out, p.out_dtype, ob + i, acc[i] * inv);
+  if (p.lse && lane == 0) p.lse[row] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994531f : -INFINITY;
 }
 
 }  // namespace hkv

@@ -141,11 +141,12 @@ class DenseKV:
 _ws_cache: dict = {}
 
 
-def workspace(nbytes: int, device: torch.device, stream=None) -> torch.Tensor:
-    """A per-(device, stream) scratch buffer for split-KV partials, grown on
-    demand. Zeroed at allocation: its tail holds the per-unit merge counters,
-    which the decode kernel leaves at zero after every call."""
-    key = (device.index, (stream or torch.cuda.current_stream(device)).cuda_stream)
+def workspace(nbytes: int, device: torch.device, stream=None, kind: str = "decode") -> torch.Tensor:
+    """A per-(device, stream, kind) scratch buffer for split partials, grown on
+    demand. Zeroed at allocation: a decode workspace holds the per-unit merge
+    counters, which the decode kernel leaves at zero after every call, so the
+    prefill's partials (kind "prefill") live in a buffer of their own."""
+    key = (device.index, (stream or torch.cuda.current_stream(device)).cuda_stream, kind)
     buf = _ws_cache.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -276,14 +277,16 @@ def decode_scored(q: torch.Tensor, store: Int4KVStore, dense: Optional[DenseKV],
 def prefill_attn(q: torch.Tensor, store: Int4KVStore, sm_scale: Optional[float] = None,
                  out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None,
                  body_len: Optional[int] = None, causal: bool = False, lse: Optional[torch.Tensor] = None,
-                 stream=None) -> torch.Tensor:
+                 splits: int = 0, stream=None) -> torch.Tensor:
     """Multi-query attention of q [B, Hq, Sq, 128] over the INT4 body of each
     sequence on the tcgen05 tensor cores. Returns [B, Hq, Sq, 128].
 
     causal: the queries are the last Sq positions of the body, so query s sees
     tokens t <= len - Sq + s. lse: optional contiguous f32 [B, Hq, Sq] that
     receives ln sum_t exp(sm_scale q.k_t) per row (-inf for a row that sees no
-    token), for merging with attention over other segments."""
+    token), for merging with attention over other segments. splits: CTAs per
+    query tile sharing its body (0: chosen to fill the SMs; partials merged by
+    a second launch)."""
     _require_cuda(q)
     B, Hq, Sq, D = q.shape
     if sm_scale is None:
@@ -298,10 +301,16 @@ def prefill_attn(q: torch.Tensor, store: Int4KVStore, sm_scale: Optional[float] 
             raise ValueError("lse must be a contiguous float32 [B, Hq, Sq] tensor")
         lse_ptr = lse.data_ptr()
     st = store.struct(body_len)
-    L.check(L.load().hkv_prefill_attn(
+    lib = L.load()
+    nbytes = lib.hkv_prefill_workspace_bytes(ctypes.byref(st), B, Hq, store.kv_heads, Sq, D, int(splits)) \
+        if Sq > 0 else 0
+    ws = workspace(nbytes, q.device, stream, kind="prefill") if nbytes else None
+    L.check(lib.hkv_prefill_attn(
         q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), q.stride(2), ctypes.byref(st), B, Hq,
         store.kv_heads, Sq, D, float(sm_scale), int(bool(causal)), out.data_ptr(), dtype_code(out.dtype),
-        out.stride(0), out.stride(1), out.stride(2), lse_ptr, _stream(stream)), "hkv_prefill_attn")
+        out.stride(0), out.stride(1), out.stride(2), lse_ptr, int(splits),
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0, _stream(stream)),
+        "hkv_prefill_attn")
     return out
 
 

@@ -252,12 +252,19 @@ hkv_status hkv_tile_scores(const float* tile_stats, const float* unit_ml, const 
  * f16/bf16/f32. lse (optional, [B][Hq][Sq] f32) receives ln sum_t
  * exp(sm_scale q.k_t) (-inf for an empty row), for merging with attention over
  * other segments. Runs on the tcgen05 tensor cores: 128 (query, head) rows of
- * one KV head per CTA, the body dequantised tile by tile into shared memory. */
+ * one KV head per CTA, the body dequantised tile by tile into shared memory.
+ * splits: 0 = choose how many CTAs share each query tile's body (to fill the
+ * SMs' waves), n > 0 = use n; more than one needs a workspace of
+ * hkv_prefill_workspace_bytes (16-byte aligned; NULL or too small = fewer or
+ * no splits) for the partials, merged by a second launch on `stream`. */
+size_t hkv_prefill_workspace_bytes(const hkv_int4_store* body, int32_t B, int32_t Hq, int32_t Hkv,
+                                   int32_t Sq, int32_t D, int32_t splits);
 hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
                             int64_t q_stride_s, const hkv_int4_store* body, int32_t B, int32_t Hq,
                             int32_t Hkv, int32_t Sq, int32_t D, float sm_scale, int32_t causal, void* out,
                             int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
-                            int64_t out_stride_s, float* lse, hkv_stream_t stream);
+                            int64_t out_stride_s, float* lse, int32_t splits, void* workspace,
+                            size_t workspace_bytes, hkv_stream_t stream);
 
 /* Same attention, but stops at one un-normalised partial per (b, hq):
  * part_o [B][Hq][128] f32 = sum_t 2^(x_t - m) v_t, part_ml [B][Hq][2] f32 =
