@@ -486,9 +486,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
         for (int i = 0; i < 128; ++i)
           if (i >= lim) s[i] = -INFINITY;
       }
+      // row max: four independent chains of three-input max, two scores per step
       float mx4[4] = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-      for (int i = 4; i < 128; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], s[i]);
+      for (int i = 4; i < 128; i += 2) mx4[(i >> 1) & 3] = fmax3(mx4[(i >> 1) & 3], s[i], s[i + 1]);
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * qscale;
       // the running max moves only when a score beats it by more than 2^8; the
       // warp then waits for O(j-1) and rescales its rows (ld/st are warp-collective)
