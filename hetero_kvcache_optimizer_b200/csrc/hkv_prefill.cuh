@@ -20,7 +20,10 @@
 // S(j) is issued only after O(j-2) has completed (the converters wait for it
 // before they overwrite K/Vt[j & 1]), which also frees S[j & 1].
 // Then warps 0-3 read their rows of O, divide by the row sum, store them, and
-// optionally the natural-log sum of exponentials per row.
+// optionally the natural-log sum of exponentials per row. With a body split
+// (gridDim.z > 1, to fill the SMs' waves) each CTA takes a contiguous share of
+// the tiles and stores its un-normalised partial instead; prefill_merge_kernel
+// combines the shares.
 // Every wait is bounded (HKV_WAIT_NS) and sets the device error word on expiry;
 // each role decides to stop together (barrier AND), and an aborted CTA waits
 // (bounded) for its copies and products before it frees TMEM.
