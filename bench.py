@@ -221,8 +221,7 @@ def run_cfg2(args) -> None:
         def chunked(store=eng.stores[l], k=k, v=v):
             for t0 in range(0, body, chunk):  # chunked prefill: the body in 4,096-token chunks
                 n = min(chunk, body - t0)
-                kv.quantize_pack(k[:, :, sink + t0:sink + t0 + n], store, 0, t0)
-                kv.quantize_pack(v[:, :, sink + t0:sink + t0 + n], store, 1, t0)
+                kv.quantize_pack_kv(k[:, :, sink + t0:sink + t0 + n], v[:, :, sink + t0:sink + t0 + n], store, t0)
         torch.cuda.synchronize()
         if l == 0:
             # device time of the chunk launches: captured once, replayed (the Python

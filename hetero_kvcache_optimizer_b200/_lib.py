@@ -60,6 +60,8 @@ SIGNATURES = {
     "hkv_dequantize_flat": (c_i32, [c_vp, c_vp, c_vp, c_i64, c_i32, c_vp, c_i32, c_vp]),
     "hkv_quantize_pack": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64,
                                   c_i32, P_store, c_vp, c_i32, c_vp]),
+    "hkv_quantize_pack_kv": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, c_i64,
+                                     P_store, c_vp, c_i32, c_vp]),
     "hkv_append_kv": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i64, c_i64, P_dense, c_i32,
                               c_vp, c_vp, P_store, c_vp, c_vp]),
     "hkv_dequantize_pack": (c_i32, [P_store, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i32, c_vp]),

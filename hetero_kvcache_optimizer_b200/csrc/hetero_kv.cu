@@ -499,33 +499,54 @@ hkv_status hkv_dequantize_flat(const uint8_t* codes, const float* scales, const 
   return launch_status();
 }
 
-hkv_status hkv_quantize_pack(const void* x, int32_t dtype, int32_t B, int32_t H, int32_t T, int32_t D,
-                             int64_t stride_b, int64_t stride_h, int64_t stride_t, int32_t role,
-                             const hkv_int4_store* dst, const int32_t* dst_start, int32_t start,
-                             hkv_stream_t stream) {
+namespace {
+hkv_status quantize_pack_launch(const void* x, const void* x2, int32_t dtype, int32_t B, int32_t H, int32_t T,
+                                int32_t D, int64_t stride_b, int64_t stride_h, int64_t stride_t, int32_t role,
+                                const hkv_int4_store* dst, const int32_t* dst_start, int32_t start,
+                                cudaStream_t st) {
   if (!x || B <= 0 || H <= 0 || T < 0) return HKV_ERR_ARG;
   if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
   if (role != HKV_ROLE_K && role != HKV_ROLE_V) return HKV_ERR_ARG;
   hkv_status rc = check_store(dst);
   if (rc != HKV_OK) return rc;
-  if (!aligned16(x) || stride_b % 8 || stride_h % 8 || stride_t % 8) return HKV_ERR_ARG;
+  if (!aligned16(x) || (x2 && !aligned16(x2)) || stride_b % 8 || stride_h % 8 || stride_t % 8) return HKV_ERR_ARG;
   if (!dst_start && (start < 0 || (int64_t)start + T > (int64_t)dst->max_pages * dst->page_tokens))
     return HKV_ERR_CAPACITY;
   if (T == 0) return HKV_OK;
   const int64_t ntok = (int64_t)B * H * T;
   if (ntok >= (int64_t(1) << 31) - 64) return HKV_ERR_UNSUPPORTED;
   const int per_block = 16 * hkv::kQuantTokens;
-  const int blocks = (int)((ntok + per_block - 1) / per_block);
+  const dim3 grid((unsigned)((ntok + per_block - 1) / per_block), x2 ? 2u : 1u);
   if (dtype == HKV_DT_F16) {
-    hkv::quantize_pack_kernel<__half><<<blocks, 256, 0, S(stream)>>>(static_cast<const __half*>(x), B, H, T, stride_b,
-                                                                     stride_h, stride_t, role, *dst, dst_start, start);
+    hkv::quantize_pack_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x),
+                                                           static_cast<const __half*>(x2), B, H, T, stride_b,
+                                                           stride_h, stride_t, role, *dst, dst_start, start);
   } else if (dtype == HKV_DT_BF16) {
-    hkv::quantize_pack_kernel<__nv_bfloat16><<<blocks, 256, 0, S(stream)>>>(
-        static_cast<const __nv_bfloat16*>(x), B, H, T, stride_b, stride_h, stride_t, role, *dst, dst_start, start);
+    hkv::quantize_pack_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(x2), B, H, T, stride_b, stride_h,
+        stride_t, role, *dst, dst_start, start);
   } else {
     return HKV_ERR_ARG;
   }
   return launch_status();
+}
+}  // namespace
+
+hkv_status hkv_quantize_pack(const void* x, int32_t dtype, int32_t B, int32_t H, int32_t T, int32_t D,
+                             int64_t stride_b, int64_t stride_h, int64_t stride_t, int32_t role,
+                             const hkv_int4_store* dst, const int32_t* dst_start, int32_t start,
+                             hkv_stream_t stream) {
+  return quantize_pack_launch(x, nullptr, dtype, B, H, T, D, stride_b, stride_h, stride_t, role, dst, dst_start,
+                              start, S(stream));
+}
+
+hkv_status hkv_quantize_pack_kv(const void* k, const void* v, int32_t dtype, int32_t B, int32_t H, int32_t T,
+                                int32_t D, int64_t stride_b, int64_t stride_h, int64_t stride_t,
+                                const hkv_int4_store* dst, const int32_t* dst_start, int32_t start,
+                                hkv_stream_t stream) {
+  if (!v) return HKV_ERR_ARG;
+  return quantize_pack_launch(k, v, dtype, B, H, T, D, stride_b, stride_h, stride_t, HKV_ROLE_K, dst, dst_start,
+                              start, S(stream));
 }
 
 hkv_status hkv_append_kv(const void* k_new, const void* v_new, int32_t dtype, int32_t B, int32_t H, int32_t D,

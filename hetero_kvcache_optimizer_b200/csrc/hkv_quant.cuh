@@ -150,10 +150,13 @@ __device__ __forceinline__ void store8(T* dst, const float (&v)[8]) {
 // lanes per token. grid.x covers ceil(B*H*T / (16 * kQuantTokens)) blocks of 256.
 constexpr int kQuantTokens = 1;
 template <typename T>
-__global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict__ x, int B, int H, int T_,
-                                                            int64_t sb, int64_t sh, int64_t st, int role,
-                                                            hkv_int4_store store, const int32_t* dst_start,
-                                                            int start) {
+__global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict__ x, const T* __restrict__ x2,
+                                                            int B, int H, int T_, int64_t sb, int64_t sh,
+                                                            int64_t st, int role, hkv_int4_store store,
+                                                            const int32_t* dst_start, int start) {
+  // grid.y == 2: blockIdx.y 0 quantises x as side `role`, 1 quantises x2 as V
+  const T* __restrict__ src = blockIdx.y ? x2 : x;
+  if (blockIdx.y) role = HKV_ROLE_V;
   const int ntok = B * H * T_;  // < 2^31 (checked by the host)
   const int tok0 = (blockIdx.x * 16 + (threadIdx.x >> 4)) * kQuantTokens;
   const int p = threadIdx.x & 15;
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict_
     unit[i] = valid ? u : -1;
     pos[i] = (dst_start ? dst_start[b] : start) + t;
     if (valid) {
-      load8(x + b * sb + h * sh + (int64_t)t * st + 8 * p, v[i]);
+      load8(src + b * sb + h * sh + (int64_t)t * st + 8 * p, v[i]);
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[i][e] = 0.f;

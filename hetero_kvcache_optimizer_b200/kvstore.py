@@ -171,11 +171,32 @@ def quantize_pack(x: torch.Tensor, store: Int4KVStore, role: int,
         ctypes.byref(st), dst_start, s0, _stream(stream)), "hkv_quantize_pack")
 
 
+def quantize_pack_kv(k: torch.Tensor, v: torch.Tensor, store: Int4KVStore,
+                     start: Union[int, torch.Tensor] = 0, stream=None) -> None:
+    """quantize_pack of a K chunk and its V chunk in one launch (both [B, H, T,
+    128] of one dtype; laid out alike, else two launches). Does not touch lengths."""
+    _require_cuda(k, v)
+    if k.stride(-1) != 1:
+        k = k.contiguous()
+    if v.stride(-1) != 1:
+        v = v.contiguous()
+    if k.shape != v.shape or k.dtype != v.dtype or k.stride() != v.stride():
+        quantize_pack(k, store, L.ROLE_K, start, stream)
+        quantize_pack(v, store, L.ROLE_V, start, stream)
+        return
+    B, H, T, D = k.shape
+    st = store.struct()
+    dst_start = start.data_ptr() if isinstance(start, torch.Tensor) else None
+    s0 = 0 if isinstance(start, torch.Tensor) else int(start)
+    L.check(L.load().hkv_quantize_pack_kv(
+        k.data_ptr(), v.data_ptr(), dtype_code(k.dtype), B, H, T, D, k.stride(0), k.stride(1), k.stride(2),
+        ctypes.byref(st), dst_start, s0, _stream(stream)), "hkv_quantize_pack_kv")
+
+
 def prefill(store: Int4KVStore, k: torch.Tensor, v: torch.Tensor, start: int = 0, stream=None) -> None:
     """Quantise a [B, H, T, 128] K/V chunk into body slots [start, start+T) and
     set the (uniform) lengths to start + T."""
-    quantize_pack(k, store, L.ROLE_K, start, stream)
-    quantize_pack(v, store, L.ROLE_V, start, stream)
+    quantize_pack_kv(k, v, store, start, stream)
     store.set_lengths(start + k.shape[2])
 
 

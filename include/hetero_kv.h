@@ -157,6 +157,14 @@ hkv_status hkv_quantize_pack(const void* x, int32_t dtype, int32_t B, int32_t H,
                              int32_t role, const hkv_int4_store* dst, const int32_t* dst_start,
                              int32_t start, hkv_stream_t stream);
 
+/* hkv_quantize_pack of a K chunk and its V chunk (same dtype, shape and strides)
+ * in one launch: the chunked prefill quantises both per chunk, and at 4,096-token
+ * chunks the launch latency, not HBM, bounds two separate calls. */
+hkv_status hkv_quantize_pack_kv(const void* k, const void* v, int32_t dtype, int32_t B, int32_t H,
+                                int32_t T, int32_t D, int64_t stride_b, int64_t stride_h,
+                                int64_t stride_t, const hkv_int4_store* dst,
+                                const int32_t* dst_start, int32_t start, hkv_stream_t stream);
+
 /* One decode step of the KV cache state machine of HeteroKVManager._decode_update
  * (src/memory/manager.py:621-664), for K and V in one launch: per sequence b,
  * if the recent ring (rows [sink, capacity) of `dense`) is full, its oldest row

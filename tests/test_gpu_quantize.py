@@ -129,6 +129,32 @@ def test_quantize_pack_odd_offsets_and_paged(hkv):
         assert np.array_equal(zp[:, :, :T].reshape(-1), qz)
 
 
+@pytest.mark.parametrize("fmt,dt", [("ref", "fp16"), ("fp16min", "bf16"), ("fp16min", "fp16")])
+def test_quantize_pack_kv_one_launch(hkv, fmt, dt):
+    """K and V quantised in one launch (hkv_quantize_pack_kv), at odd start slots
+    and through a shuffled page table: the same pages, byte for byte, as one
+    hkv_quantize_pack launch per side."""
+    B, H, T = 2, 2, 700
+    k = _torch_input(ko.make_input(6, (B, H, T, 128), dt), dt)
+    v = _torch_input(ko.make_input(7, (B, H, T, 128), dt), dt)
+    npages = 2 * B * H * 3
+    perm = torch.from_numpy(np.random.default_rng(1).permutation(npages)[: B * H * 3].reshape(B * H, 3)
+                            .astype(np.int32))
+    one, two = [hkv.Int4KVStore(B, H, 768, fmt=fmt, group=32, page_tokens=256, num_pages=npages)
+                for _ in range(2)]
+    for st in (one, two):
+        st.pool.zero_()
+        st.page_table.copy_(perm)
+    for a, b in ((0, 1), (1, 130), (130, 131), (131, 700)):
+        hkv.quantize_pack_kv(k[:, :, a:b], v[:, :, a:b], one, a)
+        hkv.quantize_pack(k[:, :, a:b], two, K, a)
+        hkv.quantize_pack(v[:, :, a:b], two, V, a)
+    torch.cuda.synchronize()
+    assert torch.equal(one.pool, two.pool)
+    for role in (K, V):
+        assert np.array_equal(dequant_side(one, role, T), dequant_side(two, role, T))
+
+
 def test_quantize_pack_per_batch_start(hkv):
     B, H, T = 3, 2, 5
     x = ko.make_input(9, (B, H, T, 128), "bf16")
