@@ -131,8 +131,7 @@ class HeteroKVManager:
         if start + n > st.capacity:
             raise RuntimeError(f"INT4 body of layer {layer} is full ({st.capacity} tokens); "
                                "raise body_capacity")
-        kv.quantize_pack(k, st, 0, start)
-        kv.quantize_pack(v, st, 1, start)
+        kv.quantize_pack_kv(k, v, st, start)
         self._body_len[layer] = start + n
         st.set_lengths(start + n)
         if self.legacy_dram:

@@ -111,8 +111,7 @@ class TieredOffloadDecoder:
                     ch = torch.randperm(128, device=self.device, generator=gen)[:outlier_channels]
                     k[:, h, :, ch] *= 10.0
                 v = torch.randn(self.B, self.Hkv, n, 128, device=self.device, generator=gen)
-                kv.quantize_pack(k.half(), tmp, L.ROLE_K, t0)
-                kv.quantize_pack(v.half(), tmp, L.ROLE_V, t0)
+                kv.quantize_pack_kv(k.half(), v.half(), tmp, t0)
             pages = tmp.pool.view(U, tmp.max_pages, self.page_bytes)
             self.pool[l * U * self.resident:(l + 1) * U * self.resident] = \
                 pages[:, :self.resident].reshape(-1, self.page_bytes)
