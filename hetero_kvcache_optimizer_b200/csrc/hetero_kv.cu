@@ -354,6 +354,18 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
 
 
 // --------------------------------------------------------------------------- prefill
+// Query rows per prefill CTA: 256 (two query tiles with their own softmax warps
+// sharing each dequantised body tile, prefill2_kernel) when a unit has more than
+// 128 rows, else 128. HKV_PREFILL_ROWS=128 forces one tile per CTA (comparisons).
+int prefill_rows_per_cta(int64_t unit_rows) {
+  static const int forced = [] {
+    const char* e = std::getenv("HKV_PREFILL_ROWS");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced == hkv::kPfRows) return hkv::kPfRows;
+  return unit_rows > hkv::kPfRows ? hkv::kPf2Rows : hkv::kPfRows;
+}
+
 template <int FMT, int GROUP>
 hkv_status launch_prefill_t(const hkv::PrefillParams& p, cudaStream_t st) {
   static std::once_flag once;
@@ -361,10 +373,17 @@ hkv_status launch_prefill_t(const hkv::PrefillParams& p, cudaStream_t st) {
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(hkv::prefill_kernel<FMT, GROUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     hkv::kPfSmem);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(hkv::prefill2_kernel<FMT, GROUP>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, hkv::kPf2Smem);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
-  const dim3 grid((unsigned)cdiv((int64_t)p.Sq * p.G, hkv::kPfRows), (unsigned)(p.B * p.Hkv), (unsigned)p.nsplit);
-  hkv::prefill_kernel<FMT, GROUP><<<grid, hkv::kPfThreads, hkv::kPfSmem, st>>>(p);
+  const int rpc = prefill_rows_per_cta((int64_t)p.Sq * p.G);
+  const dim3 grid((unsigned)cdiv((int64_t)p.Sq * p.G, rpc), (unsigned)(p.B * p.Hkv), (unsigned)p.nsplit);
+  if (rpc == hkv::kPf2Rows)
+    hkv::prefill2_kernel<FMT, GROUP><<<grid, hkv::kPf2Threads, hkv::kPf2Smem, st>>>(p);
+  else
+    hkv::prefill_kernel<FMT, GROUP><<<grid, hkv::kPfThreads, hkv::kPfSmem, st>>>(p);
   hkv_status rc = launch_status();
   if (rc != HKV_OK || p.nsplit == 1) return rc;
   const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
@@ -669,7 +688,8 @@ hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stri
 size_t hkv_prefill_workspace_bytes(const hkv_int4_store* body, int32_t B, int32_t Hq, int32_t Hkv, int32_t Sq,
                                    int32_t D, int32_t splits) {
   if (check_store(body) != HKV_OK || B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || Sq <= 0 || D != HKV_D) return 0;
-  const int64_t base = cdiv((int64_t)Sq * (Hq / Hkv), hkv::kPfRows) * B * Hkv;
+  const int64_t unit_rows = (int64_t)Sq * (Hq / Hkv);
+  const int64_t base = cdiv(unit_rows, prefill_rows_per_cta(unit_rows)) * B * Hkv;
   const int64_t rows = (int64_t)B * Hq * Sq;
   const int tiles = (int)cdiv((int64_t)body->len, hkv::kTileI4);
   return prefill_ws_bytes(prefill_splits(base, tiles, rows, splits), rows);
@@ -713,7 +733,8 @@ hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, 
   p.lse = lse;
   {
     // body splits (wave quantisation): as many as the workspace holds, up to the model's choice
-    const int64_t base = cdiv((int64_t)Sq * p.G, hkv::kPfRows) * B * Hkv;
+    const int64_t unit_rows = (int64_t)Sq * p.G;
+    const int64_t base = cdiv(unit_rows, prefill_rows_per_cta(unit_rows)) * B * Hkv;
     const int64_t rows = (int64_t)B * Hq * Sq;
     int sp = prefill_splits(base, (int)cdiv((int64_t)body->len, hkv::kTileI4), rows, splits);
     while (sp > 1 && (!workspace || prefill_ws_bytes(sp, rows) > workspace_bytes)) --sp;

@@ -347,6 +347,70 @@ __device__ __forceinline__ void pf_convert_v(const uint8_t* rb, uint8_t* sVt, in
   }
 }
 
+// One query row's result, read from this thread's lane of the O accumulator
+// (tO_lane; `have`: O holds data, warp-uniform): the normalised output and lse,
+// or with a body split the un-normalised partial (O, m, l) of this CTA's tiles.
+__device__ __forceinline__ void pf_store_row(const PrefillParams& p, uint32_t tO_lane, bool have, bool row_ok,
+                                             int b, int hk, int qg, int qs, float m_run, float l_run) {
+  if (p.part_o) {  // split: the un-normalised partial of this CTA's tiles
+    const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
+    const int64_t row = ((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs;
+    float4* po = reinterpret_cast<float4*>(p.part_o + ((int64_t)blockIdx.z * rows + row) * HKV_D);
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+      float o[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      if (have) tm_ld32(tO_lane + c0, o);
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) po[c0 / 4 + i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      }
+    }
+    if (row_ok)
+      *reinterpret_cast<float2*>(p.part_ml + ((int64_t)blockIdx.z * rows + row) * 2) =
+          have ? make_float2(m_run, l_run) : make_float2(-1.0e30f, 0.f);
+  } else {
+    const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
+    const int64_t ob = (int64_t)b * p.out_sb + (int64_t)(hk * p.G + qg) * p.out_sh + (int64_t)qs * p.out_ss;
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += 32) {
+      float o[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      if (have) tm_ld32(tO_lane + c0, o);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] *= inv;
+      if (!row_ok) continue;
+      if (p.out_vec && p.out_dtype == HKV_DT_F32) {
+        float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.out) + ob + c0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      } else if (p.out_vec && p.out_dtype == HKV_DT_F16) {
+        uint4* d = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + ob + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d[i] = make_uint4(pack2<__half>(o[8 * i], o[8 * i + 1]), pack2<__half>(o[8 * i + 2], o[8 * i + 3]),
+                            pack2<__half>(o[8 * i + 4], o[8 * i + 5]), pack2<__half>(o[8 * i + 6], o[8 * i + 7]));
+      } else if (p.out_vec && p.out_dtype == HKV_DT_BF16) {
+        uint4* d = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + ob + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d[i] = make_uint4(pack2<__nv_bfloat16>(o[8 * i], o[8 * i + 1]),
+                            pack2<__nv_bfloat16>(o[8 * i + 2], o[8 * i + 3]),
+                            pack2<__nv_bfloat16>(o[8 * i + 4], o[8 * i + 5]),
+                            pack2<__nv_bfloat16>(o[8 * i + 6], o[8 * i + 7]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) store_any(p.out, p.out_dtype, ob + c0 + i, o[i]);
+      }
+    }
+    if (p.lse && row_ok)
+      p.lse[((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs] =
+          (have && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
+  }
+}
+
 template <int FMT, int GROUP>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p) {
   extern __shared__ __align__(1024) uint8_t pf_raw[];
@@ -565,63 +629,298 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       have = __all_sync(0xffffffffu, w);
       tc_fence_after();
     }
-    if (p.part_o) {  // split: the un-normalised partial of this CTA's tiles
-      const int64_t rows = (int64_t)p.B * p.Hq * p.Sq;
-      const int64_t row = ((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs;
-      float4* po = reinterpret_cast<float4*>(p.part_o + ((int64_t)blockIdx.z * rows + row) * HKV_D);
+    pf_store_row(p, tO + lane_base, have, row_ok, b, hk, qg, qs, m_run, l_run);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Two query tiles per CTA, each with its own softmax warps (prefill2_kernel):
+// rows [row0, row0 + 128) are tile A (softmax warps 0-3), [row0 + 128, row0 + 256)
+// tile B (warps 4-7); both read the same dequantised K and V tiles (converter
+// warps 8-11), so the dequantisation is paid once per 256 rows while the two
+// softmax groups run side by side. TMEM: S_A, S_B, O_A, O_B (128 columns each).
+// One raw slot, whose K half and V half are refilled as soon as each half has
+// been converted. Per body tile j: the converters' first thread issues S_X(j)
+// once O_X(j-1) has completed (P_X(j-1) lives in S_X's columns); group X's first
+// thread issues O_X(j) after its softmax. S_X(j) lands only after O_X(j-1) has
+// completed, so a rescale of O_X needs no wait. Twelve warps leave 168 registers
+// a thread, so the softmax reads S twice (row max, then P).
+
+// Global 16-byte chunk that chunk `idx` of side `role`'s share of a page block
+// is: the side's 512 code chunks, then its metadata (fp16min: scales + mins,
+// 32·NG chunks; ref: fp32 scales 32·NG chunks + zero points 8·NG chunks).
+template <int FMT, int GROUP>
+__device__ __forceinline__ int pf_side_chunk(int role, int idx) {
+  constexpr int NG = HKV_D / GROUP;
+  if (idx < 512) return role * 512 + idx;
+  const int m = idx - 512;
+  if (FMT == HKV_FMT_FP16MIN || m < 32 * NG) return 1024 + role * 32 * NG + m;
+  return 1024 + 64 * NG + role * 8 * NG + (m - 32 * NG);
+}
+template <int FMT, int GROUP>
+constexpr int pf_side_chunks() {
+  return 512 + (FMT == HKV_FMT_FP16MIN ? 32 : 40) * (HKV_D / GROUP);
+}
+
+constexpr int kPf2Rows = 2 * kPfRows;
+constexpr int kPf2Threads = 384;  // softmax A warps 0-3 | softmax B warps 4-7 | converters 8-11
+constexpr int kPf2Smem = 6 * kPfTileBytes + kPfRawBytes + 1024;  // Q_A | Q_B | K[2] | Vt[2] | raw | alignment
+
+template <int FMT, int GROUP>
+__global__ void __launch_bounds__(kPf2Threads, 1) prefill2_kernel(const __grid_constant__ PrefillParams p) {
+  extern __shared__ __align__(1024) uint8_t pf_raw[];
+  // raw_full[side]: the side's half of tile j landed (one phase per tile)
+  // k_full / vt_full[j & 1]: K(j) / Vt(j) written; kfree / vfree[j & 1]: the
+  // products reading K[j & 1] / Vt[j & 1] have completed; s_full[X]: S_X(j)
+  // done; o_done[X]: O_X(j) done
+  __shared__ __align__(8) uint64_t raw_full[2], kfree[2], vfree[2], vt_full[2], s_full[2], o_done[2], drain_bar[3];
+  __shared__ uint32_t s_tmem;
+  uint8_t* sm = pf_raw + ((1024u - (smem_u32(pf_raw) & 1023u)) & 1023u);  // swizzle atoms need 1 KiB alignment
+  uint8_t* sQ = sm;                     // Q_A, Q_B
+  uint8_t* sK = sm + 2 * kPfTileBytes;  // K[0], K[1]
+  uint8_t* sV = sm + 4 * kPfTileBytes;  // Vt[0], Vt[1]
+  uint8_t* raw = sm + 6 * kPfTileBytes;
+  const int t = threadIdx.x, warp = t >> 5;
+  const int u = blockIdx.y, b = u / p.Hkv, hk = u - b * p.Hkv;
+  const int row0 = blockIdx.x * kPf2Rows, nrows = p.Sq * p.G;
+  constexpr uint32_t kBlock = block_bytes(FMT, GROUP);
+  static_assert(16 * (2 * pf_side_chunks<FMT, GROUP>()) == (int)kBlock, "the two sides cover the block");
+
+  const int len = max(0, p.body.lengths ? p.body.lengths[b] : p.body.len);
+  int span = len;
+  if (p.causal) span = min(len, len - p.Sq + 1 + (min(row0 + kPf2Rows, nrows) - 1) / p.G);
+  const int tiles_all = span > 0 ? (span + HKV_BLOCK_TOKENS - 1) / HKV_BLOCK_TOKENS : 0;
+  const int t0 = (int)(((int64_t)blockIdx.z * tiles_all) / p.nsplit);
+  const int ntiles = (int)(((int64_t)(blockIdx.z + 1) * tiles_all) / p.nsplit) - t0;
+
+  if (t == 0) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&raw_full[i], 128);  // one cp.async arrival per converter thread
+      mbar_init(&kfree[i], 1);
+      mbar_init(&vfree[i], 2);  // one commit from each softmax group's O issuer
+      mbar_init(&vt_full[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&drain_bar[i], 1);
+    }
+    mbar_init(&drain_bar[2], 1);  // drain barriers: 0 softmax A, 1 converters, 2 softmax B
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&s_tmem)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  for (int c = t; c < kPf2Rows * 16; c += kPf2Threads) {
+    const int i = c >> 4, ch = c & 15, r = row0 + i;
+    uint32_t o[4] = {0u, 0u, 0u, 0u};
+    if (r < nrows) {
+      const int qs = r / p.G, qg = r - qs * p.G;
+      const int64_t base =
+          (int64_t)b * p.q_sb + (int64_t)(hk * p.G + qg) * p.q_sh + (int64_t)qs * p.q_ss + 8 * ch;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o[e] = h2u(__floats2half2_rn(load_any(p.q, p.q_dtype, base + 2 * e),
+                                     load_any(p.q, p.q_dtype, base + 2 * e + 1)));
+    }
+    *reinterpret_cast<uint4*>(sQ + (i >> 7) * kPfTileBytes + pf_chunk(i & 127, ch)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;  // S_A 0, S_B 128, O_A 256, O_B 384
+
+  if (warp >= 8) {
+    // ---------------- converters; their first thread issues S_A(j) and S_B(j) ----------------
+    const int ct = t - 256;
+    auto load = [&](int j, int role) {  // this thread's chunks of side `role` of raw block t0 + j
+      const int tok = (t0 + j) * HKV_BLOCK_TOKENS;
+      const int64_t page = store_page(p.body, u, tok);
+      if (page >= 0) {
+        const uint8_t* src = static_cast<const uint8_t*>(p.body.pages) + page * p.body.page_stride +
+                             (int64_t)((tok % p.body.page_tokens) / HKV_BLOCK_TOKENS) * kBlock;
+#pragma unroll
+        for (int n = 0; n < (pf_side_chunks<FMT, GROUP>() + 127) / 128; ++n) {
+          const int idx = ct + 128 * n;
+          if (idx < pf_side_chunks<FMT, GROUP>()) {
+            const int gc = pf_side_chunk<FMT, GROUP>(role, idx);
+            cp_async16(raw + pf_ring_off(gc), src + 16 * gc);
+          }
+        }
+      } else if (ct == 0 && role == 0) {
+        hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+      }
+      cp_async_arrive(&raw_full[role]);
+    };
+    if (ntiles > 0) {
+      load(0, 0);
+      load(0, 1);
+    }
+    bool ok = true;
+    int n_s = 0;
+    const uint32_t q0 = smem_u32(sQ);
+    for (int j = 0; j < ntiles; ++j) {
+      const int valid = min(HKV_BLOCK_TOKENS, len - (t0 + j) * HKV_BLOCK_TOKENS);
+      // K(j)
+      ok = mbar_wait(&raw_full[0], j & 1) && ok;
+      if (j >= 2) ok = mbar_wait(&kfree[j & 1], ((j >> 1) - 1) & 1) && ok;
+      pf_convert_k<FMT, GROUP>(raw, sK + (j & 1) * kPfTileBytes, ct, ct < valid);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      ok = bar_and(2, 128, ok);
+      if (!ok) break;
+      if (j + 1 < ntiles) load(j + 1, 0);  // the raw K half is read: fetch the next one
+      if (ct == 0) {
+        const uint32_t k0 = smem_u32(sK + (j & 1) * kPfTileBytes);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (j > 0) ok = mbar_wait(&o_done[x], (j - 1) & 1) && ok;  // O_X(j-1) read P_X(j-1) from S_X
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            pf_mma(tmem + 128 * x, pf_desc(q0 + x * kPfTileBytes + off), pf_desc(k0 + off), kk > 0);
+          }
+          pf_commit(&s_full[x]);
+        }
+        pf_commit(&kfree[j & 1]);
+        ++n_s;
+      }
+      // V(j)
+      ok = mbar_wait(&raw_full[1], j & 1) && ok;
+      if (j >= 2) ok = mbar_wait(&vfree[j & 1], ((j >> 1) - 1) & 1) && ok;
+      pf_convert_v<FMT, GROUP>(raw, sV + (j & 1) * kPfTileBytes, ct, valid);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      ok = bar_and(2, 128, ok);
+      if (!ok) break;
+      if (j + 1 < ntiles) load(j + 1, 1);
+      if (ct == 0) mbar_arrive(&vt_full[j & 1]);  // Vt(j) is written: hand it to the O issuer
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (!ok && ct == 0 && n_s > 0) {  // the products already issued finish before TMEM is freed
+      pf_commit(&drain_bar[1]);
+      mbar_wait(&drain_bar[1], 0);
+    }
+  } else {
+    // ---------------- softmax group x (warps 4x .. 4x + 3): thread = row of tile x; issue O_x(j) ----------------
+    const int x = warp >> 2, st = t - 128 * x;  // group, thread in group
+    const int bar_id = 1 + 2 * x;              // named barriers 1 (A) and 3 (B); 2 is the converters'
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t ts = tmem + 128 * x + lane_base, to = tmem + 256 + 128 * x + lane_base;
+    const int r = row0 + 128 * x + st;
+    const bool row_ok = r < nrows;
+    const int qs = row_ok ? r / p.G : 0, qg = row_ok ? r - qs * p.G : 0;
+    const int lim_row = p.causal ? min(len, len - p.Sq + 1 + qs) : len;  // tokens this row sees
+    const float qscale = p.qscale;
+    float m_run = -1.0e30f, l_run = 0.f;
+    bool ok = true;
+    int n_o = 0;
+    for (int j = 0; j < ntiles; ++j) {
+      ok = mbar_wait(&s_full[x], j & 1) && ok;
+      tc_fence_after();
+      const int lim = lim_row - (t0 + j) * HKV_BLOCK_TOKENS;  // columns at or past lim are masked
+      // pass 1: the row max, 64 columns at a time
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float a[64];
+        tm_ld32_nw(ts + 64 * h, a);
+        tm_ld32_nw(ts + 64 * h + 32, a + 32);
+        tm_wait_ld();
+        if (lim < 64 * (h + 1)) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (64 * h + i >= lim) a[i] = -INFINITY;
+        }
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) mx4[(i >> 1) & 3] = fmax3(mx4[(i >> 1) & 3], a[i], a[i + 1]);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * qscale;
+      // lazy max: rescale this row's O only when a score beats the max by 2^8
+      // (O_x(j-1) has completed: S_x(j) was issued after it)
+      const bool move = mx > m_run + kPfLazy;
+      if (__any_sync(0xffffffffu, move)) {
+        const float nm = move ? mx : m_run;
+        const float a = fast_exp2(m_run - nm);
+        if (j > 0) {
 #pragma unroll 1
-      for (int c0 = 0; c0 < 128; c0 += 32) {
-        float o[32];
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tm_ld32(to + 32 * c, o);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
-        if (have) tm_ld32(tO + lane_base + c0, o);
-        if (row_ok) {
+            for (int i = 0; i < 32; ++i) o[i] *= a;
+            tm_st32(to + 32 * c, o);
+          }
+        }
+        l_run *= a;
+        m_run = nm;
+      }
+      // pass 2: P = 2^(s * qscale - m) as f16 pairs over the first 64 columns,
+      // 32 columns at a time (chunk c's P lands on columns already read)
+      const float2 qs2 = make_float2(qscale, qscale), nm2 = make_float2(-m_run, -m_run);
+      float2 lsum = make_float2(0.f, 0.f);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float a[32];
+        tm_ld32_nw(ts + 32 * c, a);
+        tm_wait_ld();
+        if (lim < 32 * (c + 1)) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) po[c0 / 4 + i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          for (int i = 0; i < 32; ++i)
+            if (32 * c + i >= lim) a[i] = -INFINITY;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float2 xx = __ffma2_rn(make_float2(a[2 * i], a[2 * i + 1]), qs2, nm2);
+          xx.x = fast_exp2(xx.x);
+          xx.y = fast_exp2(xx.y);
+          lsum = __fadd2_rn(lsum, xx);
+          pk[i] = h2u(__floats2half2_rn(xx.x, xx.y));
+        }
+        tm_st16u(ts + 16 * c, pk);
+      }
+      l_run += lsum.x + lsum.y;
+      tm_wait_st();
+      tc_fence_before();
+      ok = bar_and(bar_id, 128, ok);  // P_x(j) (and any rescale of O_x) written by the group's 128 rows
+      if (!ok) break;
+      if (st == 0) {
+        // a failed wait skips the product; the next barrier (or the one below) stops the group
+        ok = mbar_wait(&vt_full[j & 1], (j >> 1) & 1);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t v0 = smem_u32(sV + (j & 1) * kPfTileBytes), pa = tmem + 128 * x;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            pf_mma_ts(tmem + 256 + 128 * x, pa + 8 * kk, pf_desc(v0 + off), (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          pf_commit(&o_done[x]);
+          pf_commit(&vfree[j & 1]);
+          ++n_o;
         }
       }
-      if (row_ok)
-        *reinterpret_cast<float2*>(p.part_ml + ((int64_t)blockIdx.z * rows + row) * 2) =
-            have ? make_float2(m_run, l_run) : make_float2(-1.0e30f, 0.f);
-    } else {
-    const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
-    const int64_t ob = (int64_t)b * p.out_sb + (int64_t)(hk * p.G + qg) * p.out_sh + (int64_t)qs * p.out_ss;
-#pragma unroll 1
-    for (int c0 = 0; c0 < 128; c0 += 32) {
-      float o[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = 0.f;
-      if (have) tm_ld32(tO + lane_base + c0, o);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] *= inv;
-      if (!row_ok) continue;
-      if (p.out_vec && p.out_dtype == HKV_DT_F32) {
-        float4* d = reinterpret_cast<float4*>(static_cast<float*>(p.out) + ob + c0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-      } else if (p.out_vec && p.out_dtype == HKV_DT_F16) {
-        uint4* d = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + ob + c0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          d[i] = make_uint4(pack2<__half>(o[8 * i], o[8 * i + 1]), pack2<__half>(o[8 * i + 2], o[8 * i + 3]),
-                            pack2<__half>(o[8 * i + 4], o[8 * i + 5]), pack2<__half>(o[8 * i + 6], o[8 * i + 7]));
-      } else if (p.out_vec && p.out_dtype == HKV_DT_BF16) {
-        uint4* d = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + ob + c0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          d[i] = make_uint4(pack2<__nv_bfloat16>(o[8 * i], o[8 * i + 1]),
-                            pack2<__nv_bfloat16>(o[8 * i + 2], o[8 * i + 3]),
-                            pack2<__nv_bfloat16>(o[8 * i + 4], o[8 * i + 5]),
-                            pack2<__nv_bfloat16>(o[8 * i + 6], o[8 * i + 7]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) store_any(p.out, p.out_dtype, ob + c0 + i, o[i]);
-      }
     }
-    if (p.lse && row_ok)
-      p.lse[((int64_t)b * p.Hq + hk * p.G + qg) * p.Sq + qs] =
-          (have && l_run > 0.f) ? (m_run + __log2f(l_run)) * 0.69314718055994531f : -INFINITY;
+    ok = bar_and(bar_id, 128, ok);
+    if (!ok && st == 0 && n_o > 0) {  // the products already issued finish before TMEM is freed
+      pf_commit(&drain_bar[2 * x]);
+      mbar_wait(&drain_bar[2 * x], 0);
     }
+    bool have = ok && ntiles > 0;
+    if (have) {
+      const bool w = mbar_wait(&o_done[x], (ntiles - 1) & 1);
+      have = __all_sync(0xffffffffu, w);
+      tc_fence_after();
+    }
+    pf_store_row(p, to, have, row_ok, b, hk, qg, qs, m_run, l_run);
   }
   tc_fence_before();
   __syncthreads();
