@@ -331,6 +331,12 @@ def run_prefill(args) -> None:
     clocks = sampler.stop()
     ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
     flops = 4.0 * B * Hq * Sq * S * 128
+    # launches per step: the attention kernel, plus the merge when the library splits the body
+    import ctypes
+    pst = store.struct()
+    split = _lib.load().hkv_prefill_workspace_bytes(ctypes.byref(pst), B, Hq, Hkv, Sq, 128, 0) > 0
+    kname = ("prefill2_kernel (two query tiles per CTA)" if Sq * (Hq // Hkv) > 128 else "prefill_kernel") + \
+        (" + prefill_merge_kernel (body split)" if split else "")
     tflops = flops / (ms * 1e-3) / 1e12
     peak, kind = measured_tensor_peak(sustained=False)
 
@@ -382,13 +388,13 @@ def run_prefill(args) -> None:
                    "l2": "flushed (256 MB write) before every timed launch"},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(tflops / peak, 4), "traffic": None,
-                     "kernel": "prefill_kernel (one launch per step)", "flops_per_launch": flops,
+                     "kernel": kname, "flops_per_launch": flops,
                      "peak_kind": f"{kind} (cuBLAS bf16 burst)"},
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": qh.numel() * qh.element_size(),
                 "d2h_bytes_per_step": oh.numel() * oh.element_size(), "ms_per_step": round(e2e_ms, 4),
                 "api": "kvstore.prefill_attn (pinned host q in, bf16 out back to pinned host)"},
-        "gpu_launches": args.steps, "clocks": clocks,
+        "gpu_launches": args.steps * (2 if split else 1), "clocks": clocks,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
