@@ -136,10 +136,11 @@ hkv_status static_scratch(void** out) {
 
 // --------------------------------------------------------------------------- decode plan
 constexpr int kDynSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in, static barriers aside)
-// Schedule charge per segment start, in 128-byte steps: 160 KiB, about 8 fp16min
-// group-32 tiles (tuned on config 1; overridable at build time for sweeps).
+// Schedule charge per segment start, in 128-byte steps: 120 KiB, about 6 fp16min
+// group-32 tiles (swept on config 1: 640-960 best within 0.3 %, 1,600 and 2,048
+// 1-2.5 % slower; overridable at build time for sweeps).
 #ifndef HKV_PIECE_STEPS
-#define HKV_PIECE_STEPS 1280
+#define HKV_PIECE_STEPS 960
 #endif
 constexpr int64_t kPieceSteps = HKV_PIECE_STEPS;
 
