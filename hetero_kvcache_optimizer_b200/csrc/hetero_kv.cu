@@ -749,6 +749,8 @@ hkv_status hkv_prefill_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, 
     const int64_t e = out_dtype == HKV_DT_F32 ? 4 : 8;  // elements per 16 bytes
     p.out_vec = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && out_stride_b % e == 0 && out_stride_h % e == 0 &&
                 out_stride_s % e == 0;
+    p.q_vec = (reinterpret_cast<uintptr_t>(q) % 16 == 0) && q_stride_b % 8 == 0 && q_stride_h % 8 == 0 &&
+              q_stride_s % 8 == 0;
   }
   if (body->format == HKV_FMT_REF) return launch_prefill_f<HKV_FMT_REF>(p, body->group, S(stream));
   return launch_prefill_f<HKV_FMT_FP16MIN>(p, body->group, S(stream));

@@ -50,6 +50,7 @@ struct PrefillParams {
   void* out;          // [B][Hq][Sq][128]
   int out_dtype;
   int out_vec;        // out 16-byte aligned with strides in 16-byte units
+  int q_vec;          // q 16-byte aligned with strides in 16-byte units (one vector load per 8 values)
   int64_t out_sb, out_sh, out_ss;
   float* lse;         // optional [B][Hq][Sq]: ln sum_t exp(sm_scale q.k_t)
   // split of the body over gridDim.z CTAs per query tile (nsplit > 1): each
@@ -212,6 +213,25 @@ __device__ __forceinline__ void vload_h2(const uint8_t* p, __half2 (&v)[N]) {
   } else {
     v[0] = u2h_(*reinterpret_cast<const uint32_t*>(p));
   }
+}
+
+// Eight query values from element `base` of q as four f16 pairs (bf16 converted).
+__device__ __forceinline__ void pf_load_q8(const PrefillParams& p, int64_t base, uint32_t (&o)[4]) {
+  if (p.q_vec) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + base));
+    if (p.q_dtype == HKV_DT_F16) {
+      o[0] = r.x, o[1] = r.y, o[2] = r.z, o[3] = r.w;
+    } else {
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o[e] = h2u(__float22half2_rn(__bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[e]))));
+    }
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    o[e] = h2u(__floats2half2_rn(load_any(p.q, p.q_dtype, base + 2 * e), load_any(p.q, p.q_dtype, base + 2 * e + 1)));
 }
 
 // Ring layout of a raw block: the page block as stored, except that the four
@@ -461,10 +481,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_kernel(const __grid_con
       const int qs = r / p.G, qg = r - qs * p.G;
       const int64_t base =
           (int64_t)b * p.q_sb + (int64_t)(hk * p.G + qg) * p.q_sh + (int64_t)qs * p.q_ss + 8 * ch;
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        o[e] = h2u(__floats2half2_rn(load_any(p.q, p.q_dtype, base + 2 * e),
-                                     load_any(p.q, p.q_dtype, base + 2 * e + 1)));
+      pf_load_q8(p, base, o);
     }
     *reinterpret_cast<uint4*>(sQ + pf_chunk(i, ch)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -724,10 +741,7 @@ __global__ void __launch_bounds__(kPf2Threads, 1) prefill2_kernel(const __grid_c
       const int qs = r / p.G, qg = r - qs * p.G;
       const int64_t base =
           (int64_t)b * p.q_sb + (int64_t)(hk * p.G + qg) * p.q_sh + (int64_t)qs * p.q_ss + 8 * ch;
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        o[e] = h2u(__floats2half2_rn(load_any(p.q, p.q_dtype, base + 2 * e),
-                                     load_any(p.q, p.q_dtype, base + 2 * e + 1)));
+      pf_load_q8(p, base, o);
     }
     *reinterpret_cast<uint4*>(sQ + (i >> 7) * kPfTileBytes + pf_chunk(i & 127, ch)) = make_uint4(o[0], o[1], o[2], o[3]);
   }

@@ -220,3 +220,18 @@ def test_split_chosen_for_waves(hkv):
     # each split keeps its own running max, so P rounds to f16 differently
     assert ko.rel_err(auto.cpu().numpy(), one.cpu().numpy()) < 5e-4
     assert L.device_error() == 0
+
+
+def test_unaligned_query_rows(hkv):
+    """q rows that are not 16-byte aligned (a view one element into a wider
+    buffer) take the element-wise load path: same attention as the oracle."""
+    B, Hkv, G, Sq, S = 1, 2, 4, 70, 400
+    k, v = ko.make_kv(97, B, Hkv, S)
+    store = _store(hkv, k, v, fmt="fp16min", group=32)
+    wide = torch.from_numpy(ko.rng_for(97).standard_normal((B, Hkv * G, Sq, 130), dtype=np.float32))
+    wide = wide.to("cuda", torch.bfloat16)
+    qt = wide[..., 1:129]  # element strides (.., 130, 1), data pointer 2 bytes past an aligned one
+    assert qt.data_ptr() % 16 != 0
+    ref = ko.prefill_attention(qt.float().cpu().numpy(), dequant_side(store, K, S), dequant_side(store, V, S))
+    out = hkv.prefill_attn(qt, store).cpu().numpy()
+    assert ko.rel_err(out, ref) < TOL
