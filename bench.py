@@ -169,8 +169,11 @@ def run_cpu_reference(steps: int, warmup: int, fmt_bytes_fn, sample_batch: int =
     nbytes = fmt_bytes_fn(sample_batch, body + 1)
     return {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"1 of 32 layers, {sample_batch} of 8 sequences, {len(times)} decode steps "
-                      f"(append-compress + dequant + SDPA, reference torch CPU path); "
-                      f"{sec * 1e3:.0f} ms per layer-step",
+                      f"(append-compress + dequant + SDPA, reference torch CPU path, pinned to the "
+                      f"reference's goldens by tests/test_ref_port.py); {sec * 1e3:.0f} ms per layer-step; "
+                      f"GB/s = the GPU workload's algorithmic bytes for the same tokens "
+                      f"({nbytes / (sample_batch * (body + 1)):.1f} B per body token, packed format) "
+                      f"/ time, a normalisation, not the CPU's own traffic (it reads 1 B per code)",
             "ms_per_layer_step": sec * 1e3}
 
 

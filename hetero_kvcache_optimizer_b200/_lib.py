@@ -37,7 +37,7 @@ P_i32 = ctypes.POINTER(ctypes.c_int32)
 class HkvInt4Store(ctypes.Structure):
     _fields_ = [("pages", c_vp), ("page_stride", c_i64), ("format", c_i32), ("group", c_i32),
                 ("page_tokens", c_i32), ("max_pages", c_i32), ("page_table", c_vp),
-                ("lengths", c_vp), ("len", c_i32), ("reserved", c_i32)]
+                ("lengths", c_vp), ("len", c_i32), ("num_pages", c_i32)]
 
 
 class HkvDenseKV(ctypes.Structure):
@@ -88,6 +88,8 @@ SIGNATURES = {
     "hkv_prefetch_submit": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, c_vp]),
     "hkv_prefetch_bytes": (c_i64, [c_vp]),
     "hkv_event_wait": (c_i32, [c_vp, c_i64]),
+    "hkv_qk_scores_flat": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
+    "hkv_selftest_bounded_wait": (c_i32, [c_i64, c_i32, c_vp]),
 }
 
 _lib = None
@@ -133,8 +135,23 @@ def check(status: int, what: str = "") -> None:
         raise HkvError(status, what)
 
 
+# Called with the error bits whenever device_error() sees a bounded wait that
+# expired: a decode kernel that gave up leaves merge counters non-zero in its
+# workspace, so the owners of cached workspaces re-zero them here.
+_timeout_hooks = []
+
+
+def on_device_timeout(fn) -> None:
+    if fn not in _timeout_hooks:
+        _timeout_hooks.append(fn)
+
+
 def device_error(clear: bool = True) -> int:
-    """Sticky device error bits (synchronises the device)."""
+    """Sticky device error bits (synchronises the device). A timeout bit also
+    runs the registered workspace-reset hooks."""
     bits = c_u32(0)
     check(load().hkv_device_error(ctypes.byref(bits), 1 if clear else 0), "hkv_device_error")
+    if bits.value & DEVERR_TIMEOUT:
+        for fn in _timeout_hooks:
+            fn()
     return int(bits.value)

@@ -115,20 +115,43 @@ hkv_status check_dense(const hkv_dense_kv* d) {
   return HKV_OK;
 }
 
-// Address of g_hkv_decode_scratch on the current device, looked up once per device.
+// The calling thread's current driver context (cuCtxGetCurrent through the
+// runtime's entry-point query: no link dependency on libcuda), or nullptr.
+CUcontext current_context() {
+  typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(f);
+  });
+  CUcontext c = nullptr;
+  if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
+
+// Address of g_hkv_decode_scratch on the current device, looked up on the first
+// call per device and again whenever the device's current context differs from
+// the one the address was taken in (a cudaDeviceReset loads the module anew).
 hkv_status static_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {nullptr};
+  static CUcontext ctx[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
   if (dev < 0 || dev >= 64) return HKV_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> g(mu);
-  if (!addr[dev]) {
+  const CUcontext cur = current_context();
+  if (!addr[dev] || cur != ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_hkv_decode_scratch);
     if (e != cudaSuccess) return cuda_fail(e);
     addr[dev] = p;
+    ctx[dev] = current_context();  // the lookup makes the primary context current
   }
   *out = addr[dev];
   return HKV_OK;
@@ -417,6 +440,51 @@ int prefill_splits(int64_t base_ctas, int tiles, int64_t rows, int forced) {
 }
 inline size_t prefill_ws_bytes(int splits, int64_t rows) {
   return splits > 1 ? (size_t)splits * (size_t)rows * (HKV_D + 2) * sizeof(float) : 0;
+}
+
+// --------------------------------------------------------------------------- small kernels
+// Bounded-wait self-test: one warp initialises an mbarrier that expects one
+// arrival, lane 0 arrives only when `arrive` is set, and every lane waits on
+// the phase with a limit of limit_ns. Without the arrival the wait gives up,
+// flags HKV_DEVERR_TIMEOUT and the kernel returns normally: the same bounded
+// wait the decode and prefill kernels use, made to run out on purpose without
+// a fault or a hang.
+__device__ int g_hkv_selftest_completed;
+__global__ void __launch_bounds__(32) selftest_wait_kernel(uint64_t limit_ns, int arrive) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (arrive && threadIdx.x == 0) mbar_arrive(&bar);
+  __syncwarp();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_limit(&bar, 0, 0, limit_ns));
+  if (threadIdx.x == 0) g_hkv_selftest_completed = ok ? 1 : 0;
+}
+
+// Pre-softmax scores of one query row against S INT4 keys in the reference's
+// unpacked layout (one code per byte, flat fp32 scales / u8 zero-points over
+// groups of `group` values): out[s] = sum_d q[d] (c[s][d] - z) * scale, fp32,
+// one warp per key.
+template <typename QT>
+__global__ void __launch_bounds__(256) qk_scores_flat_kernel(const QT* __restrict__ q, const uint8_t* __restrict__ c,
+                                                            const float* __restrict__ sc,
+                                                            const uint8_t* __restrict__ zp, int64_t S, int D,
+                                                            int group, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < S; s += nw) {
+    float acc = 0.f;
+    for (int d = lane; d < D; d += 32) {
+      const int64_t i = s * D + d;
+      const int64_t g = i / group;
+      acc = fmaf(to_f32(q[d]), (static_cast<float>(c[i]) - static_cast<float>(zp[g])) * sc[g], acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[s] = acc;
+  }
 }
 
 template <int FMT>
@@ -780,9 +848,11 @@ hkv_status hkv_decode_attn_static(const void* q, int32_t q_dtype, int64_t q_stri
                                   int32_t Hkv, int32_t D, float sm_scale, int32_t ctas, void* out, int32_t out_dtype,
                                   int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream) {
   if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
-  // size the request on the host first: an oversized one fails before any CUDA call
+  // validate and size the request on the host first: an invalid or oversized one
+  // fails before any CUDA call (nothing queued on the stream)
   hkv_status rc = check_decode_args(q, q_dtype, body, dense, B, Hq, Hkv, D);
   if (rc != HKV_OK) return rc;
+  if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
   Plan pl;
   if ((rc = make_plan(B, Hq, Hkv, body, dense, ctas, &pl)) != HKV_OK) return rc;
   if (pl.ws_bytes > HKV_STATIC_SCRATCH_BYTES) return HKV_ERR_CAPACITY;
@@ -816,6 +886,43 @@ hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, i
   mp.out_sh = out_stride_h;
   hkv::lse_merge_kernel<<<B * Hq, 128, 0, S(stream)>>>(mp);
   return launch_status();
+}
+
+hkv_status hkv_qk_scores_flat(const void* q, int32_t q_dtype, const uint8_t* codes, const float* scales,
+                              const uint8_t* zps, int64_t n_keys, int32_t D, int32_t group, float* out,
+                              hkv_stream_t stream) {
+  if (!q || !codes || !scales || !zps || !out || n_keys < 0 || D <= 0 || group <= 0) return HKV_ERR_ARG;
+  if (n_keys == 0) return HKV_OK;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((n_keys + 7) / 8, (int64_t)device_sms() * 16));
+  switch (q_dtype) {
+    case HKV_DT_F16:
+      qk_scores_flat_kernel<__half><<<blocks, 256, 0, S(stream)>>>(static_cast<const __half*>(q), codes, scales,
+                                                                   zps, n_keys, D, group, out);
+      break;
+    case HKV_DT_BF16:
+      qk_scores_flat_kernel<__nv_bfloat16><<<blocks, 256, 0, S(stream)>>>(
+          static_cast<const __nv_bfloat16*>(q), codes, scales, zps, n_keys, D, group, out);
+      break;
+    case HKV_DT_F32:
+      qk_scores_flat_kernel<float><<<blocks, 256, 0, S(stream)>>>(static_cast<const float*>(q), codes, scales, zps,
+                                                                  n_keys, D, group, out);
+      break;
+    default: return HKV_ERR_ARG;
+  }
+  return launch_status();
+}
+
+hkv_status hkv_selftest_bounded_wait(int64_t limit_ns, int32_t arrive, hkv_stream_t stream) {
+  if (limit_ns <= 0 || limit_ns > 1000000000LL) return HKV_ERR_ARG;
+  selftest_wait_kernel<<<1, 32, 0, S(stream)>>>((uint64_t)limit_ns, arrive ? 1 : 0);
+  hkv_status rc = launch_status();
+  if (rc != HKV_OK) return rc;
+  cudaError_t e = cudaStreamSynchronize(S(stream));
+  if (e != cudaSuccess) return cuda_fail(e);
+  int completed = 0;
+  if ((e = cudaMemcpyFromSymbol(&completed, g_hkv_selftest_completed, sizeof(int))) != cudaSuccess)
+    return cuda_fail(e);
+  return completed ? HKV_OK : HKV_ERR_DEVICE;
 }
 
 // --------------------------------------------------------------------------- prefetch

@@ -111,20 +111,25 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 // Bounded wait on an mbarrier phase. Returns false (and flags the device error
-// word) if the phase has not completed within HKV_WAIT_NS. With sleep_ns > 0 a
+// word) if the phase has not completed within limit_ns. With sleep_ns > 0 a
 // pending try_wait may sleep that long (woken by the phase completion).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns = 0) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
+                                                uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (sleep_ns ? mbar_try_wait_sleep(bar, parity, sleep_ns) : mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > HKV_WAIT_NS) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       hkv_flag_error(HKV_DEVERR_TIMEOUT);
       return false;
     }
   }
+}
+// The kernels' bounded wait: gives up after HKV_WAIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns = 0) {
+  return mbar_wait_limit(bar, parity, sleep_ns, HKV_WAIT_NS);
 }
 
 // 1-D bulk async copy global -> this CTA's shared memory, completion counted on bar.
@@ -267,12 +272,19 @@ __host__ __device__ constexpr int mn_min_off(int role, int w, int ng, int g) {
 // loads (chunk r of pairs j = 0..3 in one quarter-warp) hit 8 distinct bank groups.
 __host__ __device__ constexpr int v_chunk_off(int q, int c) { return q * 128 + (((c + 2 * q) & 7) << 4); }
 
-// Page of token t of unit u, or -1 when the page id is out of the pool's table.
+// Whether a page id may be dereferenced: non-negative, and inside the pool when
+// the store declares its size (num_pages > 0).
+__device__ __forceinline__ bool page_ok(const hkv_int4_store& s, int64_t page) {
+  return page >= 0 && (s.num_pages <= 0 || page < s.num_pages);
+}
+// Page of token t of unit u, or -1 when the slot is outside the unit's table or
+// the table holds an id outside the pool.
 __device__ __forceinline__ int64_t store_page(const hkv_int4_store& s, int u, int t) {
   const int pi = t / s.page_tokens;
   if (t < 0 || pi >= s.max_pages) return -1;
-  if (s.page_table) return s.page_table[(int64_t)u * s.max_pages + pi];
-  return (int64_t)u * s.max_pages + pi;
+  const int64_t page = s.page_table ? (int64_t)s.page_table[(int64_t)u * s.max_pages + pi]
+                                    : (int64_t)u * s.max_pages + pi;
+  return page_ok(s, page) ? page : -1;
 }
 
 // Block holding token slot `off` of page `page`, and the token's index in it.

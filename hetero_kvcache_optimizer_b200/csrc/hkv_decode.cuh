@@ -930,7 +930,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
           }
           const int page = __shfl_sync(0xffffffffu, pg_lane, pi - pg0);
           if (lane == 0) {
-            if (page < 0) {
+            if (!page_ok(p.body, page)) {
               hkv_flag_error(HKV_DEVERR_BAD_PAGE);
               mbar_arrive(fb);
             } else {

@@ -94,6 +94,7 @@ class Int4KVStore:
         s.page_table = self.page_table.data_ptr() if self.paged else None
         s.lengths = self.lengths.data_ptr()
         s.len = int(self.len_hint if len_hint is None else len_hint)
+        s.num_pages = self.num_pages
         return s
 
     def set_lengths(self, n: Union[int, torch.Tensor]) -> None:
@@ -152,6 +153,20 @@ def workspace(nbytes: int, device: torch.device, stream=None, kind: str = "decod
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _ws_cache[key] = buf
     return buf
+
+
+def reset_workspaces() -> None:
+    """Zero every cached workspace. A decode kernel whose bounded wait expired
+    stops early and leaves some merge counters non-zero, which would make the
+    next call on that workspace merge too soon; ``_lib.device_error`` runs this
+    whenever it reports a timeout. Synchronises the device."""
+    for buf in _ws_cache.values():
+        buf.zero_()
+    if _ws_cache:
+        torch.cuda.synchronize()
+
+
+L.on_device_timeout(reset_workspaces)
 
 
 # ----------------------------------------------------------------------------- operations
@@ -464,6 +479,32 @@ def dequantize_flat(codes: torch.Tensor, scales: torch.Tensor, zps: torch.Tensor
                                          out.data_ptr(), dtype_code(dtype), _stream(stream)),
             "hkv_dequantize_flat")
     return out
+
+
+def qk_scores_flat(q: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, zps: torch.Tensor,
+                   group: int, stream=None) -> torch.Tensor:
+    """Scores q . dequant(K)^T of one query row q [D] against codes [S, D] in the
+    reference's unpacked layout (flat f32 scales / zero-points over groups of
+    ``group`` values): [S] fp32."""
+    _require_cuda(q, codes, scales, zps)
+    S, D = codes.shape
+    qc = q.reshape(-1).contiguous()
+    c = codes.contiguous()
+    s = scales.contiguous().to(torch.float32)
+    z = zps.contiguous()
+    if z.dtype != torch.uint8:
+        z = z.round().clamp(0, 255).to(torch.uint8)
+    out = torch.empty(S, dtype=torch.float32, device=q.device)
+    L.check(L.load().hkv_qk_scores_flat(qc.data_ptr(), dtype_code(qc.dtype), c.data_ptr(), s.data_ptr(),
+                                        z.data_ptr(), S, D, group, out.data_ptr(), _stream(stream)),
+            "hkv_qk_scores_flat")
+    return out
+
+
+def selftest_bounded_wait(limit_ns: int, arrive: bool, stream=None) -> int:
+    """Run the bounded device wait self-test; returns the library status
+    (HKV_OK when the phase completed, HKV_ERR_DEVICE when the wait ran out)."""
+    return int(L.load().hkv_selftest_bounded_wait(int(limit_ns), 1 if arrive else 0, _stream(stream)))
 
 
 def repack_ref(codes: torch.Tensor, scales: torch.Tensor, zps: torch.Tensor, group: int,

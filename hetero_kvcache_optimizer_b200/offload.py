@@ -48,6 +48,7 @@ class _LayerStore:
         s.page_table = self.page_table.data_ptr()
         s.lengths = self.lengths.data_ptr()
         s.len = int(self.len_tokens if len_hint is None else len_hint)
+        s.num_pages = int(self.pool.shape[0])
         return s
 
 

@@ -20,7 +20,6 @@ the event right before layer l+1's attention).
 from __future__ import annotations
 
 import ctypes
-from contextlib import nullcontext
 from typing import Any, Dict, Optional, Sequence, Tuple
 
 import numpy as np
@@ -150,5 +149,3 @@ class PagePrefetcher:
         except Exception:
             pass
 
-
-_ = nullcontext

@@ -9,7 +9,9 @@ split-KV kernel runs. A packed ``Int4KVStore`` may be passed directly as
 """
 from __future__ import annotations
 
+import collections
 import math
+import weakref
 from typing import Optional
 
 import torch
@@ -26,9 +28,50 @@ def _as_4d(t: torch.Tensor, meta: bool = False) -> torch.Tensor:
     return t
 
 
+# Packed stores of recent calls, keyed by the identity and version counter of
+# the six argument tensors: a caller that decodes step after step with the same
+# (unchanged) INT4 tensors pays the repack once, not O(S) per call. Entries hold
+# weak references, so a freed tensor (whose address may be reused) never hits.
+_STORE_CACHE: "collections.OrderedDict" = collections.OrderedDict()
+_STORE_CACHE_SIZE = 4
+
+
+def _cache_key(ts):
+    return tuple((id(t), t._version) for t in ts)
+
+
+def _cache_get(ts):
+    key = _cache_key(ts)
+    hit = _STORE_CACHE.get(key)
+    if hit is None:
+        return None
+    refs, store = hit
+    if any(r() is not t for r, t in zip(refs, ts)):
+        del _STORE_CACHE[key]
+        return None
+    _STORE_CACHE.move_to_end(key)
+    return store
+
+
+def _cache_put(ts, store) -> None:
+    _STORE_CACHE[_cache_key(ts)] = (tuple(weakref.ref(t) for t in ts), store)
+    while len(_STORE_CACHE) > _STORE_CACHE_SIZE:
+        _STORE_CACHE.popitem(last=False)
+
+
 def build_store(k_quant, k_scales, k_zps, v_quant, v_scales, v_zps) -> kv.Int4KVStore:
     if isinstance(k_quant, kv.Int4KVStore):
         return k_quant
+    args = (k_quant, k_scales, k_zps, v_quant, v_scales, v_zps)
+    cached = _cache_get(args)
+    if cached is not None:
+        return cached
+    store = _repack(*args)
+    _cache_put(args, store)
+    return store
+
+
+def _repack(k_quant, k_scales, k_zps, v_quant, v_scales, v_zps) -> kv.Int4KVStore:
     kq = _as_4d(k_quant)
     vq = _as_4d(v_quant)
     B, H, S, D = kq.shape
@@ -85,11 +128,6 @@ def forward(q, store: kv.Int4KVStore, sm_scale: Optional[float], out_dtype) -> t
         n = s1 - s0
         # [B, Hq, n, D] -> [B, Hkv, G, n, D] -> [B, Hkv*G*n, D]: KV head of row = row // (G*n)
         qq = q[:, :, s0:s1].reshape(B, Hkv, G * n, D).reshape(B, Hkv * G * n, D).contiguous()
-        o = kv.decode(qq, _regroup(store, Hkv), None, sm_scale=sm_scale, out_dtype=out_dtype)
+        o = kv.decode(qq, store, None, sm_scale=sm_scale, out_dtype=out_dtype)
         out[:, :, s0:s1] = o.reshape(B, Hkv, G, n, D).reshape(B, Hq, n, D)
     return out
-
-
-def _regroup(store, Hkv):
-    assert store.kv_heads == Hkv
-    return store

@@ -34,10 +34,10 @@ def fused_dequant_attn_decode(q: torch.Tensor, k_quant, k_scales: torch.Tensor, 
 
 def fused_dequant_attention(q: torch.Tensor, k_quant: torch.Tensor, k_scales: torch.Tensor,
                             k_zps: torch.Tensor, group_size: int = 128) -> torch.Tensor:
-    """Legacy single-head scores q . dequant(K)^T (reference :338-381): [S] fp32."""
+    """Legacy single-head scores q . dequant(K)^T (reference :338-381): [S] fp32.
+    The reference reads one scale and zero-point per key (k_scales.reshape(seq_k),
+    :354-355), i.e. groups of head_dim values; so does this call."""
     q_flat = q.reshape(-1)
     D = q_flat.shape[0]
     S = k_quant.shape[0] if k_quant.dim() >= 1 else 1
-    kq = k_quant.reshape(S, D)
-    k_f32 = kv.dequantize_flat(kq, k_scales.reshape(-1), k_zps.reshape(-1), D, dtype=torch.float32)
-    return torch.mv(k_f32, q_flat.float())
+    return kv.qk_scores_flat(q_flat, k_quant.reshape(S, D), k_scales.reshape(S), k_zps.reshape(S), D)

@@ -19,8 +19,7 @@ def fused_dequant_attention(q, k_q, k_s, k_z):
     """Legacy single-head scores (reference :283-298): [seq_len] in q.dtype."""
     qf = q.reshape(-1)
     S, D = k_q.shape[0], qf.shape[0]
-    k_f32 = kv.dequantize_flat(k_q.reshape(S, D), k_s.reshape(-1), k_z.reshape(-1), D, dtype=torch.float32)
-    return torch.mv(k_f32, qf.float()).to(q.dtype)
+    return kv.qk_scores_flat(qf, k_q.reshape(S, D), k_s.reshape(-1), k_z.reshape(-1), D).to(q.dtype)
 
 
 def fused_dequant_attn_decode(q: torch.Tensor, k_data, k_scales, k_zps, v_data, v_scales, v_zps,

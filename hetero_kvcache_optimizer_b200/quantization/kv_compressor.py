@@ -15,7 +15,6 @@ from typing import Optional, Tuple
 
 import torch
 
-from .. import _lib
 from .. import kvstore as kv
 
 
@@ -81,4 +80,3 @@ class KVCompressor:
 PackedKV = kv.Int4KVStore
 
 __all__ = ["KVCompressor", "PackedKV"]
-_ = _lib  # the library is loaded lazily on first use

@@ -19,7 +19,8 @@
  *  - Every device pointer is caller-owned; nothing on these paths allocates.
  *  - Every launch is stream-ordered on the cudaStream_t passed as `stream`
  *    (NULL = legacy default stream). No call synchronises the device, except the
- *    diagnostic hkv_device_error() and the bounded hkv_event_wait().
+ *    diagnostic hkv_device_error(), the bounded hkv_event_wait() and the
+ *    self-test hkv_selftest_bounded_wait() (its own stream).
  *  - Strides are in ELEMENTS; the last (head-dim) axis must be contiguous.
  *  - Errors are integer statuses; no exception crosses the ABI.
  *  - Kernels never trap: a bounded wait that expires, or a page id outside the
@@ -102,7 +103,9 @@ typedef struct hkv_int4_store {
   const int32_t* page_table; /* [units][max_pages] int32 on device, or NULL */
   const int32_t* lengths;    /* [B] int32 on device (tokens per sequence), or NULL */
   int32_t len;               /* tokens when lengths == NULL; else an upper bound */
-  int32_t reserved;
+  int32_t num_pages;         /* pages in the pool: a page id outside [0, num_pages) is
+                                skipped and flagged HKV_DEVERR_BAD_PAGE; 0 = ids are
+                                trusted (only negative ids are caught) */
 } hkv_int4_store;
 
 /* Dense fp16/bf16 K/V segment [B][Hkv][capacity][D] (e.g. sink + recent ring). */
@@ -204,7 +207,9 @@ hkv_status hkv_repack_ref(const uint8_t* codes, const float* scales, const uint8
  * followed by the split partials. The counter region must be zero-filled before
  * the first call; every completed call leaves it at zero again, so one
  * workspace serves calls of any shape. Calls that overlap on the GPU must use
- * different workspaces. */
+ * different workspaces. A call whose bounded wait expired (hkv_device_error
+ * reports HKV_DEVERR_TIMEOUT) may leave counters non-zero: zero the counter
+ * region again before the workspace's next use. */
 size_t hkv_decode_workspace_bytes(const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t B,
                                   int32_t Hq, int32_t Hkv, int32_t D, int32_t ctas);
 
@@ -297,12 +302,15 @@ hkv_status hkv_decode_attn_partial(const void* q, int32_t q_dtype, int64_t q_str
  * (its Python path allocates freely).
  * - The first call on a device looks up the array's address (and sets the
  *   kernel's shared-memory attribute); make that first call before any stream
- *   capture.
+ *   capture. The address is looked up again when the device's current context
+ *   changes (after a cudaDeviceReset the module, and the array, are new); a
+ *   call that would do so inside a capture fails with HKV_ERR_CUDA.
  * - Every call on a device shares the one array: calls whose kernels may
  *   overlap (different streams, or threads without ordering) race on it.
  *   Each call clears the merge counters it uses on `stream` before its kernel.
- * - Returns HKV_ERR_CAPACITY, without touching the device, when the request's
- *   workspace (hkv_decode_workspace_bytes) exceeds HKV_STATIC_SCRATCH_BYTES. */
+ * - Argument errors, and a request whose workspace (hkv_decode_workspace_bytes)
+ *   exceeds HKV_STATIC_SCRATCH_BYTES (HKV_ERR_CAPACITY), return before anything
+ *   is queued on `stream`. */
 hkv_status hkv_decode_attn_static(const void* q, int32_t q_dtype, int64_t q_stride_b,
                                   int64_t q_stride_h, const hkv_int4_store* body,
                                   const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
@@ -336,6 +344,25 @@ int64_t hkv_prefetch_bytes(const hkv_prefetcher* pf);
 /* Host-side bounded wait: polls the event until it completes or timeout_us
  * elapses (HKV_ERR_TIMEOUT). Never blocks forever. */
 hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us);
+
+/* ---------------------------------------------------------------- 4. legacy scores, self-test
+ * Pre-softmax scores of one query row against n_keys keys in the reference's
+ * unpacked INT4 layout: out[s] = sum_d q[d] * (codes[s*D+d] - zps[g]) * scales[g],
+ * g = (s*D+d) / group, fp32 (replaces the score-only fused_dequant_attention,
+ * src/quantization/fused_dequant_attn.py:338-381, and its twin
+ * kernels/fused_dequant_attn.py:283-298). q: D elements (f16/bf16/f32). */
+hkv_status hkv_qk_scores_flat(const void* q, int32_t q_dtype, const uint8_t* codes, const float* scales,
+                              const uint8_t* zps, int64_t n_keys, int32_t D, int32_t group, float* out,
+                              hkv_stream_t stream);
+
+/* Failure-detection self-test of the bounded device wait the kernels use: a
+ * one-warp kernel waits on an mbarrier phase with a limit of limit_ns
+ * (0 < limit_ns <= 1e9). With arrive != 0 the phase completes and the call
+ * returns HKV_OK; with arrive == 0 nothing completes it, the wait gives up,
+ * sets HKV_DEVERR_TIMEOUT in the device error word and the call returns
+ * HKV_ERR_DEVICE, the context still usable. Synchronises `stream`. No
+ * counterpart in the reference (it has no device-side waits). */
+hkv_status hkv_selftest_bounded_wait(int64_t limit_ns, int32_t arrive, hkv_stream_t stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -66,32 +66,39 @@ def decode_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale
 class RefLayer:
     """One layer of the reference's cache in its own representation: unpacked
     uint8 codes + fp32 scales + uint8 zero-points for the body, fp16 sink and
-    recent tail."""
+    recent tail. The groups lie inside a token (group divides 128), so the flat
+    scale/zero-point arrays are kept per token, [B, Hkv, T, 128/group], and
+    grow along the token axis exactly like the codes."""
 
     def __init__(self, B, Hkv, body, sink, recent, group=32, seed=0):
         g = torch.Generator().manual_seed(seed)
         kb = torch.randn(B, Hkv, body, 128, generator=g).half()
         vb = torch.randn(B, Hkv, body, 128, generator=g).half()
         self.group = group
-        self.kq, self.ks, self.kz = compress(kb, group)
-        self.vq, self.vs, self.vz = compress(vb, group)
+        self.kq, self.ks, self.kz = self._compress(kb)
+        self.vq, self.vs, self.vz = self._compress(vb)
         self.sink_k = torch.randn(B, Hkv, sink, 128, generator=g).half()
         self.sink_v = torch.randn(B, Hkv, sink, 128, generator=g).half()
         self.tail_k = torch.randn(B, Hkv, recent, 128, generator=g).half()
         self.tail_v = torch.randn(B, Hkv, recent, 128, generator=g).half()
 
+    def _compress(self, x: torch.Tensor):
+        q, s, z = compress(x, self.group)
+        meta = (*x.shape[:3], x.shape[3] // self.group)
+        return q, s.reshape(meta), z.reshape(meta)
+
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor) -> torch.Tensor:
         """Evict the oldest tail token into INT4 (compress), slide the tail,
         dequantise the body and attend over [body ; sink ; tail]."""
         ek, ev = self.tail_k[:, :, :1], self.tail_v[:, :, :1]
-        qk, sk, zk = compress(ek, self.group)
-        qv, sv, zv = compress(ev, self.group)
+        qk, sk, zk = self._compress(ek)
+        qv, sv, zv = self._compress(ev)
         self.kq = torch.cat([self.kq, qk], dim=2)
-        self.ks = torch.cat([self.ks, sk])
-        self.kz = torch.cat([self.kz, zk])
+        self.ks = torch.cat([self.ks, sk], dim=2)
+        self.kz = torch.cat([self.kz, zk], dim=2)
         self.vq = torch.cat([self.vq, qv], dim=2)
-        self.vs = torch.cat([self.vs, sv])
-        self.vz = torch.cat([self.vz, zv])
+        self.vs = torch.cat([self.vs, sv], dim=2)
+        self.vz = torch.cat([self.vz, zv], dim=2)
         self.tail_k = torch.cat([self.tail_k[:, :, 1:], k_new[:, :, None]], dim=2)
         self.tail_v = torch.cat([self.tail_v[:, :, 1:], v_new[:, :, None]], dim=2)
         kd = decompress(self.kq, self.ks, self.kz, self.group)

@@ -2,7 +2,8 @@
 
 Run in the build container, where the reference package is importable:
 
-    python tests/golden/make_golden.py [path-to-reference-checkout]
+    python tests/golden/make_golden.py <path-to-reference-checkout>
+    (or HKV_REFERENCE=<path-to-reference-checkout> python tests/golden/make_golden.py)
 
 It imports ``src.quantization.kv_compressor.KVCompressor`` and the PyTorch
 fallbacks of ``src.quantization.fused_dequant_attn.fused_dequant_attn_decode``
@@ -26,7 +27,9 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle import kv_oracle as ko  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HKV_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HKV_REFERENCE")
+if not REF:
+    sys.exit("usage: make_golden.py <reference checkout> (or set HKV_REFERENCE)")
 sys.path.insert(0, REF)
 from src.quantization.kv_compressor import KVCompressor  # noqa: E402
 from src.quantization.fused_dequant_attn import fused_dequant_attn_decode, fused_dequant_attn_forward  # noqa: E402
