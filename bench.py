@@ -63,6 +63,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-fused", action="store_true",
+                    help="cfg1/cfg2: run each layer's step as two launches (append, then decode) "
+                         "instead of the fused decode-append launch")
     return ap.parse_args()
 
 
@@ -84,11 +87,11 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(bytes_per_launch: float):
-    """DRAM bytes (read + write) per decode launch from the committed ncu capture
-    (profiles/decode_kernel_cfg1_traffic.json), scaled to this launch's
-    algorithmic bytes; None when no capture is recorded."""
-    p = os.path.join(REPO, "profiles", "decode_kernel_cfg1_traffic.json")
+def profiled_traffic(bytes_per_launch: float, name: str = "decode_kernel_cfg1_traffic.json"):
+    """DRAM bytes (read + write) per launch from a committed ncu capture
+    (profiles/<name>), scaled to this launch's algorithmic bytes; None when no
+    capture is recorded."""
+    p = os.path.join(REPO, "profiles", name)
     try:
         with open(p) as f:
             t = json.load(f)
@@ -202,7 +205,8 @@ def run_cfg2(args) -> None:
     body = ctx - sink - recent
     total_steps = args.warmup + args.steps + 4
     eng = TieredKVDecoder(layers, B, Hq, Hkv, sink=sink, recent=recent, body_capacity=body + total_steps + 8,
-                          fmt=args.fmt, group=32, kv_dtype=torch.float16, out_dtype=torch.float32, device=dev)
+                          fmt=args.fmt, group=32, kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
+                          fused_append=not args.no_fused)
     gen = torch.Generator(device=dev).manual_seed(2)
     st_ = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -287,7 +291,7 @@ def run_cfg2(args) -> None:
         "prefill_quantize": {"chunk_tokens": chunk, "ms_all_layers": round(q_ms, 3),
                              "gbs": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
                              "tokens_per_s": round(layers * B * body / (q_ms * 1e-3), 0)},
-        "gpu_launches": args.steps * layers * 2, "clocks": clocks}))
+        "gpu_launches": args.steps * layers * eng.launches_per_layer, "clocks": clocks}))
 
 
 # --------------------------------------------------------------------------- prefill
@@ -621,7 +625,7 @@ def main():
     eng = TieredKVDecoder(args.layers, c["batch"], c["q_heads"], c["kv_heads"], sink=c["sink"],
                           recent=c["recent"], body_capacity=body + total_steps + 8, fmt=args.fmt,
                           group=c["group"], kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
-                          ctas=args.ctas)
+                          ctas=args.ctas, fused_append=not args.no_fused)
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     B, Hkv = c["batch"], c["kv_heads"]
     for l in range(args.layers):
@@ -697,7 +701,22 @@ def main():
     dec_ms = e0.elapsed_time(e1) / (R * args.layers)
     dec_bytes = eng.layer_attn_bytes(eng.body_len)
     peak, peak_kind = measured_peak()
-    achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
+    dec_achieved = dec_bytes / (dec_ms * 1e-3) / 1e9
+    if eng.fused_append:
+        # the dominant (only) kernel of the timed step is the fused decode-append
+        # launch: one per layer, back to back in the step graph, so its average
+        # launch duration is the timed step / layers (CUDA events on the stream
+        # that replays the graph; gaps between launches count against it)
+        kern_us = ms * 1e3 / args.layers
+        kern_bytes = step_bytes / args.layers
+        kern_name = ("decode_kernel<APPEND> (fused decode-step append + split-KV attention + merge), "
+                     "one launch per layer")
+        traffic = profiled_traffic(kern_bytes, "decode_append_kernel_cfg1_traffic.json")
+    else:
+        kern_us, kern_bytes = dec_ms * 1e3, dec_bytes
+        kern_name = "decode_kernel (split-KV + fused merge), one launch per layer"
+        traffic = profiled_traffic(dec_bytes)
+    achieved = kern_bytes / (kern_us * 1e-6) / 1e9
 
     # ---- e2e through the public API from pinned host buffers: the engine's own
     # pinned buffers, so step_host replays the pipelined graph (layer l's copies
@@ -749,15 +768,20 @@ def main():
             "pct_of_8TBs": round(100 * gbs / (NOMINAL_HBM_GBS * world), 2),
             "pct_of_measured_peak": round(100 * gbs / (peak * world), 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": profiled_traffic(dec_bytes),
-                         "kernel": "decode_kernel (split-KV + fused merge), one launch per layer",
-                         "bytes_per_launch": dec_bytes, "us_per_launch": round(dec_ms * 1e3, 2),
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "kernel": kern_name,
+                         "bytes_per_launch": round(kern_bytes), "us_per_launch": round(kern_us, 2),
                          "peak_kind": f"{peak_kind} (copy)"},
+            # the attention alone (decode_kernel without the append, a graph of
+            # `layers` launches over the same cache), for comparison
+            "attention_only": {"achieved": round(dec_achieved, 1), "frac": round(dec_achieved / peak, 4),
+                               "bytes_per_launch": dec_bytes, "us_per_launch": round(dec_ms * 1e3, 2),
+                               "traffic": profiled_traffic(dec_bytes)},
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "api": "TieredKVDecoder.step_host (pinned host q/k/v in, fp32 out; per-layer copies "
                            "pipelined with the kernels)"},
-            "gpu_launches": world * args.steps * args.layers * 2,  # append_kv + decode per layer, all ranks
+            # one fused decode-append launch per layer (two without fusion), all ranks
+            "gpu_launches": world * args.steps * args.layers * eng.launches_per_layer,
             "clocks": clocks,
         }
         if cpu is not None:

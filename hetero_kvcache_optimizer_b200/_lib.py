@@ -28,6 +28,7 @@ FMT_REF, FMT_FP16MIN = 0, 1
 ROLE_K, ROLE_V = 0, 1
 
 DEVERR_TIMEOUT, DEVERR_BAD_PAGE, DEVERR_CAPACITY = 1, 2, 4
+APPEND_EARLY = 1  # HKV_APPEND_EARLY
 
 c_i32, c_i64, c_u32, c_f32, c_vp, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
                                           ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t)
@@ -70,6 +71,9 @@ SIGNATURES = {
     "hkv_decode_plan": (c_i32, [P_store, P_dense, c_i32, c_i32, c_i32, c_i32, P_i32, P_i32]),
     "hkv_decode_attn": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32, c_i32,
                                 c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_i32, c_i64, c_i64, c_vp]),
+    "hkv_decode_append": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, P_store, P_dense, c_i32,
+                                  c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_f32, c_i32, c_vp, c_sz, c_vp,
+                                  c_i32, c_i64, c_i64, c_i32, c_vp]),
     "hkv_decode_attn_scored": (c_i32, [c_vp, c_i32, c_i64, c_i64, P_store, P_dense, c_i32, c_i32, c_i32,
                                        c_i32, c_f32, c_i32, c_vp, c_sz, c_vp, c_i32, c_i64, c_i64, c_vp,
                                        c_i32, c_vp, c_vp]),

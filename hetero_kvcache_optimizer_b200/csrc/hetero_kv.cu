@@ -9,8 +9,8 @@
 #include <thread>
 
 #include "hkv_common.cuh"
+#include "hkv_quant.cuh"   // before the decode kernel: its fused append quantises with it
 #include "hkv_decode.cuh"
-#include "hkv_quant.cuh"
 #include "hkv_prefill.cuh"
 
 #define HKV_VERSION 100
@@ -205,29 +205,32 @@ hkv_status dense_map(CUtensorMap* m, const void* base, const hkv_dense_kv* d, in
   return r == CUDA_SUCCESS ? HKV_OK : HKV_ERR_ARG;
 }
 
-template <int FMT, int GROUP, typename DTy, bool STATS>
+template <int FMT, int GROUP, typename DTy, bool STATS, bool APPEND>
 hkv_status launch_decode_t(const hkv::DecodeParams& p, int smem, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(hkv::decode_kernel<FMT, GROUP, DTy, STATS>,
+    attr_err = cudaFuncSetAttribute(hkv::decode_kernel<FMT, GROUP, DTy, STATS, APPEND>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmemBudget);
   });
   if (attr_err != cudaSuccess) return cuda_fail(attr_err);
-  const cudaError_t e =
-      launch_pdl(1, hkv::decode_kernel<FMT, GROUP, DTy, STATS>, dim3(p.sc.C), dim3(hkv::decode_threads(FMT)), smem, st, p);
+  const cudaError_t e = launch_pdl(1, hkv::decode_kernel<FMT, GROUP, DTy, STATS, APPEND>, dim3(p.sc.C),
+                                   dim3(hkv::decode_threads(FMT, APPEND)), smem, st, p);
   if (e != cudaSuccess) return cuda_fail(e);
   return launch_status();
 }
 
+template <int FMT, int GROUP, typename DTy>
+hkv_status launch_decode_m(const hkv::DecodeParams& p, int smem, cudaStream_t st) {
+  if (p.tile_stats) return launch_decode_t<FMT, GROUP, DTy, true, false>(p, smem, st);
+  if (p.state_counter) return launch_decode_t<FMT, GROUP, DTy, false, true>(p, smem, st);
+  return launch_decode_t<FMT, GROUP, DTy, false, false>(p, smem, st);
+}
+
 template <int FMT, int GROUP>
 hkv_status launch_decode_g(const hkv::DecodeParams& p, int ddt, int smem, cudaStream_t st) {
-  const bool stats = p.tile_stats != nullptr;
-  if (ddt == HKV_DT_BF16)
-    return stats ? launch_decode_t<FMT, GROUP, __nv_bfloat16, true>(p, smem, st)
-                 : launch_decode_t<FMT, GROUP, __nv_bfloat16, false>(p, smem, st);
-  return stats ? launch_decode_t<FMT, GROUP, __half, true>(p, smem, st)
-               : launch_decode_t<FMT, GROUP, __half, false>(p, smem, st);
+  if (ddt == HKV_DT_BF16) return launch_decode_m<FMT, GROUP, __nv_bfloat16>(p, smem, st);
+  return launch_decode_m<FMT, GROUP, __half>(p, smem, st);
 }
 
 template <int FMT>
@@ -286,7 +289,9 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   sc.Btot = (uint32_t)Btot;
   sc.q = (uint32_t)(Btot / C);
   sc.r = (uint32_t)(Btot % C);
-  sc.S = (int)(Ub / (Btot / C)) + 4;
+  // partial slots per unit: the CTAs whose ranges meet the unit (with margin),
+  // plus one for the fused append's partial
+  sc.S = (int)(Ub / (Btot / C)) + 5;
   Plan pl;
   pl.sc = sc;
   // the piece-end combine area, then the prefetched query rows of the next piece (f16/bf16)
@@ -319,11 +324,21 @@ hkv_status check_decode_args(const void* q, int q_dtype, const hkv_int4_store* b
   return HKV_OK;
 }
 
+// The decode step's new token and cache state for the fused append (hkv_decode_append).
+struct AppendArgs {
+  const void* k_new;
+  const void* v_new;
+  int64_t new_sb, new_sh;
+  int sink;
+  int32_t *dense_len, *ring_head, *body_len;
+  int early;
+};
+
 hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, const hkv_int4_store* body,
                       const hkv_dense_kv* dense, int B, int Hq, int Hkv, int D, float sm_scale, int ctas,
                       void* workspace, size_t workspace_bytes, void* out, int out_dtype, int64_t out_sb,
                       int64_t out_sh, float* out_o, float* out_ml, cudaStream_t st, float* tile_stats = nullptr,
-                      int stat_tiles = 0, float* unit_ml = nullptr) {
+                      int stat_tiles = 0, float* unit_ml = nullptr, const AppendArgs* app = nullptr) {
   hkv_status rc = check_decode_args(q, q_dtype, body, dense, B, Hq, Hkv, D);
   if (rc != HKV_OK) return rc;
   if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return HKV_ERR_ARG;
@@ -369,6 +384,19 @@ hkv_status run_decode(const void* q, int q_dtype, int64_t q_sb, int64_t q_sh, co
   p.tile_stats = tile_stats;
   p.stat_tiles = stat_tiles;
   p.unit_ml = unit_ml;
+  if (app) {
+    p.k_new = app->k_new;
+    p.v_new = app->v_new;
+    p.new_sb = app->new_sb;
+    p.new_sh = app->new_sh;
+    p.sink = app->sink;
+    p.dense_len = app->dense_len;
+    p.ring_head = app->ring_head;
+    p.body_len = app->body_len;
+    p.early = app->early;
+    // the last counter of the reserved region (units are limited to kMaxUnits - 1)
+    p.state_counter = p.counters + (kMaxUnits - 1);
+  }
   const int fmt = body ? body->format : HKV_FMT_REF;
   const int group = body ? body->group : 32;
   const int ddt = dense ? dense->dtype : HKV_DT_F16;
@@ -739,6 +767,28 @@ hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b, i
   if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
   return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
                     workspace_bytes, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr, S(stream));
+}
+
+hkv_status hkv_decode_append(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                             const void* k_new, const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                             const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t sink,
+                             int32_t* dense_len, int32_t* ring_head, int32_t* body_len, int32_t B, int32_t Hq,
+                             int32_t Hkv, int32_t D, float sm_scale, int32_t ctas, void* workspace,
+                             size_t workspace_bytes, void* out, int32_t out_dtype, int64_t out_stride_b,
+                             int64_t out_stride_h, int32_t flags, hkv_stream_t stream) {
+  if (!out || (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32)) return HKV_ERR_ARG;
+  if (!body || !dense || !k_new || !v_new || !dense_len || !ring_head || !body_len) return HKV_ERR_ARG;
+  if (flags & ~HKV_APPEND_EARLY) return HKV_ERR_ARG;
+  // the attention reads the lengths the append advances: one set of state arrays
+  if (body->lengths != body_len || dense->lengths != dense_len) return HKV_ERR_ARG;
+  if (!aligned16(k_new) || !aligned16(v_new) || new_stride_b % 8 || new_stride_h % 8) return HKV_ERR_ARG;
+  if (sink < 0 || sink > dense->capacity) return HKV_ERR_ARG;
+  if ((int64_t)B * Hkv > kMaxUnits - 1) return HKV_ERR_UNSUPPORTED;  // the last counter is the state counter
+  AppendArgs app{k_new, v_new, new_stride_b, new_stride_h, sink, dense_len, ring_head, body_len,
+                 (flags & HKV_APPEND_EARLY) ? 1 : 0};
+  return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
+                    workspace_bytes, out, out_dtype, out_stride_b, out_stride_h, nullptr, nullptr, S(stream), nullptr,
+                    0, nullptr, &app);
 }
 
 hkv_status hkv_decode_attn_scored(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,

@@ -48,9 +48,22 @@ constexpr int kExpandWarp = kIssueWarp + kIssueWarps;  // HKV_FMT_REF metadata e
 // HKV_FMT_REF tiles get their metadata rewritten by two expansion warps (alternate
 // tiles); HKV_FMT_FP16MIN blocks are stored in the layout the consumers read.
 __host__ __device__ constexpr int expand_warps(int fmt) { return fmt == HKV_FMT_REF ? 2 : 0; }
-__host__ __device__ constexpr int decode_threads(int fmt) {
-  return (kConsumerWarps + kIssueWarps + expand_warps(fmt)) * 32;
+// The fused decode-step append (APPEND instantiation) runs on warp kAppendWarp:
+// a warp of its own for fp16min, the first expansion warp (before it starts
+// expanding) for ref, whose 12 warps leave no registers for a 13th. (Run by an
+// issue warp while its share of the ring fills, the append's chain of loaded
+// round trips held back half the ring: a 32-layer step took 3.07 instead of
+// 2.56 ms.)
+constexpr int kAppendWarp = kIssueWarp + kIssueWarps;
+__host__ __device__ constexpr int append_warps(int fmt, bool append) { return append && fmt != HKV_FMT_REF ? 1 : 0; }
+__host__ __device__ constexpr int decode_threads(int fmt, bool append = false) {
+  return (kConsumerWarps + kIssueWarps + expand_warps(fmt) + append_warps(fmt, append)) * 32;
 }
+// Arrivals per CTA on the grid-wide state counter in the APPEND instantiation,
+// one by each role once it has read the cache state (sequence lengths, ring
+// head) for the last time: the two issue warps, the consumers (as one), and
+// the append job.
+constexpr int kStateRoles = kIssueWarps + 2;
 constexpr int kTileI4 = 128;  // tokens per INT4 tile (32 per consumer warp)
 constexpr int kTileD = 32;    // tokens per dense tile (8 per consumer warp)
 constexpr int kMaxSlots = 12;
@@ -113,6 +126,19 @@ struct DecodeParams {
   float* tile_stats;
   int stat_tiles;
   float* unit_ml;
+  // fused decode-step append (APPEND instantiation): per (b, KV head) the new
+  // token's K and V rows [B][Hkv][128] (the dense segment's dtype), the cache
+  // state arrays (dense_len and body_len are dense.lengths and body.lengths),
+  // and the grid-wide counter of state-reading roles (kStateRoles per CTA)
+  const void* k_new;
+  const void* v_new;
+  int64_t new_sb, new_sh;
+  int sink;
+  int32_t* dense_len;
+  int32_t* ring_head;
+  int32_t* body_len;
+  int* state_counter;
+  int early;  // the cache may be read before griddep_wait (HKV_APPEND_EARLY)
 };
 
 // Records one body tile's share of the attention for the unit's heads (see
@@ -177,8 +203,10 @@ __device__ __forceinline__ int owner_of(const Sched& s, uint32_t x) {
 
 // A piece: tiles [k0, k1) of segment seg of unit u (k1 includes tiles past the
 // hint when the true length needs them); tiles at or past kd hold no tokens.
+// skip: a dense row the piece must leave out (-1: none), the ring row the fused
+// append overwrites in this launch.
 struct Piece {
-  int u, seg, k0, k1, kd, len;
+  int u, seg, k0, k1, kd, len, skip;
   bool valid;
 };
 
@@ -186,6 +214,18 @@ __device__ __forceinline__ int seg_len(const DecodeParams& p, int u, int seg) {
   const int b = u / p.Hkv;
   if (seg == 0) return p.body.lengths ? p.body.lengths[b] : p.body.len;
   return p.dense.lengths ? p.dense.lengths[b] : p.dense.len;
+}
+// (length, skipped row) of a segment. With the fused append the attention runs
+// over the state before the append: the body without the evicted token and the
+// dense segment without the ring row being overwritten (when the ring is full);
+// the append warp's own partial covers the evicted token and the new one.
+template <bool APPEND>
+__device__ __forceinline__ int2 seg_state(const DecodeParams& p, int u, int seg) {
+  if (!APPEND || seg == 0) return make_int2(seg_len(p, u, seg), -1);
+  // both loads in one round trip (the ring head is read whether or not it is used)
+  const int b = u / p.Hkv, cap = p.dense.capacity;
+  const int len = p.dense_len[b], head = p.ring_head[b];
+  return make_int2(len, len >= cap && cap > p.sink ? p.sink + head : -1);
 }
 
 __device__ __forceinline__ void piece_fill_len(const DecodeParams& p, uint32_t end, Piece& pc, int len) {
@@ -197,6 +237,7 @@ __device__ __forceinline__ void piece_fill_len(const DecodeParams& p, uint32_t e
   const uint32_t kq = (end - 1 - seg0) / ts;
   const int kl = kq < (uint32_t)(T - 1) ? (int)kq : T - 1;  // last hinted tile starting in range
   pc.len = len;
+  pc.skip = -1;
   const int kneed = (pc.len + tile - 1) / tile;
   pc.k1 = kl + 1;
   // past its last hinted tile a segment continues while the true length needs it
@@ -847,21 +888,273 @@ __device__ __forceinline__ void cursor_next(const DecodeParams& p, uint32_t end,
   cursor_settle(p, end, cu);
 }
 
+// ---------------------------------------------------------------- merge of a unit's partials
+// One warp merges head h of unit u over its n partials (slots 0..n-1 of the
+// unit in the workspace) and writes the output row (or, in partial mode, the
+// merged un-normalised partial). Partials are read from L2 (__ldcg): other CTAs
+// wrote them, ordered by the unit counter's release / acquire.
+template <bool STATS>
+__device__ __forceinline__ void merge_head(const DecodeParams& p, int u, int h, int n) {
+  const Sched& sc = p.sc;
+  const int lane = threadIdx.x & 31;
+  const int b = u / p.Hkv, hk = u - b * p.Hkv;
+  const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
+  const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
+  // partial k's (m, l) in lane k; the first 8 partials' o rows load in
+  // the same round trip (the usual unit has at most 8 partials)
+  const float2* mlp = reinterpret_cast<const float2*>(ml_u) + h;
+  const float4* op = reinterpret_cast<const float4*>(o_u + h * HKV_D) + lane;
+  const int ostep = p.G * HKV_D / 4;  // float4s per partial
+  const float2 ml0 = lane < n ? __ldcg(mlp + lane * p.G) : make_float2(kNoMax, 0.f);
+  float4 v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = i < n ? __ldcg(op + i * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float M = ml0.x;
+  for (int k = lane + 32; k < n; k += 32) M = fmaxf(M, __ldcg(mlp + k * p.G).x);
+#pragma unroll
+  for (int sft = 16; sft > 0; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
+  float wk = lane < n ? fast_exp2(ml0.x - M) : 0.f;
+  float L = wk * ml0.y;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float w = __shfl_sync(0xffffffffu, wk, i);
+    acc.x = fmaf(w, v[i].x, acc.x);
+    acc.y = fmaf(w, v[i].y, acc.y);
+    acc.z = fmaf(w, v[i].z, acc.z);
+    acc.w = fmaf(w, v[i].w, acc.w);
+  }
+  // partials 8.. (8 per batch, all loads in flight before the first use)
+  for (int k0 = 8; k0 < n; k0 += 8) {
+    if (k0 % 32 == 0) {
+      const float2 mlk = k0 + lane < n ? __ldcg(mlp + (k0 + lane) * p.G) : make_float2(kNoMax, 0.f);
+      wk = k0 + lane < n ? fast_exp2(mlk.x - M) : 0.f;
+      L = fmaf(wk, mlk.y, L);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = k0 + i < n ? __ldcg(op + (k0 + i) * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float w = __shfl_sync(0xffffffffu, wk, (k0 + i) & 31);
+      acc.x = fmaf(w, v[i].x, acc.x);
+      acc.y = fmaf(w, v[i].y, acc.y);
+      acc.z = fmaf(w, v[i].z, acc.z);
+      acc.w = fmaf(w, v[i].w, acc.w);
+    }
+  }
+#pragma unroll
+  for (int sft = 16; sft > 0; sft >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sft);
+  if (STATS && lane == 0) {
+    p.unit_ml[((int64_t)u * 8 + h) * 2] = M;
+    p.unit_ml[((int64_t)u * 8 + h) * 2 + 1] = L;
+  }
+  const int hq = hk * p.G + h;
+  if (p.out_o) {
+    reinterpret_cast<float4*>(p.out_o + ((int64_t)b * p.Hq + hq) * HKV_D)[lane] = acc;
+    if (lane == 0) {
+      // a row that attended to no token reports m = -inf
+      p.out_ml[((int64_t)b * p.Hq + hq) * 2] = L > 0.f ? M : -INFINITY;
+      p.out_ml[((int64_t)b * p.Hq + hq) * 2 + 1] = L;
+    }
+  } else {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    const int64_t o = (int64_t)b * p.out_sb + (int64_t)hq * p.out_sh + 4 * lane;
+    store_any(p.out, p.out_dtype, o + 0, acc.x * inv);
+    store_any(p.out, p.out_dtype, o + 1, acc.y * inv);
+    store_any(p.out, p.out_dtype, o + 2, acc.z * inv);
+    store_any(p.out, p.out_dtype, o + 3, acc.w * inv);
+  }
+}
+
+// ---------------------------------------------------------------- fused decode-step append
+// A role that has finished reading the cache state (lengths, ring head)
+// arrives; a whole warp calls this, lane 0 counts. The kStateRoles roles of a
+// CTA meet on a shared-memory counter (acquire-release at CTA scope), and the
+// CTA's last role arrives for all of them on the grid-wide counter (release at
+// GPU scope, cumulative over the reads the CTA's roles made before their own
+// arrivals). The last of the C grid arrivals applies every sequence's state
+// transition of the decode step, as the standalone append kernel does
+// (HeteroKVManager._decode_update, src/memory/manager.py:621-664): a ring with
+// room grows by one row, a full ring evicts its oldest row to the INT4 body
+// (body_len + 1, ring head + 1), no ring sends the token to the body. Every
+// read of the state in this launch happens before its reader's arrival, so the
+// update never races a reader; the next launch sees it after griddep_wait.
+// One global atomic per CTA instead of one per role: a launch of 4 x 148 of
+// them on one address measured ~1 us slower.
+// The arrival is split so that a warp need not wait for the global atomic: its
+// old count stays in a register that only state_arrive_finish consumes; the
+// last arriver fences (acquire) before it writes the state.
+__device__ __forceinline__ int atom_add_release_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+// -1 for lanes other than 0 and for roles that are not their CTA's last.
+__device__ __forceinline__ int state_arrive_start(const DecodeParams& p, int* s_roles) {
+  __syncwarp();
+  int old = -1;
+  if ((threadIdx.x & 31) == 0) {
+    int local;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;" : "=r"(local) : "r"(smem_u32(s_roles)) : "memory");
+    if (local == kStateRoles - 1) old = atom_add_release_gpu(p.state_counter, 1);
+  }
+  return old;
+}
+__device__ __forceinline__ void state_arrive_finish(const DecodeParams& p, int old) {
+  const int lane = threadIdx.x & 31;
+  const int last = __shfl_sync(0xffffffffu, old == p.sc.C - 1, 0);
+  if (!last) return;
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  const int cap = p.dense.capacity, cap_r = cap - p.sink;
+  for (int b = lane; b < p.B; b += 32) {
+    const int dl = p.dense_len[b];
+    if (dl < cap) {
+      p.dense_len[b] = dl + 1;
+    } else {
+      p.body_len[b] = p.body_len[b] + 1;
+      if (cap_r > 0) p.ring_head[b] = (p.ring_head[b] + 1) % cap_r;
+    }
+  }
+  __syncwarp();
+  if (lane == 0) *p.state_counter = 0;
+}
+
+// The append of unit u = (b, KV head h) for every u of this CTA (u = c, c + C,
+// ...), by one warp (lanes 0-15: K, 16-31: V, 8 dims a lane), on the state
+// before the step:
+//  * the ring row to evict (full ring), or the new token itself (no ring), is
+//    quantised into body slot body_len[b] exactly as the standalone append
+//    kernel does it, and the new token is written into the ring (or the next
+//    free row);
+//  * the attention of the unit's G heads over the tokens the streaming pipeline
+//    leaves out, the evicted token as dequantised and the new one, becomes the
+//    unit's extra partial (slot nb + nd, after the pipeline's), so the merged
+//    output is the attention over the cache after the append.
+// The warp that delivers a unit's last partial merges it, as the consumers do.
+// Not inlined: its code stays out of the kernel's main body (inlined, the
+// launches of a 32-layer step measured ~2.5 us slower each).
+template <int FMT, int GROUP, typename DTy>
+__device__ __noinline__ void append_units(const DecodeParams& p, int c, int* s_roles) {
+  griddep_wait();  // the query and the new token come from the grid before (a no-op if waited)
+  const Sched& sc = p.sc;
+  const int lane = threadIdx.x & 31, side = lane >> 4, pq = lane & 15;
+  const int cap = p.dense.capacity, cap_r = cap - p.sink;
+  for (int u = c; u < sc.U; u += sc.C) {
+    const int b = u / p.Hkv, h = u - b * p.Hkv;
+    const int dl = p.dense_len[b], head = p.ring_head[b], bl = p.body_len[b];
+    const bool fill = dl < cap;                // a free row: nothing is evicted
+    const bool direct = !fill && cap_r <= 0;   // no ring: the new token goes to the body
+    const int row = fill ? dl : p.sink + head;
+    DTy* seg = static_cast<DTy*>(side ? p.dense.v : p.dense.k);
+    DTy* rowp = seg + b * p.dense.stride_b + h * p.dense.stride_h + (int64_t)row * p.dense.stride_t + 8 * pq;
+    const DTy* src = static_cast<const DTy*>(side ? p.v_new : p.k_new) + b * p.new_sb + h * p.new_sh + 8 * pq;
+    float nv[8], dq[8];
+    load8(src, nv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dq[i] = 0.f;
+    if (!fill) {
+      float ev[8];
+      if (direct) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ev[i] = nv[i];
+      } else {
+        load8(rowp, ev);
+      }
+      bool ok = bl < p.body.max_pages * p.body.page_tokens;
+      int64_t page = 0;
+      if (!ok) {
+        if (lane == 0) hkv_flag_error(HKV_DEVERR_CAPACITY);
+      } else {
+        page = store_page(p.body, u, bl);
+        if (page < 0) {
+          ok = false;
+          if (lane == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+        }
+      }
+      quantise_token(ev, ok, side ? HKV_ROLE_V : HKV_ROLE_K, FMT, GROUP, p.body, page,
+                     ok ? bl % p.body.page_tokens : 0, dq);
+    }
+    if (!direct) store8(rowp, nv);
+    // scores (base-2 logits) of the evicted and the new token for each head:
+    // K lanes dot their 8 dims, the half-warp sums, lane 0 broadcasts
+    float xe[8], xn[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      float se = 0.f, sn = 0.f;
+      if (side == 0 && g < p.G) {
+        const int64_t qo = (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.q_sh + 8 * pq;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float qv = load_any(p.q, p.q_dtype, qo + i);
+          se = fmaf(qv, dq[i], se);
+          sn = fmaf(qv, nv[i], sn);
+        }
+      }
+#pragma unroll
+      for (int s = 1; s < 16; s <<= 1) {
+        se += __shfl_xor_sync(0xffffffffu, se, s);
+        sn += __shfl_xor_sync(0xffffffffu, sn, s);
+      }
+      xe[g] = fill ? -INFINITY : __shfl_sync(0xffffffffu, se, 0) * p.qscale;
+      xn[g] = direct ? -INFINITY : __shfl_sync(0xffffffffu, sn, 0) * p.qscale;
+    }
+    int b0, nb, d0, nd;
+    unit_pieces(sc, u, b0, nb, d0, nd);
+    float* po = p.part_o + ((int64_t)u * sc.S + nb + nd) * p.G * HKV_D;
+    float* pml = p.part_ml + ((int64_t)u * sc.S + nb + nd) * p.G * 2;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      if (g < p.G) {
+        const float m = fmaxf(xe[g], xn[g]);  // at least one token is finite
+        const float pe = fill ? 0.f : fast_exp2(xe[g] - m), pn = direct ? 0.f : fast_exp2(xn[g] - m);
+        if (side == 1) {
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = fmaf(pe, dq[i], pn * nv[i]);
+          float4* d = reinterpret_cast<float4*>(po + g * HKV_D + 8 * pq);
+          d[0] = make_float4(o[0], o[1], o[2], o[3]);
+          d[1] = make_float4(o[4], o[5], o[6], o[7]);
+        }
+        if (lane == 16) *reinterpret_cast<float2*>(pml + 2 * g) = make_float2(m, pe + pn);
+      }
+    }
+    // publish the partial (release by lane 0 after the warp's writes), then
+    // the unit's last contributor merges
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atom_add_acq_rel_gpu(&p.counters[u], 1) == nb + nd;
+    __syncwarp();
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      for (int g = 0; g < p.G; ++g) merge_head<false>(p, u, g, nb + nd + 1);
+      __syncwarp();
+      if (lane == 0) p.counters[u] = 0;
+    }
+  }
+  state_arrive_finish(p, state_arrive_start(p, s_roles));
+}
+
 // ---------------------------------------------------------------- the persistent kernel
 // STATS: record where the attention mass falls (DecodeParams::tile_stats); a
 // separate instantiation so that the plain kernel's tile loop stays unchanged.
-template <int FMT, int GROUP, typename DTy, bool STATS>
-__global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+// APPEND: the decode step's append runs in the same launch (append_units).
+template <int FMT, int GROUP, typename DTy, bool STATS, bool APPEND>
+__global__ void __launch_bounds__(decode_threads(FMT, APPEND), 1)
+    decode_kernel(const __grid_constant__ DecodeParams p) {
+  static_assert(!(STATS && APPEND), "the statistics and the fused append are separate instantiations");
   constexpr int NG = HKV_D / GROUP;
   constexpr int NM = kTileI4 * NG;  // metadata entries per array of a tile
   constexpr int kSlot = slot_bytes(FMT, GROUP);
   constexpr int kExp = expand_warps(FMT);
+  constexpr int kExtra = APPEND ? 1 : 0;  // partials per unit besides the pipeline's: the append's
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t ready_bar[kMaxSlots];
   __shared__ __align__(8) uint64_t empty_bar[kMaxSlots];
   __shared__ int2 s_info[kMaxSlots];  // ref: per slot, from the issue warp: (segment or -1 = done, valid tokens)
   __shared__ int s_last;
+  __shared__ int s_roles;  // APPEND: roles of this CTA done reading the cache state
 
   // the 128-byte swizzle of the dense tiles repeats every 1024 bytes: align the ring
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -874,8 +1167,12 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   // The next grid in the stream may start its prologue now (it waits for this one
-  // before touching global memory, as this one does below).
-  griddep_launch_dependents();
+  // before touching global memory, as this one does below). In early mode the
+  // trigger waits until this grid has waited for the one before it (thread 0,
+  // consumer section): a grid then starts only once every grid two or more
+  // launches back has completed, which is what lets it read its cache early.
+  const bool early = APPEND && p.early;
+  if (!early) griddep_launch_dependents();
   Piece first = first_piece_head(p, c, end);  // parameters only
   uint8_t* qbuf = reinterpret_cast<uint8_t*>(comb + kConsumerWarps * p.G * HKV_D + kConsumerWarps * 16);
   if (warp == kConsumerWarps - 1 && lane < nsl) {  // a warp whose first work waits anyway
@@ -884,13 +1181,21 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
     mbar_init(&empty_bar[lane], kGroupWarps);
     fence_barrier_init();
   }
+  if (APPEND && threadIdx.x == 0) s_roles = 0;
   // Global memory from here on. The first piece's sequence length (and, for the
-  // consumers, its query rows) load across the barrier.
-  griddep_wait();
-  const int first_len = first.valid ? seg_len(p, first.u, first.seg) : 0;
-  if (warp < kConsumerWarps && p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
+  // consumers, its query rows) load across the barrier. Early mode: the cache
+  // (state, page table, pages, dense rows) was completed by a grid two or more
+  // launches back, so it is read, and the ring filled, before the wait; every
+  // role waits on its own before it reads the query or the new token (made by
+  // the grid just before) and before its first global write.
+  if (!early) griddep_wait();
+  const int2 first_st = first.valid ? seg_state<APPEND>(p, first.u, first.seg) : make_int2(0, -1);
+  if (!early && warp < kConsumerWarps && p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
   __syncthreads();
-  if (first.valid) piece_fill_len(p, end, first, first_len);
+  if (first.valid) {
+    piece_fill_len(p, end, first, first_st.x);
+    first.skip = first_st.y;
+  }
 
   if (warp >= kConsumerWarps) {
     if (warp < kIssueWarp + kIssueWarps) {
@@ -908,8 +1213,18 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       // page ids of pages [pg0, pg0 + 32) of unit pg_u, one per lane (fetched 32 at a time)
       int pg_u = -1, pg0 = 0, pg_lane = -1;
       constexpr uint32_t kTileBytes = block_bytes(FMT, GROUP);  // one 128-token block = one tile
+      bool waited = !early;  // early mode: griddep_wait not yet done by this warp
       while (cu.valid) {
-        if (n >= nsl && !warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u, HKV_ISSUE_SLEEP_NS)) break;
+        if (n >= nsl) {
+          // early mode: the ring share is full; the consumers free slots only after
+          // the wait, so wait here first (a long preceding grid must not run the
+          // bounded slot wait out)
+          if (!waited) {
+            griddep_wait();
+            waited = true;
+          }
+          if (!warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u, HKV_ISSUE_SLEEP_NS)) break;
+        }
         uint8_t* sb = ring + ri.slot * kSlot;
         uint64_t* fb = &full_bar[ri.slot];
         const int u = cu.pc.u;
@@ -955,6 +1270,10 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
         cursor_next(p, end, cu);
         if (cu.valid) cursor_next(p, end, cu);
       }
+      if constexpr (APPEND) {
+        if (!waited) griddep_wait();  // before the first global write (the arrival)
+        state_arrive_finish(p, state_arrive_start(p, &s_roles));  // the cursor has read its last length
+      }
       // an end-of-work load (a plain arrive, no copy) for expansion warp w, which
       // takes the loads of this warp's parity
       if (kExp > 0 && (n < nsl || warp_wait(&empty_bar[ri.slot], ri.phase ^ 1u))) {
@@ -968,7 +1287,12 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       if (lane == 0) {
         for (int i = max(w, n - nsl); i < n; i += 2) mbar_wait(&full_bar[i % nsl], (i / nsl) & 1);
       }
-    } else if constexpr (kExp > 0) {
+    } else {
+      // ================================================================ fused append (APPEND)
+      if constexpr (APPEND) {
+        if (warp == kAppendWarp) append_units<FMT, GROUP, DTy>(p, c, &s_roles);
+      }
+      if constexpr (kExp > 0) {
       // ================================================================ metadata expansion warps (ref)
       // expansion warp x takes the loads n with n % 2 == x (those of issue warp x),
       // until that warp's end-of-work load
@@ -989,6 +1313,7 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready_bar[re.slot]);
         for (int i = 0; i < kExp; ++i) re.advance(nsl);
+      }
       }
     }
     return;
@@ -1018,7 +1343,15 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
   const int vs_off = (t0 / 2) * NG;  // f16x2 words
   // the query rows of the current piece's unit (qbuf) are prefetched during the
   // previous piece (the first piece's before the barrier setup)
+  if (early) {
+    griddep_wait();
+    if (threadIdx.x == 0) griddep_launch_dependents();
+    if (p.q_async && first.valid) q_prefetch(p, first.u, qbuf);
+  }
   Piece pc = first;
+  bool state_done = false;   // APPEND: the consumers' arrival on the state counter is made
+  bool arr_pending = false;  // ... and its count (arr_old, warp 0) not yet consumed
+  int arr_old = 0;
   while (pc.valid) {
     const int u = pc.u, b = u / p.Hkv, hk = u - b * p.Hkv;
     // ---- begin piece: query fragments for this unit
@@ -1080,10 +1413,19 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
     // the next piece: its length and its query rows load while this piece runs
     Piece nx = pc;
     next_piece_head(p, end, nx);
-    const int nlen = nx.valid ? seg_len(p, nx.u, nx.seg) : 0;
+    const int2 nst = nx.valid ? seg_state<APPEND>(p, nx.u, nx.seg) : make_int2(0, -1);
     if (p.q_async && nx.valid) {
       consumer_sync();  // every consumer has read qbuf
       q_prefetch(p, nx.u, qbuf);
+    }
+    if constexpr (APPEND) {
+      // the consumers' last state read lies behind them (and behind a consumer
+      // barrier: the prologue's __syncthreads or the previous piece's end):
+      // warp 0 arrives for all of them, the count is consumed after the tiles
+      if (!nx.valid && !state_done) {
+        if (warp == 0) arr_old = state_arrive_start(p, &s_roles);
+        state_done = arr_pending = true;
+      }
     }
     ws_reset<NG>(ws);
 
@@ -1155,7 +1497,8 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
           }
         }
         const uint32_t slot = smem_u32(sl);
-        dense_subtile<DTy, NG>(ws, slot, dt0, k * kTileD + dt0 + r < pc.len, qf, qs);
+        const int trow = k * kTileD + dt0 + r;  // this thread's score row in the segment
+        dense_subtile<DTy, NG>(ws, slot, dt0, trow < pc.len && trow != pc.skip, qf, qs);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[rc.slot]);
         rc.advance(nsl);
@@ -1163,6 +1506,10 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       }
     }
     n_base = n_end;
+    if (APPEND && arr_pending) {
+      if (warp == 0) state_arrive_finish(p, arr_old);
+      arr_pending = false;
+    }
 
     // ---- end piece: per-warp partials -> shared memory -> one partial for the piece
     {
@@ -1234,80 +1581,11 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
       // and whose acquire, followed by the barrier, orders the merge's loads of the
       // other CTAs' partials after their releases.
       consumer_sync();
-      if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.counters[u], 1) == nb + nd - 1;
+      if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.counters[u], 1) == nb + nd + kExtra - 1;
       consumer_sync();
       if (s_last) {
         // last piece of the unit: merge all its partials (warp h: head h)
-        const int n = nb + nd;
-        const float* ml_u = p.part_ml + (int64_t)u * sc.S * p.G * 2;
-        const float* o_u = p.part_o + (int64_t)u * sc.S * p.G * HKV_D;
-        for (int h = warp; h < p.G; h += kConsumerWarps) {
-          // partial k's (m, l) in lane k; the first 8 partials' o rows load in
-          // the same round trip (the usual unit has at most 8 partials)
-          const float2* mlp = reinterpret_cast<const float2*>(ml_u) + h;
-          const float4* op = reinterpret_cast<const float4*>(o_u + h * HKV_D) + lane;
-          const int ostep = p.G * HKV_D / 4;  // float4s per partial
-          const float2 ml0 = lane < n ? __ldcg(mlp + lane * p.G) : make_float2(kNoMax, 0.f);
-          float4 v[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = i < n ? __ldcg(op + i * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
-          float M = ml0.x;
-          for (int k = lane + 32; k < n; k += 32) M = fmaxf(M, __ldcg(mlp + k * p.G).x);
-#pragma unroll
-          for (int sft = 16; sft > 0; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
-          float wk = lane < n ? fast_exp2(ml0.x - M) : 0.f;
-          float L = wk * ml0.y;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float w = __shfl_sync(0xffffffffu, wk, i);
-            acc.x = fmaf(w, v[i].x, acc.x);
-            acc.y = fmaf(w, v[i].y, acc.y);
-            acc.z = fmaf(w, v[i].z, acc.z);
-            acc.w = fmaf(w, v[i].w, acc.w);
-          }
-          // partials 8.. (8 per batch, all loads in flight before the first use)
-          for (int k0 = 8; k0 < n; k0 += 8) {
-            if (k0 % 32 == 0) {
-              const float2 mlk = k0 + lane < n ? __ldcg(mlp + (k0 + lane) * p.G) : make_float2(kNoMax, 0.f);
-              wk = k0 + lane < n ? fast_exp2(mlk.x - M) : 0.f;
-              L = fmaf(wk, mlk.y, L);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              v[i] = k0 + i < n ? __ldcg(op + (k0 + i) * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float w = __shfl_sync(0xffffffffu, wk, (k0 + i) & 31);
-              acc.x = fmaf(w, v[i].x, acc.x);
-              acc.y = fmaf(w, v[i].y, acc.y);
-              acc.z = fmaf(w, v[i].z, acc.z);
-              acc.w = fmaf(w, v[i].w, acc.w);
-            }
-          }
-#pragma unroll
-          for (int sft = 16; sft > 0; sft >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sft);
-          if (STATS && lane == 0) {
-            p.unit_ml[((int64_t)u * 8 + h) * 2] = M;
-            p.unit_ml[((int64_t)u * 8 + h) * 2 + 1] = L;
-          }
-          const int hq = hk * p.G + h;
-          if (p.out_o) {
-            reinterpret_cast<float4*>(p.out_o + ((int64_t)b * p.Hq + hq) * HKV_D)[lane] = acc;
-            if (lane == 0) {
-              // a row that attended to no token reports m = -inf
-              p.out_ml[((int64_t)b * p.Hq + hq) * 2] = L > 0.f ? M : -INFINITY;
-              p.out_ml[((int64_t)b * p.Hq + hq) * 2 + 1] = L;
-            }
-          } else {
-            const float inv = L > 0.f ? 1.f / L : 0.f;
-            const int64_t o = (int64_t)b * p.out_sb + (int64_t)hq * p.out_sh + 4 * lane;
-            store_any(p.out, p.out_dtype, o + 0, acc.x * inv);
-            store_any(p.out, p.out_dtype, o + 1, acc.y * inv);
-            store_any(p.out, p.out_dtype, o + 2, acc.z * inv);
-            store_any(p.out, p.out_dtype, o + 3, acc.w * inv);
-          }
-        }
+        for (int h = warp; h < p.G; h += kConsumerWarps) merge_head<STATS>(p, u, h, nb + nd + kExtra);
         consumer_sync();
         if (threadIdx.x == 0) p.counters[u] = 0;
       }
@@ -1315,7 +1593,16 @@ __global__ void __launch_bounds__(decode_threads(FMT), 1) decode_kernel(const __
     }
     if (!alive) break;
     pc = nx;
-    if (pc.valid) piece_fill_len(p, end, pc, nlen);
+    if (pc.valid) {
+      piece_fill_len(p, end, pc, nst.x);
+      pc.skip = nst.y;
+    }
+  }
+  if constexpr (APPEND) {
+    if (!state_done) {  // no piece at all, or a timed-out wait ended the loop early
+      consumer_sync();
+      if (warp == 0) state_arrive_finish(p, state_arrive_start(p, &s_roles));
+    }
   }
   cp_async_wait_all();
 }

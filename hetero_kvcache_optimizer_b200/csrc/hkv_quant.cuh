@@ -66,9 +66,13 @@ __device__ __forceinline__ uint32_t min_code(float x, const MinParams& p) {
 // packed codes + metadata of the token into the K or V half (role) of store
 // slot (page, off).
 // All 32 lanes of the warp must call it (the shuffles use the full mask);
-// lanes with active == false only take part in the shuffles.
+// lanes with active == false only take part in the shuffles. With deq != null
+// the lane also gets its 8 values back as the dequantiser computes them, in
+// fp32: (q - zp) * scale (ref, KVCompressor.decompress) or q * scale + min
+// (fp16min).
 __device__ __forceinline__ void quantise_token(const float (&v)[8], bool active, int role, int fmt, int group,
-                                               const hkv_int4_store& st, int64_t page, int off) {
+                                               const hkv_int4_store& st, int64_t page, int off,
+                                               float* deq = nullptr) {
   const int lane = threadIdx.x & 31;
   const int p = lane & 15;
   float mn = v[0], mx = v[0];
@@ -93,6 +97,13 @@ __device__ __forceinline__ void quantise_token(const float (&v)[8], bool active,
     mp = min_params(mn, mx);
 #pragma unroll
     for (int i = 0; i < 8; ++i) packed |= min_code(v[i], mp) << (4 * i);
+  }
+  if (deq) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float c = static_cast<float>((packed >> (4 * i)) & 0xFu);
+      deq[i] = fmt == HKV_FMT_REF ? __fmul_rn(__fsub_rn(c, rp.zpf), rp.scale) : __fadd_rn(__fmul_rn(c, mp.sf), mp.mf);
+    }
   }
   // Gather: lane (4w + j) collects byte j of the four lanes of its 32-dim block w.
   const int w = p >> 2, j = p & 3;

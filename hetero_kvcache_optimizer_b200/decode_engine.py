@@ -2,13 +2,14 @@
 
 Per layer it keeps the three zones of HeteroKVManager (src/memory/manager.py:
 sink + recent tail in fp16/bf16 HBM, the evicted body as packed INT4 pages)
-and runs one decode step as
+and runs one decode step as ONE launch (``fused_append``, the default):
 
-    append_kv  (new token -> recent ring; oldest ring row -> INT4 body)
-    decode     (split-KV GQA attention over body + sink/recent, LSE merge)
+    decode_append  (new token -> recent ring; oldest ring row -> INT4 body;
+                    split-KV GQA attention over body + sink/recent, LSE merge)
 
-All state (lengths, ring heads) lives on the device, so a whole multi-layer
-step can be captured once into a CUDA graph and replayed every token.
+or, with ``fused_append=False``, as the two launches it fuses (append_kv, then
+decode). All state (lengths, ring heads) lives on the device, so a whole
+multi-layer step can be captured once into a CUDA graph and replayed every token.
 """
 from __future__ import annotations
 
@@ -25,7 +26,8 @@ class TieredKVDecoder:
                  sink: int = 64, recent: int = 1024, body_capacity: int = 32768,
                  fmt: str = "fp16min", group: int = 32, page_tokens: int = 256,
                  kv_dtype: torch.dtype = torch.float16, out_dtype: torch.dtype = torch.float32,
-                 device="cuda", ctas: int = 0):
+                 device="cuda", ctas: int = 0, fused_append: bool = True):
+        self.fused_append = fused_append
         self.num_layers, self.batch = num_layers, batch
         self.q_heads, self.kv_heads = q_heads, kv_heads
         self.sink, self.recent = sink, recent
@@ -78,12 +80,31 @@ class TieredKVDecoder:
 
     # ------------------------------------------------------------------ decode
     def step_layer(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
-                   out: Optional[torch.Tensor] = None, len_hint: Optional[int] = None) -> torch.Tensor:
+                   out: Optional[torch.Tensor] = None, len_hint: Optional[int] = None,
+                   early: bool = False) -> torch.Tensor:
+        """One layer's decode step. ``early``: the launch just before this one on
+        the stream does not write this layer's cache (another layer's step), so
+        the fused launch may stream the cache while that one finishes."""
         st, d = self.stores[layer], self.dense[layer]
-        kv.append_kv(k_new, v_new, d, self.sink, st)
         hint = len_hint if len_hint is not None else self.body_len + 1
+        if self.fused_append:
+            return kv.decode_append(q, k_new, v_new, d, self.sink, st, out_dtype=self.out_dtype, out=out,
+                                    ctas=self.ctas, body_len=hint, dense_len=self.sink + self.recent,
+                                    early=early)
+        kv.append_kv(k_new, v_new, d, self.sink, st)
         return kv.decode(q, st, d, out_dtype=self.out_dtype, out=out, ctas=self.ctas,
                          body_len=hint, dense_len=self.sink + self.recent)
+
+    @property
+    def launches_per_layer(self) -> int:
+        """Kernel launches of one layer's decode step."""
+        return 1 if self.fused_append else 2
+
+    @property
+    def _early(self) -> bool:
+        # a step runs the layers in order, so with two or more layers the launch
+        # before a layer's is always another layer's (which never writes its cache)
+        return self.num_layers >= 2
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
              out: Optional[torch.Tensor] = None, len_hint: Optional[int] = None) -> torch.Tensor:
@@ -92,7 +113,7 @@ class TieredKVDecoder:
             out = torch.empty(self.num_layers, self.batch, self.q_heads, 128, dtype=self.out_dtype,
                               device=self.device)
         for l in range(self.num_layers):
-            self.step_layer(l, q[l], k_new[l], v_new[l], out=out[l], len_hint=len_hint)
+            self.step_layer(l, q[l], k_new[l], v_new[l], out=out[l], len_hint=len_hint, early=self._early)
         self.body_len += 1
         return out
 
@@ -123,12 +144,12 @@ class TieredKVDecoder:
         snap = self._snapshot()
         with torch.cuda.stream(s):
             for l in range(Lyr):
-                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint, early=self._early)
         s.synchronize()
         self._restore(snap)
         with torch.cuda.graph(g, stream=s):
             for l in range(Lyr):
-                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint, early=self._early)
         torch.cuda.current_stream(self.device).wait_stream(s)
         self.graph = g
         self._static = (q, kn, vn, out)
@@ -168,7 +189,7 @@ class TieredKVDecoder:
         snap = self._snapshot()
         with torch.cuda.stream(s):
             for l in range(Lyr):
-                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint, early=self._early)
         s.synchronize()
         self._restore(snap)
         g = torch.cuda.CUDAGraph()
@@ -186,7 +207,7 @@ class TieredKVDecoder:
                 for i, (a, _) in enumerate(in_chunks):
                     if l == a:  # the first layer that reads input copy i
                         s.wait_event(ev_in[i])
-                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint)
+                self.step_layer(l, q[l], kn[l], vn[l], out=out[l], len_hint=hint, early=self._early)
                 a, b = chunks[ci]
                 if l == b - 1:
                     ev_out[ci].record(s)

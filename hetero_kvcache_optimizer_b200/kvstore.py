@@ -267,6 +267,48 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
     return out[:, :, None, :] if squeeze else out
 
 
+def decode_append(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, dense: DenseKV, sink: int,
+                  store: Int4KVStore, sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
+                  ctas: int = 0, out: Optional[torch.Tensor] = None, body_len: Optional[int] = None,
+                  dense_len: Optional[int] = None, early: bool = False, stream=None) -> torch.Tensor:
+    """One decode step in one launch: ``append_kv(k_new, v_new, dense, sink,
+    store)`` then ``decode(q, store, dense)``, with the same cache contents and
+    state afterwards and the attention over the cache after the append.
+    ``body_len`` / ``dense_len``: host-side length hints sizing the schedule
+    (upper bounds of the lengths after the step). ``early``: the kernel launched
+    just before this one on the stream does not write this cache (e.g. another
+    layer's step), so the launch may stream the cache while it finishes."""
+    _require_cuda(q, k_new, v_new)
+    if q.dim() == 4:
+        q = q[:, :, 0]
+    if k_new.dim() == 4:
+        k_new, v_new = k_new[:, :, 0], v_new[:, :, 0]
+    if k_new.dtype != dense.dtype or v_new.dtype != dense.dtype:
+        raise TypeError("k_new / v_new must have the dense segment's dtype")
+    if k_new.stride(-1) != 1 or k_new.stride() != v_new.stride():
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    B, Hq, D = q.shape
+    Hkv = store.kv_heads
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=out_dtype, device=q.device)
+    st = store.struct(body_len)
+    ds = dense.struct(dense_len)
+    lib = L.load()
+    nbytes = lib.hkv_decode_workspace_bytes(ctypes.byref(st), ctypes.byref(ds), B, Hq, Hkv, D, ctas)
+    if nbytes == 0:
+        raise RuntimeError("hkv_decode_workspace_bytes: unsupported decode configuration")
+    ws = workspace(nbytes, q.device, stream)
+    L.check(lib.hkv_decode_append(
+        q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1), k_new.data_ptr(), v_new.data_ptr(),
+        k_new.stride(0), k_new.stride(1), ctypes.byref(st), ctypes.byref(ds), sink, dense.lengths.data_ptr(),
+        dense.ring_head.data_ptr(), store.lengths.data_ptr(), B, Hq, Hkv, D, float(sm_scale), ctas,
+        ws.data_ptr(), ws.numel(), out.data_ptr(), dtype_code(out.dtype), out.stride(0), out.stride(1),
+        L.APPEND_EARLY if early else 0, _stream(stream)), "hkv_decode_append")
+    return out
+
+
 def decode_scored(q: torch.Tensor, store: Int4KVStore, dense: Optional[DenseKV],
                   sm_scale: Optional[float] = None, out_dtype: torch.dtype = torch.float32,
                   ctas: int = 0, out: Optional[torch.Tensor] = None,

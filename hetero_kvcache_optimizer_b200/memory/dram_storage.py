@@ -87,21 +87,31 @@ class DRAMStorageManager:
         return True
 
     def _put(self, chunk_key: str, entry: Dict[str, torch.Tensor], nbytes: int) -> None:
+        # page-locked space for every tensor first: if an allocation fails the
+        # exception leaves the table (and an entry being replaced) untouched
+        raw_of: Dict[str, torch.Tensor] = {}
+        try:
+            for k, t in entry.items():
+                if not (t.device.type == "cpu" and t.is_pinned()):
+                    raw_of[k] = self._arena.alloc(t.element_size() * t.nelement())
+        except BaseException:
+            for r in raw_of.values():
+                self._arena.release(r)
+            raise
         if chunk_key in self._table:
             self._drop(chunk_key)
         pinned: Dict[str, torch.Tensor] = {}
-        raws: List[torch.Tensor] = []
+        raws: List[torch.Tensor] = list(raw_of.values())
         ev = None
         on_gpu = any(t.is_cuda for t in entry.values())
         if on_gpu and self._stream is None:
             dev = next(t.device for t in entry.values() if t.is_cuda)
             self._stream = torch.cuda.Stream(device=dev)
         for k, t in entry.items():
-            if t.device.type == "cpu" and t.is_pinned():
+            if k not in raw_of:
                 pinned[k] = t
                 continue
-            raw = self._arena.alloc(t.element_size() * t.nelement())
-            raws.append(raw)
+            raw = raw_of[k]
             dst = raw[: t.element_size() * t.nelement()].view(t.dtype).view(t.shape)
             if t.is_cuda:
                 self._stream.wait_stream(torch.cuda.current_stream(t.device))

@@ -221,13 +221,49 @@ hkv_status hkv_decode_plan(const hkv_int4_store* body, const hkv_dense_kv* dense
 /* out[b][hq][:] = softmax(q[b][hq] . K^T * sm_scale) V over the union of the
  * INT4 body and the dense segment of KV head hq / (Hq/Hkv) (G = Hq/Hkv <= 8).
  * q: [B][Hq][128] fp16/bf16; out: [B][Hq][128] in out_dtype (f32/f16/bf16).
- * Either body or dense may be NULL. */
+ * Either body or dense may be NULL.
+ * Precision: the INT4 tiles multiply on the f16 tensor cores with fp32
+ * accumulation, so a bf16 query is rounded to f16 for them (|q| must stay below
+ * the f16 range, 65504, or its products overflow to inf); the dense tiles use
+ * the dense segment's dtype (a query is rounded to it: use bf16 queries with a
+ * bf16 cache) and P is rounded to that dtype for P.V. The tests hold
+ * max |out - ref| <= 2e-3 * ||ref||_2 per row against fp32 attention. */
 hkv_status hkv_decode_attn(const void* q, int32_t q_dtype, int64_t q_stride_b,
                            int64_t q_stride_h, const hkv_int4_store* body,
                            const hkv_dense_kv* dense, int32_t B, int32_t Hq, int32_t Hkv,
                            int32_t D, float sm_scale, int32_t ctas, void* workspace,
                            size_t workspace_bytes, void* out, int32_t out_dtype,
                            int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream);
+
+/* One whole decode step of a layer in ONE launch: hkv_append_kv followed by
+ * hkv_decode_attn (replaces HeteroKVManager._decode_update,
+ * src/memory/manager.py:588-664, plus the attention over the updated cache,
+ * fused_dequant_attn_decode, src/quantization/fused_dequant_attn.py:254-331).
+ * The new token k_new/v_new [B][Hkv][128] (the dense segment's dtype, strides in
+ * elements, 16-byte aligned rows) enters the cache exactly as hkv_append_kv
+ * would put it there (same codes, same ring row, same state transition of
+ * dense_len / ring_head / body_len), and `out` is the attention of q over the
+ * cache after the append. The attention streams the cache as it was before the
+ * step (the ring row the step overwrites is left out) and folds the evicted
+ * token (as quantised) and the new token in as one extra partial per unit.
+ * body->lengths must be body_len and dense->lengths dense_len (device arrays,
+ * updated in place once every CTA has read them). Workspace as
+ * hkv_decode_attn (same size); B*Hkv < 65536.
+ * flags: 0, or HKV_APPEND_EARLY: the caller guarantees that the kernel
+ * launched on `stream` just before this call does not write this cache (body
+ * pages, dense rows, the three state arrays); e.g. the layers of a
+ * multi-layer step, each layer's cache touched once per step. The launch then
+ * reads its cache and streams the first tiles while that kernel finishes
+ * (programmatic dependent launch), and only the query, the new token and its
+ * own writes wait for it. Without the guarantee pass 0. */
+#define HKV_APPEND_EARLY 1
+hkv_status hkv_decode_append(const void* q, int32_t q_dtype, int64_t q_stride_b, int64_t q_stride_h,
+                             const void* k_new, const void* v_new, int64_t new_stride_b, int64_t new_stride_h,
+                             const hkv_int4_store* body, const hkv_dense_kv* dense, int32_t sink,
+                             int32_t* dense_len, int32_t* ring_head, int32_t* body_len, int32_t B, int32_t Hq,
+                             int32_t Hkv, int32_t D, float sm_scale, int32_t ctas, void* workspace,
+                             size_t workspace_bytes, void* out, int32_t out_dtype, int64_t out_stride_b,
+                             int64_t out_stride_h, int32_t flags, hkv_stream_t stream);
 
 /* hkv_decode_attn, plus where the attention mass fell, for the prefetch policy
  * (the reference aggregates accumulated token scores into block means on the

@@ -213,18 +213,25 @@ def test_append_then_decode_equals_oracle(hkv):
 
 def test_full_size_cfg1_layer_vs_torch_fp32(hkv):
     """Configuration-1 layer at full size (B8, Hq32/Hkv8, 31,680 INT4 + 1,088
-    fp16 tokens, fp16min), against an fp32 torch SDPA over the dequantised
-    cache (dequantize_pack is pinned bit-exact to the oracle above)."""
+    fp16 tokens, fp16min), K/V ~ N(0, 1) with 4 seeded K channels per KV head
+    scaled x10 (the configuration's outliers, in the INT4 body and in the
+    dense sink/recent rows alike), against an fp32 torch SDPA over the
+    dequantised cache (dequantize_pack is pinned bit-exact to the oracle above)."""
     B, Hkv, G, nb, sink, recent = 8, 8, 4, 31680, 64, 1024
     gen = torch.Generator(device="cuda").manual_seed(1)
-    k = torch.randn(B, Hkv, nb, 128, device="cuda", generator=gen).half()
+    k = torch.randn(B, Hkv, nb, 128, device="cuda", generator=gen)
     v = torch.randn(B, Hkv, nb, 128, device="cuda", generator=gen).half()
-    store = hkv.Int4KVStore(B, Hkv, nb, fmt="fp16min", group=32)
-    hkv.prefill(store, k, v)
-    del k, v
     dense = hkv.DenseKV(B, Hkv, sink + recent)
     dense.k.normal_(generator=gen)
     dense.v.normal_(generator=gen)
+    for h in range(Hkv):
+        ch = torch.randperm(128, device="cuda", generator=gen)[:4]
+        k[:, h, :, ch] *= 10.0
+        dense.k[:, h, :, ch] *= 10.0
+    k = k.half()
+    store = hkv.Int4KVStore(B, Hkv, nb, fmt="fp16min", group=32)
+    hkv.prefill(store, k, v)
+    del k, v
     dense.set_lengths(sink + recent)
     q = torch.randn(B, Hkv * G, 128, device="cuda", generator=gen).to(torch.bfloat16)
     out = hkv.decode(q, store, dense)

@@ -32,20 +32,24 @@ def _oracle_step(eng, q: torch.Tensor) -> np.ndarray:
     return np.stack(outs)
 
 
-def _engine(fmt, group):
+def _engine(fmt, group, fused=True):
     from hetero_kvcache_optimizer_b200.decode_engine import TieredKVDecoder
     L_, B, Hq, Hkv, S = 2, 2, 8, 2, 300
-    eng = TieredKVDecoder(L_, B, Hq, Hkv, sink=16, recent=64, body_capacity=1024, fmt=fmt, group=group)
+    eng = TieredKVDecoder(L_, B, Hq, Hkv, sink=16, recent=64, body_capacity=1024, fmt=fmt, group=group,
+                          fused_append=fused)
     k, v = ko.make_kv(7, B, Hkv, S)
     for l in range(L_):
         eng.prefill_layer(l, t16(k * (1 + 0.1 * l)), t16(v * (1 - 0.1 * l)))
     return eng
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("fmt,group", [("fp16min", 32), ("ref", 32), ("fp16min", 128)])
-def test_engine_steps_eager_and_graph(fmt, group):
+def test_engine_steps_eager_and_graph(fmt, group, fused):
+    """Eager steps and graph replays; fused: one decode-append launch per layer,
+    else append_kv then decode."""
     rng = np.random.default_rng(11)
-    eager, graph = _engine(fmt, group), _engine(fmt, group)
+    eager, graph = _engine(fmt, group, fused), _engine(fmt, group, fused)
     L_, B, Hq, Hkv = eager.num_layers, eager.batch, eager.q_heads, eager.kv_heads
     graph.capture(max_steps=4)
     q_s, kn_s, vn_s, out_s = graph.static_buffers

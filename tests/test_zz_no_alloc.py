@@ -54,4 +54,13 @@ def test_static_matches_workspace_entry_point_twice():
             torch.cuda.synchronize()
             err = (out - ref).abs().max().item()
             assert np.isfinite(err) and err <= 1e-6 * max(1.0, ref.abs().max().item()), err
+            # and directly against the CPU oracle (dequant-then-softmax over the
+            # same cache), at the tolerance every decode parity test uses
+            from oracle import kv_oracle as ko
+            from tests.hkv_testutil import dequant_side
+            nb, nd = int(st.lengths[0]), int(d.lengths[0])
+            kd = np.concatenate([dequant_side(st, 0, nb), d.k[:, :, :nd].float().cpu().numpy()], axis=2)
+            vd = np.concatenate([dequant_side(st, 1, nb), d.v[:, :, :nd].float().cpu().numpy()], axis=2)
+            oracle = ko.decode_attention(q.float().cpu().numpy(), kd, vd)
+            assert ko.rel_err(out.cpu().numpy(), oracle) < 2e-3
     assert L.device_error() == 0
