@@ -4,9 +4,9 @@
 Default workload (benchmark spec configuration 1, Llama-3.1-8B-shaped decode):
 32 layers, batch 8, 32 query / 8 KV heads, head_dim 128, 32768-token context
 per sequence: 64 sink + 1024 recent tokens in fp16, 31,680 INT4 tokens
-(group 32, fp16 scale + fp16 zero = min). One step = for every layer, append
-the new token (ring eviction -> INT4 quantise) + split-KV decode attention over
-the whole context + LSE merge. Synthetic seeded data (K/V ~ N(0,1) with four x10
+(group 32, fp16 scale + fp16 zero = min). One step = for every layer, one fused
+launch: append the new token (ring eviction -> INT4 quantise) + split-KV decode
+attention over the whole context + LSE merge (--no-fused: two launches). Synthetic seeded data (K/V ~ N(0,1) with four x10
 outlier K channels per head, bf16 queries); the per-step working set (12 GB)
 is far larger than L2, so no flush is needed between steps.
 
@@ -16,7 +16,9 @@ is far larger than L2, so no flush is needed between steps.
 
 With N > 1 (torchrun, one rank per GPU) every rank decodes its own 8
 sequences (batch x KV-head sharding, no collective on the data path): weak
-scaling, value = all ranks' bytes / max-over-ranks time.
+scaling, value = all ranks' bytes / max-over-ranks time. The N > 1 line also
+carries a short config-4 variant-B measurement (``seqsplit_cfg4b``: each
+sequence split over the ranks, one NCCL all-gather of the partials per layer).
 """
 from __future__ import annotations
 
@@ -479,28 +481,26 @@ def run_cfg3(args) -> None:
 
 
 # --------------------------------------------------------------------------- config 4, variant B
-def run_cfg4b(args, world: int, rank: int, local: int) -> None:
-    """Llama-3.1-8B shape, B sequences of `ctx` tokens, each sequence's INT4 body
-    split in contiguous page-aligned slices over the ranks (the last rank also
-    holds the 64 sink + 1024 recent fp16 tokens); per layer: partial attention on
-    every rank, one all-gather of the partials, LSE merge."""
+def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt: str, world: int, rank: int,
+                     dev) -> dict:
+    """Config 4 variant B on this process group: Llama-3.1-8B shape, B sequences
+    of `ctx` tokens, each sequence's INT4 body split in contiguous page-aligned
+    slices over the ranks (the last rank also holds the 64 sink + 1024 recent
+    fp16 tokens); per layer: partial attention on every rank, one all-gather of
+    the partials, LSE merge. Returns the max-over-ranks step time and the
+    aggregate figures (every rank gets the same dict)."""
     import torch
     import torch.distributed as dist
-    from datetime import timedelta
     from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv, seqsplit
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    B, Hq, Hkv, layers = args.batch, 32, 8, args.layers
+    Hq, Hkv = 32, 8
     sink, recent = 64, 1024
-    body_pages = (args.ctx - sink - recent) // 256
+    body_pages = (ctx - sink - recent) // 256
     p0, p1 = seqsplit.shard_range(body_pages, world, rank)
     ntok = (p1 - p0) * 256
     gen = torch.Generator(device=dev).manual_seed(40 + rank)
     stores, denses = [], []
     for l in range(layers):
-        st = kv.Int4KVStore(B, Hkv, max(ntok, 256), fmt=args.fmt, group=32, device=dev)
+        st = kv.Int4KVStore(B, Hkv, max(ntok, 256), fmt=fmt, group=32, device=dev)
         for t0 in range(0, ntok, 4096):
             n = min(4096, ntok - t0)
             x = torch.randn(B, Hkv, n, 128, device=dev, generator=gen).half()
@@ -523,7 +523,7 @@ def run_cfg4b(args, world: int, rank: int, local: int) -> None:
         for l in range(layers):
             seqsplit.decode(q[l], stores[l] if ntok else None, denses[l], out=out[l])
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -531,35 +531,52 @@ def run_cfg4b(args, world: int, rank: int, local: int) -> None:
     st_ = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st_)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record(st_)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / steps
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     derr = _lib.device_error(clear=True)
     if derr:
-        raise RuntimeError(f"device error bits {derr} during the benchmark")
-    per_tok = 2 * (64 + 4 * 4 + (4 if args.fmt == "ref" else 0))
+        raise RuntimeError(f"device error bits {derr} during the sequence-split benchmark")
+    per_tok = 2 * (64 + 4 * 4 + (4 if fmt == "ref" else 0))
     step_bytes = layers * (B * Hkv * (body_pages * 256 * per_tok + (sink + recent) * 512) + B * Hq * 128 * 6)
+    peak, _ = measured_peak()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    del stores, denses, q, out
+    return {"ms_per_step": round(ms, 4), "gbs": round(gbs, 2), "tokens_per_s": round(B / (ms * 1e-3), 1),
+            "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
+            "workload": f"config4 B: Llama-3.1-8B shape, B{B}, ctx {ctx} ({body_pages} INT4 pages + 64 sink + "
+                        f"1024 recent fp16 per unit), {layers} layers, sequence split over {world} GPU(s), one "
+                        f"NCCL all-gather of the partials per layer + LSE merge",
+            "gpu_launches": world * steps * layers * 2}
+
+
+def run_cfg4b(args, world: int, rank: int, local: int) -> None:
+    """Config 4 variant B as its own line (see seqsplit_measure)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    r = seqsplit_measure(args.batch, args.ctx, args.layers, args.steps, args.warmup, args.fmt, world, rank, dev)
     if rank == 0:
-        peak, _ = measured_peak()
-        gbs = step_bytes / (ms * 1e-3) / 1e9
         print(json.dumps({
             "metric": "config4 variant B: sequence-split INT4 decode attention, aggregate HBM GB/s and tokens/s",
-            "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "value": r["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16 mma (int4 storage, fp32 accum)", "data": "synthetic",
-            "config": {"workload": f"config4 B: Llama-3.1-8B shape, B{B}, ctx {args.ctx} ({body_pages} INT4 "
-                                   f"pages + 64 sink + 1024 recent fp16 per unit), {layers} layers, sequence "
-                                   f"split over {world} GPU(s), NCCL all-gather of partials + LSE merge",
-                       "kv_format": args.fmt, "layers": layers, "parallelism": f"seqsplit{world}"},
-            "tokens_per_s": round(B / (ms * 1e-3), 1),
-            "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
-            "gpu_launches": world * args.steps * layers * 2}))
+            "config": {"workload": r["workload"], "kv_format": args.fmt, "layers": args.layers,
+                       "parallelism": f"seqsplit{world}"},
+            "tokens_per_s": r["tokens_per_s"],
+            "pct_of_aggregate_measured_peak": r["pct_of_aggregate_measured_peak"],
+            "gpu_launches": r["gpu_launches"]}))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -749,6 +766,13 @@ def main():
     if derr:
         raise RuntimeError(f"device error bits {derr} during the benchmark")
 
+    # ---- N > 1: variant B of config 4 as well (sequence split + one NCCL
+    # all-gather of the partials per layer + LSE merge), short: 2 layers at
+    # B 64, 131,072-token context, strong scaling over this run's ranks
+    split = None
+    if world > 1:
+        split = seqsplit_measure(64, 131072, 2, 5, 3, args.fmt, world, rank, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = run_cpu_reference(args.cpu_steps, 1, lambda b, n: layer_bytes(b, n, args.fmt))
@@ -784,6 +808,8 @@ def main():
             "gpu_launches": world * args.steps * args.layers * eng.launches_per_layer,
             "clocks": clocks,
         }
+        if split is not None:
+            line["seqsplit_cfg4b"] = split
         if cpu is not None:
             line["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cpu.items()
                                     if k in ("value", "unit", "cores", "kind", "sample")}

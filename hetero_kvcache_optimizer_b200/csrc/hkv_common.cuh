@@ -133,7 +133,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 }
 
 // 1-D bulk async copy global -> this CTA's shared memory, completion counted on bar.
-// src, dst 16-byte aligned; bytes a multiple of 16. No multicast.
+// src, dst 16-byte aligned; bytes a multiple of 16. Into this CTA alone.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

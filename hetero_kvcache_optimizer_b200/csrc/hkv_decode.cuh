@@ -13,7 +13,7 @@
 // Pipeline. The loaded HBM latency on B200 is several microseconds, so an SM
 // needs ~200 KB of reads in flight: the ring has an even number (up to 12) of
 // slots, ten 20 KiB slots for fp16min group 32. Warps 8-9 issue the TMA copies
-// (no multicast), each the loads of one parity: INT4 tiles as one 1-D bulk copy
+// (each CTA its own copies), each the loads of one parity: INT4 tiles as one 1-D bulk copy
 // of their page block, dense tiles as one 5-D tensor copy per side with 128-byte
 // swizzle. fp16min blocks are consumed as stored; for ref blocks warps 10-11
 // first expand the group metadata in place into fp32 / f16x2 and zero what lies
@@ -763,7 +763,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32
 }
 
 // One tiled TMA load of a 5-D box (coordinates innermost first; x = 0 here, so
-// the 16-byte rule on the innermost coordinate holds). No multicast.
+// the 16-byte rule on the innermost coordinate holds), into this CTA alone.
 __device__ __forceinline__ void tma_tile_5d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w, int v,
                                             uint64_t* bar) {
   asm volatile(
