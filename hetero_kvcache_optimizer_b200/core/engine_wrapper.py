@@ -13,9 +13,12 @@ in front of them, so a stock attention layer sees the whole context. The fast
 path does not materialise anything: ``attend(q, layer_idx)`` runs the fused
 INT4 decode kernel over [sink ; INT4 body ; tail] of that layer.
 
-Policy features of the reference that are not rebuilt here (Method D
-query-aware retrieval, the adaptive window controller of paths A/B) are
-accepted as keywords and rejected when enabled, rather than silently ignored.
+With ``adaptive_self_healing`` the decode step follows the reference's paths A
+(``enable_triton``: the top-w_t DRAM chunks stay INT4 on the device in
+``_dram_quant_kv``) and B (they are dequantised to bf16 in front of [sink ;
+tail]), w_t from the manager's window controller. Method D (query-aware
+retrieval) is accepted as a keyword and rejected when enabled, rather than
+silently ignored.
 """
 from __future__ import annotations
 
@@ -35,9 +38,9 @@ class FusedHeteroCache(DynamicCache):
                  bandwidth_limiter=None, self_healing: bool = True, adaptive_self_healing: bool = False,
                  enable_method_d: bool = False, method_d_alpha: float = 1.0, **manager_kwargs):
         super().__init__()
-        if enable_method_d or adaptive_self_healing:
-            raise NotImplementedError("Method D and the adaptive retrieval window are policy features "
-                                      "outside this build's INT4 hot path")
+        if enable_method_d:
+            raise NotImplementedError("Method D (query-aware retrieval) is a policy feature outside this "
+                                      "build's INT4 hot path")
         self.sink_tokens = sink_tokens
         self.keep_tail = keep_tail
         self.chunk_size = chunk_size
@@ -57,6 +60,8 @@ class FusedHeteroCache(DynamicCache):
         self.real_seq_len = 0
         self._swap_in_tokens = 0
         self._pending_attention_weights: Optional[torch.Tensor] = None
+        self._dram_quant_kv: Optional[Dict[str, torch.Tensor]] = None  # path A's INT4 chunks
+        self._dram_quant_layer = -1
 
     def _ensure_manager(self, layer_idx: int) -> HeteroKVManager:
         if self._manager is None:
@@ -80,7 +85,21 @@ class FusedHeteroCache(DynamicCache):
         if mode == "decode" and last and self._pending_attention_weights is not None:
             m.update_attention_scores(self._pending_attention_weights)
             self._pending_attention_weights = None
-        if mode == "decode" and self.self_healing and self._swap_in_tokens > 0:
+        adaptive_count = None
+        if mode == "decode" and self.self_healing and self.adaptive_self_healing and self.enable_triton:
+            # path A (reference engine_wrapper.py:205-221): the top-w_t chunks stay
+            # INT4 on the device for a fused consumer; nothing is concatenated
+            self._dram_quant_kv = m.get_dram_chunks_quantized_adaptive(layer_idx)
+            self._dram_quant_layer = layer_idx
+        elif mode == "decode" and self.self_healing and self.adaptive_self_healing:
+            # path B (:223-234): the top-w_t chunks dequantised to bf16 in front
+            dk, dv, n = m.decompress_dram_chunks_adaptive(layer_idx)
+            adaptive_count = n
+            if dk is not None and n > 0:
+                out_k = torch.cat([dk.to(out_k.dtype), out_k], dim=-2)
+                out_v = torch.cat([dv.to(out_v.dtype), out_v], dim=-2)
+        elif mode == "decode" and self.self_healing and self._swap_in_tokens > 0:
+            # path C (:236-245): the whole INT4 body dequantised to bf16 in front
             dk, dv, n = m.decompress_dram_chunks(layer_idx)
             if dk is not None and n > 0:
                 out_k = torch.cat([dk.to(out_k.dtype), out_k], dim=-2)
@@ -88,7 +107,9 @@ class FusedHeteroCache(DynamicCache):
         if layer_idx == 0:
             self.real_seq_len += new_len
             if mode == "decode" and self.self_healing:
-                self._swap_in_tokens = m.count_dram_tokens(layer_idx=0)
+                self._swap_in_tokens = (adaptive_count if adaptive_count is not None
+                                        else 0 if self.adaptive_self_healing and self.enable_triton
+                                        else m.count_dram_tokens(layer_idx=0))
         return out_k, out_v
 
     def attend(self, q: torch.Tensor, layer_idx: int, sm_scale: Optional[float] = None,

@@ -16,15 +16,25 @@ Storage per layer (all on the device, sizes fixed at the first prefill):
 Decode attention runs over [sink ; INT4 body ; tail] in one fused kernel
 (``attend``): nothing is decompressed, concatenated or synchronised per step.
 
+With ``hbm_body_pages`` set, the INT4 body gets a host (DRAM) tier
+(``host_tier.HostTier``): the last ``hbm_body_pages`` pages per (layer,
+sequence x KV head) stay in HBM, older pages move to pinned host memory as the
+body grows, and ``attend`` stages a layer's host pages into a shared staging
+area (copied while the previous layer's attention runs) and reads them through
+the page table, as the reference's eviction to DRAM and swap-in do
+(manager.py:1231-1299, :779-821).
+
 Prefill evictions are also kept as the reference's DRAM entries
 (``l{layer}_e{n}``: unpacked u8 codes, f32 scales, u8 zero-points in pinned
 host memory, bit-exact with ``KVCompressor.compress``) when ``legacy_dram`` is
-set, so ``_dram_table``, ``swap_in_quantized`` and ``schedule_prefetch`` keep
-working for callers of the old API.
+set, so ``_dram_table``, ``swap_in_quantized``, ``schedule_prefetch`` and the
+adaptive self-healing retrievals (``get_dram_chunks_quantized_adaptive``,
+``decompress_dram_chunks_adaptive``: the top-w_t chunks by attention score,
+w_t from the window controller) keep working for callers of the old API.
 
 Not rebuilt (policy, outside the INT4 hot path): the HeavyHitter zone and its
 attention-competition queue (decode evictions go straight to the INT4 body),
-Method D query-aware retrieval, the adaptive/predictive prefetch controllers
+Method D query-aware retrieval, the predictive prefetch scheduler
 (``predictive_prefetch_step`` returns no keys). ``get_oracle_scores`` returns
 the attention mass accumulated per token by ``update_attention_scores``.
 """
@@ -35,9 +45,11 @@ from typing import Any, Dict, List, Optional, Tuple
 import torch
 
 from .. import kvstore as kv
+from ..policy.chunk_scores import DeviceWindowController
 from ..policy.prefetcher import AsyncPrefetcher
 from ..quantization.kv_compressor import KVCompressor
 from .dram_storage import DRAMStorageManager
+from .host_tier import HostTier
 
 
 class HeteroKVManager:
@@ -46,7 +58,7 @@ class HeteroKVManager:
                  group_size: int = 128, bits: int = 4, bandwidth_limiter=None,
                  enable_method_d: bool = False, method_d_alpha: float = 1.0, *,
                  body_capacity: Optional[int] = None, legacy_dram: bool = True,
-                 page_tokens: int = 256, kv_format: str = "ref"):
+                 page_tokens: int = 256, kv_format: str = "ref", hbm_body_pages: Optional[int] = None):
         if not enable_quant:
             raise ValueError("the INT4 body is the point of this build: enable_quant=False is not supported")
         if bits != 4:
@@ -78,6 +90,16 @@ class HeteroKVManager:
         self._chunk_tokens: Dict[str, int] = {}
         self._token_scores: Optional[torch.Tensor] = None
         self._last_attention_weights: Optional[torch.Tensor] = None
+        # host (DRAM) tier of the INT4 body: the last hbm_body_pages pages per
+        # (layer, sequence x KV head) stay in HBM, older ones in pinned host
+        # memory, staged layer-ahead for the attention (None: all in HBM)
+        self.hbm_body_pages = hbm_body_pages
+        self._tier: Optional[HostTier] = None
+        # reference bookkeeping for the adaptive self-healing retrieval
+        # (manager.py:138, :1261-1272): score of every legacy DRAM chunk, and the
+        # window controller (adaptive_prefetch_controller.py:77-133)
+        self._chunk_attention_scores: Dict[str, float] = {}
+        self._adaptive_controller = DeviceWindowController(device=device) if torch.cuda.is_available() else None
 
     # ------------------------------------------------------------------ geometry
     @property
@@ -106,8 +128,15 @@ class HeteroKVManager:
         self._dense[layer].set_lengths(0)
         self._dense[layer].ring_head.zero_()
         cap = self._body_capacity or max(total_tokens, 1) * 2 + 4096
-        self._body[layer] = kv.Int4KVStore(B, H, cap, fmt=self.kv_format, group=self.group_size,
-                                           page_tokens=self.page_tokens, device=ref.device)
+        if self.hbm_body_pages is not None:
+            if self._tier is None:
+                self._tier = HostTier(self.num_layers, B, H, cap, resident_pages=self.hbm_body_pages,
+                                      fmt=self.kv_format, group=self.group_size, page_tokens=self.page_tokens,
+                                      device=ref.device)
+            self._body[layer] = self._tier.views[layer]
+        else:
+            self._body[layer] = kv.Int4KVStore(B, H, cap, fmt=self.kv_format, group=self.group_size,
+                                               page_tokens=self.page_tokens, device=ref.device)
         self._body[layer].set_lengths(0)
 
     # ------------------------------------------------------------------ update
@@ -131,7 +160,10 @@ class HeteroKVManager:
         if start + n > st.capacity:
             raise RuntimeError(f"INT4 body of layer {layer} is full ({st.capacity} tokens); "
                                "raise body_capacity")
-        kv.quantize_pack_kv(k, v, st, start)
+        if self._tier is not None:
+            self._tier.write(layer, start, k, v)
+        else:
+            kv.quantize_pack_kv(k, v, st, start)
         self._body_len[layer] = start + n
         st.set_lengths(start + n)
         if self.legacy_dram:
@@ -142,6 +174,7 @@ class HeteroKVManager:
                                          "v_data": qv, "v_scales": sv, "v_zps": zv})
             self._chunk_eviction_order.append(key)
             self._chunk_tokens[key] = n
+            self._chunk_attention_scores[key] = self._chunk_score(layer, start, n)
         if layer == 0:  # chunk keys advance with layer 0, as the reference's (manager.py:1311-1313)
             self._eviction_counter += 1
 
@@ -195,6 +228,8 @@ class HeteroKVManager:
         if self._dense[layer] is None:
             self._ensure_layer(layer, k, 1)
         d, st = self._dense[layer], self._body[layer]
+        if self._tier is not None and self._dense_len[layer] >= d.capacity:
+            self._tier.prepare_write(layer, self._body_len[layer] + 1)  # the step adds a body token
         kv.append_kv(k.to(d.dtype), v.to(d.dtype), d, self.sink_tokens, st)
         cap = d.capacity
         if self._dense_len[layer] < cap:
@@ -221,9 +256,18 @@ class HeteroKVManager:
         st, d = self._body[layer_idx], self._dense[layer_idx]
         if d is None:
             raise RuntimeError(f"Layer {layer_idx} has not been allocated yet.")
-        return kv.decode(q, st if self._body_len[layer_idx] > 0 else None, d, sm_scale=sm_scale,
-                         out=out, out_dtype=out_dtype, body_len=self._body_len[layer_idx],
-                         dense_len=self._dense_len[layer_idx])
+        tier = self._tier
+        if tier is not None:
+            tier.gate(layer_idx)  # this layer's host pages are in its staging area
+            nxt = layer_idx + 1
+            if nxt < self.num_layers and self._body[nxt] is not None:
+                tier.stage(nxt)  # layer-ahead: copied while this layer's attention runs
+        o = kv.decode(q, st if self._body_len[layer_idx] > 0 else None, d, sm_scale=sm_scale,
+                      out=out, out_dtype=out_dtype, body_len=self._body_len[layer_idx],
+                      dense_len=self._dense_len[layer_idx])
+        if tier is not None:
+            tier.release(layer_idx)
+        return o
 
     # ------------------------------------------------------------------ reference API
     def compress(self, layer: int, device: str = "DRAM") -> int:
@@ -309,17 +353,109 @@ class HeteroKVManager:
         if n == 0:
             return None, None, 0
         st = self._body[layer_idx]
+        if self._tier is not None:
+            self._tier.gate(layer_idx)
         k = kv.dequantize_pack(st, 0, 0, n, dtype=torch.bfloat16)
         v = kv.dequantize_pack(st, 1, 0, n, dtype=torch.bfloat16)
+        if self._tier is not None:
+            self._tier.release(layer_idx)
         return k, v, n
+
+    # ------------------------------------------------------------------ adaptive retrieval (legacy entries)
+    def _chunk_score(self, layer: int, start: int, n: int) -> float:
+        """Score of a chunk at eviction (reference manager.py:1261-1272): the mean
+        accumulated attention score of its tokens when scores exist, else the
+        FIFO fallback 1 / (eviction counter + 1). The chunk's tokens are body
+        slots [start, start + n), absolute positions sink + start onwards."""
+        ts = self._token_scores
+        if ts is not None:
+            a = self.sink_tokens + start
+            seg = ts[a:a + n]
+            return float(seg.mean().item()) if seg.numel() else 0.0
+        return 1.0 / (self._eviction_counter + 1)
+
+    def _layer_chunk_keys(self, layer_idx: int) -> List[str]:
+        prefix = f"l{layer_idx}_"
+        return [k for k in self._chunk_eviction_order if k.startswith(prefix) and k in self._dram]
+
+    def _window(self, n_keys: int, window_size: Optional[int]) -> int:
+        if window_size is None:
+            w = (int(self._adaptive_controller.compute_window(attention_weights=self._last_attention_weights))
+                 if self._adaptive_controller is not None else 2)
+            window_size = w
+        return max(1, min(int(window_size), n_keys))
+
+    def _select_chunks(self, layer_idx: int, window_size: Optional[int]) -> List[str]:
+        """Top-w chunks of the layer by score, returned in eviction order
+        (reference manager.py:859-872, :904-906)."""
+        keys = self._layer_chunk_keys(layer_idx)
+        if not keys:
+            return []
+        w = self._window(len(keys), window_size)
+        ranked = sorted(keys, key=lambda k: self._chunk_attention_scores.get(k, 0.0), reverse=True)[:w]
+        order = {k: i for i, k in enumerate(self._chunk_eviction_order)}
+        return sorted(ranked, key=lambda k: order[k])
+
+    @staticmethod
+    def _per_token_meta(entry: Dict[str, torch.Tensor], name: str) -> torch.Tensor:
+        """A chunk's flat scales / zero-points as [..., tokens, groups] so that
+        chunks concatenate along the token axis like their codes do."""
+        data = entry["k_data" if name.startswith("k") else "v_data"]
+        t = entry[name]
+        ng = t.numel() // max(1, data.numel() // data.shape[-1])
+        return t.reshape(*data.shape[:-1], ng)
+
+    def get_dram_chunks_quantized_adaptive(self, layer_idx: int,
+                                           window_size: Optional[int] = None) -> Optional[Dict[str, torch.Tensor]]:
+        """The top-w_t DRAM chunks of the layer by attention score, still INT4,
+        on the device and concatenated in eviction order (reference
+        manager.py:931-1056): k_data / v_data along the token axis; scales and
+        zero-points flat, in the order of the concatenated codes (the
+        reference concatenates 1-D metadata chunk after chunk, which matches
+        the codes only for one sequence and one head). None without chunks."""
+        keys = self._select_chunks(layer_idx, window_size)
+        if not keys:
+            return None
+        parts: Dict[str, List[torch.Tensor]] = {k: [] for k in ("k_data", "k_scales", "k_zps", "v_data",
+                                                                 "v_scales", "v_zps")}
+        for key in keys:
+            e = self._dram.transfer_to_device(key, torch.device(self.device))
+            for name in parts:
+                parts[name].append(e[name] if name.endswith("data") else self._per_token_meta(e, name))
+        out = {name: torch.cat(ts, dim=-2) for name, ts in parts.items()}
+        for name in ("k_scales", "k_zps", "v_scales", "v_zps"):
+            out[name] = out[name].reshape(-1)
+        return out
+
+    def decompress_dram_chunks_adaptive(self, layer_idx: int, window_size: Optional[int] = None):
+        """(k, v, tokens): the top-w_t DRAM chunks of the layer dequantised to
+        bf16 and concatenated in eviction order (reference manager.py:823-929),
+        or (None, None, 0)."""
+        q = self.get_dram_chunks_quantized_adaptive(layer_idx, window_size)
+        if q is None:
+            return None, None, 0
+        k = self._compressor.decompress(q["k_data"], q["k_scales"], q["k_zps"], target_dtype=torch.bfloat16)
+        v = self._compressor.decompress(q["v_data"], q["v_scales"], q["v_zps"], target_dtype=torch.bfloat16)
+        return k, v, int(k.shape[-2])
+
+    def _get_dram_kv_quantized(self, layer_idx: int) -> Optional[Dict[str, torch.Tensor]]:
+        """Every DRAM chunk of the layer, INT4, concatenated in eviction order
+        (reference manager.py:1160-1216; here on the device)."""
+        keys = self._layer_chunk_keys(layer_idx)
+        return self.get_dram_chunks_quantized_adaptive(layer_idx, len(keys)) if keys else None
 
     def memory_summary(self) -> Dict[str, Any]:
         hbm = sum(self._dense_len)
         dram = self._dram.memory_summary()
         int4_bytes = sum(st.page_bytes * st.num_pages for st in self._body if st is not None)
-        return {"hbm_tokens": hbm, "dram_entries": dram["num_entries"], "dram_bytes": dram["total_bytes"],
-                "max_hbm_tokens": self.max_hbm_tokens(), "int4_tokens": sum(self._body_len),
-                "int4_bytes": int4_bytes}
+        if self._tier is not None:
+            int4_bytes = self._tier.summary()["device_pool_bytes"]
+        out = {"hbm_tokens": hbm, "dram_entries": dram["num_entries"], "dram_bytes": dram["total_bytes"],
+               "max_hbm_tokens": self.max_hbm_tokens(), "int4_tokens": sum(self._body_len),
+               "int4_bytes": int4_bytes}
+        if self._tier is not None:
+            out["host_tier"] = self._tier.summary()
+        return out
 
     def max_hbm_tokens(self) -> int:
         return self.sink_tokens + self.tail_budget
