@@ -11,7 +11,7 @@ outlier K channels per head, bf16 queries); the per-step working set (12 GB)
 is far larger than L2, so no flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-  python bench.py --workload cfg3 [--window PAGES]   # config 3: tiered offload + prefetch
+  python bench.py --workload cfg3 [--window PAGES [--delta D]] [--sweep]   # config 3: tiered offload
   python bench.py --workload prefill [--sq N]          # multi-query attention over the INT4 body
 
 With N > 1 (torchrun, one rank per GPU) every rank decodes its own 8
@@ -30,6 +30,7 @@ import statistics
 import subprocess
 import sys
 import time
+from typing import Optional
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
@@ -62,9 +63,19 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=64, help="cfg4b: sequences")
     ap.add_argument("--window", type=int, default=0,
                     help="cfg3: cold pages copied and attended per unit and layer (0 = all of them)")
+    ap.add_argument("--delta", type=int, default=-1,
+                    help="cfg3: with --window, keep the window cached in HBM and slide it by this many pages "
+                         "per step (only those are copied); -1 = copy the whole window every step")
+    ap.add_argument("--sweep", action="store_true",
+                    help="cfg3: add the exposed-transfer curve over window slides of 0, 1, 2, 4, 8 pages")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-offload", action="store_true",
+                    help="cfg1: leave out the short config-3 offload measurement on the 1-GPU line")
+    ap.add_argument("--no-early", action="store_true",
+                    help="cfg1/cfg2: fused launches wait for the previous launch before reading the cache "
+                         "(default: stream it while the previous layer's launch finishes)")
     ap.add_argument("--no-fused", action="store_true",
                     help="cfg1/cfg2: run each layer's step as two launches (append, then decode) "
                          "instead of the fused decode-append launch")
@@ -108,14 +119,15 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval_ms: int = 200):
         self.gpu = gpu_index
+        self.interval = interval_ms
         self.proc = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", str(self.interval),
                  "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -208,7 +220,7 @@ def run_cfg2(args) -> None:
     total_steps = args.warmup + args.steps + 4
     eng = TieredKVDecoder(layers, B, Hq, Hkv, sink=sink, recent=recent, body_capacity=body + total_steps + 8,
                           fmt=args.fmt, group=32, kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
-                          fused_append=not args.no_fused)
+                          fused_append=not args.no_fused, early=False if args.no_early else None)
     gen = torch.Generator(device=dev).manual_seed(2)
     st_ = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -268,7 +280,7 @@ def run_cfg2(args) -> None:
         eng.replay()
     torch.cuda.synchronize()
     body0 = eng.body_len
-    sampler = ClockSampler(0)
+    sampler = ClockSampler(0, 50)
     sampler.start()
     e0.record(st_)
     for _ in range(args.steps):
@@ -411,73 +423,178 @@ def run_prefill(args) -> None:
 
 
 # --------------------------------------------------------------------------- config 3
-def run_cfg3(args) -> None:
+def cfg3_measure(layers: int, window: int, delta: Optional[int], steps: int, warmup: int, fmt: str, dev,
+                 clocks: bool = False, sweep_ctas: bool = False) -> dict:
     """InternLM2-7B-shaped tiered offload: 32 layers, B4, Hq32/Hkv8, 131,072-token
     context of which 8,256 stay in HBM (64 sink + 1,024 recent fp16, 28 INT4 pages)
     and 480 INT4 pages of 256 tokens per (sequence, KV head) live in pinned host
-    DRAM, copied one layer ahead of their attention."""
+    DRAM. delta None: every step copies the layer's cold pages (all 480, or the
+    last `window`), one layer ahead of their attention; delta d: the window of
+    `window` cold pages stays cached in HBM and slides by d pages per step, so a
+    step copies only the d pages entering it (SlidingWindowOffload). Exposed
+    transfer = step time with the copies - step time without them."""
     import torch
     from hetero_kvcache_optimizer_b200 import _lib
-    from hetero_kvcache_optimizer_b200.offload import TieredOffloadDecoder
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    layers = args.layers
-    dec = TieredOffloadDecoder(layers, 4, 32, 8, resident_pages=28, cold_pages=480,
-                               window_pages=args.window or None, fmt=args.fmt, device=dev)
+    from hetero_kvcache_optimizer_b200.offload import SlidingWindowOffload, TieredOffloadDecoder
+    if delta is None:
+        dec = TieredOffloadDecoder(layers, 4, 32, 8, resident_pages=28, cold_pages=480,
+                                   window_pages=window or None, fmt=fmt, device=dev)
+    else:
+        dec = SlidingWindowOffload(layers, 4, 32, 8, resident_pages=28, cold_pages=480, window_pages=window,
+                                   delta=delta, fmt=fmt, device=dev)
     gen = torch.Generator(device=dev).manual_seed(3)
     dec.fill(gen)
     q = torch.randn(layers, 4, 32, 128, device=dev, generator=gen).bfloat16()
     out = torch.empty(layers, 4, 32, 128, device=dev)
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    graphs = delta is not None
+    if graphs:  # one graph replay per step: gathers + attentions, no host work per layer
+        dec.capture(q, out)
 
     def timed(transfer: bool) -> float:
-        for _ in range(args.warmup):
-            dec.step(q, out, transfer)
+        run = (lambda: dec.replay(transfer)) if graphs else (lambda: dec.step(q, out, transfer))
+        for _ in range(warmup):
+            run()
         torch.cuda.synchronize()
         e0.record(st)
-        for _ in range(args.steps):
-            dec.step(q, out, transfer)
+        for _ in range(steps):
+            run()
         e1.record(st)
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / args.steps
+        return e0.elapsed_time(e1) / steps
 
-    sampler = ClockSampler(0)
-    sampler.start()
+    sampler = ClockSampler(dev.index, 50) if clocks else None
+    if sampler:
+        sampler.start()
     ms_with = timed(True)
-    clocks = sampler.stop()
     ms_without = timed(False)
-    # host link alone: the same per-layer copies back to back on the side stream
-    ps = dec.prefetcher.stream
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    c0.record(ps)
-    for l in range(layers):
-        dec.prefetcher.submit(dec.src_pages, dec.dst_slots[l % 2])
-    c1.record(ps)
-    torch.cuda.synchronize()
-    copy_ms = c0.elapsed_time(c1)
+    clk = sampler.stop() if sampler else None
     h2d = dec.h2d_bytes_per_step()
+    copy_ms, ctas_gbs = None, None
+    if h2d:
+        # the host link alone: one step's copies back to back on the side stream
+        ps = dec.prefetcher.stream
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        c0.record(ps)
+        if delta is None:
+            for l in range(layers):
+                dec.prefetcher.submit(dec.src_pages, dec.dst_slots[l % 2])
+        else:  # the gathers a replayed step issues, back to back
+            for l in range(layers):
+                dec.prefetcher.gather(dec.g_src, dec.g_dst[l][0], dec.step_dev, delta * dec.units, 0,
+                                      ctas=dec.gather_ctas)
+        c1.record(ps)
+        torch.cuda.synchronize()
+        copy_ms = c0.elapsed_time(c1)
+        if delta is not None and sweep_ctas:  # the gather alone at other grid sizes
+            ctas_gbs = {}
+            for ct in (16, 32, 64, 128, 148):
+                torch.cuda.synchronize()
+                c0.record(ps)
+                for l in range(layers):
+                    dec.prefetcher.gather(dec.g_src, dec.g_dst[l][0], dec.step_dev, delta * dec.units, 0, ctas=ct)
+                c1.record(ps)
+                torch.cuda.synchronize()
+                ctas_gbs[ct] = round(h2d / (c0.elapsed_time(c1) * 1e-3) / 1e9, 2)
     derr = _lib.device_error(clear=True)
     if derr:
-        raise RuntimeError(f"device error bits {derr} during the benchmark")
+        raise RuntimeError(f"device error bits {derr} during the config-3 benchmark")
+    r = {"mode": "full cold set" if delta is None and not window else
+             f"window of the last {window} pages, copied every step" if delta is None else
+             f"window of {window} pages cached in HBM, sliding {delta} page(s) per step "
+             "(CUDA graph per step, zero-copy gather kernels)",
+         "layers": layers, "window_pages": dec.window, "delta_pages": delta,
+         "h2d_bytes_per_step": h2d, "ms_per_step": round(ms_with, 4),
+         "decode_ms_per_step_without_transfer": round(ms_without, 4),
+         "exposed_ms_per_step": round(ms_with - ms_without, 4),
+         "exposed_pct_of_step": round(100 * (ms_with - ms_without) / ms_with, 2),
+         "h2d_gbs_in_step": round(h2d / (ms_with * 1e-3) / 1e9, 2),
+         "h2d_copy_only_ms_per_step": round(copy_ms, 4) if copy_ms else None,
+         "h2d_copy_only_gbs": round(h2d / (copy_ms * 1e-3) / 1e9, 2) if copy_ms else None,
+         "attn_gbs_without_transfer": round(dec.attn_bytes_per_step() / (ms_without * 1e-3) / 1e9, 1),
+         "attended_tokens": dec.tokens + dec.dense[0].len_hint, "gpu_launches": steps * layers}
+    if ctas_gbs is not None:
+        r["gather_gbs_by_ctas"] = ctas_gbs
+    if clk is not None:
+        r["clocks"] = clk
+    del dec
+    return r
+
+
+def run_cfg3(args) -> None:
+    """Config 3 as its own line (see cfg3_measure); --delta d selects the
+    residency-aware sliding window, --sweep the exposed-transfer curve over
+    d = 0, 1, 2, 4, 8 with an 8-page window beside the full-cold-set figure."""
+    import torch
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    delta = None if args.delta < 0 else args.delta
+    r = cfg3_measure(args.layers, args.window, delta, args.steps, args.warmup, args.fmt, dev, clocks=True,
+                     sweep_ctas=True)
     line = {"metric": "config3 tiered offload: H2D GB/s and exposed transfer ms per decode step",
-            "value": round(h2d / (ms_with * 1e-3) / 1e9, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_with, 4), "higher_is_better": True,
+            "value": r["h2d_gbs_in_step"], "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 mma (int4 storage, fp32 accum)",
             "data": "synthetic",
             "config": {"workload": "config3: InternLM2-7B-shaped tiered offload, 32 layers, B4, Hq32/Hkv8, "
                                    "ctx 131072: 64 sink + 1024 recent fp16 + 28 INT4 pages in HBM, 480 INT4 "
                                    "pages of 256 tokens per unit in pinned host DRAM",
-                       "layers": layers, "kv_format": args.fmt, "window_pages": dec.window,
-                       "attended_tokens": dec.tokens + dec.dense[0].len_hint},
-            "h2d_bytes_per_step": h2d, "exposed_ms_per_step": round(ms_with - ms_without, 4),
-            "decode_ms_per_step_without_transfer": round(ms_without, 4),
-            "h2d_copy_only_ms_per_step": round(copy_ms, 4),
-            "h2d_copy_only_gbs": round(h2d / (copy_ms * 1e-3) / 1e9, 2),
-            "attn_gbs_without_transfer": round(dec.attn_bytes_per_step() / (ms_without * 1e-3) / 1e9, 1),
-            "gpu_launches": args.steps * layers, "clocks": clocks}
+                       "layers": args.layers, "kv_format": args.fmt},
+            **{k: v for k, v in r.items() if k not in ("clocks",)}, "clocks": r.get("clocks")}
+    if args.sweep:
+        line["sweep"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev)
+                         for d in (0, 1, 2, 4, 8)]
     print(json.dumps(line))
+
+
+# --------------------------------------------------------------------------- ref format
+def ref_format_measure(args, dev, peak: float, layers: int = 4, steps: int = 20, warmup: int = 5) -> dict:
+    """The fused decode step of config 1 in the reference-bit-exact format (codes,
+    fp32 scales and u8 zero-points equal to KVCompressor.compress; the decode
+    kernel expands the metadata in shared memory): per-launch time and GB/s over
+    a graph of `layers` launches, CUDA events on the replaying stream."""
+    import torch
+    from hetero_kvcache_optimizer_b200 import kvstore as kv
+    from hetero_kvcache_optimizer_b200.decode_engine import TieredKVDecoder
+    c = CFG1
+    body = c["ctx"] - c["sink"] - c["recent"]
+    eng = TieredKVDecoder(layers, c["batch"], c["q_heads"], c["kv_heads"], sink=c["sink"], recent=c["recent"],
+                          body_capacity=body + warmup + steps + 8, fmt="ref", group=c["group"],
+                          kv_dtype=torch.float16, out_dtype=torch.float32, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    for l in range(layers):
+        k = torch.randn(c["batch"], c["kv_heads"], body, 128, device=dev, generator=gen).half()
+        v = torch.randn(c["batch"], c["kv_heads"], body, 128, device=dev, generator=gen).half()
+        kv.prefill(eng.stores[l], k, v)
+        del k, v
+        eng.dense[l].k.normal_(generator=gen)
+        eng.dense[l].v.normal_(generator=gen)
+    eng.set_state(body)
+    eng.capture(max_steps=warmup + steps + 2)
+    q, kn, vn, _ = eng.static_buffers
+    q.copy_(torch.randn(q.shape, device=dev, generator=gen))
+    kn.copy_(torch.randn(kn.shape, device=dev, generator=gen))
+    vn.copy_(torch.randn(vn.shape, device=dev, generator=gen))
+    for _ in range(warmup):
+        eng.replay()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    body0 = eng.body_len
+    e0.record(st)
+    for _ in range(steps):
+        eng.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (steps * layers)
+    nbytes = sum(eng.step_bytes(body0 + i) for i in range(steps)) / (steps * layers)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del eng
+    return {"kernel": "decode_kernel<APPEND>, HKV_FMT_REF group 32 (168 B per token)", "layers_timed": layers,
+            "us_per_launch": round(us, 2), "bytes_per_launch": round(nbytes), "achieved": round(gbs, 1),
+            "frac": round(gbs / peak, 4), "unit": "GB/s"}
 
 
 # --------------------------------------------------------------------------- config 4, variant B
@@ -642,7 +759,7 @@ def main():
     eng = TieredKVDecoder(args.layers, c["batch"], c["q_heads"], c["kv_heads"], sink=c["sink"],
                           recent=c["recent"], body_capacity=body + total_steps + 8, fmt=args.fmt,
                           group=c["group"], kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
-                          ctas=args.ctas, fused_append=not args.no_fused)
+                          ctas=args.ctas, fused_append=not args.no_fused, early=False if args.no_early else None)
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     B, Hkv = c["batch"], c["kv_heads"]
     for l in range(args.layers):
@@ -766,6 +883,22 @@ def main():
     if derr:
         raise RuntimeError(f"device error bits {derr} during the benchmark")
 
+    # ---- the reference-bit-exact INT4 format (fp32 scale + u8 zero-point, 168 B
+    # per token) on the same decode step: 4 layers of config 1 (the per-launch
+    # figures do not depend on the layer count), one rank, after the main line
+    ref_fmt = None
+    if world == 1 and args.fmt != "ref" and eng.fused_append:
+        ref_fmt = ref_format_measure(args, dev, peak)
+
+    # ---- config 3 in short (4 of its 32 layers, one rank): exposed host->device
+    # transfer when every step copies the whole cold set, and when a window of
+    # 8 cold pages stays cached in HBM and slides by one page per step
+    offload = None
+    if world == 1 and not args.no_offload:
+        offload = {"layers": 4,
+                   "full_cold_set": cfg3_measure(4, 0, None, 4, 3, args.fmt, dev),
+                   "sliding_window": cfg3_measure(4, 8, 1, 10, 3, args.fmt, dev)}
+
     # ---- N > 1: variant B of config 4 as well (sequence split + one NCCL
     # all-gather of the partials per layer + LSE merge), short: 2 layers at
     # B 64, 131,072-token context, strong scaling over this run's ranks
@@ -810,6 +943,10 @@ def main():
         }
         if split is not None:
             line["seqsplit_cfg4b"] = split
+        if ref_fmt is not None:
+            line["ref_format"] = ref_fmt
+        if offload is not None:
+            line["offload_cfg3"] = offload
         if cpu is not None:
             line["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cpu.items()
                                     if k in ("value", "unit", "cores", "kind", "sample")}

@@ -91,6 +91,7 @@ SIGNATURES = {
     "hkv_prefetcher_destroy": (c_i32, [c_vp]),
     "hkv_prefetch_submit": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, c_vp]),
     "hkv_prefetch_bytes": (c_i64, [c_vp]),
+    "hkv_prefetch_gather": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_vp]),
     "hkv_event_wait": (c_i32, [c_vp, c_i64]),
     "hkv_qk_scores_flat": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
     "hkv_selftest_bounded_wait": (c_i32, [c_i64, c_i32, c_vp]),

@@ -631,19 +631,29 @@ hkv_status quantize_pack_launch(const void* x, const void* x2, int32_t dtype, in
   if (T == 0) return HKV_OK;
   const int64_t ntok = (int64_t)B * H * T;
   if (ntok >= (int64_t(1) << 31) - 64) return HKV_ERR_UNSUPPORTED;
-  const int per_block = 16 * hkv::kQuantTokens;
-  const dim3 grid((unsigned)((ntok + per_block - 1) / per_block), x2 ? 2u : 1u);
+  // 64-position tiles aligned in position space: a chunk starting mid-tile spans one more
+  const int tiles = (T + hkv::kQPTile - 1) / hkv::kQPTile + 1;
+  if ((int64_t)tiles * B * H >= (int64_t(1) << 31)) return HKV_ERR_UNSUPPORTED;
+  const dim3 grid((unsigned)(tiles * B * H), x2 ? 2u : 1u);
+  const bool ref = dst->format == HKV_FMT_REF;
+  const int g = dst->group;
+#define HKV_QP_LAUNCH(TY, FMT, G)                                                                              \
+  hkv::quantize_pack_kernel<TY, FMT, G><<<grid, 256, 0, st>>>(static_cast<const TY*>(x), static_cast<const TY*>(x2), \
+                                                              H, T, tiles, stride_b, stride_h, stride_t, role, *dst, \
+                                                              dst_start, start)
+#define HKV_QP_GROUPS(TY, FMT)        \
+  if (g == 32) HKV_QP_LAUNCH(TY, FMT, 32);      \
+  else if (g == 64) HKV_QP_LAUNCH(TY, FMT, 64); \
+  else HKV_QP_LAUNCH(TY, FMT, 128)
   if (dtype == HKV_DT_F16) {
-    hkv::quantize_pack_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x),
-                                                           static_cast<const __half*>(x2), B, H, T, stride_b,
-                                                           stride_h, stride_t, role, *dst, dst_start, start);
+    if (ref) { HKV_QP_GROUPS(__half, HKV_FMT_REF); } else { HKV_QP_GROUPS(__half, HKV_FMT_FP16MIN); }
   } else if (dtype == HKV_DT_BF16) {
-    hkv::quantize_pack_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(x2), B, H, T, stride_b, stride_h,
-        stride_t, role, *dst, dst_start, start);
+    if (ref) { HKV_QP_GROUPS(__nv_bfloat16, HKV_FMT_REF); } else { HKV_QP_GROUPS(__nv_bfloat16, HKV_FMT_FP16MIN); }
   } else {
     return HKV_ERR_ARG;
   }
+#undef HKV_QP_GROUPS
+#undef HKV_QP_LAUNCH
   return launch_status();
 }
 }  // namespace
@@ -978,12 +988,62 @@ hkv_status hkv_selftest_bounded_wait(int64_t limit_ns, int32_t arrive, hkv_strea
 // --------------------------------------------------------------------------- prefetch
 struct hkv_prefetcher {
   const uint8_t* host;
+  const uint8_t* host_dev;  // the host pool as kernels address it (mapped pinned memory), or null
   int64_t host_pages;
   uint8_t* dev;
   int64_t dev_pages;
   int64_t page_bytes;
   std::atomic<int64_t> bytes;
 };
+
+namespace {
+// Zero-copy page gather: the pages' 16-byte vectors are cut into chunks of
+// kGatherThreads * kGatherUnroll; CTAs take chunks blockIdx.x, blockIdx.x +
+// gridDim.x, ... and every thread keeps kGatherUnroll loads in flight (16 KB per
+// CTA) over the host link from mapped pinned host memory, then writes them to
+// the page's device slot. 128 threads of few registers: a CTA fits beside a
+// persistent decode CTA on the same SM, so gathers overlap attention.
+// Host page of entry k: (src[k] + (step ? (*step + step_add) * step_mul : 0))
+// mod host_pages, so a graph can replay a sliding selection whose ids advance
+// with a device-side step counter. Ids outside the pools are skipped and
+// flagged HKV_DEVERR_BAD_PAGE.
+constexpr int kGatherThreads = 128;
+constexpr int kGatherUnroll = 8;
+__global__ void __launch_bounds__(kGatherThreads) page_gather_kernel(
+    const uint4* __restrict__ host, uint4* __restrict__ dev, const int32_t* __restrict__ src,
+    const int32_t* __restrict__ dst, int n, int64_t page_vecs, int64_t host_pages, int64_t dev_pages,
+    const int64_t* __restrict__ step, int64_t step_mul, int32_t step_add) {
+  constexpr int64_t kChunk = (int64_t)kGatherThreads * kGatherUnroll;
+  const int64_t shift = step ? (*step + step_add) * step_mul : 0;
+  const int64_t cpp = (page_vecs + kChunk - 1) / kChunk;  // chunks per page
+  const int64_t items = (int64_t)n * cpp;
+  for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const int k = (int)(it / cpp);
+    const int64_t c0 = (it - (int64_t)k * cpp) * kChunk;
+    const int64_t raw = src[k], dp = dst[k];
+    int64_t sp = (raw + shift) % host_pages;
+    if (sp < 0) sp += host_pages;
+    if (raw < 0 || (!step && raw >= host_pages) || dp < 0 || dp >= dev_pages) {
+      if (threadIdx.x == 0 && c0 == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
+      continue;
+    }
+    const uint4* s = host + sp * page_vecs + c0;
+    uint4* d = dev + dp * page_vecs + c0;
+    const int64_t lim = page_vecs - c0;
+    uint4 r[kGatherUnroll];
+#pragma unroll
+    for (int j = 0; j < kGatherUnroll; ++j) {
+      const int64_t i = threadIdx.x + (int64_t)j * kGatherThreads;
+      if (i < lim) r[j] = s[i];
+    }
+#pragma unroll
+    for (int j = 0; j < kGatherUnroll; ++j) {
+      const int64_t i = threadIdx.x + (int64_t)j * kGatherThreads;
+      if (i < lim) d[i] = r[j];
+    }
+  }
+}
+}  // namespace
 
 hkv_status hkv_prefetcher_create(const void* host_pool, int64_t host_pages, void* dev_pool, int64_t dev_pages,
                                  int64_t page_bytes, hkv_prefetcher** out) {
@@ -998,6 +1058,14 @@ hkv_status hkv_prefetcher_create(const void* host_pool, int64_t host_pages, void
   hkv_prefetcher* pf = new (std::nothrow) hkv_prefetcher;
   if (!pf) return HKV_ERR_CAPACITY;
   pf->host = static_cast<const uint8_t*>(host_pool);
+  // the kernel-side address of the pinned pool (the same pointer under unified
+  // addressing); null when the pool is not mapped, which only disables the gather
+  void* hd = nullptr;
+  if (cudaHostGetDevicePointer(&hd, const_cast<void*>(host_pool), 0) != cudaSuccess) {
+    cudaGetLastError();
+    hd = nullptr;
+  }
+  pf->host_dev = static_cast<const uint8_t*>(hd);
   pf->host_pages = host_pages;
   pf->dev = static_cast<uint8_t*>(dev_pool);
   pf->dev_pages = dev_pages;
@@ -1042,6 +1110,26 @@ hkv_status hkv_prefetch_submit(hkv_prefetcher* pf, const int32_t* src_pages, con
 }
 
 int64_t hkv_prefetch_bytes(const hkv_prefetcher* pf) { return pf ? pf->bytes.load() : -1; }
+
+hkv_status hkv_prefetch_gather(hkv_prefetcher* pf, const int32_t* src_pages, const int32_t* dst_slots, int32_t n,
+                               const int64_t* step, int64_t step_mul, int32_t step_add, int32_t ctas,
+                               hkv_stream_t stream) {
+  if (!pf || n < 0 || (n > 0 && (!src_pages || !dst_slots)) || ctas < 0) return HKV_ERR_ARG;
+  if (!pf->host_dev) return HKV_ERR_UNSUPPORTED;
+  if (pf->page_bytes % 16 || reinterpret_cast<uintptr_t>(pf->host_dev) % 16 ||
+      reinterpret_cast<uintptr_t>(pf->dev) % 16)
+    return HKV_ERR_UNSUPPORTED;
+  if (n == 0) return HKV_OK;
+  const int64_t chunks = (int64_t)n * ((pf->page_bytes / 16 + kGatherThreads * kGatherUnroll - 1) /
+                                        (kGatherThreads * kGatherUnroll));
+  const int grid = (int)std::min<int64_t>(chunks, ctas > 0 ? ctas : 64);
+  page_gather_kernel<<<grid, kGatherThreads, 0, S(stream)>>>(
+      reinterpret_cast<const uint4*>(pf->host_dev), reinterpret_cast<uint4*>(pf->dev), src_pages, dst_slots, n,
+      pf->page_bytes / 16, pf->host_pages, pf->dev_pages, step, step_mul, step_add);
+  const hkv_status rc = launch_status();
+  if (rc == HKV_OK) pf->bytes.fetch_add((int64_t)n * pf->page_bytes);
+  return rc;
+}
 
 hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us) {
   if (!ev) return HKV_ERR_ARG;

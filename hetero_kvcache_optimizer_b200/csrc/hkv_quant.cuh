@@ -155,58 +155,194 @@ __device__ __forceinline__ void store8(T* dst, const float (&v)[8]) {
   *reinterpret_cast<uint4*>(dst) = raw;
 }
 
-// ------------------------------------------------------------------ quantise + pack
-// Each half-warp quantises kQuantTokens consecutive tokens: their 16-byte loads
-// are all issued before the first token is processed (latency overlap), 16
-// lanes per token. grid.x covers ceil(B*H*T / (16 * kQuantTokens)) blocks of 256.
-constexpr int kQuantTokens = 1;
-template <typename T>
+// ------------------------------------------------------------------ quantise + pack (bulk)
+// One thread = one token x one 32-dim block w (dims 32w..32w+31): it loads the
+// block's 64 bytes, takes the group's min / max (a group of 64 or 128 dims
+// spans 2 or 4 neighbouring lanes), quantises its 32 values and writes its
+// block's four K code words (K side) or V words (V side) and the group's
+// metadata. A CTA = 256 threads = 64 consecutive token POSITIONS of one unit
+// and one side, the tile aligned to 64 positions: all its tokens lie in one
+// 128-token page block, and the two tokens of a V pair (positions 2q, 2q+1) sit
+// in lanes l and l ^ 4 of one warp, which swap their words with a shuffle and
+// write whole 32-bit words. Compared with 16 lanes per token (quantise_token),
+// the group parameters are computed once per 32 values instead of once per 8,
+// no gather shuffles are needed, and the element arithmetic runs two lanes at a
+// time in packed f32x2 operations with the same IEEE roundings.
+constexpr int kQPTile = 64;
+// 1.5 * 2^23: for 0 <= t <= 15, RN(t + 1.5 * 2^23) has rint(t) (ties to even,
+// like rintf) in its low mantissa bits, i.e. bits = kMagicBits + rint(t).
+constexpr float kMagicF = 12582912.0f;
+constexpr uint32_t kMagicBits = 0x4B400000u;
+// word_j accumulates bits(c) << shift for 8 codes; the magic parts sum to this
+// constant (mod 2^32), removed once per word.
+constexpr uint32_t kWordMagic = (kMagicBits << 0) + (kMagicBits << 4) + (kMagicBits << 8) + (kMagicBits << 12) +
+                                (kMagicBits << 16) + (kMagicBits << 20) + (kMagicBits << 24) +
+                                (kMagicBits << 28);
+
+__device__ __forceinline__ float2 to_f32x2(const __half2 h) { return __half22float2(h); }
+__device__ __forceinline__ float2 to_f32x2(const __nv_bfloat162 h) { return __bfloat1622float2(h); }
+
+template <typename T> struct Vec2;
+template <> struct Vec2<__half> { using type = __half2; };
+template <> struct Vec2<__nv_bfloat16> { using type = __nv_bfloat162; };
+
+template <typename T, int FMT, int GROUP>
 __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict__ x, const T* __restrict__ x2,
-                                                            int B, int H, int T_, int64_t sb, int64_t sh,
+                                                            int H, int T_, int tiles, int64_t sb, int64_t sh,
                                                             int64_t st, int role, hkv_int4_store store,
-                                                            const int32_t* dst_start, int start) {
-  // grid.y == 2: blockIdx.y 0 quantises x as side `role`, 1 quantises x2 as V
+                                                            const int32_t* __restrict__ dst_start, int start) {
+  using T2 = typename Vec2<T>::type;
+  constexpr int kLanesPerGroup = GROUP / 32;  // 1, 2 or 4
+  constexpr int ng = HKV_D / GROUP;
+  // blockIdx.y 0: x as side `role`; 1: x2 as V
   const T* __restrict__ src = blockIdx.y ? x2 : x;
   if (blockIdx.y) role = HKV_ROLE_V;
-  const int ntok = B * H * T_;  // < 2^31 (checked by the host)
-  const int tok0 = (blockIdx.x * 16 + (threadIdx.x >> 4)) * kQuantTokens;
-  const int p = threadIdx.x & 15;
+  const int u = blockIdx.x / tiles, tile = blockIdx.x - u * tiles;
+  const int b = u / H, h = u - b * H;
+  const int s0 = dst_start ? dst_start[b] : start;
+  const int lane = threadIdx.x & 31, w = threadIdx.x & 3;
+  const int pos = (s0 & ~(kQPTile - 1)) + kQPTile * tile + (threadIdx.x >> 2);
+  const int t = pos - s0;
+  const bool valid = t >= 0 && t < T_;
+  if (!__any_sync(0xffffffffu, valid)) return;  // warp-uniform: none of its 8 positions is in the chunk
+  // the CTA's positions share one page block: one bounds check and lookup for all
   const int cap = store.max_pages * store.page_tokens;
-  float v[kQuantTokens][8];
-  int pos[kQuantTokens], unit[kQuantTokens];
+  const int pos0 = (s0 & ~(kQPTile - 1)) + kQPTile * tile;
+  int64_t page = -1;
+  bool tile_ok = pos0 >= 0 && pos0 < cap;
+  if (tile_ok) {
+    page = store_page(store, u, pos0);
+    tile_ok = page >= 0;
+  }
+  if (!tile_ok) {
+    if (valid && w == 0) hkv_flag_error(pos0 >= 0 && pos0 < cap ? HKV_DEVERR_BAD_PAGE : HKV_DEVERR_CAPACITY);
+    return;  // warp-uniform (tile_ok is uniform over the CTA)
+  }
+
+  // ---- load the block's 32 values (four 16-byte loads) and the group's range
+  uint4 raw[4];
+  if (valid) {
+    const uint4* p = reinterpret_cast<const uint4*>(src + b * sb + h * sh + (int64_t)t * st + 32 * w);
 #pragma unroll
-  for (int i = 0; i < kQuantTokens; ++i) {
-    const int tok = tok0 + i;
-    const bool valid = tok < ntok;
-    const int tt = valid ? tok : 0;
-    const int u = tt / T_, t = tt - u * T_;
-    const int b = u / H, h = u - b * H;
-    unit[i] = valid ? u : -1;
-    pos[i] = (dst_start ? dst_start[b] : start) + t;
-    if (valid) {
-      load8(src + b * sb + h * sh + (int64_t)t * st + 8 * p, v[i]);
+    for (int i = 0; i < 4; ++i) raw[i] = p[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) raw[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  const T2* v2 = reinterpret_cast<const T2*>(raw);  // 16 pairs: dims 32w + 2i, 32w + 2i + 1
+  T2 lo2 = v2[0], hi2 = v2[0];
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    lo2 = __hmin2(lo2, v2[i]);
+    hi2 = __hmax2(hi2, v2[i]);
+  }
+  const float2 lof = to_f32x2(lo2), hif = to_f32x2(hi2);
+  float mn = fminf(lof.x, lof.y), mx = fmaxf(hif.x, hif.y);
+#pragma unroll
+  for (int sft = 1; sft < kLanesPerGroup; sft <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, sft));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, sft));
+  }
+
+  // ---- codes: t = x / s + zp (ref) or (x - min) / s (fp16min), the division
+  // by Markstein's correction step (div_by), clamped to [0, 15], rounded by the
+  // magic add; word j gets codes of dims 8m + 2j (low half) and 8m + 2j + 1
+  // (high half), m = 0..3, at nibble m.
+  float2 s2, r2, ns2, z2;
+  RefParams rp;
+  MinParams mp;
+  bool zero_scale = false;
+  if constexpr (FMT == HKV_FMT_REF) {
+    rp = ref_params(mn, mx);
+    s2 = make_float2(rp.scale, rp.scale);
+    r2 = make_float2(rp.rcp, rp.rcp);
+    z2 = make_float2(rp.zpf, rp.zpf);
+  } else {
+    mp = min_params(mn, mx);
+    s2 = make_float2(mp.sf, mp.sf);
+    r2 = make_float2(mp.rcp, mp.rcp);
+    z2 = make_float2(-mp.mf, -mp.mf);
+    zero_scale = !(mp.sf > 0.0f);
+  }
+  ns2 = make_float2(-s2.x, -s2.y);
+  const float2 magic2 = make_float2(kMagicF, kMagicF);
+  uint32_t word[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {  // pair i = dims 2i, 2i + 1 of the block: m = i / 4, j = i % 4
+    float2 a = to_f32x2(v2[i]);
+    float2 q;
+    if constexpr (FMT == HKV_FMT_REF) {
+      const float2 q0 = __fmul2_rn(a, r2);
+      const float2 e = __ffma2_rn(q0, ns2, a);
+      q = __fadd2_rn(__ffma2_rn(e, r2, q0), z2);
     } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+      a = __fadd2_rn(a, z2);  // x - min, exact as in __fsub_rn
+      const float2 q0 = __fmul2_rn(a, r2);
+      const float2 e = __ffma2_rn(q0, ns2, a);
+      q = __ffma2_rn(e, r2, q0);
     }
+    q.x = fminf(fmaxf(q.x, 0.0f), 15.0f);
+    q.y = fminf(fmaxf(q.y, 0.0f), 15.0f);
+    const float2 rb = __fadd2_rn(q, magic2);
+    const int m = i >> 2, j = i & 3;
+    word[j] += (__float_as_uint(rb.x) << (4 * m)) + (__float_as_uint(rb.y) << (16 + 4 * m));
   }
 #pragma unroll
-  for (int i = 0; i < kQuantTokens; ++i) {
-    bool ok = unit[i] >= 0;
-    int64_t page = 0;
-    if (ok) {
-      if (pos[i] < 0 || pos[i] >= cap) {
-        if (p == 0) hkv_flag_error(HKV_DEVERR_CAPACITY);
-        ok = false;
-      } else {
-        page = store_page(store, unit[i], pos[i]);
-        if (page < 0) {
-          if (p == 0) hkv_flag_error(HKV_DEVERR_BAD_PAGE);
-          ok = false;
-        }
+  for (int j = 0; j < 4; ++j) word[j] = zero_scale ? 0u : word[j] - kWordMagic;
+
+  // ---- stores
+  const BlockRef br = block_ref(store, page, pos % store.page_tokens);
+  const int gi = w / kLanesPerGroup;
+  const bool meta_lane = (w % kLanesPerGroup) == 0;
+  uint32_t partner[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, word[j], 4);
+  const bool partner_valid = __shfl_xor_sync(0xffffffffu, valid, 4);
+  uint32_t meta16 = 0u, meta16_partner = 0u;  // fp16min V: scale | min << 16 of this token and its partner
+  if constexpr (FMT == HKV_FMT_FP16MIN) {
+    meta16 = static_cast<uint32_t>(__half_as_ushort(mp.sh)) | (static_cast<uint32_t>(__half_as_ushort(mp.mh)) << 16);
+    meta16_partner = __shfl_xor_sync(0xffffffffu, meta16, 4);
+  }
+  if (!valid) return;
+  if (role == HKV_ROLE_K) {
+    uint32_t* kw = reinterpret_cast<uint32_t*>(br.base + br.w * HKV_CODE_BYTES);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) kw[4 * j + w] = word[j];
+  } else {
+    uint8_t* vc = br.base + HKV_V_CODES_OFF;
+    const int q = br.w >> 1, tau = br.w & 1;
+    if (partner_valid) {
+      // the even token writes the pair's words of chunks 2j (low halves of both
+      // tokens), the odd token those of chunks 2j + 1 (high halves)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t v = tau ? __byte_perm(partner[j], word[j], 0x7632) : __byte_perm(word[j], partner[j], 0x5410);
+        *reinterpret_cast<uint32_t*>(vc + v_chunk_off(q, 2 * j + tau) + 4 * w) = v;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        *reinterpret_cast<uint16_t*>(vc + v_chunk_off(q, 2 * j) + 4 * w + 2 * tau) = static_cast<uint16_t>(word[j]);
+        *reinterpret_cast<uint16_t*>(vc + v_chunk_off(q, 2 * j + 1) + 4 * w + 2 * tau) =
+            static_cast<uint16_t>(word[j] >> 16);
       }
     }
-    quantise_token(v[i], ok, role, store.format, store.group, store, page, ok ? pos[i] % store.page_tokens : 0);
+  }
+  if (!meta_lane) return;
+  if constexpr (FMT == HKV_FMT_REF) {
+    *reinterpret_cast<float*>(br.base + meta_off(role, ng) + 4 * (br.w * ng + gi)) = rp.scale;
+    br.base[zps_off(role, ng) + br.w * ng + gi] = static_cast<uint8_t>(rp.zpf);
+  } else if (role == HKV_ROLE_K) {
+    *reinterpret_cast<__half*>(br.base + mn_scale_off(0, br.w, ng, gi)) = mp.sh;
+    *reinterpret_cast<__half*>(br.base + mn_min_off(0, br.w, ng, gi)) = mp.mh;
+  } else if (partner_valid) {
+    // the pair's two scales side by side (even token), the two mins (odd token)
+    const int tau = br.w & 1, w0 = br.w & ~1;
+    const uint32_t v = tau ? __byte_perm(meta16_partner, meta16, 0x7632) : __byte_perm(meta16, meta16_partner, 0x5410);
+    *reinterpret_cast<uint32_t*>(br.base + (tau ? mn_min_off(1, w0, ng, gi) : mn_scale_off(1, w0, ng, gi))) = v;
+  } else {
+    *reinterpret_cast<__half*>(br.base + mn_scale_off(1, br.w, ng, gi)) = mp.sh;
+    *reinterpret_cast<__half*>(br.base + mn_min_off(1, br.w, ng, gi)) = mp.mh;
   }
 }
 

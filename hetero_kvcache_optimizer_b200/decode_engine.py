@@ -26,8 +26,9 @@ class TieredKVDecoder:
                  sink: int = 64, recent: int = 1024, body_capacity: int = 32768,
                  fmt: str = "fp16min", group: int = 32, page_tokens: int = 256,
                  kv_dtype: torch.dtype = torch.float16, out_dtype: torch.dtype = torch.float32,
-                 device="cuda", ctas: int = 0, fused_append: bool = True):
+                 device="cuda", ctas: int = 0, fused_append: bool = True, early: Optional[bool] = None):
         self.fused_append = fused_append
+        self.early = early
         self.num_layers, self.batch = num_layers, batch
         self.q_heads, self.kv_heads = q_heads, kv_heads
         self.sink, self.recent = sink, recent
@@ -104,7 +105,7 @@ class TieredKVDecoder:
     def _early(self) -> bool:
         # a step runs the layers in order, so with two or more layers the launch
         # before a layer's is always another layer's (which never writes its cache)
-        return self.num_layers >= 2
+        return self.num_layers >= 2 if self.early is None else (self.early and self.num_layers >= 2)
 
     def step(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
              out: Optional[torch.Tensor] = None, len_hint: Optional[int] = None) -> torch.Tensor:

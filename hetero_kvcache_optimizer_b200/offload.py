@@ -157,3 +157,253 @@ class TieredOffloadDecoder:
         per_tok = 2 * (64 + 4 * (128 // self.group) + (128 // self.group if self.fmt == "ref" else 0))
         dense = self.dense[0].len_hint * 2 * 128 * 2
         return self.L * self.units * (self.tokens * per_tok + dense)
+
+
+class SlidingWindowOffload:
+    """Tiered offload with pages that stay in HBM across steps: each layer and
+    unit attends its ``resident_pages`` plus a window of ``window_pages`` cold
+    pages, and the window slides by ``delta`` pages per step (the pages the
+    window policy picks change slowly: the reference's adaptive window is
+    w_t in [2, 8] chunks, src/policy/adaptive_prefetch_controller.py:44-45, and
+    its ranking follows accumulated attention scores). Cold pages that are in
+    the window stay in a per-(layer, unit) cache ring of window + delta device
+    slots, so a step copies only the ``delta`` pages entering the window, one
+    layer ahead of their attention, on the page prefetcher's side stream. The
+    ring never overwrites a page the current or previous step attends: the
+    pages leaving it (p - window - delta) left the window a step earlier.
+
+    Host arena and ring are page-major ([page][unit]): the pages entering the
+    window of every unit of a layer are one contiguous run on both sides, so a
+    layer's fetch is one cudaMemcpyAsync (two when the ring or the cold set
+    wraps) instead of one per unit; per-copy overhead (a few µs) would
+    otherwise dominate copies of single 40 KB pages.
+
+    The page table of step s maps window entry i to slot (s * delta + i) mod
+    (window + delta); the distinct tables of a layer (the ring's period) are
+    built once, so a step passes a pointer and writes no table.
+
+    As in ``TieredOffloadDecoder`` one layer's cold pages (``cold_pages`` per
+    unit) live in the pinned host arena and every layer reads them (a
+    benchmark harness: the attention differs per layer through its queries)."""
+
+    def __init__(self, num_layers: int, batch: int, q_heads: int, kv_heads: int, *, resident_pages: int,
+                 cold_pages: int, window_pages: int, delta: int, sink: int = 64, recent: int = 1024,
+                 fmt: str = "fp16min", group: int = 32, page_tokens: int = 256,
+                 kv_dtype: torch.dtype = torch.float16, device="cuda", gather_ctas: int = 0):
+        if not 0 <= delta <= window_pages <= cold_pages:
+            raise ValueError("need 0 <= delta <= window_pages <= cold_pages")
+        self.L, self.B, self.Hq, self.Hkv = num_layers, batch, q_heads, kv_heads
+        self.units = U = batch * kv_heads
+        self.resident, self.cold, self.window, self.delta = resident_pages, cold_pages, window_pages, delta
+        self.C = window_pages + delta  # cache ring slots per (layer, unit)
+        self.fmt, self.group, self.P = fmt, group, page_tokens
+        self.device = torch.device(device)
+        self.page_bytes = kv.page_bytes(fmt, group, page_tokens)
+        n_res = num_layers * U * resident_pages
+        self.cache_base = n_res
+        self.pool = torch.empty(n_res + num_layers * U * self.C, self.page_bytes, dtype=torch.uint8,
+                                device=self.device)
+        self.host = torch.empty(U * cold_pages, self.page_bytes, dtype=torch.uint8).pin_memory()
+        self.prefetcher = PagePrefetcher(self.host, self.pool)
+        attended = resident_pages + window_pages
+        self.tokens = attended * page_tokens
+        self.dense = [kv.DenseKV(batch, kv_heads, sink + recent, dtype=kv_dtype, device=self.device)
+                      for _ in range(num_layers)]
+        for d in self.dense:
+            d.set_lengths(sink + recent)
+        # the ring's period: window start s * delta mod C repeats after C / gcd(C, delta) steps
+        import math
+        self.period = self.C // math.gcd(self.C, delta) if delta else 1
+        self.tables = []  # [layer][phase] -> [U, attended] int32 on the device
+        for l in range(num_layers):
+            per = []
+            for ph in range(self.period):
+                t = torch.empty(U, attended, dtype=torch.int32)
+                for u in range(U):
+                    t[u, :resident_pages] = torch.arange(resident_pages) + (l * U + u) * resident_pages
+                    t[u, resident_pages:] = self._slot(l, u, torch.arange(window_pages) + ph * delta)
+                per.append(t.to(self.device))
+            self.tables.append(per)
+        self.lengths = torch.full((batch,), self.tokens, dtype=torch.int32, device=self.device)
+        self.step_idx = 0
+        self.done: List[Optional[torch.cuda.Event]] = [None] * num_layers  # layer's last attention
+        self.ready: List[Optional[torch.cuda.Event]] = [None] * num_layers
+        self.fetched_pages = 0
+        # device-side form of a step's fetch, for the zero-copy gather kernel
+        # (graph replays): entry (i, u) of the pages entering the window reads
+        # host page (src + step * delta * U) mod (cold * U), i.e. page
+        # (step * delta + window - delta + i) mod cold of unit u, and writes ring
+        # slot dst[layer][phase]; step_dev counts steps on the device.
+        enter = range(window_pages - delta, window_pages)
+        self.g_src = torch.tensor([j * U + u for j in enter for u in range(U)], dtype=torch.int32,
+                                  device=self.device)
+        self.g_dst = [[torch.tensor([self._slot(l, u, ph * delta + j) for j in enter for u in range(U)],
+                                    dtype=torch.int32, device=self.device) for ph in range(self.period)]
+                      for l in range(num_layers)]
+        self.step_dev = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.gather_ctas = gather_ctas  # grid of the captured gathers (0: the library's default)
+        self._graphs = None
+
+    def _slot(self, l: int, u: int, p):
+        """Ring slot of window page p (any integer) of layer l, unit u."""
+        return self.cache_base + (l * self.C + p % self.C) * self.units + u
+
+    def _store(self, l: int, phase: int) -> _LayerStore:
+        return _LayerStore(self.pool, self.page_bytes, self.tables[l][phase], self.lengths, self.B, self.Hkv,
+                           self.fmt, self.group, self.P, self.tokens)
+
+    def fill(self, gen: torch.Generator, outlier_channels: int = 4) -> None:
+        """Seeded synthetic K/V as TieredOffloadDecoder.fill: resident pages in the
+        pool, cold pages in the host arena; the window of step 0 copied into
+        every layer's ring."""
+        U, P = self.units, self.P
+        ntok = (self.resident + self.cold) * P
+        for l in range(self.L):
+            tmp = kv.Int4KVStore(self.B, self.Hkv, ntok, fmt=self.fmt, group=self.group, page_tokens=P,
+                                 device=self.device)
+            for t0 in range(0, ntok, 8192):
+                n = min(8192, ntok - t0)
+                k = torch.randn(self.B, self.Hkv, n, 128, device=self.device, generator=gen)
+                for h in range(self.Hkv):
+                    ch = torch.randperm(128, device=self.device, generator=gen)[:outlier_channels]
+                    k[:, h, :, ch] *= 10.0
+                v = torch.randn(self.B, self.Hkv, n, 128, device=self.device, generator=gen)
+                kv.quantize_pack_kv(k.half(), v.half(), tmp, t0)
+            pages = tmp.pool.view(U, tmp.max_pages, self.page_bytes)
+            self.pool[l * U * self.resident:(l + 1) * U * self.resident] = \
+                pages[:, :self.resident].reshape(-1, self.page_bytes)
+            if l == 0:  # host page p of unit u at p * U + u
+                self.host.copy_(pages[:, self.resident:self.resident + self.cold].transpose(0, 1)
+                                .reshape(-1, self.page_bytes))
+            d = self.dense[l]
+            d.k.normal_(generator=gen)
+            d.v.normal_(generator=gen)
+            del tmp
+        torch.cuda.synchronize(self.device)
+        for l in range(self.L):  # step 0's window, before the first step
+            self._fetch(l, 0, range(self.window))
+        torch.cuda.synchronize(self.device)
+
+    def _fetch(self, l: int, step: int, idx) -> None:
+        """Copy window pages ``idx`` (positions in step ``step``'s window) of layer
+        l into their ring slots on the side stream."""
+        first = step * self.delta
+        src, dst = [], []
+        for i in idx:  # page-major: consecutive units are consecutive on both sides
+            p = (first + i) % self.cold
+            for u in range(self.units):
+                src.append(p * self.units + u)
+                dst.append(self._slot(l, u, first + i))
+        if self.done[l] is not None:  # the ring slots' previous readers
+            self.prefetcher.stream.wait_event(self.done[l])
+        self.ready[l] = self.prefetcher.submit(src, dst)
+        self.fetched_pages += len(src)
+
+    def prefetch(self, l: int, step: int) -> None:
+        """The pages entering layer l's window at ``step`` (its last ``delta``)."""
+        if self.delta:
+            self._fetch(l, step, range(self.window - self.delta, self.window))
+        else:
+            self.ready[l] = None
+
+    def step(self, q: torch.Tensor, out: torch.Tensor, transfer: bool = True) -> None:
+        """Attention of every layer over its resident pages + the current window,
+        the next layer's new window pages copied during the current layer (step
+        0's window is in the ring since ``fill``). transfer=False skips the
+        copies, for timing: the step then attends whatever the ring holds."""
+        s = self.step_idx
+        cs = torch.cuda.current_stream(self.device)
+        phase = s % self.period
+        if transfer and s > 0 and self.ready[0] is None:
+            self.prefetch(0, s)
+        for l in range(self.L):
+            if transfer:
+                if l + 1 < self.L and s > 0:
+                    self.prefetch(l + 1, s)
+                if self.ready[l] is not None:
+                    cs.wait_event(self.ready[l])
+            d = self.dense[l]
+            kv.decode(q[l], self._store(l, phase), d, out=out[l], body_len=self.tokens, dense_len=d.len_hint)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+            self.done[l] = ev
+            self.ready[l] = None
+        self.step_idx += 1
+        self.step_dev.add_(1)
+        if transfer:
+            self.prefetch(0, self.step_idx)  # the next step's first layer, behind this step's last attention
+
+    # ------------------------------------------------------------------ graphs
+    def capture(self, q: torch.Tensor, out: torch.Tensor) -> None:
+        """Capture one step per phase of the ring as CUDA graphs over the static
+        q [L, B, Hq, 128] / out, with and without the transfer. A transfer graph
+        forks the page prefetcher's side stream, which gathers layer l+1's
+        entering pages (``hkv_prefetch_gather``: one zero-copy kernel, ids on the
+        device, host pages advancing with the device step counter) while layer l
+        attends, each layer's attention waiting for its own pages; the next
+        step's layer-0 pages are gathered behind the last layers and joined
+        before the graph ends; the last node advances the step counter. A step
+        is then one replay, with no host work per layer. Needs a mapped pinned
+        host arena (HKV_ERR_UNSUPPORTED otherwise)."""
+        U, cs, side = self.units, torch.cuda.Stream(device=self.device), self.prefetcher.stream
+        cs.wait_stream(torch.cuda.current_stream(self.device))
+        torch.cuda.synchronize(self.device)
+        self.step_dev.fill_(self.step_idx)
+
+        def body(ph: int, transfer: bool) -> None:
+            ready: List[Optional[torch.cuda.Event]] = [None] * self.L
+            if transfer and self.delta:
+                fork = torch.cuda.Event()
+                fork.record(cs)
+                side.wait_event(fork)
+            for l in range(self.L):
+                if transfer and self.delta:
+                    if l + 1 < self.L:
+                        self.prefetcher.gather(self.g_src, self.g_dst[l + 1][ph], self.step_dev,
+                                               self.delta * U, 0, ctas=self.gather_ctas, stream=side)
+                        ready[l + 1] = torch.cuda.Event()
+                        ready[l + 1].record(side)
+                    if l > 0:
+                        cs.wait_event(ready[l])
+                d = self.dense[l]
+                kv.decode(q[l], self._store(l, ph), d, out=out[l], body_len=self.tokens, dense_len=d.len_hint)
+            if transfer and self.delta:
+                self.prefetcher.gather(self.g_src, self.g_dst[0][(ph + 1) % self.period], self.step_dev,
+                                       self.delta * U, 1, ctas=self.gather_ctas, stream=side)
+                join = torch.cuda.Event()
+                join.record(side)
+                cs.wait_event(join)
+            self.step_dev.add_(1)
+
+        with torch.cuda.stream(cs):  # warm: the decode workspace of the capture stream
+            for l in range(self.L):
+                d = self.dense[l]
+                kv.decode(q[l], self._store(l, 0), d, out=out[l], body_len=self.tokens, dense_len=d.len_hint)
+        cs.synchronize()
+        graphs = {True: [], False: []}
+        for transfer in (True, False):
+            for ph in range(self.period):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cs):
+                    body(ph, transfer)
+                graphs[transfer].append(g)
+        torch.cuda.current_stream(self.device).wait_stream(cs)
+        self._graphs = graphs
+
+    def replay(self, transfer: bool = True) -> None:
+        """One captured step (``capture``) on the current stream."""
+        if self.ready[0] is not None:  # layer 0's pages of an eager prefetch
+            torch.cuda.current_stream(self.device).wait_event(self.ready[0])
+            self.ready[0] = None
+        self._graphs[transfer][self.step_idx % self.period].replay()
+        if transfer:
+            self.fetched_pages += self.L * self.units * self.delta
+        self.step_idx += 1
+
+    def h2d_bytes_per_step(self) -> int:
+        return self.L * self.units * self.delta * self.page_bytes
+
+    def attn_bytes_per_step(self) -> int:
+        per_tok = 2 * (64 + 4 * (128 // self.group) + (128 // self.group if self.fmt == "ref" else 0))
+        dense = self.dense[0].len_hint * 2 * 128 * 2
+        return self.L * self.units * (self.tokens * per_tok + dense)

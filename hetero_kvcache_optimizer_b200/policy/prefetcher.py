@@ -124,6 +124,26 @@ class PagePrefetcher:
         ev.record(self.stream)
         return ev
 
+    def gather(self, src_pages: torch.Tensor, dst_slots: torch.Tensor, step: Optional[torch.Tensor] = None,
+               step_mul: int = 0, step_add: int = 0, ctas: int = 0, stream=None) -> None:
+        """One zero-copy gather kernel (``hkv_prefetch_gather``) on ``stream``
+        (default: the side stream): host page (src_pages[k] + (step + step_add) *
+        step_mul) mod host_pages (just src_pages[k] without ``step``) -> device
+        slot dst_slots[k]. The id tensors (int32) and the step counter (int64,
+        one element) live on the device, so the call can be captured in a CUDA
+        graph and the page set chosen by device code. Records no event."""
+        if src_pages.dtype != torch.int32 or dst_slots.dtype != torch.int32:
+            raise TypeError("page ids must be int32")
+        if not (src_pages.is_cuda and dst_slots.is_cuda) or src_pages.numel() != dst_slots.numel():
+            raise ValueError("src_pages / dst_slots: device tensors of one length")
+        if step is not None and (step.dtype != torch.int64 or not step.is_cuda):
+            raise TypeError("step must be a device int64 tensor")
+        s = stream or self.stream
+        L.check(L.load().hkv_prefetch_gather(
+            self._h, src_pages.data_ptr(), dst_slots.data_ptr(), int(src_pages.numel()),
+            step.data_ptr() if step is not None else None, int(step_mul), int(step_add), int(ctas),
+            ctypes.c_void_p(s.cuda_stream)), "hkv_prefetch_gather")
+
     @staticmethod
     def gate(event: torch.cuda.Event, stream: Optional[torch.cuda.Stream] = None) -> None:
         """Make ``stream`` (default: current) wait for the pages of ``event`` on the device."""

@@ -377,6 +377,21 @@ hkv_status hkv_prefetch_submit(hkv_prefetcher* pf, const int32_t* src_pages,
                                hkv_event_t done);
 /* Bytes submitted so far (for H2D GB/s accounting). */
 int64_t hkv_prefetch_bytes(const hkv_prefetcher* pf);
+/* Zero-copy gather: one kernel on `stream` reads n host pages over the host
+ * link (the pinned pool mapped into the device address space) and writes them
+ * to device slots. src_pages / dst_slots are DEVICE int32 arrays, so the page
+ * set can be chosen on the device and the launch captured in a CUDA graph;
+ * host page of entry k = (src_pages[k] + (*step + step_add) * step_mul) mod
+ * host_pages when `step` (a device int64 counter) is given, else src_pages[k].
+ * ctas = 0: 64 CTAs of 128 threads (a small grid whose CTAs fit beside a
+ * persistent decode kernel's).
+ * Ids outside the pools are skipped and set HKV_DEVERR_BAD_PAGE.
+ * HKV_ERR_UNSUPPORTED when the host pool is not mapped. Replaces the six
+ * per-chunk copies of AsyncPrefetcher.submit_prefetch_task
+ * (src/policy/prefetcher.py:74-79) for scattered page sets. */
+hkv_status hkv_prefetch_gather(hkv_prefetcher* pf, const int32_t* src_pages, const int32_t* dst_slots,
+                               int32_t n, const int64_t* step, int64_t step_mul, int32_t step_add,
+                               int32_t ctas, hkv_stream_t stream);
 /* Host-side bounded wait: polls the event until it completes or timeout_us
  * elapses (HKV_ERR_TIMEOUT). Never blocks forever. */
 hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us);

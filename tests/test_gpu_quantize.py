@@ -155,6 +155,51 @@ def test_quantize_pack_kv_one_launch(hkv, fmt, dt):
         assert np.array_equal(dequant_side(one, role, T), dequant_side(two, role, T))
 
 
+@pytest.mark.parametrize("group", [32, 64, 128])
+@pytest.mark.parametrize("dt", ["fp16", "bf16"])
+def test_quantize_pack_special_values(hkv, group, dt):
+    """Groups the random sweeps never hit, written at an odd start slot (partial
+    64-position tiles, V pairs split across the chunk edge): constant groups
+    (zero range: ref scale clamps to 1e-8, fp16min scale 0 -> codes 0), all
+    zeros, a range whose fp16 scale is subnormal with quotients exactly on .5
+    (ties to even), values at the fp16 extremes, negative-only groups, and for
+    ref with bf16 inputs values near 1e30. Bit-exact with the oracle."""
+    B, H, T, start = 1, 2, 100, 37
+    base = ko.make_input(91 + group, (B, H, T, 128), dt).astype(np.float32)
+    x = base.copy()
+    x[0, 0, 0, :] = 3.0
+    x[0, 0, 1, :] = 0.0
+    x[0, 1, 2, :] = np.arange(128, dtype=np.float32) % 32 * np.float32(2.0 ** -24)
+    # fp16 extremes that bf16 also holds (fp16min keeps the group min as fp16,
+    # so inputs beyond the fp16 range are outside that format)
+    x[0, 0, 3, :] = np.where(np.arange(128) % 2 == 0, 65280.0, -65280.0)
+    x[0, 1, 4, :] = -1.0 - np.arange(128, dtype=np.float32) / 16
+    x[0, 0, 5, :64] = 60000.0
+    big = x.copy()
+    big[0, 1, 6, :] = np.where(np.arange(128) % 3 == 0, 1e30, -3e29)
+    for fmt in ("ref", "fp16min"):
+        xin = big if (fmt == "ref" and dt == "bf16") else x
+        xin = (xin.astype(np.float16) if dt == "fp16" else ko.round_bf16(xin))
+        store = hkv.Int4KVStore(B, H, 256, fmt=fmt, group=group, page_tokens=256)
+        store.pool.zero_()
+        xt = _torch_input(xin.astype(np.float32), dt)
+        hkv.quantize_pack_kv(xt, xt, store, start)
+        for role in (K, V):
+            codes, a, z = read_side(store, role)
+            if fmt == "ref":
+                qc, qs, qz = ko.quantize_ref(xin.astype(np.float32), group)
+                assert np.array_equal(codes[:, :, start:start + T], qc), (fmt, role)
+                assert np.array_equal(a[:, :, start:start + T].reshape(-1), qs), (fmt, role)
+                assert np.array_equal(z[:, :, start:start + T].reshape(-1), qz), (fmt, role)
+            else:
+                qc, qs, qm = ko.quantize_fp16min(xin.astype(np.float32), group)
+                assert np.array_equal(codes[:, :, start:start + T], qc), (fmt, role)
+                assert np.array_equal(a[:, :, start:start + T].view(np.uint16), qs.view(np.uint16)), (fmt, role)
+                assert np.array_equal(z[:, :, start:start + T].view(np.uint16), qm.view(np.uint16)), (fmt, role)
+            # slots outside [start, start + T) untouched
+            assert not codes[:, :, :start].any() and not codes[:, :, start + T:].any(), (fmt, role)
+
+
 def test_quantize_pack_per_batch_start(hkv):
     B, H, T = 3, 2, 5
     x = ko.make_input(9, (B, H, T, 128), "bf16")
