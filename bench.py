@@ -424,7 +424,8 @@ def run_prefill(args) -> None:
 
 # --------------------------------------------------------------------------- config 3
 def cfg3_measure(layers: int, window: int, delta: Optional[int], steps: int, warmup: int, fmt: str, dev,
-                 clocks: bool = False, sweep_ctas: bool = False) -> dict:
+                 clocks: bool = False, sweep_ctas: bool = False, transport: str = "copy",
+                 copy_streams: int = 2) -> dict:
     """InternLM2-7B-shaped tiered offload: 32 layers, B4, Hq32/Hkv8, 131,072-token
     context of which 8,256 stay in HBM (64 sink + 1,024 recent fp16, 28 INT4 pages)
     and 480 INT4 pages of 256 tokens per (sequence, KV head) live in pinned host
@@ -449,8 +450,8 @@ def cfg3_measure(layers: int, window: int, delta: Optional[int], steps: int, war
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     graphs = delta is not None
-    if graphs:  # one graph replay per step: gathers + attentions, no host work per layer
-        dec.capture(q, out)
+    if graphs:  # one graph replay per step: page moves + attentions, no host work per layer
+        dec.capture(q, out, transport=transport, copy_streams=copy_streams)
 
     def timed(transfer: bool) -> float:
         run = (lambda: dec.replay(transfer)) if graphs else (lambda: dec.step(q, out, transfer))
@@ -481,10 +482,16 @@ def cfg3_measure(layers: int, window: int, delta: Optional[int], steps: int, war
         if delta is None:
             for l in range(layers):
                 dec.prefetcher.submit(dec.src_pages, dec.dst_slots[l % 2])
-        else:  # the gathers a replayed step issues, back to back
+        elif transport == "gather":  # the gathers a replayed step issues, back to back
             for l in range(layers):
                 dec.prefetcher.gather(dec.g_src, dec.g_dst[l][0], dec.step_dev, delta * dec.units, 0,
                                       ctas=dec.gather_ctas)
+        else:  # the copies a replayed step issues (one per page row of all units), back to back
+            for l in range(layers):
+                for i in range(delta):
+                    p = (dec.window - delta + i) % dec.cold
+                    dec.prefetcher.submit([p * dec.units + u for u in range(dec.units)],
+                                          [dec._slot(l, u, dec.window - delta + i) for u in range(dec.units)])
         c1.record(ps)
         torch.cuda.synchronize()
         copy_ms = c0.elapsed_time(c1)
@@ -504,7 +511,8 @@ def cfg3_measure(layers: int, window: int, delta: Optional[int], steps: int, war
     r = {"mode": "full cold set" if delta is None and not window else
              f"window of the last {window} pages, copied every step" if delta is None else
              f"window of {window} pages cached in HBM, sliding {delta} page(s) per step "
-             "(CUDA graph per step, zero-copy gather kernels)",
+             f"(CUDA graph per step, page moves by "
+             f"{f'copy engines, {copy_streams} stream(s)' if transport == 'copy' else 'zero-copy gather kernel'})",
          "layers": layers, "window_pages": dec.window, "delta_pages": delta,
          "h2d_bytes_per_step": h2d, "ms_per_step": round(ms_with, 4),
          "decode_ms_per_step_without_transfer": round(ms_without, 4),
@@ -546,6 +554,10 @@ def run_cfg3(args) -> None:
     if args.sweep:
         line["sweep"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev)
                          for d in (0, 1, 2, 4, 8)]
+        line["sweep_gather"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev,
+                                             transport="gather") for d in (1, 2)]
+        line["sweep_one_copy_stream"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev,
+                                                      copy_streams=1) for d in (1, 2)]
     print(json.dumps(line))
 
 

@@ -92,6 +92,8 @@ SIGNATURES = {
     "hkv_prefetch_submit": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, c_vp]),
     "hkv_prefetch_bytes": (c_i64, [c_vp]),
     "hkv_prefetch_gather": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_vp]),
+    "hkv_graph_copy_nodes": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp]),
+    "hkv_graph_exec_set_copy_srcs": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "hkv_event_wait": (c_i32, [c_vp, c_i64]),
     "hkv_qk_scores_flat": (c_i32, [c_vp, c_i32, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
     "hkv_selftest_bounded_wait": (c_i32, [c_i64, c_i32, c_vp]),

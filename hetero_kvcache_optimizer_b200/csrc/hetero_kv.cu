@@ -7,6 +7,7 @@
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "hkv_common.cuh"
 #include "hkv_quant.cuh"   // before the decode kernel: its fused append quantises with it
@@ -794,6 +795,9 @@ hkv_status hkv_decode_append(const void* q, int32_t q_dtype, int64_t q_stride_b,
   if (!aligned16(k_new) || !aligned16(v_new) || new_stride_b % 8 || new_stride_h % 8) return HKV_ERR_ARG;
   if (sink < 0 || sink > dense->capacity) return HKV_ERR_ARG;
   if ((int64_t)B * Hkv > kMaxUnits - 1) return HKV_ERR_UNSUPPORTED;  // the last counter is the state counter
+  // a unit's last pipeline piece waits for the append warp of another CTA, so
+  // every CTA must be resident at once: at most one CTA per SM
+  if (ctas > device_sms()) return HKV_ERR_ARG;
   AppendArgs app{k_new, v_new, new_stride_b, new_stride_h, sink, dense_len, ring_head, body_len,
                  (flags & HKV_APPEND_EARLY) ? 1 : 0};
   return run_decode(q, q_dtype, q_stride_b, q_stride_h, body, dense, B, Hq, Hkv, D, sm_scale, ctas, workspace,
@@ -1129,6 +1133,46 @@ hkv_status hkv_prefetch_gather(hkv_prefetcher* pf, const int32_t* src_pages, con
   const hkv_status rc = launch_status();
   if (rc == HKV_OK) pf->bytes.fetch_add((int64_t)n * pf->page_bytes);
   return rc;
+}
+
+hkv_status hkv_graph_copy_nodes(void* graph, int32_t max_nodes, void** nodes, void** dsts, int32_t* n) {
+  if (!graph || !n || max_nodes < 0 || (max_nodes > 0 && (!nodes || !dsts))) return HKV_ERR_ARG;
+  cudaGraph_t g = static_cast<cudaGraph_t>(graph);
+  size_t count = 0;
+  cudaError_t e = cudaGraphGetNodes(g, nullptr, &count);
+  if (e != cudaSuccess) return cuda_fail(e);
+  std::vector<cudaGraphNode_t> all(count);
+  if (count && (e = cudaGraphGetNodes(g, all.data(), &count)) != cudaSuccess) return cuda_fail(e);
+  int32_t k = 0;
+  for (size_t i = 0; i < count; ++i) {
+    cudaGraphNodeType t;
+    if ((e = cudaGraphNodeGetType(all[i], &t)) != cudaSuccess) return cuda_fail(e);
+    if (t != cudaGraphNodeTypeMemcpy) continue;
+    cudaMemcpy3DParms prm;
+    std::memset(&prm, 0, sizeof(prm));
+    if ((e = cudaGraphMemcpyNodeGetParams(all[i], &prm)) != cudaSuccess) return cuda_fail(e);
+    if (k < max_nodes) {
+      nodes[k] = all[i];
+      dsts[k] = static_cast<char*>(prm.dstPtr.ptr) + prm.dstPos.x +
+                (prm.dstPos.y + prm.dstPos.z * prm.dstPtr.ysize) * prm.dstPtr.pitch;
+    }
+    ++k;
+  }
+  *n = k;
+  return k > max_nodes ? HKV_ERR_CAPACITY : HKV_OK;
+}
+
+hkv_status hkv_graph_exec_set_copy_srcs(void* graph_exec, int32_t n, void* const* nodes, void* const* dsts,
+                                        const void* const* srcs, const int64_t* bytes) {
+  if (!graph_exec || n < 0 || (n > 0 && (!nodes || !dsts || !srcs || !bytes))) return HKV_ERR_ARG;
+  cudaGraphExec_t x = static_cast<cudaGraphExec_t>(graph_exec);
+  for (int32_t i = 0; i < n; ++i) {
+    if (!nodes[i] || !dsts[i] || !srcs[i] || bytes[i] <= 0) return HKV_ERR_ARG;
+    const cudaError_t e = cudaGraphExecMemcpyNodeSetParams1D(x, static_cast<cudaGraphNode_t>(nodes[i]), dsts[i],
+                                                             srcs[i], (size_t)bytes[i], cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return HKV_OK;
 }
 
 hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us) {

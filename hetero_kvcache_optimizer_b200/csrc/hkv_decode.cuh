@@ -984,6 +984,23 @@ __device__ __forceinline__ void merge_head(const DecodeParams& p, int u, int h, 
 // The arrival is split so that a warp need not wait for the global atomic: its
 // old count stays in a register that only state_arrive_finish consumes; the
 // last arriver fences (acquire) before it writes the state.
+// The fused append's arrival on a unit's merge counter: a count of its own
+// above the pipeline pieces' (fewer than 2^16 per unit).
+constexpr int kAppendArrival = 1 << 16;
+// Bounded wait of the unit's last pipeline piece for the append's arrival.
+__device__ __forceinline__ bool wait_append_arrival(const int* addr) {
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    if (v >= kAppendArrival) return true;
+    if (globaltimer_ns() - t0 > HKV_WAIT_NS) {
+      hkv_flag_error(HKV_DEVERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(256);
+  }
+}
 __device__ __forceinline__ int atom_add_release_gpu(int* addr, int v) {
   int old;
   asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
@@ -1118,16 +1135,16 @@ __device__ __noinline__ void append_units(const DecodeParams& p, int c, int* s_r
         if (lane == 16) *reinterpret_cast<float2*>(pml + 2 * g) = make_float2(m, pe + pn);
       }
     }
-    // publish the partial (release by lane 0 after the warp's writes), then
-    // the unit's last contributor merges
+    // publish the partial: the release add of kAppendArrival after the warp's
+    // writes. The merge stays with the consumers (one warp per head) even when
+    // this partial comes last: a unit split over many CTAs has tens of
+    // partials, which one warp merging every head alone took tens of us for.
+    // Only a unit without pipeline pieces is merged here.
     __threadfence();
     __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atom_add_acq_rel_gpu(&p.counters[u], 1) == nb + nd;
-    __syncwarp();
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      for (int g = 0; g < p.G; ++g) merge_head<false>(p, u, g, nb + nd + 1);
+    if (lane == 0) atom_add_release_gpu(&p.counters[u], kAppendArrival);
+    if (nb + nd == 0) {
+      for (int g = 0; g < p.G; ++g) merge_head<false>(p, u, g, 1);
       __syncwarp();
       if (lane == 0) p.counters[u] = 0;
     }
@@ -1581,7 +1598,14 @@ __global__ void __launch_bounds__(decode_threads(FMT, APPEND), 1)
       // and whose acquire, followed by the barrier, orders the merge's loads of the
       // other CTAs' partials after their releases.
       consumer_sync();
-      if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&p.counters[u], 1) == nb + nd + kExtra - 1;
+      if (threadIdx.x == 0) {
+        const int old = atom_add_acq_rel_gpu(&p.counters[u], 1);
+        bool last = (old & (kAppendArrival - 1)) == nb + nd - 1;
+        // APPEND: the last pipeline piece also merges the append's partial, once
+        // it is published (a bounded wait; the append warp depends on nothing here)
+        if (APPEND && last && old < kAppendArrival) last = wait_append_arrival(&p.counters[u]);
+        s_last = last;
+      }
       consumer_sync();
       if (s_last) {
         // last piece of the unit: merge all its partials (warp h: head h)

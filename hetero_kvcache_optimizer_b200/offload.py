@@ -19,6 +19,7 @@ synchronisation.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import List, Optional
 
 import torch
@@ -243,6 +244,8 @@ class SlidingWindowOffload:
         self.step_dev = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.gather_ctas = gather_ctas  # grid of the captured gathers (0: the library's default)
         self._graphs = None
+        self.transport = "copy"
+        self._copy_nodes: list = []
 
     def _slot(self, l: int, u: int, p):
         """Ring slot of window page p (any integer) of layer l, unit u."""
@@ -334,45 +337,73 @@ class SlidingWindowOffload:
             self.prefetch(0, self.step_idx)  # the next step's first layer, behind this step's last attention
 
     # ------------------------------------------------------------------ graphs
-    def capture(self, q: torch.Tensor, out: torch.Tensor) -> None:
+    def capture(self, q: torch.Tensor, out: torch.Tensor, transport: str = "copy", copy_streams: int = 2) -> None:
         """Capture one step per phase of the ring as CUDA graphs over the static
-        q [L, B, Hq, 128] / out, with and without the transfer. A transfer graph
-        forks the page prefetcher's side stream, which gathers layer l+1's
-        entering pages (``hkv_prefetch_gather``: one zero-copy kernel, ids on the
-        device, host pages advancing with the device step counter) while layer l
-        attends, each layer's attention waiting for its own pages; the next
-        step's layer-0 pages are gathered behind the last layers and joined
-        before the graph ends; the last node advances the step counter. A step
-        is then one replay, with no host work per layer. Needs a mapped pinned
-        host arena (HKV_ERR_UNSUPPORTED otherwise)."""
-        U, cs, side = self.units, torch.cuda.Stream(device=self.device), self.prefetcher.stream
+        q [L, B, Hq, 128] / out, with and without the transfer, so a step is one
+        graph launch with no host work per layer. A transfer graph forks the page
+        prefetcher's side stream, which moves layer l+1's entering pages while
+        layer l attends, each layer's attention waiting for its own pages; the
+        next step's layer-0 pages move behind the last layers and are joined
+        before the graph ends.
+
+        transport "copy": one host -> device copy per entering page row (the
+        row of all U units, contiguous on both sides), on the copy engines; the
+        host rows move with the step, so ``replay`` points the graph's copy
+        nodes at the step's rows first (``hkv_graph_exec_set_copy_srcs``, one
+        library call per step). "gather": one zero-copy gather kernel per layer
+        (``hkv_prefetch_gather``) whose host rows follow the device step
+        counter, so nothing changes between replays (SM loads over the host
+        link: ~42 GB/s measured here against ~45-48 for the copy engines); needs
+        a mapped pinned arena. ``copy_streams`` side streams take the layers in
+        turn, so one layer's copy starts while the previous one is in flight
+        (each copy costs microseconds of set-up besides its bytes)."""
+        if transport not in ("copy", "gather"):
+            raise ValueError("transport: 'copy' or 'gather'")
+        U, cs = self.units, torch.cuda.Stream(device=self.device)
+        sides = [self.prefetcher.stream] + [torch.cuda.Stream(device=self.device)
+                                            for _ in range(max(1, copy_streams) - 1)]
+        W, dl, pb = self.window, self.delta, self.page_bytes
         cs.wait_stream(torch.cuda.current_stream(self.device))
         torch.cuda.synchronize(self.device)
         self.step_dev.fill_(self.step_idx)
+        self.transport = transport
+
+        def fetch(l: int, ph: int, add: int, side: torch.cuda.Stream) -> None:
+            if transport == "gather":
+                self.prefetcher.gather(self.g_src, self.g_dst[l][ph], self.step_dev, dl * U, add,
+                                       ctas=self.gather_ctas, stream=side)
+                return
+            for i in range(dl):  # one copy node per page row; its source is retargeted per replay
+                j = W - dl + i
+                p = ((ph + add) * dl + j) % self.cold
+                self.prefetcher.submit([p * U + u for u in range(U)],
+                                       [self._slot(l, u, ph * dl + j) for u in range(U)], stream=side)
 
         def body(ph: int, transfer: bool) -> None:
             ready: List[Optional[torch.cuda.Event]] = [None] * self.L
-            if transfer and self.delta:
+            move = transfer and dl > 0
+            if move:
                 fork = torch.cuda.Event()
                 fork.record(cs)
-                side.wait_event(fork)
+                for side in sides:
+                    side.wait_event(fork)
             for l in range(self.L):
-                if transfer and self.delta:
+                if move:
                     if l + 1 < self.L:
-                        self.prefetcher.gather(self.g_src, self.g_dst[l + 1][ph], self.step_dev,
-                                               self.delta * U, 0, ctas=self.gather_ctas, stream=side)
+                        side = sides[(l + 1) % len(sides)]
+                        fetch(l + 1, ph, 0, side)
                         ready[l + 1] = torch.cuda.Event()
                         ready[l + 1].record(side)
                     if l > 0:
                         cs.wait_event(ready[l])
                 d = self.dense[l]
                 kv.decode(q[l], self._store(l, ph), d, out=out[l], body_len=self.tokens, dense_len=d.len_hint)
-            if transfer and self.delta:
-                self.prefetcher.gather(self.g_src, self.g_dst[0][(ph + 1) % self.period], self.step_dev,
-                                       self.delta * U, 1, ctas=self.gather_ctas, stream=side)
-                join = torch.cuda.Event()
-                join.record(side)
-                cs.wait_event(join)
+            if move:
+                fetch(0, (ph + 1) % self.period, 1, sides[0])
+                for side in sides:  # join every side stream
+                    join = torch.cuda.Event()
+                    join.record(side)
+                    cs.wait_event(join)
             self.step_dev.add_(1)
 
         with torch.cuda.stream(cs):  # warm: the decode workspace of the capture stream
@@ -381,20 +412,67 @@ class SlidingWindowOffload:
                 kv.decode(q[l], self._store(l, 0), d, out=out[l], body_len=self.tokens, dense_len=d.len_hint)
         cs.synchronize()
         graphs = {True: [], False: []}
+        self._copy_nodes = []  # per phase: (nodes, dsts, row, step offset) of its copy nodes
         for transfer in (True, False):
             for ph in range(self.period):
-                g = torch.cuda.CUDAGraph()
+                g = torch.cuda.CUDAGraph(keep_graph=True)
                 with torch.cuda.graph(g, stream=cs):
                     body(ph, transfer)
+                g.instantiate()
                 graphs[transfer].append(g)
+                if transfer and transport == "copy" and dl:
+                    self._copy_nodes.append(self._map_copy_nodes(g, ph))
         torch.cuda.current_stream(self.device).wait_stream(cs)
         self._graphs = graphs
+
+    def _map_copy_nodes(self, g: "torch.cuda.CUDAGraph", ph: int):
+        """The copy nodes of phase ph's transfer graph, matched to (layer, row)
+        through their destinations: layers 1..L-1 copy step s's rows, layer 0
+        step s+1's rows (into phase ph+1's ring slots)."""
+        import numpy as np
+        lib = L.load()
+        cap = self.L * self.delta
+        nodes = (ctypes.c_void_p * cap)()
+        dsts = (ctypes.c_void_p * cap)()
+        n = ctypes.c_int32(0)
+        L.check(lib.hkv_graph_copy_nodes(ctypes.c_void_p(int(g.raw_cuda_graph())), cap, nodes, dsts,
+                                         ctypes.byref(n)), "hkv_graph_copy_nodes")
+        by_dst = {int(dsts[k]): int(nodes[k]) for k in range(n.value)}
+        base, U, W, dl, pb = self.pool.data_ptr(), self.units, self.window, self.delta, self.page_bytes
+        ent_nodes, ent_dsts, layer, row, add = [], [], [], [], []
+        for l in range(self.L):
+            a, ph_dst = (1, (ph + 1) % self.period) if l == 0 else (0, ph)
+            for i in range(dl):
+                dst = base + self._slot(l, 0, ph_dst * dl + W - dl + i) * pb
+                if dst not in by_dst:
+                    raise RuntimeError("captured copy node not found for a window row")
+                ent_nodes.append(by_dst[dst])
+                ent_dsts.append(dst)
+                layer.append(l)
+                row.append(W - dl + i)
+                add.append(a)
+        return (np.array(ent_nodes, np.uint64), np.array(ent_dsts, np.uint64), np.array(row, np.int64),
+                np.array(add, np.int64))
+
+    def _retarget(self, s: int) -> None:
+        """Point phase (s mod period)'s copy nodes at step s's host rows."""
+        import numpy as np
+        nodes, dsts, row, add = self._copy_nodes[s % self.period]
+        p = ((s + add) * self.delta + row) % self.cold
+        srcs = (self.host.data_ptr() + p * (self.units * self.page_bytes)).astype(np.uint64)
+        nbytes = np.full(len(nodes), self.units * self.page_bytes, np.int64)
+        g = self._graphs[True][s % self.period]
+        L.check(L.load().hkv_graph_exec_set_copy_srcs(
+            ctypes.c_void_p(int(g.raw_cuda_graph_exec())), len(nodes), nodes.ctypes.data, dsts.ctypes.data,
+            srcs.ctypes.data, nbytes.ctypes.data), "hkv_graph_exec_set_copy_srcs")
 
     def replay(self, transfer: bool = True) -> None:
         """One captured step (``capture``) on the current stream."""
         if self.ready[0] is not None:  # layer 0's pages of an eager prefetch
             torch.cuda.current_stream(self.device).wait_event(self.ready[0])
             self.ready[0] = None
+        if transfer and self.delta and self.transport == "copy":
+            self._retarget(self.step_idx)
         self._graphs[transfer][self.step_idx % self.period].replay()
         if transfer:
             self.fetched_pages += self.L * self.units * self.delta

@@ -111,17 +111,20 @@ class PagePrefetcher:
         self._h = h
 
     def submit(self, src_pages: Sequence[int], dst_slots: Sequence[int],
-               event: Optional[torch.cuda.Event] = None) -> torch.cuda.Event:
-        """Issue the copies on the side stream; returns an event recorded after them."""
+               event: Optional[torch.cuda.Event] = None,
+               stream: Optional[torch.cuda.Stream] = None) -> torch.cuda.Event:
+        """Issue the copies on ``stream`` (default: the side stream); returns an
+        event recorded after them."""
+        s = stream or self.stream
         src = np.ascontiguousarray(np.asarray(src_pages, dtype=np.int32))
         dst = np.ascontiguousarray(np.asarray(dst_slots, dtype=np.int32))
         if src.shape != dst.shape:
             raise ValueError("src_pages and dst_slots differ in length")
         L.check(L.load().hkv_prefetch_submit(self._h, src.ctypes.data, dst.ctypes.data, int(src.size),
-                                             ctypes.c_void_p(self.stream.cuda_stream), None),
+                                             ctypes.c_void_p(s.cuda_stream), None),
                 "hkv_prefetch_submit")
         ev = event or torch.cuda.Event()
-        ev.record(self.stream)
+        ev.record(s)
         return ev
 
     def gather(self, src_pages: torch.Tensor, dst_slots: torch.Tensor, step: Optional[torch.Tensor] = None,

@@ -392,6 +392,18 @@ int64_t hkv_prefetch_bytes(const hkv_prefetcher* pf);
 hkv_status hkv_prefetch_gather(hkv_prefetcher* pf, const int32_t* src_pages, const int32_t* dst_slots,
                                int32_t n, const int64_t* step, int64_t step_mul, int32_t step_add,
                                int32_t ctas, hkv_stream_t stream);
+/* Page copies inside a CUDA graph whose host source moves between replays (a
+ * sliding window over a host arena): hkv_graph_copy_nodes lists the memcpy
+ * nodes of a captured graph (a cudaGraph_t) and their destination addresses
+ * (at most max_nodes; *n = how many exist, HKV_ERR_CAPACITY if more), and
+ * hkv_graph_exec_set_copy_srcs points n of those nodes of the instantiated
+ * graph (a cudaGraphExec_t) at new host sources (host -> device, bytes[i]
+ * each) for every later launch; a launch already queued keeps its copies. The
+ * copies stay on the copy engines at full host-link bandwidth, and a step is
+ * one graph launch. */
+hkv_status hkv_graph_copy_nodes(void* graph, int32_t max_nodes, void** nodes, void** dsts, int32_t* n);
+hkv_status hkv_graph_exec_set_copy_srcs(void* graph_exec, int32_t n, void* const* nodes, void* const* dsts,
+                                        const void* const* srcs, const int64_t* bytes);
 /* Host-side bounded wait: polls the event until it completes or timeout_us
  * elapses (HKV_ERR_TIMEOUT). Never blocks forever. */
 hkv_status hkv_event_wait(hkv_event_t ev, int64_t timeout_us);

@@ -39,14 +39,15 @@ def test_prefetched_pages_match_resident(window):
 
 
 @pytest.mark.parametrize("window,delta", [(4, 1), (4, 2), (3, 0), (4, 4)])
-@pytest.mark.parametrize("mode", ["eager", "graph"])
+@pytest.mark.parametrize("mode", ["eager", "graph-copy", "graph-gather"])
 def test_sliding_window_cache_matches_resident(window, delta, mode):
     """Residency-aware window: the pages cached in HBM across steps plus the
     ``delta`` new ones copied each step give exactly the attention of the same
     pages (resident pages, then the window's pages in window order) held in a
-    plain store; the copies per step are the delta only. ``graph``: the steps
-    replay CUDA graphs whose page moves are zero-copy gather kernels driven by
-    the device step counter (two eager steps first, so the counter starts > 0)."""
+    plain store; the copies per step are the delta only. ``graph-*``: the steps
+    replay CUDA graphs (two eager steps first, so the step starts > 0) whose page
+    moves are copy nodes retargeted to each step's host rows (``copy``) or
+    zero-copy gather kernels driven by the device step counter (``gather``)."""
     from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv
     from hetero_kvcache_optimizer_b200.offload import SlidingWindowOffload
     dev = torch.device("cuda", 0)
@@ -60,11 +61,12 @@ def test_sliding_window_cache_matches_resident(window, delta, mode):
     U, W = dec.units, dec.window
     host = dec.host.to(dev).view(C, U, dec.page_bytes).transpose(0, 1)  # page-major arena
     fetched0 = dec.fetched_pages
-    for s in range(12 if mode == "graph" else 7):  # past the ring's period and around the cold set
-        if mode == "graph" and s == 2:
-            dec.capture(q, out)
+    graph = mode.startswith("graph")
+    for s in range(12 if graph else 7):  # past the ring's period and around the cold set
+        if graph and s == 2:
+            dec.capture(q, out, transport=mode.split("-")[1])
         out.fill_(float("nan"))
-        if mode == "graph" and s >= 2:
+        if graph and s >= 2:
             dec.replay(transfer=True)
         else:
             dec.step(q, out, transfer=True)
@@ -81,7 +83,7 @@ def test_sliding_window_cache_matches_resident(window, delta, mode):
             assert torch.equal(out[l], ref), (s, l)
     assert _lib.device_error() == 0
     # after step 0, each step copies only the pages entering the window
-    steps_after_first = 11 if mode == "graph" else 6
+    steps_after_first = 11 if graph else 6
     per_step = Lyr * U * delta
     assert dec.fetched_pages - fetched0 <= (steps_after_first + 2) * per_step + Lyr * U * delta
     assert dec.h2d_bytes_per_step() == per_step * dec.page_bytes
