@@ -425,7 +425,7 @@ def run_prefill(args) -> None:
 # --------------------------------------------------------------------------- config 3
 def cfg3_measure(layers: int, window: int, delta: Optional[int], steps: int, warmup: int, fmt: str, dev,
                  clocks: bool = False, sweep_ctas: bool = False, transport: str = "copy",
-                 copy_streams: int = 2) -> dict:
+                 copy_streams: int = 1) -> dict:
     """InternLM2-7B-shaped tiered offload: 32 layers, B4, Hq32/Hkv8, 131,072-token
     context of which 8,256 stay in HBM (64 sink + 1,024 recent fp16, 28 INT4 pages)
     and 480 INT4 pages of 256 tokens per (sequence, KV head) live in pinned host
@@ -556,8 +556,8 @@ def run_cfg3(args) -> None:
                          for d in (0, 1, 2, 4, 8)]
         line["sweep_gather"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev,
                                              transport="gather") for d in (1, 2)]
-        line["sweep_one_copy_stream"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev,
-                                                      copy_streams=1) for d in (1, 2)]
+        line["sweep_two_copy_streams"] = [cfg3_measure(args.layers, 8, d, args.steps, args.warmup, args.fmt, dev,
+                                                       copy_streams=2) for d in (1, 2)]
     print(json.dumps(line))
 
 

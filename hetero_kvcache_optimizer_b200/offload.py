@@ -337,7 +337,7 @@ class SlidingWindowOffload:
             self.prefetch(0, self.step_idx)  # the next step's first layer, behind this step's last attention
 
     # ------------------------------------------------------------------ graphs
-    def capture(self, q: torch.Tensor, out: torch.Tensor, transport: str = "copy", copy_streams: int = 2) -> None:
+    def capture(self, q: torch.Tensor, out: torch.Tensor, transport: str = "copy", copy_streams: int = 1) -> None:
         """Capture one step per phase of the ring as CUDA graphs over the static
         q [L, B, Hq, 128] / out, with and without the transfer, so a step is one
         graph launch with no host work per layer. A transfer graph forks the page
@@ -354,9 +354,9 @@ class SlidingWindowOffload:
         (``hkv_prefetch_gather``) whose host rows follow the device step
         counter, so nothing changes between replays (SM loads over the host
         link: ~42 GB/s measured here against ~45-48 for the copy engines); needs
-        a mapped pinned arena. ``copy_streams`` side streams take the layers in
-        turn, so one layer's copy starts while the previous one is in flight
-        (each copy costs microseconds of set-up besides its bytes)."""
+        a mapped pinned arena. ``copy_streams`` > 1 side streams take the layers
+        in turn, so one layer's copy may start while the previous one is in
+        flight (measured: no gain, the host link is the bound)."""
         if transport not in ("copy", "gather"):
             raise ValueError("transport: 'copy' or 'gather'")
         U, cs = self.units, torch.cuda.Stream(device=self.device)
