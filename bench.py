@@ -52,10 +52,11 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None,
                     help="layers (default: the workload's own, 32 for cfg1/cfg3, 28 for cfg2)")
     ap.add_argument("--ctas", type=int, default=0, help="persistent decode grid (0 = one CTA per SM)")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4b", "prefill"],
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg4b", "prefill"],
                     help="cfg1: the headline decode benchmark (default); cfg2: long multimodal context "
                          "(chunked prefill quantise + decode); cfg3: tiered offload, layer-ahead "
-                         "host->device page prefetch; cfg4b: sequence split across ranks + NCCL all-gather "
+                         "host->device page prefetch; cfg4: B64 context sweep 4K-128K, unit shard and "
+                         "sequence split; cfg4b: sequence split across ranks + NCCL all-gather "
                          "of partials + LSE merge; prefill: tcgen05 multi-query attention over a "
                          "32K INT4 body (each prints its own line)")
     ap.add_argument("--sq", type=int, default=2048, help="prefill: query positions per sequence")
@@ -72,7 +73,7 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-offload", action="store_true",
-                    help="cfg1: leave out the short config-3 offload measurement on the 1-GPU line")
+                    help="cfg1: leave out the short config-2 and config-3 measurements on the 1-GPU line")
     ap.add_argument("--no-early", action="store_true",
                     help="cfg1/cfg2: fused launches wait for the previous launch before reading the cache "
                          "(default: stream it while the previous layer's launch finishes)")
@@ -204,7 +205,8 @@ def layer_bytes(batch, body_tokens, fmt, kv_heads=8, q_heads=32, sink=64, recent
 
 
 # --------------------------------------------------------------------------- config 2
-def run_cfg2(args) -> None:
+def cfg2_measure(layers: int, steps: int, warmup: int, fmt: str, dev, fused: bool = True,
+                 early: Optional[bool] = None) -> dict:
     """Qwen2-VL-7B-shaped long multimodal decode: 28 layers, B1, Hq28/Hkv4 (GQA 7),
     131,072-token context (positions < 100,000 'vision' K/V ~ N(0, 0.5^2), the rest
     'text' ~ N(0, 1) with 4 x10 outlier K channels per head); chunked prefill
@@ -213,14 +215,12 @@ def run_cfg2(args) -> None:
     import torch
     from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv
     from hetero_kvcache_optimizer_b200.decode_engine import TieredKVDecoder
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    layers, B, Hq, Hkv, ctx, sink, recent, chunk = args.layers, 1, 28, 4, 131072, 64, 1024, 4096
+    B, Hq, Hkv, ctx, sink, recent, chunk = 1, 28, 4, 131072, 64, 1024, 4096
     body = ctx - sink - recent
-    total_steps = args.warmup + args.steps + 4
+    total_steps = warmup + steps + 4
     eng = TieredKVDecoder(layers, B, Hq, Hkv, sink=sink, recent=recent, body_capacity=body + total_steps + 8,
-                          fmt=args.fmt, group=32, kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
-                          fused_append=not args.no_fused, early=False if args.no_early else None)
+                          fmt=fmt, group=32, kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
+                          fused_append=fused, early=early)
     gen = torch.Generator(device=dev).manual_seed(2)
     st_ = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -270,42 +270,49 @@ def run_cfg2(args) -> None:
         del k, v
     eng.set_state(body)
     ng = 4
-    q_bytes = layers * B * Hkv * body * 2 * (128 * 2 + 64 + 4 * ng + (ng if args.fmt == "ref" else 0))
+    q_bytes = layers * B * Hkv * body * 2 * (128 * 2 + 64 + 4 * ng + (ng if fmt == "ref" else 0))
     eng.capture(max_steps=total_steps)
     q, kn, vn, out = eng.static_buffers
     q.copy_(torch.randn(q.shape, device=dev, generator=gen))
     kn.copy_(torch.randn(kn.shape, device=dev, generator=gen))
     vn.copy_(torch.randn(vn.shape, device=dev, generator=gen))
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         eng.replay()
     torch.cuda.synchronize()
     body0 = eng.body_len
-    sampler = ClockSampler(0, 50)
+    sampler = ClockSampler(dev.index, 50)
     sampler.start()
     e0.record(st_)
-    for _ in range(args.steps):
+    for _ in range(steps):
         eng.replay()
     e1.record(st_)
     torch.cuda.synchronize()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    step_bytes = sum(eng.step_bytes(body0 + i) for i in range(args.steps)) / args.steps
+    ms = e0.elapsed_time(e1) / steps
+    step_bytes = sum(eng.step_bytes(body0 + i) for i in range(steps)) / steps
     derr = _lib.device_error(clear=True)
     if derr:
         raise RuntimeError(f"device error bits {derr} during the benchmark")
-    print(json.dumps({
+    return {
         "metric": "config2 long-context decode: HBM GB/s and tokens/s; chunked prefill quantise GB/s",
-        "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "n_gpus": 1, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16 mma (int4 storage, fp32 accum)", "data": "synthetic",
         "config": {"workload": "config2: Qwen2-VL-7B-shaped, 28 layers, B1, Hq28/Hkv4 (GQA 7), ctx 131072 "
                                "(100,000 vision tokens N(0,0.5^2), text N(0,1) + outliers); 64 sink + 1024 "
-                               "recent fp16 + 129,984 INT4 g32", "layers": layers, "kv_format": args.fmt},
+                               "recent fp16 + 129,984 INT4 g32", "layers": layers, "kv_format": fmt},
         "tokens_per_s": round(B / (ms * 1e-3), 1),
         "prefill_quantize": {"chunk_tokens": chunk, "ms_all_layers": round(q_ms, 3),
                              "gbs": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
                              "tokens_per_s": round(layers * B * body / (q_ms * 1e-3), 0)},
-        "gpu_launches": args.steps * layers * eng.launches_per_layer, "clocks": clocks}))
+        "gpu_launches": steps * layers * eng.launches_per_layer, "clocks": clocks}
+
+
+def run_cfg2(args) -> None:
+    import torch
+    torch.cuda.set_device(0)
+    print(json.dumps(cfg2_measure(args.layers, args.steps, args.warmup, args.fmt, torch.device("cuda", 0),
+                                  fused=not args.no_fused, early=False if args.no_early else None)))
 
 
 # --------------------------------------------------------------------------- prefill
@@ -685,6 +692,112 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
             "gpu_launches": world * steps * layers * 2}
 
 
+def batchshard_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt: str, world: int, rank: int,
+                       dev) -> dict:
+    """Config 4 variant A on this process group: Llama-3.1-8B shape, B sequences
+    of `ctx` tokens (64 sink + 1024 recent fp16, the rest INT4), the B x Hkv
+    units sharded by sequence over the ranks (B / world each), every rank running
+    the single-GPU decode on its shard: no collective. Max-over-ranks step time
+    and aggregate figures (every rank gets the same dict)."""
+    import torch
+    import torch.distributed as dist
+    from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv
+    Hq, Hkv, sink, recent = 32, 8, 64, 1024
+    if B % world:
+        raise ValueError("batch must divide over the ranks")
+    Br = B // world
+    ntok = ctx - sink - recent
+    gen = torch.Generator(device=dev).manual_seed(50 + rank)
+    stores, denses = [], []
+    for l in range(layers):
+        st = kv.Int4KVStore(Br, Hkv, ntok, fmt=fmt, group=32, device=dev)
+        for t0 in range(0, ntok, 4096):
+            n = min(4096, ntok - t0)
+            x = torch.randn(Br, Hkv, n, 128, device=dev, generator=gen).half()
+            kv.quantize_pack(x, st, 0, t0)
+            kv.quantize_pack(x, st, 1, t0)
+        st.set_lengths(ntok)
+        d = kv.DenseKV(Br, Hkv, sink + recent, device=dev)
+        d.k.normal_(generator=gen)
+        d.v.normal_(generator=gen)
+        d.set_lengths(sink + recent)
+        stores.append(st)
+        denses.append(d)
+    q = torch.randn(layers, Br, Hq, 128, device=dev, generator=gen).bfloat16()
+    out = torch.empty(layers, Br, Hq, 128, device=dev)
+
+    def step():
+        for l in range(layers):
+            kv.decode(q[l], stores[l], denses[l], out=out[l])
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    st_ = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st_)
+    for _ in range(steps):
+        step()
+    e1.record(st_)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    derr = _lib.device_error(clear=True)
+    if derr:
+        raise RuntimeError(f"device error bits {derr} during the batch-shard benchmark")
+    per_tok = 2 * (64 + 4 * 4 + (4 if fmt == "ref" else 0))
+    step_bytes = layers * (B * Hkv * (ntok * per_tok + (sink + recent) * 512) + B * Hq * 128 * 6)
+    peak, _ = measured_peak()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    del stores, denses, q, out
+    return {"ms_per_step": round(ms, 4), "gbs": round(gbs, 2), "tokens_per_s": round(B / (ms * 1e-3), 1),
+            "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
+            "pct_of_aggregate_8TBs": round(100 * gbs / (world * NOMINAL_HBM_GBS), 2),
+            "gpu_launches": world * steps * layers}
+
+
+def run_cfg4(args, world: int, rank: int, local: int) -> None:
+    """Config 4: Llama-3.1-8B decode at B 64 over contexts of 4K, 16K, 64K and
+    128K tokens, variant A (batch x KV-head units sharded over the ranks, no
+    collective) and variant B (each sequence split over the ranks, one NCCL
+    all-gather of the partials per layer, LSE merge): tokens/s and % of the
+    aggregate HBM roofline, 2 layers per step (per-layer figures)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rows = []
+    for ctx in (4096, 16384, 65536, 131072):
+        a = batchshard_measure(args.batch, ctx, 2, args.steps, args.warmup, args.fmt, world, rank, dev)
+        b = seqsplit_measure(args.batch, ctx, 2, args.steps, args.warmup, args.fmt, world, rank, dev)
+        rows.append({"ctx": ctx, "variant_a": a, "variant_b": {k: v for k, v in b.items() if k != "workload"}})
+    if rank == 0:
+        top = rows[-1]["variant_a"]
+        print(json.dumps({
+            "metric": "config4: Llama-3.1-8B INT4-KV decode attention at B64, tokens/s and % of aggregate HBM "
+                      "roofline, contexts 4K-128K, variants A (unit shard) and B (sequence split)",
+            "value": top["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": top["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 mma (int4 storage, fp32 accum)",
+            "data": "synthetic",
+            "config": {"workload": "config4: Llama-3.1-8B shape (Hq32/Hkv8, D128), B64, 2 layers, contexts "
+                                   "4096/16384/65536/131072 (64 sink + 1024 recent fp16, the rest INT4 g32); "
+                                   "value = variant A at 131072", "kv_format": args.fmt,
+                       "parallelism": f"A: shard{world} / B: seqsplit{world}"},
+            "sweep": rows, "gpu_launches": sum(r["variant_a"]["gpu_launches"] + r["variant_b"]["gpu_launches"]
+                                               for r in rows)}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_cfg4b(args, world: int, rank: int, local: int) -> None:
     """Config 4 variant B as its own line (see seqsplit_measure)."""
     import torch
@@ -724,6 +837,10 @@ def main():
         return
     if args.workload == "prefill" and args.impl == "ours":
         run_prefill(args)
+        return
+    if args.workload == "cfg4" and args.impl == "ours":
+        run_cfg4(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+                 int(os.environ.get("LOCAL_RANK", "0")))
         return
     if args.workload == "cfg4b" and args.impl == "ours":
         run_cfg4b(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
@@ -905,11 +1022,17 @@ def main():
     # ---- config 3 in short (4 of its 32 layers, one rank): exposed host->device
     # transfer when every step copies the whole cold set, and when a window of
     # 8 cold pages stays cached in HBM and slides by one page per step
-    offload = None
+    offload = cfg2 = None
     if world == 1 and not args.no_offload:
         offload = {"layers": 4,
                    "full_cold_set": cfg3_measure(4, 0, None, 4, 3, args.fmt, dev),
                    "sliding_window": cfg3_measure(4, 8, 1, 10, 3, args.fmt, dev)}
+        # config 2 in short: 4 of its 28 layers (the per-layer figures do not
+        # depend on the layer count beyond the first)
+        c2 = cfg2_measure(4, 30, 5, args.fmt, dev)
+        cfg2 = {"layers": 4, "ms_per_step": c2["ms_per_step"], "ms_per_layer": round(c2["ms_per_step"] / 4, 4),
+                "gbs": c2["value"], "tokens_per_s": c2["tokens_per_s"], "prefill_quantize": c2["prefill_quantize"],
+                "workload": c2["config"]["workload"]}
 
     # ---- N > 1: variant B of config 4 as well (sequence split + one NCCL
     # all-gather of the partials per layer + LSE merge), short: 2 layers at
@@ -959,6 +1082,8 @@ def main():
             line["ref_format"] = ref_fmt
         if offload is not None:
             line["offload_cfg3"] = offload
+        if cfg2 is not None:
+            line["long_context_cfg2"] = cfg2
         if cpu is not None:
             line["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cpu.items()
                                     if k in ("value", "unit", "cores", "kind", "sample")}
