@@ -167,6 +167,25 @@ constexpr int kDynSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in, st
 #define HKV_PIECE_STEPS 960
 #endif
 constexpr int64_t kPieceSteps = HKV_PIECE_STEPS;
+constexpr int64_t kDenseWeightPct = 100;  // a dense tile weighs its bytes
+// Schedule weights (HKV_SCHED_DENSE: percent of its bytes a dense tile weighs,
+// HKV_SCHED_PIECE: steps charged per segment start) can be overridden for sweeps.
+int64_t sched_dense_pct() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("HKV_SCHED_DENSE");
+    const int64_t x = e ? std::atoll(e) : kDenseWeightPct;
+    return x > 0 && x <= 400 ? x : kDenseWeightPct;
+  }();
+  return v;
+}
+int64_t sched_piece_steps() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("HKV_SCHED_PIECE");
+    const int64_t x = e ? std::atoll(e) : kPieceSteps;
+    return x >= 0 && x <= 16384 ? x : kPieceSteps;
+  }();
+  return v;
+}
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime (no link
 // dependency on libcuda).
@@ -270,11 +289,13 @@ hkv_status make_plan(int B, int Hq, int Hkv, const hkv_int4_store* body, const h
   if (sc.Tb + sc.Td == 0) sc.Td = 1;  // nothing to attend to: one empty tile yields zeros
   // tile weights in 128-byte steps (the kernel's schedule is 32-bit arithmetic)
   const int64_t tb = block_bytes(fmt, group) / hkv::kSchedStep;
-  const int64_t td = (int64_t)hkv::kTileD * 2 * HKV_D * 2 / hkv::kSchedStep;
+  // dense tiles weighted by their bytes times sched_dense_pct() / 100
+  const int64_t td = std::max<int64_t>(
+      1, (int64_t)hkv::kTileD * 2 * HKV_D * 2 / hkv::kSchedStep * sched_dense_pct() / 100);
   // a segment also costs its piece start and end (query rows, partial, merge):
   // charged as steps before it, so that CTAs whose range holds more segment
   // starts get fewer tiles
-  const int64_t wb = sc.Tb > 0 ? kPieceSteps : 0, wd = sc.Td > 0 ? kPieceSteps : 0;
+  const int64_t wb = sc.Tb > 0 ? sched_piece_steps() : 0, wd = sc.Td > 0 ? sched_piece_steps() : 0;
   const int64_t Ub = wb + sc.Tb * tb + wd + sc.Td * td;
   const int64_t Btot = Ub * sc.U;
   if (Btot >= (int64_t(1) << 31)) return HKV_ERR_UNSUPPORTED;  // > 256 GiB in one call
