@@ -160,14 +160,18 @@ hkv_status static_scratch(void** out) {
 
 // --------------------------------------------------------------------------- decode plan
 constexpr int kDynSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in, static barriers aside)
-// Schedule charge per segment start, in 128-byte steps: 120 KiB, about 6 fp16min
-// group-32 tiles (swept on config 1: 640-960 best within 0.3 %, 1,600 and 2,048
-// 1-2.5 % slower; overridable at build time for sweeps).
+// Schedule weights, fitted to per-CTA end times of a config-1 layer (globaltimer
+// probes in a copy of the kernel) and then swept on the 32-layer step: a dense
+// tile costs ~0.7 of an INT4 tile per byte, so it weighs 75 % of its bytes; a
+// segment start (piece start and end: query rows, partial, merge) is charged
+// 1,440 steps of 128 B (180 KiB, ~9 fp16min group-32 tiles). Config-1 step:
+// 2.522 ms with (100 %, 960) -> 2.489-2.492 ms; the region (70-85 %,
+// 1,440-1,760) is flat within 0.5 %.
 #ifndef HKV_PIECE_STEPS
-#define HKV_PIECE_STEPS 960
+#define HKV_PIECE_STEPS 1440
 #endif
 constexpr int64_t kPieceSteps = HKV_PIECE_STEPS;
-constexpr int64_t kDenseWeightPct = 100;  // a dense tile weighs its bytes
+constexpr int64_t kDenseWeightPct = 75;
 // Schedule weights (HKV_SCHED_DENSE: percent of its bytes a dense tile weighs,
 // HKV_SCHED_PIECE: steps charged per segment start) can be overridden for sweeps.
 int64_t sched_dense_pct() {

@@ -1036,9 +1036,11 @@ __device__ __forceinline__ void state_arrive_finish(const DecodeParams& p, int o
   if (lane == 0) *p.state_counter = 0;
 }
 
-// The append of unit u = (b, KV head h) for every u of this CTA (u = c, c + C,
-// ...), by one warp (lanes 0-15: K, 16-31: V, 8 dims a lane), on the state
-// before the step:
+// The append of unit u = (b, KV head h) for every unit whose last schedule step
+// lies in this CTA's range (the CTA that holds the unit's end: its dense
+// segment, whose tiles cost less per byte than INT4 tiles, so those CTAs have
+// time to spare), by one warp (lanes 0-15: K, 16-31: V, 8 dims a lane), on the
+// state before the step:
 //  * the ring row to evict (full ring), or the new token itself (no ring), is
 //    quantised into body slot body_len[b] exactly as the standalone append
 //    kernel does it, and the new token is written into the ring (or the next
@@ -1047,7 +1049,7 @@ __device__ __forceinline__ void state_arrive_finish(const DecodeParams& p, int o
 //    leaves out, the evicted token as dequantised and the new one, becomes the
 //    unit's extra partial (slot nb + nd, after the pipeline's), so the merged
 //    output is the attention over the cache after the append.
-// The warp that delivers a unit's last partial merges it, as the consumers do.
+// The unit's last pipeline piece merges it (see the consumers' end of piece).
 // Not inlined: its code stays out of the kernel's main body (inlined, the
 // launches of a 32-layer step measured ~2.5 us slower each).
 template <int FMT, int GROUP, typename DTy>
@@ -1056,7 +1058,11 @@ __device__ __noinline__ void append_units(const DecodeParams& p, int c, int* s_r
   const Sched& sc = p.sc;
   const int lane = threadIdx.x & 31, side = lane >> 4, pq = lane & 15;
   const int cap = p.dense.capacity, cap_r = cap - p.sink;
-  for (int u = c; u < sc.U; u += sc.C) {
+  const uint32_t x0 = cta_begin(sc, c), x1 = cta_begin(sc, c + 1);
+  for (int u = (int)(x0 / sc.Ub); u < sc.U; ++u) {
+    const uint32_t last = (uint32_t)(u + 1) * sc.Ub - 1u;  // the unit's last step
+    if (last < x0) continue;
+    if (last >= x1) break;
     const int b = u / p.Hkv, h = u - b * p.Hkv;
     const int dl = p.dense_len[b], head = p.ring_head[b], bl = p.body_len[b];
     const bool fill = dl < cap;                // a free row: nothing is evicted
