@@ -654,10 +654,12 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
             denses.append(None)
     q = torch.randn(layers, B, Hq, 128, device=dev, generator=gen).bfloat16()
     out = torch.empty(layers, B, Hq, 128, device=dev)
+    # one CUDA graph per step: partial -> NCCL all-gather -> in-place merge per layer
+    dec = seqsplit.SeqSplitDecoder([st if ntok else None for st in stores], denses, B, Hq, device=dev)
+    dec.capture(q, out)
 
     def step():
-        for l in range(layers):
-            seqsplit.decode(q[l], stores[l] if ntok else None, denses[l], out=out[l])
+        dec.replay()
 
     for _ in range(warmup):
         step()
@@ -683,12 +685,13 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
     step_bytes = layers * (B * Hkv * (body_pages * 256 * per_tok + (sink + recent) * 512) + B * Hq * 128 * 6)
     peak, _ = measured_peak()
     gbs = step_bytes / (ms * 1e-3) / 1e9
-    del stores, denses, q, out
+    dec.close()  # the graph holds NCCL calls: release it before the process group goes
+    del dec, stores, denses, q, out
     return {"ms_per_step": round(ms, 4), "gbs": round(gbs, 2), "tokens_per_s": round(B / (ms * 1e-3), 1),
             "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
             "workload": f"config4 B: Llama-3.1-8B shape, B{B}, ctx {ctx} ({body_pages} INT4 pages + 64 sink + "
                         f"1024 recent fp16 per unit), {layers} layers, sequence split over {world} GPU(s), one "
-                        f"NCCL all-gather of the partials per layer + LSE merge",
+                        f"NCCL all-gather of the partials per layer + LSE merge, one CUDA graph per step",
             "gpu_launches": world * steps * layers * 2}
 
 

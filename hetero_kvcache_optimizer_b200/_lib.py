@@ -87,6 +87,8 @@ SIGNATURES = {
                                        c_i32, c_f32, c_i32, c_vp, c_i32, c_i64, c_i64, c_vp]),
     "hkv_lse_merge": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i32, c_i64, c_i64,
                               c_vp]),
+    "hkv_lse_merge_strided": (c_i32, [c_vp, c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_i32, c_i64,
+                                      c_i64, c_vp]),
     "hkv_prefetcher_create": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_i64, ctypes.POINTER(c_vp)]),
     "hkv_prefetcher_destroy": (c_i32, [c_vp]),
     "hkv_prefetch_submit": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_vp, c_vp]),

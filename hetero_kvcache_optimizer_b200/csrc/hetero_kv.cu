@@ -958,17 +958,25 @@ hkv_status hkv_decode_attn_static(const void* q, int32_t q_dtype, int64_t q_stri
 hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B, int32_t Hq, int32_t D,
                          void* out, int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
                          hkv_stream_t stream) {
+  return hkv_lse_merge_strided(part_o, part_ml, n, (int64_t)B * Hq * HKV_D, (int64_t)B * Hq * 2, B, Hq, D, out,
+                               out_dtype, out_stride_b, out_stride_h, stream);
+}
+
+hkv_status hkv_lse_merge_strided(const float* part_o, const float* part_ml, int32_t n, int64_t split_o,
+                                 int64_t split_ml, int32_t B, int32_t Hq, int32_t D, void* out, int32_t out_dtype,
+                                 int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream) {
   if (!part_o || !part_ml || !out || n <= 0 || B <= 0 || Hq <= 0) return HKV_ERR_ARG;
   if (D != HKV_D) return HKV_ERR_UNSUPPORTED;
   if (out_dtype != HKV_DT_F16 && out_dtype != HKV_DT_BF16 && out_dtype != HKV_DT_F32) return HKV_ERR_ARG;
+  if (split_o < 0 || split_ml < 0) return HKV_ERR_ARG;
   hkv::MergeParams mp;
   std::memset(&mp, 0, sizeof(mp));
   mp.part_o = part_o;
   mp.part_ml = part_ml;
   mp.S = n;
   mp.Hq = Hq;
-  mp.split_o = (int64_t)B * Hq * HKV_D;
-  mp.split_ml = (int64_t)B * Hq * 2;
+  mp.split_o = split_o;
+  mp.split_ml = split_ml;
   mp.out = out;
   mp.out_dtype = out_dtype;
   mp.out_sb = out_stride_b;

@@ -10,11 +10,13 @@ NVLink.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+import ctypes
+from typing import List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from . import kvstore as kv
 
 
@@ -51,3 +53,69 @@ def decode(q: torch.Tensor, store: Optional[kv.Int4KVStore], dense: Optional[kv.
     o, ml = kv.decode_partial(q, store, dense, sm_scale=sm_scale)
     parts_o, parts_ml = all_gather_partials(o, ml, group)
     return kv.lse_merge(parts_o, parts_ml, out_dtype=out_dtype, out=out)
+
+
+class SeqSplitDecoder:
+    """The sequence-split decode of a multi-layer step without host work per
+    layer: every layer's partial is written straight into its all-gather send
+    buffer ([o | (m, l)] of B*Hq*130 floats), one NCCL ``all_gather_into_tensor``
+    per layer gathers the ranks' buffers, and ``hkv_lse_merge_strided`` merges
+    from the gathered buffer in place (no concatenation, no copy). ``capture``
+    records the whole step, NCCL calls included, as one CUDA graph; ``close``
+    releases it (before the process group is destroyed)."""
+
+    def __init__(self, stores: List[Optional[kv.Int4KVStore]], denses: List[Optional[kv.DenseKV]],
+                 batch: int, q_heads: int, group: Optional[dist.ProcessGroup] = None,
+                 device: Optional[torch.device] = None):
+        if len(stores) != len(denses) or not stores:
+            raise ValueError("one (store, dense) pair per layer")
+        self.stores, self.denses = stores, denses
+        self.L, self.B, self.Hq = len(stores), batch, q_heads
+        self.group = group
+        self.n = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.F = batch * q_heads * (kv.HEAD_DIM + 2)
+        self.send = torch.empty(self.L, self.F, dtype=torch.float32, device=self.device)
+        self.recv = (torch.empty(self.L, self.n * self.F, dtype=torch.float32, device=self.device)
+                     if self.n > 1 else self.send)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    def _layer(self, l: int, q: torch.Tensor, out: torch.Tensor) -> None:
+        B, Hq, D = self.B, self.Hq, kv.HEAD_DIM
+        o = self.send[l, :B * Hq * D].view(B, Hq, D)
+        ml = self.send[l, B * Hq * D:].view(B, Hq, 2)
+        kv.decode_partial(q, self.stores[l], self.denses[l], out_o=o, out_ml=ml)
+        if self.n > 1:
+            dist.all_gather_into_tensor(self.recv[l], self.send[l], group=self.group)
+        src = self.recv[l]
+        L.check(L.load().hkv_lse_merge_strided(
+            src.data_ptr(), src.data_ptr() + B * Hq * D * 4, self.n, self.F, self.F, B, Hq, D, out.data_ptr(),
+            kv.dtype_code(out.dtype), out.stride(0), out.stride(1),
+            ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)), "hkv_lse_merge_strided")
+
+    def step(self, q: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """q [L, B, Hq, 128] -> out [L, B, Hq, 128] (every rank gets the full output)."""
+        for l in range(self.L):
+            self._layer(l, q[l], out[l])
+        return out
+
+    def capture(self, q: torch.Tensor, out: torch.Tensor) -> None:
+        """Record ``step(q, out)`` over these static buffers as one CUDA graph
+        (run once eagerly first: NCCL's communicator and the decode workspace of
+        the capture stream come up outside the capture)."""
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step(q, out)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.step(q, out)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.graph = g
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def close(self) -> None:
+        self.graph = None

@@ -359,6 +359,14 @@ hkv_status hkv_decode_attn_static(const void* q, int32_t q_dtype, int64_t q_stri
 hkv_status hkv_lse_merge(const float* part_o, const float* part_ml, int32_t n, int32_t B,
                          int32_t Hq, int32_t D, void* out, int32_t out_dtype,
                          int64_t out_stride_b, int64_t out_stride_h, hkv_stream_t stream);
+/* hkv_lse_merge over partial sets spaced split_o / split_ml floats apart (partial
+ * set s of row (b, hq) at part_o + s*split_o + (b*Hq + hq)*128 and part_ml +
+ * s*split_ml + (b*Hq + hq)*2): merges straight from an all-gather buffer that
+ * holds every rank's o and (m, l) side by side, with no copy. */
+hkv_status hkv_lse_merge_strided(const float* part_o, const float* part_ml, int32_t n, int64_t split_o,
+                                 int64_t split_ml, int32_t B, int32_t Hq, int32_t D, void* out,
+                                 int32_t out_dtype, int64_t out_stride_b, int64_t out_stride_h,
+                                 hkv_stream_t stream);
 
 /* ---------------------------------------------------------------- 3. prefetch
  * A prefetcher moves whole pages from a caller-owned pinned host pool to a
