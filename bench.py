@@ -621,10 +621,11 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
                      dev) -> dict:
     """Config 4 variant B on this process group: Llama-3.1-8B shape, B sequences
     of `ctx` tokens, each sequence's INT4 body split in contiguous page-aligned
-    slices over the ranks (the last rank also holds the 64 sink + 1024 recent
-    fp16 tokens); per layer: partial attention on every rank, one all-gather of
-    the partials, LSE merge. Returns the max-over-ranks step time and the
-    aggregate figures (every rank gets the same dict)."""
+    slices over the ranks and its 64 sink + 1024 recent fp16 rows split in
+    contiguous row slices (attention does not depend on the order of the keys,
+    so any rank may hold any rows); per layer: partial attention on every rank,
+    one all-gather of the partials, LSE merge. Returns the max-over-ranks step
+    time and the aggregate figures (every rank gets the same dict)."""
     import torch
     import torch.distributed as dist
     from hetero_kvcache_optimizer_b200 import _lib, kvstore as kv, seqsplit
@@ -633,6 +634,8 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
     body_pages = (ctx - sink - recent) // 256
     p0, p1 = seqsplit.shard_range(body_pages, world, rank)
     ntok = (p1 - p0) * 256
+    r0, r1 = seqsplit.shard_range(sink + recent, world, rank)  # this rank's dense rows
+    nrows = r1 - r0
     gen = torch.Generator(device=dev).manual_seed(40 + rank)
     stores, denses = [], []
     for l in range(layers):
@@ -644,11 +647,11 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
             kv.quantize_pack(x, st, 1, t0)
         st.set_lengths(ntok)
         stores.append(st)
-        if rank == world - 1:
-            d = kv.DenseKV(B, Hkv, sink + recent, device=dev)
+        if nrows:
+            d = kv.DenseKV(B, Hkv, nrows, device=dev)
             d.k.normal_(generator=gen)
             d.v.normal_(generator=gen)
-            d.set_lengths(sink + recent)
+            d.set_lengths(nrows)
             denses.append(d)
         else:
             denses.append(None)
@@ -690,7 +693,8 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
     return {"ms_per_step": round(ms, 4), "gbs": round(gbs, 2), "tokens_per_s": round(B / (ms * 1e-3), 1),
             "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
             "workload": f"config4 B: Llama-3.1-8B shape, B{B}, ctx {ctx} ({body_pages} INT4 pages + 64 sink + "
-                        f"1024 recent fp16 per unit), {layers} layers, sequence split over {world} GPU(s), one "
+                        f"1024 recent fp16 rows per unit, both split over the ranks), "
+                        f"{layers} layers, sequence split over {world} GPU(s), one "
                         f"NCCL all-gather of the partials per layer + LSE merge, one CUDA graph per step",
             "gpu_launches": world * steps * layers * 2}
 

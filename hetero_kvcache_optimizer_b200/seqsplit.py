@@ -1,7 +1,8 @@
 """Sequence-split decode attention across GPUs (config 4, variant B).
 
 Every rank holds a contiguous, page-aligned slice of each sequence's INT4 body
-(the last rank also holds the fp16/bf16 sink + recent segment), computes the
+and any share of its fp16/bf16 sink + recent rows (attention does not depend on
+the order of the keys, so ``shard_range`` over the rows balances them too), computes the
 un-normalised partial (o, m, l) of the attention over its slice with
 ``hkv_decode_attn_partial``, and one NCCL all-gather of those partials
 (B*Hq*130 floats per rank) feeds ``hkv_lse_merge``, which every rank runs to get
