@@ -205,7 +205,7 @@ def layer_bytes(batch, body_tokens, fmt, kv_heads=8, q_heads=32, sink=64, recent
 
 
 # --------------------------------------------------------------------------- config 2
-def cfg2_measure(layers: int, steps: int, warmup: int, fmt: str, dev, fused: bool = True,
+def cfg2_measure(layers: int, steps: int, warmup: int, fmt: str, dev, fused: Optional[bool] = None,
                  early: Optional[bool] = None) -> dict:
     """Qwen2-VL-7B-shaped long multimodal decode: 28 layers, B1, Hq28/Hkv4 (GQA 7),
     131,072-token context (positions < 100,000 'vision' K/V ~ N(0, 0.5^2), the rest
@@ -312,7 +312,8 @@ def run_cfg2(args) -> None:
     import torch
     torch.cuda.set_device(0)
     print(json.dumps(cfg2_measure(args.layers, args.steps, args.warmup, args.fmt, torch.device("cuda", 0),
-                                  fused=not args.no_fused, early=False if args.no_early else None)))
+                                  fused=False if args.no_fused else None,
+                                  early=False if args.no_early else None)))
 
 
 # --------------------------------------------------------------------------- prefill
@@ -570,10 +571,12 @@ def run_cfg3(args) -> None:
 
 # --------------------------------------------------------------------------- ref format
 def ref_format_measure(args, dev, peak: float, layers: int = 4, steps: int = 20, warmup: int = 5) -> dict:
-    """The fused decode step of config 1 in the reference-bit-exact format (codes,
+    """The decode step of config 1 in the reference-bit-exact format (codes,
     fp32 scales and u8 zero-points equal to KVCompressor.compress; the decode
-    kernel expands the metadata in shared memory): per-launch time and GB/s over
-    a graph of `layers` launches, CUDA events on the replaying stream."""
+    kernel expands the metadata in shared memory), as the engine runs it for
+    that format (two launches per layer: append, then attention): time per
+    layer and GB/s over a graph of `layers` layers, CUDA events on the
+    replaying stream."""
     import torch
     from hetero_kvcache_optimizer_b200 import kvstore as kv
     from hetero_kvcache_optimizer_b200.decode_engine import TieredKVDecoder
@@ -611,8 +614,9 @@ def ref_format_measure(args, dev, peak: float, layers: int = 4, steps: int = 20,
     nbytes = sum(eng.step_bytes(body0 + i) for i in range(steps)) / (steps * layers)
     gbs = nbytes / (us * 1e-6) / 1e9
     del eng
-    return {"kernel": "decode_kernel<APPEND>, HKV_FMT_REF group 32 (168 B per token)", "layers_timed": layers,
-            "us_per_launch": round(us, 2), "bytes_per_launch": round(nbytes), "achieved": round(gbs, 1),
+    return {"kernel": "append_kv_kernel + decode_kernel, HKV_FMT_REF group 32 (168 B per token), two launches "
+                      "per layer", "layers_timed": layers,
+            "us_per_layer": round(us, 2), "bytes_per_layer": round(nbytes), "achieved": round(gbs, 1),
             "frac": round(gbs / peak, 4), "unit": "GB/s"}
 
 
@@ -895,7 +899,8 @@ def main():
     eng = TieredKVDecoder(args.layers, c["batch"], c["q_heads"], c["kv_heads"], sink=c["sink"],
                           recent=c["recent"], body_capacity=body + total_steps + 8, fmt=args.fmt,
                           group=c["group"], kv_dtype=torch.float16, out_dtype=torch.float32, device=dev,
-                          ctas=args.ctas, fused_append=not args.no_fused, early=False if args.no_early else None)
+                          ctas=args.ctas, fused_append=False if args.no_fused else None,
+                          early=False if args.no_early else None)
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
     B, Hkv = c["batch"], c["kv_heads"]
     for l in range(args.layers):
@@ -1023,7 +1028,7 @@ def main():
     # per token) on the same decode step: 4 layers of config 1 (the per-launch
     # figures do not depend on the layer count), one rank, after the main line
     ref_fmt = None
-    if world == 1 and args.fmt != "ref" and eng.fused_append:
+    if world == 1 and args.fmt != "ref":
         ref_fmt = ref_format_measure(args, dev, peak)
 
     # ---- config 3 in short (4 of its 32 layers, one rank): exposed host->device
