@@ -6,12 +6,16 @@ Default workload (benchmark spec configuration 1, Llama-3.1-8B-shaped decode):
 per sequence: 64 sink + 1024 recent tokens in fp16, 31,680 INT4 tokens
 (group 32, fp16 scale + fp16 zero = min). One step = for every layer, one fused
 launch: append the new token (ring eviction -> INT4 quantise) + split-KV decode
-attention over the whole context + LSE merge (--no-fused: two launches). Synthetic seeded data (K/V ~ N(0,1) with four x10
+attention over the whole context + LSE merge (--no-fused, and the default for
+--fmt ref: two launches). Synthetic seeded data (K/V ~ N(0,1) with four x10
 outlier K channels per head, bf16 queries); the per-step working set (12 GB)
-is far larger than L2, so no flush is needed between steps.
+is far larger than L2, so no flush is needed between steps. The 1-GPU line
+also carries short config-2, config-3 and ref-format measurements.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload cfg2                       # config 2: long multimodal context
   python bench.py --workload cfg3 [--window PAGES [--delta D]] [--sweep]   # config 3: tiered offload
+  python bench.py --workload cfg4 | cfg4b               # config 4: B64 context sweep / sequence split
   python bench.py --workload prefill [--sq N]          # multi-query attention over the INT4 body
 
 With N > 1 (torchrun, one rank per GPU) every rank decodes its own 8
