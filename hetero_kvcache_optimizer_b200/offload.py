@@ -468,6 +468,8 @@ class SlidingWindowOffload:
 
     def replay(self, transfer: bool = True) -> None:
         """One captured step (``capture``) on the current stream."""
+        if self._graphs is None:
+            raise RuntimeError("SlidingWindowOffload.replay: call capture() first")
         if self.ready[0] is not None:  # layer 0's pages of an eager prefetch
             torch.cuda.current_stream(self.device).wait_event(self.ready[0])
             self.ready[0] = None

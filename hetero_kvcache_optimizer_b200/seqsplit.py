@@ -116,6 +116,8 @@ class SeqSplitDecoder:
         self.graph = g
 
     def replay(self) -> None:
+        if self.graph is None:
+            raise RuntimeError("SeqSplitDecoder.replay: call capture() first (or it was closed)")
         self.graph.replay()
 
     def close(self) -> None:
