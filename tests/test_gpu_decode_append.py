@@ -219,3 +219,19 @@ def test_fused_rejects_mismatched_state_arrays(hkv):
                                     128, 0.088, 0, ws.data_ptr(), ws.numel(), out.data_ptr(), L.DT_F32,
                                     out.stride(0), out.stride(1), 0, None)
     assert rc == L.HKV_ERR_ARG
+
+
+def test_fused_refuses_more_ctas_than_sms(hkv):
+    """A unit's last pipeline piece waits for the append job of another CTA, so
+    every CTA must be resident at once: a grid larger than the SM count is
+    refused before anything is launched, and the cache is left untouched."""
+    store, dense = _cache(hkv, 7, 1, 2, 128, 8, 8, [16], "fp16min", 32, torch.float16)
+    before = (store.pool.clone(), dense.k.clone(), store.lengths.clone(), dense.lengths.clone())
+    q = torch.zeros(1, 8, 128, dtype=torch.float16, device="cuda")
+    kn = torch.zeros(1, 2, 128, dtype=torch.float16, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    with pytest.raises(RuntimeError, match="ARG"):
+        hkv.decode_append(q, kn, kn, dense, 8, store, ctas=sms + 1)
+    torch.cuda.synchronize()
+    after = (store.pool, dense.k, store.lengths, dense.lengths)
+    assert all(torch.equal(a, b) for a, b in zip(before, after))
