@@ -43,14 +43,16 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // the kernel may start while the previous kernel in the stream finishes, and
 // waits for it (griddep_wait) before its first global access. Used for the
 // decode kernel (its barrier setup then overlaps the tail of the kernel before
-// it: 2.586 -> 2.561 ms per config-1 step); the append kernel, whose blocks
-// would wait resident beside the decode kernel's, measured slower with it
-// (2.608 ms) and launches normally. HKV_PDL (bit mask: 1 decode, 2 append;
-// default 1) overrides this for experiments.
+// it: 2.586 -> 2.561 ms per config-1 step) and for the quantise-pack kernel
+// (a chunked prefill's launches overlap their start with the previous one's
+// drain: 4.82 -> 4.68 ms for config 2's 896 chunk launches); the append kernel,
+// whose blocks would wait resident beside the decode kernel's, measured slower
+// with it (2.608 ms) and launches normally. HKV_PDL (bit mask: 1 decode,
+// 2 append, 4 quantise-pack; default 5) overrides this for experiments.
 bool pdl_enabled(int which) {
   static const int mask = [] {
     const char* e = std::getenv("HKV_PDL");
-    return e ? std::atoi(e) : 1;
+    return e ? std::atoi(e) : 5;
   }();
   return (mask & which) != 0;
 }
@@ -663,10 +665,11 @@ hkv_status quantize_pack_launch(const void* x, const void* x2, int32_t dtype, in
   const dim3 grid((unsigned)(tiles * B * H), x2 ? 2u : 1u);
   const bool ref = dst->format == HKV_FMT_REF;
   const int g = dst->group;
-#define HKV_QP_LAUNCH(TY, FMT, G)                                                                              \
-  hkv::quantize_pack_kernel<TY, FMT, G><<<grid, 256, 0, st>>>(static_cast<const TY*>(x), static_cast<const TY*>(x2), \
-                                                              H, T, tiles, stride_b, stride_h, stride_t, role, *dst, \
-                                                              dst_start, start)
+  cudaError_t qerr = cudaSuccess;
+#define HKV_QP_LAUNCH(TY, FMT, G)                                                                            \
+  qerr = launch_pdl(4, hkv::quantize_pack_kernel<TY, FMT, G>, grid, dim3(256), 0, st, static_cast<const TY*>(x), \
+                    static_cast<const TY*>(x2), (int)H, (int)T, tiles, stride_b, stride_h, stride_t, (int)role, *dst, \
+                    dst_start, (int)start)
 #define HKV_QP_GROUPS(TY, FMT)        \
   if (g == 32) HKV_QP_LAUNCH(TY, FMT, 32);      \
   else if (g == 64) HKV_QP_LAUNCH(TY, FMT, 64); \
@@ -680,6 +683,7 @@ hkv_status quantize_pack_launch(const void* x, const void* x2, int32_t dtype, in
   }
 #undef HKV_QP_GROUPS
 #undef HKV_QP_LAUNCH
+  if (qerr != cudaSuccess) return cuda_fail(qerr);
   return launch_status();
 }
 }  // namespace

@@ -194,6 +194,11 @@ __global__ void __launch_bounds__(256) quantize_pack_kernel(const T* __restrict_
   using T2 = typename Vec2<T>::type;
   constexpr int kLanesPerGroup = GROUP / 32;  // 1, 2 or 4
   constexpr int ng = HKV_D / GROUP;
+  // Launched with programmatic stream serialization (when enabled): the next
+  // launch on the stream may start its blocks as this one's drain, and this one
+  // waits for the launch before it before touching global memory.
+  griddep_launch_dependents();
+  griddep_wait();
   // blockIdx.y 0: x as side `role`; 1: x2 as V
   const T* __restrict__ src = blockIdx.y ? x2 : x;
   if (blockIdx.y) role = HKV_ROLE_V;
