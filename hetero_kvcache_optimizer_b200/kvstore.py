@@ -240,7 +240,9 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
     """Decode attention of q [B, Hq, 128] (or [B, Hq, 1, 128]) over the INT4
     body and/or the dense segment. Returns [B, Hq, 128] in ``out_dtype``.
     ``ctas`` sets the persistent grid (0: one CTA per SM); ``body_len`` /
-    ``dense_len`` override the host-side length hints that size the schedule."""
+    ``dense_len`` override the host-side length hints that size the schedule.
+    More than 8 query heads per KV head (the kernel's limit) run as several
+    launches over groups of at most 8 of them, each reading the cache again."""
     _require_cuda(q)
     squeeze = q.dim() == 4
     if squeeze:
@@ -251,6 +253,19 @@ def decode(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseK
         sm_scale = 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty(B, Hq, D, dtype=out_dtype, device=q.device)
+    G = Hq // Hkv if Hkv else 0
+    if G > 8 and Hq % Hkv == 0:
+        # heads [k*gs, (k+1)*gs) of every KV head's group, as a [B, Hkv*gs, D] copy
+        gs = max(d for d in range(1, 9) if G % d == 0)
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
+            qg = q.reshape(B, Hkv, G // gs, gs, D)
+            og = torch.empty(B, Hkv, G // gs, gs, D, dtype=out.dtype, device=q.device)
+            for k in range(G // gs):
+                part = decode(qg[:, :, k].reshape(B, Hkv * gs, D), store, dense, sm_scale, out.dtype, ctas,
+                              None, body_len, dense_len)
+                og[:, :, k] = part.view(B, Hkv, gs, D)
+            out.copy_(og.view(B, Hq, D))
+        return out[:, :, None, :] if squeeze else out
     st = store.struct(body_len) if store is not None else None
     ds = dense.struct(dense_len) if dense is not None else None
     pst = ctypes.byref(st) if st is not None else None

@@ -92,6 +92,26 @@ def test_formats_gqa_vs_oracle(hkv, fmt, group, G):
         assert ko.rel_err(out, qref) < TOL, (qdt, fmt, group, G)
 
 
+@pytest.mark.parametrize("G", [12, 16, 28])
+def test_many_query_heads_per_kv_head(hkv, G):
+    """More query heads per KV head than the kernel's 8: decode runs groups of at
+    most 8 of them (12 -> 6 + 6, 16 -> 8 + 8, 28 -> 7 x 4) and matches the
+    oracle, with an INT4 body and a dense segment."""
+    B, Hkv, S, ND = 2, 2, 300, 40
+    k, v = ko.make_kv(200 + G, B, Hkv, S + ND)
+    store = _body_store(hkv, k[:, :, :S], v[:, :, :S], fmt="fp16min", group=32)
+    dense = hkv.DenseKV(B, Hkv, ND)
+    dense.k.copy_(t16(k[:, :, S:]))
+    dense.v.copy_(t16(v[:, :, S:]))
+    dense.set_lengths(ND)
+    q = ko.make_q(200 + G, B, Hkv * G).astype(np.float16).astype(np.float32)
+    kd = np.concatenate([dequant_side(store, K, S), k[:, :, S:].astype(np.float16).astype(np.float32)], axis=2)
+    vd = np.concatenate([dequant_side(store, V, S), v[:, :, S:].astype(np.float16).astype(np.float32)], axis=2)
+    ref = ko.decode_attention(q, kd, vd)
+    out = hkv.decode(t16(q), store, dense).cpu().numpy()
+    assert ko.rel_err(out, ref) < TOL, G
+
+
 @pytest.mark.parametrize("S", [1, 2, 15, 16, 17, 127, 128, 129, 255, 1000])
 def test_ragged_lengths_and_odd_sizes(hkv, S):
     """Per-sequence device lengths; tails of every residue mod the tile size."""
