@@ -33,7 +33,12 @@ class TieredKVDecoder:
                  kv_dtype: torch.dtype = torch.float16, out_dtype: torch.dtype = torch.float32,
                  device="cuda", ctas: int = 0, fused_append: Optional[bool] = None,
                  early: Optional[bool] = None):
-        self.fused_append = (fmt != "ref") if fused_append is None else fused_append
+        # the fused launch takes at most 8 query heads per KV head; more run as
+        # the two launches (the attention split in groups of at most 8)
+        fused_ok = q_heads // kv_heads <= 8
+        self.fused_append = (fmt != "ref" and fused_ok) if fused_append is None else fused_append
+        if self.fused_append and not fused_ok:
+            raise ValueError("fused_append needs at most 8 query heads per KV head")
         self.early = early
         self.num_layers, self.batch = num_layers, batch
         self.q_heads, self.kv_heads = q_heads, kv_heads

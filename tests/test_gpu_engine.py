@@ -105,3 +105,37 @@ def test_pipelined_host_step_matches_graph():
         torch.cuda.synchronize()
         assert torch.equal(out_s.cpu(), ho), step
         assert a.body_len == b.body_len
+
+
+def test_engine_many_query_heads_per_kv_head():
+    """16 query heads per KV head: the engine runs the two launches (append, then
+    the attention in groups of 8 heads), eager and replayed, against the oracle."""
+    from hetero_kvcache_optimizer_b200.decode_engine import TieredKVDecoder
+    L_, B, Hq, Hkv, S = 2, 2, 32, 2, 300
+    rng = np.random.default_rng(13)
+    engs = []
+    for _ in range(2):
+        eng = TieredKVDecoder(L_, B, Hq, Hkv, sink=16, recent=64, body_capacity=1024, fmt="fp16min", group=32)
+        assert not eng.fused_append
+        k, v = ko.make_kv(9, B, Hkv, S)
+        for l in range(L_):
+            eng.prefill_layer(l, t16(k), t16(v))
+        engs.append(eng)
+    eager, graph = engs
+    graph.capture(max_steps=3)
+    q_s, kn_s, vn_s, out_s = graph.static_buffers
+    for step in range(2):
+        q = torch.from_numpy(rng.standard_normal((L_, B, Hq, 128)).astype(np.float32)).cuda().bfloat16()
+        kn = torch.from_numpy(rng.standard_normal((L_, B, Hkv, 128)).astype(np.float32)).cuda().half()
+        vn = torch.from_numpy(rng.standard_normal((L_, B, Hkv, 128)).astype(np.float32)).cuda().half()
+        out_e = eager.step(q, kn, vn).cpu().numpy()
+        q_s.copy_(q)
+        kn_s.copy_(kn)
+        vn_s.copy_(vn)
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = _oracle_step(eager, q)
+        assert ko.rel_err(out_e, ref) < TOL, step
+        assert ko.rel_err(out_s.cpu().numpy(), ref) < TOL, step
+    with pytest.raises(ValueError):
+        TieredKVDecoder(1, B, Hq, Hkv, sink=16, recent=64, body_capacity=1024, fused_append=True)
