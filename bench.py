@@ -934,7 +934,7 @@ def main():
     if world > 1:
         dist.barrier()
     body0 = eng.body_len
-    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else dev.index)
+    sampler = ClockSampler(dev.index, 50)
     sampler.start()
     time.sleep(0.3)
     st = torch.cuda.current_stream()
