@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--sq", type=int, default=2048, help="prefill: query positions per sequence")
     ap.add_argument("--ctx", type=int, default=131072, help="cfg4b: context per sequence")
     ap.add_argument("--batch", type=int, default=64, help="cfg4b: sequences")
+    ap.add_argument("--seq-chunks", type=int, default=1,
+                    help="cfg4b: pipelined batch slices per layer (all-gather of one overlaps the next's partial)")
     ap.add_argument("--window", type=int, default=0,
                     help="cfg3: cold pages copied and attended per unit and layer (0 = all of them)")
     ap.add_argument("--delta", type=int, default=-1,
@@ -626,13 +628,14 @@ def ref_format_measure(args, dev, peak: float, layers: int = 4, steps: int = 20,
 
 # --------------------------------------------------------------------------- config 4, variant B
 def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt: str, world: int, rank: int,
-                     dev) -> dict:
+                     dev, chunks: int = 1) -> dict:
     """Config 4 variant B on this process group: Llama-3.1-8B shape, B sequences
-    of `ctx` tokens, each sequence's INT4 body split in contiguous page-aligned
-    slices over the ranks and its 64 sink + 1024 recent fp16 rows split in
-    contiguous row slices (attention does not depend on the order of the keys,
-    so any rank may hold any rows); per layer: partial attention on every rank,
-    one all-gather of the partials, LSE merge. Returns the max-over-ranks step
+    of `ctx` tokens; each unit's byte line [INT4 body pages | 64 sink + 1024
+    recent fp16 rows] cut into equal contiguous spans, one per rank
+    (``seqsplit.shard_spans``: attention does not depend on the order of the
+    keys, so any rank may hold any rows, and most ranks hold one segment); per
+    layer: partial attention on every rank, one all-gather of the partials, LSE
+    merge, in ``chunks`` pipelined batch slices. Returns the max-over-ranks step
     time and the aggregate figures (every rank gets the same dict)."""
     import torch
     import torch.distributed as dist
@@ -640,9 +643,9 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
     Hq, Hkv = 32, 8
     sink, recent = 64, 1024
     body_pages = (ctx - sink - recent) // 256
-    p0, p1 = seqsplit.shard_range(body_pages, world, rank)
+    (p0, p1), (r0, r1) = seqsplit.shard_spans(body_pages, sink + recent, world, rank,
+                                              kv.page_bytes(fmt, 32, 256), 2 * 128 * 2)
     ntok = (p1 - p0) * 256
-    r0, r1 = seqsplit.shard_range(sink + recent, world, rank)  # this rank's dense rows
     nrows = r1 - r0
     gen = torch.Generator(device=dev).manual_seed(40 + rank)
     stores, denses = [], []
@@ -666,7 +669,8 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
     q = torch.randn(layers, B, Hq, 128, device=dev, generator=gen).bfloat16()
     out = torch.empty(layers, B, Hq, 128, device=dev)
     # one CUDA graph per step: partial -> NCCL all-gather -> in-place merge per layer
-    dec = seqsplit.SeqSplitDecoder([st if ntok else None for st in stores], denses, B, Hq, device=dev)
+    dec = seqsplit.SeqSplitDecoder([st if ntok else None for st in stores], denses, B, Hq, device=dev,
+                                   chunks=chunks)
     dec.capture(q, out)
 
     def step():
@@ -701,10 +705,11 @@ def seqsplit_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt
     return {"ms_per_step": round(ms, 4), "gbs": round(gbs, 2), "tokens_per_s": round(B / (ms * 1e-3), 1),
             "pct_of_aggregate_measured_peak": round(100 * gbs / (world * peak), 2),
             "workload": f"config4 B: Llama-3.1-8B shape, B{B}, ctx {ctx} ({body_pages} INT4 pages + 64 sink + "
-                        f"1024 recent fp16 rows per unit, both split over the ranks), "
+                        f"1024 recent fp16 rows per unit, byte-balanced spans over the ranks), "
                         f"{layers} layers, sequence split over {world} GPU(s), one "
-                        f"NCCL all-gather of the partials per layer + LSE merge, one CUDA graph per step",
-            "gpu_launches": world * steps * layers * 2}
+                        f"NCCL all-gather of the partials per layer and batch slice + LSE merge, "
+                        f"{chunks} pipelined batch slice(s), one CUDA graph per step",
+            "chunks": chunks, "gpu_launches": world * steps * layers * 2 * chunks}
 
 
 def batchshard_measure(B: int, ctx: int, layers: int, steps: int, warmup: int, fmt: str, world: int, rank: int,
@@ -792,7 +797,11 @@ def run_cfg4(args, world: int, rank: int, local: int) -> None:
     for ctx in (4096, 16384, 65536, 131072):
         a = batchshard_measure(args.batch, ctx, 2, args.steps, args.warmup, args.fmt, world, rank, dev)
         b = seqsplit_measure(args.batch, ctx, 2, args.steps, args.warmup, args.fmt, world, rank, dev)
-        rows.append({"ctx": ctx, "variant_a": a, "variant_b": {k: v for k, v in b.items() if k != "workload"}})
+        row = {"ctx": ctx, "variant_a": a, "variant_b": {k: v for k, v in b.items() if k != "workload"}}
+        if world > 1:  # the same step pipelined over two batch slices (gathers overlap partials)
+            b2 = seqsplit_measure(args.batch, ctx, 2, args.steps, args.warmup, args.fmt, world, rank, dev, chunks=2)
+            row["variant_b_pipelined"] = {k: v for k, v in b2.items() if k != "workload"}
+        rows.append(row)
     if rank == 0:
         top = rows[-1]["variant_a"]
         print(json.dumps({
@@ -807,6 +816,7 @@ def run_cfg4(args, world: int, rank: int, local: int) -> None:
                                    "value = variant A at 131072", "kv_format": args.fmt,
                        "parallelism": f"A: shard{world} / B: seqsplit{world}"},
             "sweep": rows, "gpu_launches": sum(r["variant_a"]["gpu_launches"] + r["variant_b"]["gpu_launches"]
+                                               + r.get("variant_b_pipelined", {}).get("gpu_launches", 0)
                                                for r in rows)}))
     if world > 1:
         dist.barrier()
@@ -822,7 +832,8 @@ def run_cfg4b(args, world: int, rank: int, local: int) -> None:
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    r = seqsplit_measure(args.batch, args.ctx, args.layers, args.steps, args.warmup, args.fmt, world, rank, dev)
+    r = seqsplit_measure(args.batch, args.ctx, args.layers, args.steps, args.warmup, args.fmt, world, rank, dev,
+                         chunks=args.seq_chunks)
     if rank == 0:
         print(json.dumps({
             "metric": "config4 variant B: sequence-split INT4 decode attention, aggregate HBM GB/s and tokens/s",

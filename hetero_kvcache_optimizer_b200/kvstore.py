@@ -83,18 +83,28 @@ class Int4KVStore:
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=self.device)
         self.len_hint = 0  # host-side upper bound of lengths (sizes the split-KV grid)
 
-    def struct(self, len_hint: Optional[int] = None) -> L.HkvInt4Store:
+    def struct(self, len_hint: Optional[int] = None, b0: int = 0) -> L.HkvInt4Store:
+        """The C view of this store; ``b0`` > 0 views sequences [b0, batch)
+        only (a launch over a batch slice starting at sequence b0)."""
+        if not 0 <= b0 < self.batch:
+            raise ValueError(f"b0={b0} outside the batch of {self.batch}")
+        skip = b0 * self.kv_heads * self.max_pages  # page slots of the skipped units
         s = L.HkvInt4Store()
-        s.pages = self.pool.data_ptr()
-        s.page_stride = self.page_bytes
         s.format = FORMATS[self.fmt]
         s.group = self.group
         s.page_tokens = self.page_tokens
         s.max_pages = self.max_pages
-        s.page_table = self.page_table.data_ptr() if self.paged else None
-        s.lengths = self.lengths.data_ptr()
+        if self.paged:
+            s.pages = self.pool.data_ptr()
+            s.page_table = self.page_table.data_ptr() + skip * 4
+            s.num_pages = self.num_pages
+        else:
+            s.pages = self.pool.data_ptr() + skip * self.page_bytes
+            s.page_table = None
+            s.num_pages = self.num_pages - skip
+        s.page_stride = self.page_bytes
+        s.lengths = self.lengths.data_ptr() + b0 * 4
         s.len = int(self.len_hint if len_hint is None else len_hint)
-        s.num_pages = self.num_pages
         return s
 
     def set_lengths(self, n: Union[int, torch.Tensor]) -> None:
@@ -122,14 +132,18 @@ class DenseKV:
         self.ring_head = torch.zeros(batch, dtype=torch.int32, device=self.k.device)
         self.len_hint = 0
 
-    def struct(self, len_hint: Optional[int] = None) -> L.HkvDenseKV:
+    def struct(self, len_hint: Optional[int] = None, b0: int = 0) -> L.HkvDenseKV:
+        """The C view of this segment; ``b0`` > 0 views sequences [b0, batch)."""
+        if not 0 <= b0 < self.batch:
+            raise ValueError(f"b0={b0} outside the batch of {self.batch}")
+        es = self.k.element_size()
         d = L.HkvDenseKV()
-        d.k = self.k.data_ptr()
-        d.v = self.v.data_ptr()
+        d.k = self.k.data_ptr() + b0 * self.k.stride(0) * es
+        d.v = self.v.data_ptr() + b0 * self.v.stride(0) * es
         d.dtype = dtype_code(self.dtype)
         d.capacity = self.capacity
         d.stride_b, d.stride_h, d.stride_t = self.k.stride(0), self.k.stride(1), self.k.stride(2)
-        d.lengths = self.lengths.data_ptr()
+        d.lengths = self.lengths.data_ptr() + b0 * 4
         d.len = int(self.len_hint if len_hint is None else len_hint)
         return d
 
@@ -451,20 +465,24 @@ def decode_plan(store: Optional[Int4KVStore], dense: Optional[DenseKV], batch: i
 def decode_partial(q: torch.Tensor, store: Optional[Int4KVStore], dense: Optional[DenseKV],
                    sm_scale: Optional[float] = None, ctas: int = 0,
                    out_o: Optional[torch.Tensor] = None, out_ml: Optional[torch.Tensor] = None,
-                   stream=None) -> Tuple[torch.Tensor, torch.Tensor]:
+                   stream=None, b0: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
     """Un-normalised partial (o [B,Hq,128], (m, l) [B,Hq,2], base-2 logits) of the
-    attention over this GPU's share of the context; merge with ``lse_merge``."""
+    attention over this GPU's share of the context; merge with ``lse_merge``.
+    ``b0`` > 0: q holds sequences [b0, b0 + B) of the store's batch."""
     _require_cuda(q)
     if q.dim() == 4:
         q = q[:, :, 0]
     B, Hq, D = q.shape
     Hkv = (store or dense).kv_heads
+    for seg in (store, dense):
+        if seg is not None and b0 + B > seg.batch:
+            raise ValueError(f"sequences [{b0}, {b0 + B}) outside the batch of {seg.batch}")
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     out_o = out_o if out_o is not None else torch.empty(B, Hq, D, dtype=torch.float32, device=q.device)
     out_ml = out_ml if out_ml is not None else torch.empty(B, Hq, 2, dtype=torch.float32, device=q.device)
-    st = store.struct() if store is not None else None
-    ds = dense.struct() if dense is not None else None
+    st = store.struct(b0=b0) if store is not None else None
+    ds = dense.struct(b0=b0) if dense is not None else None
     pst = ctypes.byref(st) if st is not None else None
     pds = ctypes.byref(ds) if ds is not None else None
     lib = L.load()

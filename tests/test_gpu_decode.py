@@ -202,6 +202,47 @@ def test_partial_and_lse_merge_equal_full(hkv):
     assert ko.rel_err(out, ref) < 5e-4  # fp16 P rounding differs between split layouts
 
 
+@pytest.mark.parametrize("paged", [False, True])
+def test_partial_over_batch_slices(hkv, paged):
+    """decode_partial over sequences [b0, b1) (b0 > 0 views the store's pages or
+    page table, its lengths and the dense rows from sequence b0 on) equals the
+    attention of those sequences over the whole cache."""
+    B, Hkv, G, S, ND = 5, 2, 4, 700, 40
+    k, v = ko.make_kv(15, B, Hkv, S)
+    kd, vd = ko.make_kv(16, B, Hkv, ND)
+    mp_ = 3
+    if paged:
+        npages = 2 * B * Hkv * mp_
+        store = hkv.Int4KVStore(B, Hkv, S, fmt="fp16min", group=32, page_tokens=256, num_pages=npages)
+        perm = np.random.default_rng(2).permutation(npages)[: B * Hkv * mp_].reshape(B * Hkv, mp_)
+        store.page_table.copy_(torch.from_numpy(perm.astype(np.int32)))
+    else:
+        store = hkv.Int4KVStore(B, Hkv, S, fmt="fp16min", group=32, page_tokens=256)
+    hkv.prefill(store, t16(k), t16(v))
+    lens = np.array([700, 300, 512, 1, 650], np.int32)
+    store.set_lengths(torch.from_numpy(lens).cuda())
+    dense = hkv.DenseKV(B, Hkv, ND)
+    dense.k.copy_(t16(kd))
+    dense.v.copy_(t16(vd))
+    dlens = np.array([40, 7, 0, 33, 12], np.int32)
+    dense.lengths.copy_(torch.from_numpy(dlens).cuda())
+    dense.len_hint = ND
+    q = t16(ko.make_q(15, B, Hkv * G))
+    kb, vb = dequant_side(store, K, S), dequant_side(store, V, S)
+    for b0, b1 in ((0, 2), (2, 5), (3, 4), (4, 5)):
+        o, ml = hkv.decode_partial(q[b0:b1], store, dense, b0=b0)
+        out = hkv.lse_merge(o.unsqueeze(0), ml.unsqueeze(0)).cpu().numpy()
+        for i, b in enumerate(range(b0, b1)):
+            kk = np.concatenate([kb[b:b + 1, :, :lens[b]], kd[b:b + 1, :, :dlens[b]].astype(np.float16)
+                                 .astype(np.float32)], axis=2)
+            vv = np.concatenate([vb[b:b + 1, :, :lens[b]], vd[b:b + 1, :, :dlens[b]].astype(np.float16)
+                                 .astype(np.float32)], axis=2)
+            ref = ko.decode_attention(q[b:b + 1].float().cpu().numpy(), kk, vv)
+            assert ko.rel_err(out[i:i + 1], ref) < TOL, (paged, b0, b)
+    with pytest.raises(ValueError):
+        hkv.decode_partial(q[3:5], store, dense, b0=4)
+
+
 def test_append_then_decode_equals_oracle(hkv):
     """The decode-step state machine (ring eviction -> INT4) followed by attention."""
     B, Hkv, G, sink, ring = 2, 2, 4, 4, 60

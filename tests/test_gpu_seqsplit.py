@@ -1,7 +1,8 @@
 """Sequence-split decode over NCCL (config 4, variant B) on 2 GPUs: every rank
-holds one slice of each sequence's INT4 body (the last rank also the fp16
-segment); all-gathered partials merged by hkv_lse_merge equal the oracle's
-attention over the whole sequence. Skipped with fewer than 2 GPUs."""
+holds the byte-balanced span of each sequence's INT4 body pages and fp16 rows
+(``shard_spans``); all-gathered partials merged by hkv_lse_merge equal the
+oracle's attention over the whole sequence, eagerly, as a captured step and as
+a captured step pipelined over batch slices. Skipped with fewer than 2 GPUs."""
 import os
 
 import numpy as np
@@ -28,16 +29,19 @@ def _rank(rank, world, port, errs):
         kd = rng.standard_normal((B, Hkv, ND, 128)).astype(np.float16)
         vd = rng.standard_normal((B, Hkv, ND, 128)).astype(np.float16)
         q = rng.standard_normal((B, Hq, 128)).astype(np.float32)
-        p0, p1 = seqsplit.shard_range(S // 256, world, rank)
+        (p0, p1), (r0, r1) = seqsplit.shard_spans(S // 256, ND, world, rank, kv.page_bytes("fp16min", 32, 256),
+                                                   2 * 128 * 2)
         t0, t1 = p0 * 256, p1 * 256
-        st = kv.Int4KVStore(B, Hkv, max(t1 - t0, 1), fmt="fp16min", group=32, device=dev)
-        kv.prefill(st, torch.from_numpy(k[:, :, t0:t1]).to(dev), torch.from_numpy(v[:, :, t0:t1]).to(dev))
+        st = None
+        if t1 > t0:
+            st = kv.Int4KVStore(B, Hkv, t1 - t0, fmt="fp16min", group=32, device=dev)
+            kv.prefill(st, torch.from_numpy(k[:, :, t0:t1]).to(dev), torch.from_numpy(v[:, :, t0:t1]).to(dev))
         dense = None
-        if rank == world - 1:
-            dense = kv.DenseKV(B, Hkv, ND, device=dev)
-            dense.k.copy_(torch.from_numpy(kd))
-            dense.v.copy_(torch.from_numpy(vd))
-            dense.set_lengths(ND)
+        if r1 > r0:
+            dense = kv.DenseKV(B, Hkv, r1 - r0, device=dev)
+            dense.k.copy_(torch.from_numpy(kd[:, :, r0:r1]))
+            dense.v.copy_(torch.from_numpy(vd[:, :, r0:r1]))
+            dense.set_lengths(r1 - r0)
         qd = torch.from_numpy(q).to(dev).bfloat16()
         out = seqsplit.decode(qd, st, dense)
         torch.cuda.synchronize()
@@ -50,17 +54,24 @@ def _rank(rank, world, port, errs):
         ref = ko.decode_attention(qd.float().cpu().numpy(), kall, vall)
         err = np.abs(out.cpu().numpy() - ref).max(axis=-1) / np.linalg.norm(ref, axis=-1)
         # the graph-captured step (2 layers over the same slice, NCCL inside the
-        # graph, merge straight from the gathered buffer) gives the same bits
-        dec = seqsplit.SeqSplitDecoder([st, st], [dense, dense], B, Hq, device=dev)
+        # graph, merge straight from the gathered buffer) gives the same bits;
+        # pipelined over 2 batch slices (gathers on a side stream) it matches
+        # the oracle
         q2 = torch.stack([qd, qd])
-        o2 = torch.empty(2, B, Hq, 128, device=dev)
-        dec.capture(q2, o2)
-        o2.zero_()
-        dec.replay()
-        torch.cuda.synchronize()
-        same = torch.equal(o2[0], out) and torch.equal(o2[1], out)
-        dec.close()
-        errs[rank] = float(err.max()) if same else 1.0
+        for chunks in (1, 2):
+            dec = seqsplit.SeqSplitDecoder([st, st], [dense, dense], B, Hq, device=dev, chunks=chunks)
+            o2 = torch.empty(2, B, Hq, 128, device=dev)
+            dec.capture(q2, o2)
+            o2.zero_()
+            dec.replay()
+            torch.cuda.synchronize()
+            if chunks == 1 and not (torch.equal(o2[0], out) and torch.equal(o2[1], out)):
+                err[...] = 1.0
+            for l in range(2):
+                e = np.abs(o2[l].cpu().numpy() - ref).max(axis=-1) / np.linalg.norm(ref, axis=-1)
+                err = np.maximum(err, e)
+            dec.close()
+        errs[rank] = float(err.max())
     finally:
         dist.destroy_process_group()
 
@@ -81,10 +92,12 @@ def test_seqsplit_two_gpus():
         assert len(errs) == 2 and max(errs.values()) <= 2e-3, dict(errs)
 
 
-def test_seqsplit_decoder_one_gpu():
+@pytest.mark.parametrize("chunks", [1, 3])
+def test_seqsplit_decoder_one_gpu(chunks):
     """One rank: SeqSplitDecoder (partial into the send buffer, strided merge in
-    place, graph replay) equals seqsplit.decode bit for bit and the plain decode
-    within 2e-3 * ||ref||."""
+    place, graph replay) equals seqsplit.decode bit for bit (one slice) and the
+    plain decode within 2e-3 * ||ref|| (one slice, or three batch slices); a
+    layer with neither segment gives zeros."""
     from hetero_kvcache_optimizer_b200 import kvstore as kv, seqsplit
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev).manual_seed(5)
@@ -100,17 +113,19 @@ def test_seqsplit_decoder_one_gpu():
         d.set_lengths(ND)
         stores.append(st)
         denses.append(d)
-    q = torch.randn(Lyr, B, Hq, 128, device=dev, generator=gen).bfloat16()
-    out = torch.empty(Lyr, B, Hq, 128, device=dev)
-    dec = seqsplit.SeqSplitDecoder(stores, denses, B, Hq, device=dev)
+    q = torch.randn(Lyr + 1, B, Hq, 128, device=dev, generator=gen).bfloat16()
+    out = torch.empty(Lyr + 1, B, Hq, 128, device=dev)
+    dec = seqsplit.SeqSplitDecoder(stores + [None], denses + [None], B, Hq, device=dev, chunks=chunks)
     dec.capture(q, out)
-    out.zero_()
+    out.fill_(7.0)
     dec.replay()
     torch.cuda.synchronize()
     for l in range(Lyr):
-        eager = seqsplit.decode(q[l], stores[l], denses[l])
-        assert torch.equal(out[l], eager), l
+        if chunks == 1:
+            eager = seqsplit.decode(q[l], stores[l], denses[l])
+            assert torch.equal(out[l], eager), l
         ref = kv.decode(q[l], stores[l], denses[l])
         err = ((out[l] - ref).abs().amax(-1) / ref.norm(dim=-1)).max().item()
         assert err < 2e-3, (l, err)
+    assert torch.equal(out[Lyr], torch.zeros_like(out[Lyr]))
     dec.close()

@@ -11,7 +11,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from hetero_kvcache_optimizer_b200.seqsplit import all_gather_partials, shard_range
+from hetero_kvcache_optimizer_b200.seqsplit import all_gather_partials, shard_range, shard_spans
 from oracle import kv_oracle as ko
 
 
@@ -24,6 +24,29 @@ def test_shard_ranges_tile_the_body(world):
             assert a1 == b0
         sizes = [b - a for a, b in spans]
         assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 7, 8])
+def test_shard_spans_tile_both_segments(world):
+    """Byte-balanced spans: both segments tiled in rank order, every rank's
+    bytes within one page (or row) of the equal share, and at most one rank
+    that holds both a body slice and dense rows."""
+    pb, rb = 40960, 512
+    for pages in (0, 1, 3, 11, 59, 507):
+        for rows in (0, 1, 100, 1088):
+            if pages == rows == 0:
+                continue
+            spans = [shard_spans(pages, rows, world, r, pb, rb) for r in range(world)]
+            assert spans[0][0][0] == 0 and spans[-1][0][1] == pages
+            assert spans[0][1][0] == 0 and spans[-1][1][1] == rows
+            for ((p0, p1), (r0, r1)), ((q0, q1), (s0, s1)) in zip(spans, spans[1:]):
+                assert p1 == q0 and r1 == s0
+            share = (pages * pb + rows * rb) / world
+            for (p0, p1), (r0, r1) in spans:
+                assert p1 >= p0 and r1 >= r0
+                assert abs((p1 - p0) * pb + (r1 - r0) * rb - share) <= pb + rb
+            both = sum(1 for (p0, p1), (r0, r1) in spans if p1 > p0 and r1 > r0)
+            assert both <= 1, spans
 
 
 def _partials(q, k, v, scale):
